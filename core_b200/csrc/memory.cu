@@ -1,0 +1,639 @@
+// Latent-memory write and decayed recurrence
+// (replaces core/kvpress_adapter.py:1041-1202, pre_o_proj value space).
+//
+//   mw_mass_kernel   : p = softmax(s / tau) over the whole cache, pi_E = sum of
+//                      p over evicted tokens, p_bar = p / pi_E on the evicted
+//                      list (core/indexer.py:55-72, :247-273); Z <- gamma Z + pi_E.
+//   mw_phi_kernel    : phi = K_ev Theta_f^T for 128 gathered evicted tokens on
+//                      tcgen05 (K rows gathered with cp.async into swizzled
+//                      shared memory, Theta_f as two bf16 terms, K exact in
+//                      bf16), epilogue W = p_bar * phi written as bf16 hi/lo in
+//                      (d_mem, token) order, and per-tile column sums of
+//                      p_bar * phi^2 (b_bar partials).
+//   mw_mbar_kernel   : M_bar partial = W^T V_ev on tcgen05 (A = W tiles by TMA,
+//                      B = gathered V rows, MN-major), split over token chunks.
+//   mw_update_kernel : M, b <- (gamma Z M + pi_E eta M_bar) / (Z' + eps).
+#include <cmath>
+
+#include "common.cuh"
+#include "host_util.h"
+
+namespace core {
+namespace mw {
+
+constexpr int kD = 128;
+constexpr int kTok = 128;         // evicted tokens per phi tile
+constexpr int kNCols = 256;       // d_mem columns per phi unit (MMA N)
+constexpr int kProdThreads = 128; // 4 gathering warps
+constexpr int kMbarChunk = 64;    // tokens per M_bar K chunk
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void st_shared_zero16(uint32_t dst) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
+}
+
+// ===========================================================================
+// softmax mass
+// ===========================================================================
+__global__ void __launch_bounds__(1024)
+    mw_mass_kernel(const float* __restrict__ scores, int L, const int* __restrict__ evict,
+                   int n_evict, int n_ev_pad, float inv_tau_num, float tau, float gamma,
+                   float* __restrict__ Z, float* __restrict__ pbar, float* __restrict__ coef,
+                   DeviceStatus* status) {
+  const int b = blockIdx.x;
+  const float* s = scores + (long long)b * L;
+  __shared__ float red[32];
+  __shared__ double redd[32];
+  __shared__ float s_max, s_sum;
+  __shared__ double s_pie;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  (void)inv_tau_num;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < L; i += blockDim.x) m = fmaxf(m, s[i] / tau);
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = red[0];
+    for (int w = 1; w < (int)(blockDim.x / 32); ++w) mm = fmaxf(mm, red[w]);
+    s_max = mm;
+  }
+  __syncthreads();
+  const float mx = s_max;
+  double sum = 0.0;
+  for (int i = threadIdx.x; i < L; i += blockDim.x) sum += (double)expf(s[i] / tau - mx);
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) redd[warp] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x / 32); ++w) t += redd[w];
+    s_sum = (float)t;
+  }
+  __syncthreads();
+  const float tot = s_sum;
+  const int* ev = evict + (long long)b * n_evict;
+  double pe = 0.0;
+  for (int k = threadIdx.x; k < n_evict; k += blockDim.x) {
+    const float p = expf(s[ev[k]] / tau - mx) / tot;
+    pe += (double)p;
+  }
+  for (int o = 16; o > 0; o >>= 1) pe += __shfl_xor_sync(0xffffffffu, pe, o);
+  if (lane == 0) redd[warp] = pe;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x / 32); ++w) t += redd[w];
+    s_pie = t;
+  }
+  __syncthreads();
+  const float pie = (float)s_pie;
+  const float mass = pie > 0.f ? pie : 1.0f;
+  float* pb = pbar + (long long)b * n_ev_pad;
+  for (int k = threadIdx.x; k < n_ev_pad; k += blockDim.x) {
+    float v = 0.f;
+    if (k < n_evict) v = (expf(s[ev[k]] / tau - mx) / tot) / mass;
+    pb[k] = v;
+  }
+  if (threadIdx.x == 0) {
+    const float gz = gamma * Z[b];
+    const float zt = gz + pie;
+    coef[b * 3 + 0] = gz;
+    coef[b * 3 + 1] = pie;
+    coef[b * 3 + 2] = zt + 1e-8f;
+    Z[b] = zt;
+    if (!isfinite(pie) || !isfinite(tot)) record_error(status, CORE_ERR_NONFINITE, 801, b);
+  }
+}
+
+// ===========================================================================
+// phi tile: W = p_bar * (K_ev Theta_f^T), b_bar partials
+// ===========================================================================
+struct PhiParams {
+  int B, Hkv, L, n_evict, n_ev_pad, n_et, d_mem, d_pad, n_dh;
+  long long U;
+  const __nv_bfloat16* k;
+  const int* evict;
+  const float* pbar;
+  __nv_bfloat16* wt;   // (2, d_pad, n_ev_pad)
+  float* bpart;        // (B, n_et, d_pad)
+  DeviceStatus* status;
+};
+
+constexpr uint32_t kPhiA = kTok * 128;          // 16 KB: 128 tokens x 64 columns
+constexpr uint32_t kPhiB = 2u * kNCols * 128;   // 64 KB: two terms x 256 rows x 64 columns
+constexpr uint32_t kPhiStage = kPhiA + kPhiB;
+constexpr int kPhiStages = 2;
+constexpr int kPhiThreads = 512;  // warps 0-3 gather, 4 MMA, 8-15 epilogue
+
+__global__ void __launch_bounds__(kPhiThreads, 1)
+    mw_phi_kernel(const __grid_constant__ CUtensorMap tmT, const PhiParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  const uint32_t red_off = kPhiStages * kPhiStage;            // float [4][256]
+  float* s_red = reinterpret_cast<float*>(sgen + red_off);
+  const uint32_t bar = sbase + red_off + 4 * kNCols * 4;
+  auto bar_full = [&](int s) { return bar + 8u * s; };
+  auto bar_empty = [&](int s) { return bar + 8u * (kPhiStages + s); };
+  auto bar_tfull = [&](int s) { return bar + 8u * (2 * kPhiStages + s); };
+  auto bar_tempty = [&](int s) { return bar + 8u * (2 * kPhiStages + 2 + s); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + red_off + 4 * kNCols * 4 + 200);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + red_off + 4 * kNCols * 4 + 208);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int P = gridDim.x;
+  const long long u0 = (long long)blockIdx.x * p.U / P, u1 = (long long)(blockIdx.x + 1) * p.U / P;
+  const int n_chunks = p.Hkv * 2;  // 64-column K chunks of the 1024-wide key row
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPhiStages; ++s) {
+      mbar_init(bar_full(s), 1 + kProdThreads / 32);  // TMA expect_tx + 4 gather warps
+      mbar_init(bar_empty(s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_tfull(s), 1);
+      mbar_init(bar_tempty(s), 8);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto wait = [&](uint32_t b, uint32_t parity, int where) -> bool {
+    return bounded_wait(b, parity, abort_flag, p.status, where);
+  };
+
+  if (warp < 4) {
+    // ---- producers: gather K rows with cp.async; thread 0 also loads Theta by TMA ----
+    const int tid = threadIdx.x;
+    int it = 0;
+    bool ok = true;
+    for (long long u = u0; u < u1 && ok; ++u) {
+      const int dh = (int)(u % p.n_dh);
+      const long long rest = u / p.n_dh;
+      const int et = (int)(rest % p.n_et), b = (int)(rest / p.n_et);
+      for (int c = 0; c < n_chunks && ok; ++c, ++it) {
+        const int st = it % kPhiStages;
+        if (it >= kPhiStages) {
+          if (!(ok = wait(bar_empty(st), ((it / kPhiStages) - 1) & 1, 901))) break;
+        }
+        const uint32_t a_base = sbase + st * kPhiStage;
+        if (tid == 0) {
+          mbar_arrive_expect_tx(bar_full(st), kPhiB);
+          for (int t = 0; t < 2; ++t)
+            tma_load_3d(a_base + kPhiA + t * (kNCols * 128u), &tmT, bar_full(st), c * 64,
+                        dh * kNCols, t);
+        }
+        const int h = c >> 1, e0 = (c & 1) * 64;
+        // 128 rows x 8 sixteen-byte pieces = 1024 copies, 8 per thread
+        for (int j = tid; j < kTok * 8; j += kProdThreads) {
+          const int r = j >> 3, q = j & 7;
+          const uint32_t dst = a_base + (uint32_t)r * 128u + (uint32_t)((q ^ (r & 7)) << 4);
+          const int kidx = et * kTok + r;
+          if (kidx < p.n_evict) {
+            const int tok = p.evict[(long long)b * p.n_evict + kidx];
+            cp_async16(dst, p.k + (((long long)b * p.Hkv + h) * p.L + tok) * kD + e0 + q * 8);
+          } else {
+            st_shared_zero16(dst);
+          }
+        }
+        cp_async_commit();
+        cp_async_wait_all();
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_full(st));
+      }
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, kNCols, 0, 0);
+      int it = 0, sub = 0;
+      bool ok = true;
+      for (long long u = u0; u < u1 && ok; ++u, ++sub) {
+        const int buf = sub & 1, n = sub >> 1;
+        if (sub >= 2 && !(ok = wait(bar_tempty(buf), (n - 1) & 1, 902))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * kNCols);
+        for (int c = 0; c < n_chunks && ok; ++c, ++it) {
+          const int st = it % kPhiStages;
+          if (!(ok = wait(bar_full(st), (it / kPhiStages) & 1, 903))) break;
+          tc_fence_after();
+          const uint32_t a_base = sbase + st * kPhiStage;
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t a = sdesc_kmajor(a_base + (uint32_t)ks * 32u);
+            for (int t = 0; t < 2; ++t) {
+              const uint64_t bd = sdesc_kmajor(a_base + kPhiA + (uint32_t)t * kNCols * 128u + (uint32_t)ks * 32u);
+              mma_bf16(d, a, bd, idesc, (c > 0 || ks > 0 || t > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(bar_empty(st));
+        }
+        if (ok) mma_commit(bar_tfull(buf));
+      }
+    }
+  } else if (warp >= 8) {
+    const int ew = warp - 8;
+    const int team = ew >> 2;       // column half: 0 -> 0..127, 1 -> 128..255
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    int sub = 0;
+    bool ok = true;
+    for (long long u = u0; u < u1 && ok; ++u, ++sub) {
+      const int dh = (int)(u % p.n_dh);
+      const long long rest = u / p.n_dh;
+      const int et = (int)(rest % p.n_et), b = (int)(rest / p.n_et);
+      const int buf = sub & 1, n = sub >> 1;
+      if (!(ok = wait(bar_tfull(buf), n & 1, 904))) break;
+      tc_fence_after();
+      const int kidx = et * kTok + row;
+      const float pb = p.pbar[(long long)b * p.n_ev_pad + kidx];  // 0 on padding rows
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int col0 = team * 128 + q4 * 32;
+        if (dh * kNCols + col0 >= p.d_pad) continue;  // padding columns of the last unit
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * kNCols + col0), v);
+        const int jbase = dh * kNCols + col0;
+        float u2[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float phi = v[j];
+          const float w = phi * pb;                 // phi * w (kvpress_adapter.py:1155)
+          u2[j] = (phi * phi) * pb;                 // (phi*phi) * w (:1157)
+          const __nv_bfloat16 hi = __float2bfloat16_rn(w);
+          const __nv_bfloat16 lo = __float2bfloat16_rn(w - __bfloat162float(hi));
+          const long long o = (long long)(jbase + j) * p.n_ev_pad + kidx;
+          p.wt[o] = hi;
+          p.wt[(long long)p.d_pad * p.n_ev_pad + o] = lo;
+        }
+        // column sums over the warp's 32 tokens: lane j ends with column j
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+          for (int j = 0; j < off; ++j) {
+            const bool upper = (lane & off) != 0;
+            const float send = upper ? u2[j] : u2[j + off];
+            const float keep = upper ? u2[j + off] : u2[j];
+            u2[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          }
+        }
+        s_red[wq * kNCols + col0 + lane] = u2[0];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_tempty(buf));
+      named_barrier(1, 256);
+      // fixed-order reduction of the four lane quarters
+      for (int cidx = threadIdx.x - 256; cidx < kNCols && dh * kNCols + cidx < p.d_pad; cidx += 256) {
+        const float s = ((s_red[cidx] + s_red[kNCols + cidx]) + s_red[2 * kNCols + cidx]) +
+                        s_red[3 * kNCols + cidx];
+        p.bpart[((long long)b * p.n_et + et) * p.d_pad + dh * kNCols + cidx] = s;
+      }
+      named_barrier(1, 256);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// M_bar partial = W^T V_ev over one token range, one (128 x 256) output tile
+// ===========================================================================
+struct MbarParams {
+  int Hkv, L, n_evict, n_ev_pad, d_pad, kvw, n_jt, n_ct, splits;
+  long long split_stride;  // elements between consecutive splits of mpart
+  const __nv_bfloat16* v;  // this batch row's values (Hkv, L, d)
+  const int* evict;        // this batch row's evicted indices
+  float* mpart;            // this batch row's (d_pad, kvw) slice of split 0
+  DeviceStatus* status;
+};
+
+constexpr uint32_t kMbA = 2u * 128 * 128;           // two terms x 128 rows x 64 tokens
+constexpr uint32_t kMbBMax = 4u * kMbarChunk * 128; // up to 4 MN atoms x 64 token rows x 128 B
+constexpr uint32_t kMbStage = kMbA + kMbBMax;       // 64 KB
+constexpr int kMbStages = 3;
+constexpr int kMbThreads = 384;  // warps 0-3 gather, 4 MMA, 8-11 epilogue
+
+// CT = value columns per output tile (256, or 128 when Hkv*d is an odd
+// multiple of 128).
+template <int CT>
+__global__ void __launch_bounds__(kMbThreads, 1)
+    mw_mbar_kernel(const __grid_constant__ CUtensorMap tmW, const MbarParams p) {
+  constexpr int kAtoms = CT / 64;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  const uint32_t bar = sbase + kMbStages * kMbStage;
+  auto bar_full = [&](int s) { return bar + 8u * s; };
+  auto bar_empty = [&](int s) { return bar + 8u * (kMbStages + s); };
+  const uint32_t bar_done = bar + 8u * (2 * kMbStages);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + kMbStages * kMbStage + 200);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + kMbStages * kMbStage + 208);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // unit = (split, jt, ct), one per CTA
+  long long u = blockIdx.x;
+  const int ct = (int)(u % p.n_ct); u /= p.n_ct;
+  const int jt = (int)(u % p.n_jt);
+  const int split = (int)(u / p.n_jt);
+  const int n_kc = p.n_ev_pad / kMbarChunk;
+  const int kc0 = (int)((long long)split * n_kc / p.splits);
+  const int kc1 = (int)((long long)(split + 1) * n_kc / p.splits);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kMbStages; ++s) {
+      mbar_init(bar_full(s), 1 + kProdThreads / 32);
+      mbar_init(bar_empty(s), 1);
+    }
+    mbar_init(bar_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  static_assert(CT == 128 || CT == 256, "tile width");
+  auto wait = [&](uint32_t bb, uint32_t parity, int where) -> bool {
+    return bounded_wait(bb, parity, abort_flag, p.status, where);
+  };
+
+  if (warp < 4) {
+    const int tid = threadIdx.x;
+    bool ok = true;
+    for (int kc = kc0, it = 0; kc < kc1 && ok; ++kc, ++it) {
+      const int st = it % kMbStages;
+      if (it >= kMbStages && !(ok = wait(bar_empty(st), ((it / kMbStages) - 1) & 1, 911))) break;
+      const uint32_t base = sbase + st * kMbStage;
+      if (tid == 0) {
+        mbar_arrive_expect_tx(bar_full(st), kMbA);
+        for (int t = 0; t < 2; ++t)
+          tma_load_2d(base + t * (128u * 128u), &tmW, bar_full(st), kc * kMbarChunk,
+                      t * p.d_pad + jt * 128);
+      }
+      // 64 token rows x kAtoms MN atoms x 8 pieces
+      for (int j = tid; j < kMbarChunk * kAtoms * 8; j += kProdThreads) {
+        const int r = j / (kAtoms * 8), a = (j >> 3) % kAtoms, q = j & 7;
+        const uint32_t dst = base + kMbA + (uint32_t)a * (kMbarChunk * 128u) + (uint32_t)r * 128u +
+                             (uint32_t)((q ^ (r & 7)) << 4);
+        const int kidx = kc * kMbarChunk + r;
+        if (kidx < p.n_evict) {
+          const int tok = p.evict[kidx];
+          const int col = ct * CT + a * 64 + q * 8;  // column of the (Hkv*d) value row
+          const int h = col >> 7, e = col & 127;
+          cp_async16(dst, p.v + ((long long)h * p.L + tok) * kD + e);
+        } else {
+          st_shared_zero16(dst);
+        }
+      }
+      cp_async_commit();
+      cp_async_wait_all();
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_full(st));
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, CT, 0, 1);
+      bool ok = true;
+      for (int kc = kc0, it = 0; kc < kc1 && ok; ++kc, ++it) {
+        const int st = it % kMbStages;
+        if (!(ok = wait(bar_full(st), (it / kMbStages) & 1, 912))) break;
+        tc_fence_after();
+        const uint32_t base = sbase + st * kMbStage;
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint64_t bd = sdesc_sw128(base + kMbA + (uint32_t)ks * (16u * 128u),
+                                          kMbarChunk * 128u, 1024u);
+          for (int t = 0; t < 2; ++t) {
+            const uint64_t a = sdesc_kmajor(base + (uint32_t)t * (128u * 128u) + (uint32_t)ks * 32u);
+            mma_bf16(tmem, a, bd, idesc, (it > 0 || ks > 0 || t > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(bar_empty(st));
+      }
+      mma_commit(bar_done);
+    }
+  } else if (warp >= 8) {
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const bool has_work = kc1 > kc0;
+    bool ok = true;
+    if (has_work) ok = wait(bar_done, 0, 913);
+    tc_fence_after();
+    float* dst = p.mpart + (long long)split * p.split_stride + ((long long)jt * 128 + row) * p.kvw + ct * CT;
+    for (int q = 0; q < CT / 32 && ok; ++q) {
+      float v[32];
+      if (has_work) {
+        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(q * 32), v);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      }
+      float4* d4 = reinterpret_cast<float4*>(dst + q * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ===========================================================================
+// recurrence
+// ===========================================================================
+__global__ void mw_update_kernel(const float* __restrict__ mpart, int splits, int B, int d_mem,
+                                 int d_pad, int kvw, const float* __restrict__ bpart, int n_et,
+                                 const float* __restrict__ coef, float eta, float* __restrict__ M,
+                                 float* __restrict__ bst) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long nM = (long long)B * d_mem * kvw;
+  if (i < nM) {
+    const int c = (int)(i % kvw);
+    const long long bj = i / kvw;
+    const int j = (int)(bj % d_mem);
+    const int b = (int)(bj / d_mem);
+    float s = 0.f;
+    for (int sp = 0; sp < splits; ++sp)
+      s += mpart[(((long long)sp * B + b) * d_pad + j) * kvw + c];
+    const float mbar = s * eta;
+    const float gz = coef[b * 3], pie = coef[b * 3 + 1], den = coef[b * 3 + 2];
+    M[i] = (gz * M[i] + pie * mbar) / den;
+  }
+  const long long nb = (long long)B * d_mem;
+  if (i < nb) {
+    const int j = (int)(i % d_mem);
+    const int b = (int)(i / d_mem);
+    float s = 0.f;
+    for (int t = 0; t < n_et; ++t) s += bpart[((long long)b * n_et + t) * d_pad + j];
+    const float bbar = s * eta;
+    const float gz = coef[b * 3], pie = coef[b * 3 + 1], den = coef[b * 3 + 2];
+    bst[i] = (gz * bst[i] + pie * bbar) / den;
+  }
+}
+
+}  // namespace mw
+}  // namespace core
+
+using namespace core;
+using namespace core::mw;
+
+namespace {
+struct MwPlan {
+  int n_ev_pad, n_et, d_pad, n_dh, kvw, splits, n_jt, n_ct, ct, phi_grid;
+  long long phi_units;
+};
+void plan_mw(const core_dims_t* d, int n_evict, int d_mem, MwPlan* m) {
+  m->n_et = (n_evict + kTok - 1) / kTok;
+  m->n_ev_pad = m->n_et * kTok;
+  m->d_pad = ((d_mem + 127) / 128) * 128;
+  m->n_dh = (m->d_pad + kNCols - 1) / kNCols;
+  m->kvw = d->n_kv_heads * kD;
+  m->phi_units = (long long)d->batch * m->n_et * m->n_dh;
+  const int sms = sm_count();
+  m->phi_grid = (int)(m->phi_units < sms ? m->phi_units : sms);
+  m->n_jt = m->d_pad / 128;
+  m->ct = (m->kvw % 256 == 0) ? 256 : 128;
+  m->n_ct = m->kvw / m->ct;
+  const long long tiles = (long long)m->n_jt * m->n_ct;
+  const int n_kc = m->n_ev_pad / kMbarChunk;
+  int splits = (int)((sms + tiles - 1) / tiles);
+  if (splits > n_kc) splits = n_kc;
+  if (splits < 1) splits = 1;
+  m->splits = splits;
+}
+}  // namespace
+
+extern "C" size_t core_memory_write_workspace_bytes(const core_dims_t* d, int32_t n_evict,
+                                                    int32_t d_mem) {
+  if (check_dims(d, "core_memory_write_workspace_bytes") != CORE_OK || n_evict <= 0 || d_mem <= 0)
+    return 0;
+  MwPlan m;
+  plan_mw(d, n_evict, d_mem, &m);
+  Sizer z;
+  z.take<float>((size_t)d->batch * m.n_ev_pad);                         // p_bar
+  z.take<float>((size_t)d->batch * 3);                                  // coefficients
+  z.take<__nv_bfloat16>((size_t)2 * m.d_pad * m.n_ev_pad);              // W^T (one batch row at a time)
+  z.take<float>((size_t)d->batch * m.n_et * m.d_pad);                   // b_bar partials
+  z.take<float>((size_t)m.splits * d->batch * m.d_pad * m.kvw);         // M_bar partials
+  return z.used;
+}
+
+extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void* v,
+                                 const float* scores_cal, const int32_t* evict_idx,
+                                 int32_t n_evict, const void* theta_split, int32_t d_mem,
+                                 float gamma, float eta, float student_temp, float* M,
+                                 float* b_state, float* Z, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  int rc = check_dims(d, "core_memory_write");
+  if (rc != CORE_OK) return rc;
+  if (k == nullptr || v == nullptr || scores_cal == nullptr || evict_idx == nullptr ||
+      theta_split == nullptr || M == nullptr || b_state == nullptr || Z == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_memory_write: NULL tensor");
+  if (n_evict <= 0 || n_evict > d->seq_len)
+    return set_error(CORE_ERR_INVALID_ARG, "core_memory_write: bad n_evict");
+  if (d_mem <= 0 || d_mem > 4096 || (d_mem % 8) != 0)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_memory_write: d_mem must be a positive multiple of 8");
+  if (!(student_temp > 0.f)) return set_error(CORE_ERR_INVALID_ARG, "student_temp must be > 0");
+  MwPlan m;
+  plan_mw(d, n_evict, d_mem, &m);
+  Carver cv(workspace, workspace_bytes);
+  float* pbar = cv.take<float>((size_t)d->batch * m.n_ev_pad);
+  float* coef = cv.take<float>((size_t)d->batch * 3);
+  __nv_bfloat16* wt = cv.take<__nv_bfloat16>((size_t)2 * m.d_pad * m.n_ev_pad);
+  float* bpart = cv.take<float>((size_t)d->batch * m.n_et * m.d_pad);
+  float* mpart = cv.take<float>((size_t)m.splits * d->batch * m.d_pad * m.kvw);
+  if (cv.overflow) return set_error(CORE_ERR_WORKSPACE, "core_memory_write: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceStatus* st = device_status();
+  cudaError_t e;
+
+  mw_mass_kernel<<<d->batch, 1024, 0, s>>>(scores_cal, d->seq_len, evict_idx, n_evict, m.n_ev_pad,
+                                           0.f, student_temp, gamma, Z, pbar, coef, st);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_mass_kernel launch");
+
+  CUtensorMap tmT;
+  {
+    const uint64_t kvw = (uint64_t)m.kvw;
+    uint64_t dims[3] = {kvw, (uint64_t)d_mem, 2};
+    uint64_t str[2] = {kvw * 2, kvw * 2 * (uint64_t)d_mem};
+    uint32_t box[3] = {64, (uint32_t)kNCols, 1};
+    if ((rc = make_tmap_bf16(&tmT, theta_split, 3, dims, str, box, true)) != CORE_OK) return rc;
+  }
+  // W^T is (2, d_pad, n_ev_pad); each batch row reuses the same buffer, so
+  // rows run one after another (phi of row b, then M_bar of row b).
+  CUtensorMap tmW;
+  {
+    uint64_t dims[2] = {(uint64_t)m.n_ev_pad, (uint64_t)2 * m.d_pad};
+    uint64_t str[1] = {(uint64_t)m.n_ev_pad * 2};
+    uint32_t box[2] = {64, 128};
+    if ((rc = make_tmap_bf16(&tmW, wt, 2, dims, str, box, true)) != CORE_OK) return rc;
+  }
+  const uint32_t phi_smem = kPhiStages * kPhiStage + 4 * kNCols * 4 + 256 + 1024;
+  e = cudaFuncSetAttribute(mw_phi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, phi_smem);
+  if (e != cudaSuccess) return cuda_error(e, "mw_phi_kernel attribute");
+  const uint32_t mb_smem = kMbStages * kMbStage + 256 + 1024;
+  e = cudaFuncSetAttribute(mw_mbar_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, mb_smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(mw_mbar_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, mb_smem);
+  if (e != cudaSuccess) return cuda_error(e, "mw_mbar_kernel attribute");
+
+  for (int b = 0; b < d->batch; ++b) {
+    PhiParams pp{};
+    pp.B = 1; pp.Hkv = d->n_kv_heads; pp.L = d->seq_len; pp.n_evict = n_evict;
+    pp.n_ev_pad = m.n_ev_pad; pp.n_et = m.n_et; pp.d_mem = d_mem; pp.d_pad = m.d_pad;
+    pp.n_dh = m.n_dh;
+    pp.U = (long long)m.n_et * m.n_dh;
+    pp.k = static_cast<const __nv_bfloat16*>(k) + (long long)b * d->n_kv_heads * d->seq_len * kD;
+    pp.evict = evict_idx + (long long)b * n_evict;
+    pp.pbar = pbar + (long long)b * m.n_ev_pad;
+    pp.wt = wt;
+    pp.bpart = bpart + (long long)b * m.n_et * m.d_pad;
+    pp.status = st;
+    const int sms = sm_count();
+    const int grid = (int)(pp.U < sms ? pp.U : sms);
+    mw_phi_kernel<<<grid, kPhiThreads, phi_smem, s>>>(tmT, pp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_phi_kernel launch");
+
+    MbarParams mq{};
+    mq.Hkv = d->n_kv_heads; mq.L = d->seq_len; mq.n_evict = n_evict;
+    mq.n_ev_pad = m.n_ev_pad; mq.d_pad = m.d_pad; mq.kvw = m.kvw; mq.n_jt = m.n_jt;
+    mq.n_ct = m.n_ct; mq.splits = m.splits;
+    mq.split_stride = (long long)d->batch * m.d_pad * m.kvw;
+    mq.v = static_cast<const __nv_bfloat16*>(v) + (long long)b * d->n_kv_heads * d->seq_len * kD;
+    mq.evict = evict_idx + (long long)b * n_evict;
+    mq.mpart = mpart + (long long)b * m.d_pad * m.kvw;
+    mq.status = st;
+    if (m.ct == 256)
+      mw_mbar_kernel<256><<<(unsigned)(m.splits * m.n_jt * m.n_ct), kMbThreads, mb_smem, s>>>(tmW, mq);
+    else
+      mw_mbar_kernel<128><<<(unsigned)(m.splits * m.n_jt * m.n_ct), kMbThreads, mb_smem, s>>>(tmW, mq);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_mbar_kernel launch");
+  }
+  const long long n = (long long)d->batch * d_mem * m.kvw;
+  mw_update_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(mpart, m.splits, d->batch, d_mem, m.d_pad,
+                                                             m.kvw, bpart, m.n_et, coef, eta, M, b_state);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_update_kernel launch");
+  return CORE_OK;
+}

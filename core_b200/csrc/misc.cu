@@ -1,0 +1,242 @@
+// Retained-KV gather (replaces core/kvpress_adapter.py:1204-1210) and the
+// gated latent-memory readout (replaces core/indexer.py:165-207 and
+// core/kvpress_adapter.py:1302-1352).
+#include <cmath>
+
+#include "common.cuh"
+#include "host_util.h"
+
+namespace core {
+namespace misc {
+
+constexpr int kD = 128;
+
+// out[b, h, j, :] = in[b, h, keep[b, j], :]; a half-warp moves one 256-byte row
+// with 16-byte accesses.
+__global__ void compact_kernel(const uint4* __restrict__ k, const uint4* __restrict__ v,
+                               const int* __restrict__ keep, int Hkv, int L, int n_kept,
+                               uint4* __restrict__ ok, uint4* __restrict__ ov) {
+  const long long rows = (long long)gridDim.y * Hkv * n_kept;  // gridDim.y = B
+  const int b = blockIdx.y;
+  const long long per_b = (long long)Hkv * n_kept;
+  for (long long r = (long long)blockIdx.x * (blockDim.x / 16) + (threadIdx.x >> 4); r < per_b;
+       r += (long long)gridDim.x * (blockDim.x / 16)) {
+    const int h = (int)(r / n_kept), j = (int)(r % n_kept);
+    const int src = keep[(long long)b * n_kept + j];
+    const int q = threadIdx.x & 15;
+    const long long si = (((long long)b * Hkv + h) * L + src) * 16 + q;
+    const long long di = (((long long)b * Hkv + h) * n_kept + j) * 16 + q;
+    ok[di] = k[si];
+    ov[di] = v[si];
+  }
+  (void)rows;
+}
+
+__device__ __forceinline__ float gelu(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+// Stage 1: proj = Theta q (d_mem rows) and gate pre-activations W1 q + c1 (gh
+// rows).  One warp per weight row, all q_len queries at once.
+__global__ void readout_proj_kernel(const __nv_bfloat16* __restrict__ q, int Hq, int q_len,
+                                    const float* __restrict__ theta, const float* __restrict__ gw1,
+                                    const float* __restrict__ gb1, int d_mem, int gh,
+                                    float* __restrict__ proj, float* __restrict__ gpre) {
+  extern __shared__ float sq[];  // (q_len, Hq*d) f32 of this batch row
+  const int b = blockIdx.y;
+  const int dm = Hq * kD;
+  for (int i = threadIdx.x; i < q_len * dm; i += blockDim.x) {
+    const int t = i / dm, c = i % dm;
+    const int qh = c / kD, e = c % kD;
+    sq[i] = __bfloat162float(q[(((long long)b * Hq + qh) * q_len + t) * kD + e]);
+  }
+  __syncthreads();
+  const int warps = blockDim.x / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = blockIdx.x * warps + warp; r < d_mem + gh; r += gridDim.x * warps) {
+    const float* w = (r < d_mem) ? theta + (long long)r * dm : gw1 + (long long)(r - d_mem) * dm;
+    for (int t = 0; t < q_len; ++t) {
+      const float* x = sq + t * dm;
+      float acc = 0.f;
+      for (int c = lane * 4; c < dm; c += 128) {
+        const float4 ww = *reinterpret_cast<const float4*>(w + c);
+        acc = fmaf(ww.x, x[c], acc);
+        acc = fmaf(ww.y, x[c + 1], acc);
+        acc = fmaf(ww.z, x[c + 2], acc);
+        acc = fmaf(ww.w, x[c + 3], acc);
+      }
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) {
+        if (r < d_mem) proj[((long long)b * q_len + t) * d_mem + r] = acc;
+        else gpre[((long long)b * q_len + t) * gh + (r - d_mem)] = acc + gb1[r - d_mem];
+      }
+    }
+  }
+}
+
+// Stage 2: m = proj M / sqrt(proj^2 . b + eps), gate, residual rounded to bf16.
+__global__ void readout_mem_kernel(const float* __restrict__ proj, const float* __restrict__ gpre,
+                                   const float* __restrict__ gw2, const float* __restrict__ gb2,
+                                   float gate_override, const float* __restrict__ M,
+                                   const float* __restrict__ bst, int q_len, int d_mem, int gh,
+                                   int kvw, float* __restrict__ res) {
+  extern __shared__ float sp[];  // proj (d_mem) of this (b, t)
+  __shared__ float s_den, s_g;
+  const int b = blockIdx.y, t = blockIdx.z;
+  const float* pr = proj + ((long long)b * q_len + t) * d_mem;
+  for (int j = threadIdx.x; j < d_mem; j += blockDim.x) sp[j] = pr[j];
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float den = 0.f;
+    for (int j = threadIdx.x; j < d_mem; j += 32) den = fmaf(sp[j] * sp[j], bst[(long long)b * d_mem + j], den);
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    float gl = 0.f;
+    for (int o = threadIdx.x; o < gh; o += 32)
+      gl = fmaf(gw2[o], gelu(gpre[((long long)b * q_len + t) * gh + o]), gl);
+    for (int o = 16; o > 0; o >>= 1) gl += __shfl_xor_sync(0xffffffffu, gl, o);
+    if (threadIdx.x == 0) {
+      s_den = den + 1e-8f;
+      s_g = gate_override >= 0.f ? gate_override : 1.0f / (1.0f + expf(-(gl + gb2[0])));
+    }
+  }
+  __syncthreads();
+  const float rs = 1.0f / sqrtf(s_den);
+  const float g = s_g;
+  const float* Mb = M + (long long)b * d_mem * kvw;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < kvw; c += gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < d_mem; ++j) acc = fmaf(sp[j], Mb[(long long)j * kvw + c], acc);
+    const float m = acc * rs;
+    res[((long long)b * q_len + t) * kvw + c] = bf16_round(g * m);
+  }
+}
+
+// Stage 3: out += bf16(o_fold res); one warp per output row.
+__global__ void readout_out_kernel(const float* __restrict__ res, const float* __restrict__ ofold,
+                                   int q_len, int kvw, int hidden,
+                                   __nv_bfloat16* __restrict__ out) {
+  extern __shared__ float sr[];  // (q_len, kvw)
+  const int b = blockIdx.y;
+  for (int i = threadIdx.x; i < q_len * kvw; i += blockDim.x)
+    sr[i] = res[(long long)b * q_len * kvw + i];
+  __syncthreads();
+  const int warps = blockDim.x / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int o = blockIdx.x * warps + warp; o < hidden; o += gridDim.x * warps) {
+    const float* w = ofold + (long long)o * kvw;
+    for (int t = 0; t < q_len; ++t) {
+      const float* x = sr + t * kvw;
+      float acc = 0.f;
+      for (int c = lane * 4; c < kvw; c += 128) {
+        const float4 ww = *reinterpret_cast<const float4*>(w + c);
+        acc = fmaf(ww.x, x[c], acc);
+        acc = fmaf(ww.y, x[c + 1], acc);
+        acc = fmaf(ww.z, x[c + 2], acc);
+        acc = fmaf(ww.w, x[c + 3], acc);
+      }
+      for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+      if (lane == 0) {
+        __nv_bfloat16* dst = out + ((long long)b * q_len + t) * hidden + o;
+        const float r = bf16_round(acc);
+        *dst = __float2bfloat16_rn(__bfloat162float(*dst) + r);
+      }
+    }
+  }
+}
+
+}  // namespace misc
+}  // namespace core
+
+using namespace core;
+using namespace core::misc;
+
+extern "C" int core_compact_kv(const core_dims_t* d, const void* k, const void* v,
+                               const int32_t* keep_idx, int32_t n_kept, void* out_k, void* out_v,
+                               void* stream) {
+  int rc = check_dims(d, "core_compact_kv");
+  if (rc != CORE_OK) return rc;
+  if (k == nullptr || v == nullptr || keep_idx == nullptr || out_k == nullptr || out_v == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_compact_kv: NULL tensor");
+  if (n_kept <= 0 || n_kept > d->seq_len)
+    return set_error(CORE_ERR_INVALID_ARG, "core_compact_kv: bad n_kept");
+  if (!aligned16(k) || !aligned16(v) || !aligned16(out_k) || !aligned16(out_v))
+    return set_error(CORE_ERR_INVALID_ARG, "core_compact_kv: tensors must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long rows = (long long)d->n_kv_heads * n_kept;
+  const int threads = 256;
+  long long blocks = (rows + (threads / 16) - 1) / (threads / 16);
+  const long long cap = (long long)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  dim3 grid((unsigned)blocks, (unsigned)d->batch);
+  compact_kernel<<<grid, threads, 0, s>>>(static_cast<const uint4*>(k), static_cast<const uint4*>(v),
+                                          keep_idx, d->n_kv_heads, d->seq_len, n_kept,
+                                          static_cast<uint4*>(out_k), static_cast<uint4*>(out_v));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "compact_kernel launch");
+}
+
+extern "C" size_t core_memory_readout_workspace_bytes(const core_dims_t* d, int32_t q_len,
+                                                      int32_t d_mem, int32_t gate_hidden) {
+  if (d == nullptr || q_len <= 0) return 0;
+  Sizer z;
+  z.take<float>((size_t)d->batch * q_len * d_mem);
+  z.take<float>((size_t)d->batch * q_len * gate_hidden);
+  z.take<float>((size_t)d->batch * q_len * d->n_kv_heads * kD);
+  return z.used;
+}
+
+extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const void* q,
+                                   const float* theta, const float* gate_w1, const float* gate_b1,
+                                   const float* gate_w2, const float* gate_b2, int32_t d_mem,
+                                   int32_t gate_hidden, float gate_override, const float* M,
+                                   const float* b_state, const float* o_fold, int32_t hidden,
+                                   void* attn_out, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+  if (d == nullptr || d->batch <= 0 || d->n_q_heads <= 0 || d->n_kv_heads <= 0 || d->head_dim != kD)
+    return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout: bad dims");
+  if (q == nullptr || theta == nullptr || M == nullptr || b_state == nullptr || o_fold == nullptr ||
+      attn_out == nullptr || (gate_override < 0.f && (gate_w1 == nullptr || gate_b1 == nullptr ||
+                                                      gate_w2 == nullptr || gate_b2 == nullptr)))
+    return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout: NULL tensor");
+  if (q_len <= 0 || d_mem <= 0 || hidden <= 0 || gate_hidden < 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout: bad sizes");
+  const int dm = d->n_q_heads * kD, kvw = d->n_kv_heads * kD;
+  if ((size_t)q_len * dm * 4 > 200 * 1024 || (size_t)q_len * kvw * 4 > 200 * 1024)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_memory_readout: q_len too large for one call");
+  Carver cv(workspace, workspace_bytes);
+  float* proj = cv.take<float>((size_t)d->batch * q_len * d_mem);
+  float* gpre = cv.take<float>((size_t)d->batch * q_len * (gate_hidden > 0 ? gate_hidden : 1));
+  float* res = cv.take<float>((size_t)d->batch * q_len * kvw);
+  if (cv.overflow) return set_error(CORE_ERR_WORKSPACE, "core_memory_readout: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  const int sms = sm_count();
+  const int gh = gate_override >= 0.f ? 0 : gate_hidden;
+  {
+    const size_t smem = (size_t)q_len * dm * 4;
+    e = cudaFuncSetAttribute(readout_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_error(e, "readout_proj attribute");
+    const int rows = d_mem + gh;
+    int bx = (rows + 7) / 8;
+    if (bx > sms) bx = sms;
+    readout_proj_kernel<<<dim3(bx, d->batch), 256, smem, s>>>(static_cast<const __nv_bfloat16*>(q),
+                                                             d->n_q_heads, q_len, theta, gate_w1,
+                                                             gate_b1, d_mem, gh, proj, gpre);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_proj launch");
+  }
+  {
+    const size_t smem = (size_t)d_mem * 4;
+    readout_mem_kernel<<<dim3((kvw + 255) / 256, d->batch, q_len), 256, smem, s>>>(
+        proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, res);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_mem launch");
+  }
+  {
+    const size_t smem = (size_t)q_len * kvw * 4;
+    e = cudaFuncSetAttribute(readout_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_error(e, "readout_out attribute");
+    int bx = (hidden + 7) / 8;
+    if (bx > sms) bx = sms;
+    readout_out_kernel<<<dim3(bx, d->batch), 256, smem, s>>>(res, o_fold, q_len, kvw, hidden,
+                                                            static_cast<__nv_bfloat16*>(attn_out));
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_out launch");
+  }
+  return CORE_OK;
+}

@@ -1,0 +1,1004 @@
+// QK relation features f1..f6 (replaces core/fused_qk.py:373-587).
+//
+// Three kernels run per call:
+//   1. qk_lse_kernel       : causal row log-sum-exp partials.  tcgen05 MMA,
+//                            queries on the 128 TMEM lanes (A = Q block,
+//                            B = 64-key sub-tiles), online max/sum per lane.
+//   2. lse_combine_kernel  : merges the partials into LSE (B, Hq, nq).
+//   3. qk_relation_kernel  : second MMA pass with keys on the TMEM lanes
+//                            (A = 128-key tile, B = the GQA group's queries),
+//                            the attention advantage, its GQA mean and the
+//                            per-key running statistics; one 64-byte record
+//                            per (key, KV head, query block).
+//   4. qk_merge_kernel     : per key, merges the records over KV heads and
+//                            query blocks into f1..f6, resolving the rare
+//                            f6 cases the running statistics cannot decide by
+//                            an exact recomputation.
+//
+// Work is split into units (batch b, KV head h, query block qb, key tile kt);
+// a persistent grid of one CTA per SM takes a contiguous range of units.
+#include <cfloat>
+#include <cmath>
+
+#include "common.cuh"
+#include "host_util.h"
+
+namespace core {
+namespace qk {
+
+constexpr int kD = 128;          // head dim
+constexpr int kTile = 128;       // keys per tile == queries per block
+constexpr int kThreads = 320;    // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiThreads = 256;
+constexpr int kKStages = 2;
+constexpr uint32_t kKTileBytes = kTile * kD * 2;  // 32 KB
+constexpr uint32_t kAtom = 1024;                  // 8 rows x 128 B
+// log(1e-8) as the float the reference passes to its kernels (fused_qk.py:382, :494).
+constexpr float kLogFloor = -18.420680743952367f;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kRecWords = 16;
+
+struct Params {
+  int B, Hq, Hkv, G, nq, L, q_start, n_qb, n_kt;
+  long long U;          // number of units
+  float scale;          // d^-0.5
+  float scale_log2;     // d^-0.5 * log2(e)
+  int slot_stride;      // LSE partial slots per (b, qh, t)
+  int head_topk;        // min(topk_qk, G)
+  int n_recent;         // min(n_recent_queries, nq)
+  float2* part;         // LSE partials (log2 units)
+  const float* lse;     // (B, Hq, nq) natural-log LSE
+  uint32_t* rec;        // (B, L, Hkv, n_qb, 16) records
+  DeviceStatus* status;
+};
+
+__device__ __forceinline__ long long unit_begin(int c, long long U, int P) {
+  return (long long)c * U / P;
+}
+__device__ __host__ __forceinline__ int cta_of_unit(long long u, long long U, int P) {
+  return (int)(((u + 1) * P + U - 1) / U) - 1;
+}
+
+struct Unit {
+  int b, h, qb, kt;
+  long long grp;
+};
+__device__ __forceinline__ Unit decode(long long u, const Params& p) {
+  Unit r;
+  r.kt = (int)(u % p.n_kt);
+  r.grp = u / p.n_kt;
+  r.qb = (int)(r.grp % p.n_qb);
+  long long bh = r.grp / p.n_qb;
+  r.h = (int)(bh % p.Hkv);
+  r.b = (int)(bh / p.Hkv);
+  return r;
+}
+
+__device__ __forceinline__ float logaddexp_floor(float r) {
+  // max(r, f) + log1p(exp(-|r - f|)), f = log(1e-8)  (fused_qk.py:200-202)
+  float a = fabsf(r - kLogFloor);
+  float t;
+  if (a < 16.0f) {
+    t = log1pf(expf(-a));
+  } else {
+    // exp(-a) < 1.2e-7: log1p(x) equals x to within half an ulp of x.
+    t = ex2_approx(-a * kLog2e);
+  }
+  return fmaxf(r, kLogFloor) + t;
+}
+
+// ===========================================================================
+// 1. LSE partial kernel
+// ===========================================================================
+template <int G>
+struct LseSmem {
+  static constexpr uint32_t kQBytes = 2u * G * kTile * 128u;  // [katom][g][128 rows][128 B]
+  static constexpr uint32_t kQOff = 0;
+  static constexpr uint32_t kKOff = kQOff + kQBytes;
+  static constexpr uint32_t kBarOff = kKOff + kKStages * kKTileBytes;
+  static constexpr uint32_t kTotal = kBarOff + 256;
+};
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1)
+    qk_lse_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const Params p) {
+  using S = LseSmem<G>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  const uint32_t sQ = sbase + S::kQOff;
+  const uint32_t sK = sbase + S::kKOff;
+  const uint32_t bar = sbase + S::kBarOff;
+  // barrier slots (8 bytes each)
+  const uint32_t bar_q_full = bar + 0, bar_q_empty = bar + 8;
+  auto bar_k_full = [&](int s) { return bar + 16 + 8u * s; };
+  auto bar_k_empty = [&](int s) { return bar + 16 + 8u * (kKStages + s); };
+  auto bar_t_full = [&](int s) { return bar + 16 + 8u * (2 * kKStages + s); };
+  auto bar_t_empty = [&](int s) { return bar + 16 + 8u * (2 * kKStages + 2 + s); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + S::kBarOff + 200);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + S::kBarOff + 208);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int P = gridDim.x;
+  const long long u0 = unit_begin(blockIdx.x, p.U, P), u1 = unit_begin(blockIdx.x + 1, p.U, P);
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q_full, 1);
+    mbar_init(bar_q_empty, 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(bar_k_full(s), 1);
+      mbar_init(bar_k_empty(s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_t_full(s), 1);
+      mbar_init(bar_t_empty(s), kEpiThreads / 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wait = [&](uint32_t b, uint32_t parity, int where) -> bool {
+    return bounded_wait(b, parity, abort_flag, p.status, where);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      long long cur = -1;
+      int gcount = 0, it = 0;
+      for (long long u = u0; u < u1; ++u) {
+        Unit t = decode(u, p);
+        if (t.grp != cur) {
+          if (gcount > 0 && !wait(bar_q_empty, (gcount - 1) & 1, 101)) break;
+          mbar_arrive_expect_tx(bar_q_full, S::kQBytes);
+          for (int ka = 0; ka < 2; ++ka)
+            for (int g = 0; g < G; ++g)
+              tma_load_3d(sQ + (uint32_t)(ka * G + g) * kTile * 128u, &tmQ, bar_q_full, ka * 64,
+                          t.qb * kTile, (t.b * p.Hq + t.h * G + g));
+          cur = t.grp;
+          ++gcount;
+        }
+        const int st = it % kKStages;
+        if (it >= kKStages && !wait(bar_k_empty(st), ((it / kKStages) - 1) & 1, 102)) break;
+        mbar_arrive_expect_tx(bar_k_full(st), kKTileBytes);
+        for (int ka = 0; ka < 2; ++ka)
+          tma_load_3d(sK + st * kKTileBytes + ka * (kTile * 128u), &tmK, bar_k_full(st), ka * 64,
+                      t.kt * kTile, t.b * p.Hkv + t.h);
+        ++it;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, 64, 0, 0);
+      long long cur = -1;
+      int gcount = 0, it = 0, sub = 0;
+      bool ok = true;
+      for (long long u = u0; u < u1 && ok; ++u) {
+        Unit t = decode(u, p);
+        if (t.grp != cur) {
+          if (!(ok = wait(bar_q_full, gcount & 1, 103))) break;
+          cur = t.grp;
+          ++gcount;
+        }
+        const int st = it % kKStages;
+        if (!(ok = wait(bar_k_full(st), (it / kKStages) & 1, 104))) break;
+        tc_fence_after();
+        for (int ss = 0; ss < 2 && ok; ++ss) {
+          const int buf = sub & 1, n = sub >> 1;
+          if (sub >= 2) {
+            if (!(ok = wait(bar_t_empty(buf), (n - 1) & 1, 105))) break;
+            tc_fence_after();
+          }
+          for (int g = 0; g < G; ++g) {
+            const uint32_t d = tmem + (uint32_t)(buf * G * 64 + g * 64);
+            for (int ks = 0; ks < 8; ++ks) {
+              // A: rows of q-head g inside K atom ks/4: sQ + ((ks/4)*G + g) * 16 KB
+              const uint64_t a = sdesc_kmajor(sQ + (uint32_t)((ks >> 2) * G + g) * kTile * 128u + (uint32_t)(ks & 3) * 32u);
+              const uint64_t bdesc =
+                  sdesc_kmajor(sK + st * kKTileBytes + (uint32_t)(ks >> 2) * kTile * 128u +
+                               (uint32_t)ss * 64u * 128u + (uint32_t)(ks & 3) * 32u);
+              mma_bf16(d, a, bdesc, idesc, ks > 0 ? 1u : 0u);
+            }
+          }
+          mma_commit(bar_t_full(buf));
+          ++sub;
+        }
+        if (!ok) break;
+        mma_commit(bar_k_empty(st));
+        ++it;
+        const bool last_of_group = (u + 1 >= u1) || (decode(u + 1, p).grp != t.grp);
+        if (last_of_group) mma_commit(bar_q_empty);
+      }
+    }
+  } else {
+    // ---------------- epilogue: online max / sum per (q-head, query) ----------------
+    const int ew = warp - 2;
+    const int team = ew >> 2;      // 32-key half of each 64-key sub-tile
+    const int wq = warp & 3;       // TMEM lane quarter
+    const int row = wq * 32 + lane;
+    float m[G], l[G];
+    long long cur = -1;
+    Unit cu{};
+    int sub = 0;
+    bool ok = true;
+    auto flush = [&](const Unit& t) {
+      const int tq = t.qb * kTile + row;
+      if (tq < p.nq) {
+        const int c_lo = cta_of_unit(t.grp * (long long)p.n_kt, p.U, P);
+        const int slot = (blockIdx.x - c_lo) * 2 + team;
+        for (int g = 0; g < G; ++g) {
+          const long long r = ((long long)(t.b * p.Hq + t.h * G + g) * p.nq + tq);
+          p.part[r * p.slot_stride + slot] = make_float2(m[g], l[g]);
+        }
+      }
+    };
+    for (long long u = u0; u < u1 && ok; ++u) {
+      Unit t = decode(u, p);
+      if (t.grp != cur) {
+        if (cur >= 0) flush(cu);
+        for (int g = 0; g < G; ++g) {
+          m[g] = -INFINITY;
+          l[g] = 0.f;
+        }
+        cur = t.grp;
+        cu = t;
+      }
+      const int qpos = p.q_start + t.qb * kTile + row;  // absolute query position
+      for (int ss = 0; ss < 2; ++ss) {
+        const int buf = sub & 1, n = sub >> 1;
+        if (!(ok = wait(bar_t_full(buf), n & 1, 106))) break;
+        tc_fence_after();
+        const int k0 = t.kt * kTile + ss * 64 + team * 32;
+        const bool need_mask = (k0 + 31 > p.q_start + t.qb * kTile) || (k0 + 32 > p.L);
+        for (int g = 0; g < G; ++g) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * G * 64 + g * 64 + team * 32), v);
+          float cmax = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = bf16_round(v[j]) * p.scale_log2;
+            if (need_mask) {
+              const int kk = k0 + j;
+              if (kk > qpos || kk >= p.L) x = -INFINITY;
+            }
+            v[j] = x;
+            cmax = fmaxf(cmax, x);
+          }
+          const float nm = fmaxf(m[g], cmax);
+          if (nm != -INFINITY) {
+            float s = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) s += ex2_approx(v[j] - nm);
+            l[g] = l[g] * ex2_approx(m[g] - nm) + s;
+            m[g] = nm;
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_t_empty(buf));
+        ++sub;
+      }
+    }
+    if (ok && cur >= 0) flush(cu);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// 2. LSE combine
+// ===========================================================================
+__global__ void lse_combine_kernel2(const Params p, int grid_ctas, float* __restrict__ lse_out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long n = (long long)p.B * p.Hq * p.nq;
+  if (i >= n) return;
+  const int t = (int)(i % p.nq);
+  const long long bq = i / p.nq;
+  const int qh = (int)(bq % p.Hq);
+  const int b = (int)(bq / p.Hq);
+  const int h = qh / p.G;
+  const int qb = t / kTile;
+  const long long grp = ((long long)b * p.Hkv + h) * p.n_qb + qb;
+  const int c_lo = cta_of_unit(grp * (long long)p.n_kt, p.U, grid_ctas);
+  const int c_hi = cta_of_unit((grp + 1) * (long long)p.n_kt - 1, p.U, grid_ctas);
+  const int nslots = (c_hi - c_lo + 1) * 2;
+  const float2* s = p.part + i * p.slot_stride;
+  float mm = -INFINITY;
+  for (int k = 0; k < nslots; ++k) mm = fmaxf(mm, s[k].x);
+  float ll = 0.f;
+  if (mm != -INFINITY) {
+    for (int k = 0; k < nslots; ++k) {
+      const float2 v = s[k];
+      if (v.y > 0.f) ll += v.y * ex2_approx(v.x - mm);
+    }
+  }
+  lse_out[i] = (mm == -INFINITY || ll <= 0.f) ? -INFINITY : (mm + log2f(ll)) * kLn2;
+}
+
+// ===========================================================================
+// 3. Relation kernel
+// ===========================================================================
+template <int G>
+struct RelSmem {
+  static constexpr uint32_t kQBytes = 2u * 2u * G * 64u * 128u;  // [katom][half][g][64][128 B]
+  static constexpr uint32_t kQOff = 0;
+  static constexpr uint32_t kKOff = kQOff + kQBytes;
+  static constexpr uint32_t kLseOff = kKOff + kKStages * kKTileBytes;  // float [G][128]
+  static constexpr uint32_t kCcOff = kLseOff + G * kTile * 4;          // float [128]
+  static constexpr uint32_t kXchOff = kCcOff + kTile * 4;              // uint32 [128][16]
+  static constexpr uint32_t kBarOff = kXchOff + kTile * 16 * 4;
+  static constexpr uint32_t kTotal = kBarOff + 256;
+};
+
+struct KeyStats {
+  float top[4], rtop[4];
+  float psum, mxnp;
+  uint32_t pcnt;
+  uint32_t mask[2];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) top[i] = rtop[i] = -INFINITY;
+    psum = 0.f;
+    mxnp = -INFINITY;
+    pcnt = 0;
+    mask[0] = mask[1] = 0;
+  }
+};
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1)
+    qk_relation_kernel(const __grid_constant__ CUtensorMap tmQ,
+                       const __grid_constant__ CUtensorMap tmK, const Params p) {
+  using S = RelSmem<G>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  const uint32_t sQ = sbase + S::kQOff;
+  const uint32_t sK = sbase + S::kKOff;
+  float* s_nlse = reinterpret_cast<float*>(sgen + S::kLseOff);
+  float* s_lcc = reinterpret_cast<float*>(sgen + S::kCcOff);
+  uint32_t* s_xch = reinterpret_cast<uint32_t*>(sgen + S::kXchOff);
+  const uint32_t bar = sbase + S::kBarOff;
+  const uint32_t bar_q_full = bar + 0, bar_q_empty = bar + 8;
+  auto bar_k_full = [&](int s) { return bar + 16 + 8u * s; };
+  auto bar_k_empty = [&](int s) { return bar + 16 + 8u * (kKStages + s); };
+  auto bar_t_full = [&](int s) { return bar + 16 + 8u * (2 * kKStages + s); };
+  auto bar_t_empty = [&](int s) { return bar + 16 + 8u * (2 * kKStages + 2 + s); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + S::kBarOff + 200);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + S::kBarOff + 208);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int P = gridDim.x;
+  const long long u0 = unit_begin(blockIdx.x, p.U, P), u1 = unit_begin(blockIdx.x + 1, p.U, P);
+  constexpr int kN = G * 64;  // MMA N: G query heads x 64 queries
+  constexpr uint32_t kQHalf = (uint32_t)G * 64u * 128u;  // bytes of one query half in one atom
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q_full, 1);
+    mbar_init(bar_q_empty, 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(bar_k_full(s), 1);
+      mbar_init(bar_k_empty(s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_t_full(s), 1);
+      mbar_init(bar_t_empty(s), kEpiThreads / 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wait = [&](uint32_t b, uint32_t parity, int where) -> bool {
+    return bounded_wait(b, parity, abort_flag, p.status, where);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      long long cur = -1;
+      int gcount = 0, it = 0;
+      for (long long u = u0; u < u1; ++u) {
+        Unit t = decode(u, p);
+        if (t.grp != cur) {
+          if (gcount > 0 && !wait(bar_q_empty, (gcount - 1) & 1, 201)) break;
+          mbar_arrive_expect_tx(bar_q_full, S::kQBytes);
+          for (int ka = 0; ka < 2; ++ka)
+            for (int hf = 0; hf < 2; ++hf)
+              for (int g = 0; g < G; ++g)
+                tma_load_3d(sQ + (uint32_t)ka * 2u * kQHalf + (uint32_t)hf * kQHalf +
+                                (uint32_t)g * 64u * 128u,
+                            &tmQ, bar_q_full, ka * 64, t.qb * kTile + hf * 64,
+                            t.b * p.Hq + t.h * G + g);
+          cur = t.grp;
+          ++gcount;
+        }
+        const int st = it % kKStages;
+        if (it >= kKStages && !wait(bar_k_empty(st), ((it / kKStages) - 1) & 1, 202)) break;
+        mbar_arrive_expect_tx(bar_k_full(st), kKTileBytes);
+        for (int ka = 0; ka < 2; ++ka)
+          tma_load_3d(sK + st * kKTileBytes + ka * (kTile * 128u), &tmK, bar_k_full(st), ka * 64,
+                      t.kt * kTile, t.b * p.Hkv + t.h);
+        ++it;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, kN, 0, 0);
+      long long cur = -1;
+      int gcount = 0, it = 0, sub = 0;
+      bool ok = true;
+      for (long long u = u0; u < u1 && ok; ++u) {
+        Unit t = decode(u, p);
+        if (t.grp != cur) {
+          if (!(ok = wait(bar_q_full, gcount & 1, 203))) break;
+          cur = t.grp;
+          ++gcount;
+        }
+        const int st = it % kKStages;
+        if (!(ok = wait(bar_k_full(st), (it / kKStages) & 1, 204))) break;
+        tc_fence_after();
+        for (int hf = 0; hf < 2 && ok; ++hf) {
+          const int buf = sub & 1, n = sub >> 1;
+          if (sub >= 2) {
+            if (!(ok = wait(bar_t_empty(buf), (n - 1) & 1, 205))) break;
+            tc_fence_after();
+          }
+          const uint32_t d = tmem + (uint32_t)(buf * kN);
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint64_t a = sdesc_kmajor(sK + st * kKTileBytes + (uint32_t)(ks >> 2) * kTile * 128u +
+                                            (uint32_t)(ks & 3) * 32u);
+            const uint64_t bdesc = sdesc_kmajor(sQ + (uint32_t)(ks >> 2) * 2u * kQHalf +
+                                                (uint32_t)hf * kQHalf + (uint32_t)(ks & 3) * 32u);
+            mma_bf16(d, a, bdesc, idesc, ks > 0 ? 1u : 0u);
+          }
+          mma_commit(bar_t_full(buf));
+          ++sub;
+        }
+        if (!ok) break;
+        mma_commit(bar_k_empty(st));
+        ++it;
+        const bool last_of_group = (u + 1 >= u1) || (decode(u + 1, p).grp != t.grp);
+        if (last_of_group) mma_commit(bar_q_empty);
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int ew = warp - 2;
+    const int team = ew >> 2;  // which 32 of each 64-query half
+    const int wq = warp & 3;
+    const int krow = wq * 32 + lane;  // key row inside the tile
+    const float inv_ht = 1.0f / (float)p.head_topk;
+    const bool exact_div = (p.head_topk != 1 && p.head_topk != 2 && p.head_topk != 4);
+    const float single_val = log1pf(expf(kLogFloor));
+    long long cur = -1;
+    int sub = 0;
+    bool ok = true;
+    for (long long u = u0; u < u1 && ok; ++u) {
+      Unit t = decode(u, p);
+      if (t.grp != cur) {
+        // (re)load -lse and log|C_t| of this query block
+        named_barrier(1, kEpiThreads);
+        const int tid = threadIdx.x - 64;
+        for (int i = tid; i < G * kTile; i += kEpiThreads) {
+          const int g = i / kTile, tq = i % kTile;
+          const int tt = t.qb * kTile + tq;
+          s_nlse[i] = (tt < p.nq) ? -p.lse[(long long)(t.b * p.Hq + t.h * G + g) * p.nq + tt] : 0.f;
+        }
+        for (int i = tid; i < kTile; i += kEpiThreads) {
+          const long long qpos = (long long)p.q_start + t.qb * kTile + i;
+          const long long cc = (qpos + 1 < p.L) ? qpos + 1 : p.L;
+          s_lcc[i] = logf((float)cc);
+        }
+        named_barrier(1, kEpiThreads);
+        cur = t.grp;
+      }
+      const int key = t.kt * kTile + krow;
+      KeyStats st;
+      st.init();
+      // units whose keys are all visible to all valid queries and in range
+      const int qb_first_pos = p.q_start + t.qb * kTile;
+      const int qb_valid = min(kTile, p.nq - t.qb * kTile);
+      for (int hf = 0; hf < 2; ++hf) {
+        const int buf = sub & 1, n = sub >> 1;
+        if (!(ok = wait(bar_t_full(buf), n & 1, 206))) break;
+        tc_fence_after();
+        const int tl0 = hf * 64 + team * 32;  // query index within the block of j = 0
+        const bool full = (t.kt * kTile + kTile - 1 <= qb_first_pos) &&
+                          (t.kt * kTile + kTile <= p.L) && (tl0 + 32 <= qb_valid);
+        float acc[32];
+        float mn[32];
+        for (int g = 0; g < G; ++g) {
+          float v[32];
+          tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * kN + g * 64 + team * 32), v);
+          const float* nl = s_nlse + g * kTile + tl0;
+          const float* lc = s_lcc + tl0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = bf16_round(v[j]);
+            const float r = fmaf(x, p.scale, nl[j]) + lc[j];
+            float rel = logaddexp_floor(r);
+            if (!full) {
+              const int qpos = qb_first_pos + tl0 + j;
+              if (key > qpos) rel = kLogFloor;
+              else if (qpos == 0) rel = single_val;
+            }
+            if (g == 0) {
+              acc[j] = rel;
+              mn[j] = rel;
+            } else {
+              acc[j] += rel;
+              mn[j] = fminf(mn[j], rel);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_t_empty(buf));
+        ++sub;
+        uint32_t msk = 0;
+        const int tabs0 = t.qb * kTile + tl0;  // absolute query index of j = 0
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float R;
+          if (p.head_topk < G) {
+            R = __fdiv_rn(acc[j] - mn[j], (float)p.head_topk);
+          } else {
+            R = exact_div ? __fdiv_rn(acc[j], (float)p.head_topk) : acc[j] * inv_ht;
+          }
+          if (!full) {
+            const int qpos = qb_first_pos + tl0 + j;
+            if (tl0 + j >= qb_valid || key > qpos) R = -INFINITY;
+          }
+          top4_insert(st.top, R);
+          if (tabs0 + j >= p.nq - p.n_recent) top4_insert(st.rtop, R);
+          const bool pz = R > 0.f;
+          st.psum += pz ? R : 0.f;
+          st.pcnt += pz ? 1u : 0u;
+          msk |= (pz ? 1u : 0u) << j;
+          st.mxnp = fmaxf(st.mxnp, pz ? -INFINITY : R);
+        }
+        st.mask[hf] = msk;
+      }
+      if (!ok) break;
+      // merge the two teams (same key, different query quarters) and store
+      uint32_t* x = s_xch + krow * 16;
+      if (team == 1) {
+        for (int i = 0; i < 4; ++i) {
+          x[i] = __float_as_uint(st.top[i]);
+          x[4 + i] = __float_as_uint(st.rtop[i]);
+        }
+        x[8] = __float_as_uint(st.psum);
+        x[9] = st.pcnt;
+        x[10] = st.mask[0];
+        x[11] = st.mask[1];
+        x[12] = __float_as_uint(st.mxnp);
+      }
+      named_barrier(2, kEpiThreads);
+      if (team == 0) {
+        for (int i = 0; i < 4; ++i) {
+          top4_insert(st.top, __uint_as_float(x[i]));
+          top4_insert(st.rtop, __uint_as_float(x[4 + i]));
+        }
+        const float psum = st.psum + __uint_as_float(x[8]);
+        const uint32_t pcnt = st.pcnt + x[9];
+        const float mxnp = fmaxf(st.mxnp, __uint_as_float(x[12]));
+        if (key < p.L) {
+          uint4* dst = reinterpret_cast<uint4*>(
+              p.rec + ((((long long)t.b * p.L + key) * p.Hkv + t.h) * p.n_qb + t.qb) * kRecWords);
+          dst[0] = make_uint4(__float_as_uint(st.top[0]), __float_as_uint(st.top[1]),
+                              __float_as_uint(st.top[2]), __float_as_uint(st.top[3]));
+          dst[1] = make_uint4(__float_as_uint(st.rtop[0]), __float_as_uint(st.rtop[1]),
+                              __float_as_uint(st.rtop[2]), __float_as_uint(st.rtop[3]));
+          // query words: 0 -> (half 0, team 0), 1 -> (half 0, team 1), 2 -> (1, 0), 3 -> (1, 1)
+          dst[2] = make_uint4(__float_as_uint(psum), pcnt, st.mask[0], x[10]);
+          dst[3] = make_uint4(st.mask[1], x[11], __float_as_uint(mxnp), 0u);
+        }
+      }
+      named_barrier(2, kEpiThreads);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// 4. Merge records into f1..f6
+// ===========================================================================
+struct MergeParams {
+  int B, Hq, Hkv, G, nq, L, q_start, n_qb, topk, n_recent, head_topk;
+  float scale;
+  const uint32_t* rec;
+  const __nv_bfloat16* q;  // (B, Hq, nq, d)
+  const __nv_bfloat16* k;  // (B, Hkv, L, d)
+  const float* lse;        // (B, Hq, nq)
+  float* features;
+  int stride;
+  DeviceStatus* status;
+};
+
+constexpr int kMergeThreads = 256;
+constexpr int kMaxSlowNq = 2048;
+constexpr int kSlowCap = 1024;  // undecided (key, head) pairs per merge block
+
+__device__ __forceinline__ float sum_top_desc(const float (&t)[4], int k) {
+  // cumsum of the descending values, read at k-1 (fused_qk.py:541-543)
+  float s = t[0];
+  if (k > 1) s += t[1];
+  if (k > 2) s += t[2];
+  if (k > 3) s += t[3];
+  return s;
+}
+
+// Exact relation value R[h, t, key] (one query), as the relation kernel computes it.
+__device__ float relation_exact(const MergeParams& p, int b, int h, int key, int t) {
+  const long long qpos = (long long)p.q_start + t;
+  if (key > qpos) return kLogFloor;
+  const __nv_bfloat16* kr = p.k + (((long long)b * p.Hkv + h) * p.L + key) * kD;
+  const long long cc = (qpos + 1 < p.L) ? qpos + 1 : p.L;
+  const float lcc = logf((float)cc);
+  float acc = 0.f, mn = INFINITY;
+  for (int g = 0; g < p.G; ++g) {
+    const int qh = h * p.G + g;
+    const __nv_bfloat16* qr = p.q + (((long long)b * p.Hq + qh) * p.nq + t) * kD;
+    float dot = 0.f;
+    for (int e = 0; e < kD; ++e) dot = fmaf(__bfloat162float(qr[e]), __bfloat162float(kr[e]), dot);
+    const float x = bf16_round(dot);
+    const float r = fmaf(x, p.scale, -p.lse[((long long)b * p.Hq + qh) * p.nq + t]) + lcc;
+    float rel = logaddexp_floor(r);
+    if (qpos == 0) rel = log1pf(expf(kLogFloor));
+    acc = (g == 0) ? rel : acc + rel;
+    mn = fminf(mn, rel);
+  }
+  if (p.head_topk < p.G) return __fdiv_rn(acc - mn, (float)p.head_topk);
+  return __fdiv_rn(acc, (float)p.head_topk);
+}
+
+__global__ void __launch_bounds__(kMergeThreads)
+    qk_merge_kernel(const MergeParams p) {
+  __shared__ int s_nslow;
+  __shared__ int s_slow[kSlowCap * 2];  // (local key, head) pairs
+  __shared__ int s_f6[kMergeThreads];
+  __shared__ float s_vals[kMaxSlowNq];
+  if (threadIdx.x == 0) s_nslow = 0;
+  s_f6[threadIdx.x] = 0;
+  __syncthreads();
+
+  const long long gi = (long long)blockIdx.x * kMergeThreads + threadIdx.x;
+  const bool active = gi < (long long)p.B * p.L;
+  int b = 0, key = 0, valid = 1, kf = 1;
+  float f[6] = {0, 0, 0, 0, 0, 0};
+  if (active) {
+    b = (int)(gi / p.L);
+    key = (int)(gi % p.L);
+    valid = p.nq - max(key - p.q_start, 0);
+    valid = min(max(valid, 1), p.nq);
+    const int k2max = min(p.topk, p.nq * p.Hkv);
+    const int k2 = min(max(valid * p.Hkv, 1), k2max);
+    const int nrec = p.n_recent;
+    const int rstart = p.q_start + p.nq - nrec;
+    int rvalid = p.q_start + p.nq - max(key, rstart);
+    rvalid = min(max(rvalid, 1), nrec);
+    const int k4max = min(p.topk, nrec * p.Hkv);
+    const int k4 = min(max(rvalid * p.Hkv, 1), k4max);
+    kf = max((valid + 3) / 4, 1);
+
+    float top[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    float rtop[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    float psum = 0.f;
+    unsigned long long pcnt = 0;
+    int f5cnt = 0;
+    int f6pos = 0;
+    const uint32_t* base = p.rec + ((long long)b * p.L + key) * p.Hkv * p.n_qb * kRecWords;
+    // f5: OR over heads of the per-query positive bits, per query block
+    for (int qb = 0; qb < p.n_qb; ++qb) {
+      uint32_t w[4] = {0, 0, 0, 0};
+      for (int h = 0; h < p.Hkv; ++h) {
+        const uint4 r2 = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords)[2];
+        const uint4 r3 = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords)[3];
+        w[0] |= r2.z;
+        w[1] |= r2.w;
+        w[2] |= r3.x;
+        w[3] |= r3.y;
+      }
+      f5cnt += __popc(w[0]) + __popc(w[1]) + __popc(w[2]) + __popc(w[3]);
+    }
+    for (int h = 0; h < p.Hkv; ++h) {
+      float hs = 0.f, mx = -INFINITY;
+      unsigned int hc = 0;
+      for (int qb = 0; qb < p.n_qb; ++qb) {
+        const uint4* r = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords);
+        const uint4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
+        top4_insert(top, __uint_as_float(r0.x));
+        top4_insert(top, __uint_as_float(r0.y));
+        top4_insert(top, __uint_as_float(r0.z));
+        top4_insert(top, __uint_as_float(r0.w));
+        top4_insert(rtop, __uint_as_float(r1.x));
+        top4_insert(rtop, __uint_as_float(r1.y));
+        top4_insert(rtop, __uint_as_float(r1.z));
+        top4_insert(rtop, __uint_as_float(r1.w));
+        hs += __uint_as_float(r2.x);
+        hc += r2.y;
+        mx = fmaxf(mx, __uint_as_float(r3.z));
+      }
+      psum += hs;
+      pcnt += hc;
+      // f6 for head h: sign of the mean of the top-kf relations over queries
+      if ((int)hc >= kf) {
+        ++f6pos;
+      } else if (hc > 0) {
+        const float rem = (float)(kf - (int)hc);
+        const float hi = hs + rem * mx;                       // remaining values <= mx
+        const float lo = hs + rem * (kLogFloor * 1.0001f);    // and >= the floor
+        const float tol = 1e-5f * (fabsf(hs) + rem * fabsf(kLogFloor));
+        if (hi < -tol) {
+          // definitely not positive
+        } else if (lo > tol) {
+          ++f6pos;
+        } else {
+          const int slot = atomicAdd(&s_nslow, 1);
+          if (slot < kSlowCap) {
+            s_slow[slot * 2] = threadIdx.x;
+            s_slow[slot * 2 + 1] = h;
+          } else {
+            record_error(p.status, CORE_ERR_UNSUPPORTED, 401, key);
+          }
+        }
+      }
+    }
+    f[0] = top[0];
+    f[1] = sum_top_desc(top, k2) / (float)k2;
+    f[2] = psum / (float)(pcnt > 0 ? pcnt : 1);
+    f[3] = sum_top_desc(rtop, k4) / (float)k4;
+    f[4] = (float)f5cnt / (float)p.nq;
+    s_f6[threadIdx.x] = f6pos;
+  }
+  __syncthreads();
+  // Cooperative exact resolution of undecided f6 heads: recompute the
+  // relation values of one (key, head) over all queries, sort descending and
+  // test the mean of the top ceil(valid / 4).
+  const int nslow = min(s_nslow, kSlowCap);
+  for (int it = 0; it < nslow; ++it) {
+    const int lk = s_slow[it * 2], h = s_slow[it * 2 + 1];
+    const long long gk = (long long)blockIdx.x * kMergeThreads + lk;
+    const int bb = (int)(gk / p.L), kk = (int)(gk % p.L);
+    int n2 = 1;
+    while (n2 < p.nq) n2 <<= 1;
+    for (int t = threadIdx.x; t < n2; t += kMergeThreads)
+      s_vals[t] = (t < p.nq) ? relation_exact(p, bb, h, kk, t) : -INFINITY;
+    __syncthreads();
+    // bitonic sort, descending
+    for (int size = 2; size <= n2; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = threadIdx.x; i < n2; i += kMergeThreads) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const bool desc = ((i & size) == 0);
+            const float a = s_vals[i], c = s_vals[j];
+            if (desc ? (a < c) : (a > c)) {
+              s_vals[i] = c;
+              s_vals[j] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    if (threadIdx.x == 0) {
+      int vld = p.nq - max(kk - p.q_start, 0);
+      vld = min(max(vld, 1), p.nq);
+      const int kfr = max((vld + 3) / 4, 1);
+      float s = 0.f;
+      for (int i = 0; i < kfr; ++i) s += s_vals[i];
+      if (s / (float)kfr > 0.f) s_f6[lk] += 1;
+    }
+    __syncthreads();
+  }
+  if (active) {
+    f[5] = (float)s_f6[threadIdx.x] / (float)p.Hkv;
+    float* out = p.features + ((long long)b * p.L + key) * p.stride;
+    bool finite = true;
+    for (int i = 0; i < 6; ++i) {
+      out[i] = f[i];
+      finite &= isfinite(f[i]);
+    }
+    if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 402, key);
+  }
+}
+
+}  // namespace qk
+}  // namespace core
+
+using namespace core;
+using namespace core::qk;
+
+namespace {
+
+struct QKPlan {
+  Params p;
+  int grid;
+  size_t part_elems, rec_words;
+};
+
+int plan_qk(const core_dims_t* d, int topk, int n_recent, QKPlan* out) {
+  Params& p = out->p;
+  p = Params{};
+  p.B = d->batch;
+  p.Hq = d->n_q_heads;
+  p.Hkv = d->n_kv_heads;
+  p.G = p.Hq / p.Hkv;
+  p.nq = d->n_queries;
+  p.L = d->seq_len;
+  p.q_start = p.L - p.nq;
+  p.n_qb = (p.nq + kTile - 1) / kTile;
+  p.n_kt = (p.L + kTile - 1) / kTile;
+  p.U = (long long)p.B * p.Hkv * p.n_qb * p.n_kt;
+  p.scale = 1.0f / sqrtf((float)kD);
+  p.scale_log2 = p.scale * kLog2e;
+  p.head_topk = topk < p.G ? topk : p.G;
+  p.n_recent = n_recent < p.nq ? n_recent : p.nq;
+  const int sms = sm_count();
+  out->grid = (int)(p.U < sms ? p.U : sms);
+  // slots: 2 teams x CTAs overlapping one group
+  int maxc = 1;
+  const long long groups = p.U / p.n_kt;
+  for (long long g = 0; g < groups; ++g) {
+    int lo = cta_of_unit(g * p.n_kt, p.U, out->grid);
+    int hi = cta_of_unit((g + 1) * p.n_kt - 1, p.U, out->grid);
+    if (hi - lo + 1 > maxc) maxc = hi - lo + 1;
+  }
+  p.slot_stride = 2 * maxc;
+  out->part_elems = (size_t)p.B * p.Hq * p.nq * p.slot_stride;
+  out->rec_words = (size_t)p.B * p.L * p.Hkv * p.n_qb * kRecWords;
+  return CORE_OK;
+}
+
+template <int G>
+int launch_qk(const QKPlan& plan, const CUtensorMap& tmQ_lse, const CUtensorMap& tmQ_rel,
+              const CUtensorMap& tmK, bool run_lse, float* lse_buf, cudaStream_t s) {
+  const Params& p = plan.p;
+  cudaError_t e;
+  if (run_lse) {
+    const uint32_t smem = LseSmem<G>::kTotal + 1024;
+    e = cudaFuncSetAttribute(qk_lse_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_error(e, "qk_lse_kernel attribute");
+    qk_lse_kernel<G><<<plan.grid, kThreads, smem, s>>>(tmQ_lse, tmK, p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_lse_kernel launch");
+    const long long n = (long long)p.B * p.Hq * p.nq;
+    lse_combine_kernel2<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p, plan.grid, lse_buf);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "lse_combine launch");
+  }
+  const uint32_t smem = RelSmem<G>::kTotal + 1024;
+  e = cudaFuncSetAttribute(qk_relation_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_error(e, "qk_relation_kernel attribute");
+  qk_relation_kernel<G><<<plan.grid, kThreads, smem, s>>>(tmQ_rel, tmK, p);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_relation_kernel launch");
+  return CORE_OK;
+}
+
+}  // namespace
+
+extern "C" size_t core_qk_features_workspace_bytes(const core_dims_t* d) {
+  if (check_dims(d, "core_qk_features_workspace_bytes") != CORE_OK) return 0;
+  QKPlan plan;
+  plan_qk(d, 4, 16, &plan);
+  Sizer z;
+  z.take<float2>(plan.part_elems);
+  z.take<float>((size_t)d->batch * d->n_q_heads * d->n_queries);
+  z.take<uint32_t>(plan.rec_words);
+  return z.used;
+}
+
+extern "C" int core_qk_features(const core_dims_t* d, const void* q, const void* k,
+                                int32_t topk_qk, int32_t n_recent_queries, const float* lse_in,
+                                float* lse_out, float* features, int32_t feature_stride,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_dims(d, "core_qk_features");
+  if (rc != CORE_OK) return rc;
+  if (q == nullptr || k == nullptr || features == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: NULL tensor");
+  if (d->n_queries <= 0) return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: no queries");
+  if (topk_qk <= 0 || topk_qk > 4)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_qk_features: topk_qk must be in 1..4");
+  const int G = d->n_q_heads / d->n_kv_heads;
+  if (topk_qk < G - 1)
+    return set_error(CORE_ERR_UNSUPPORTED,
+                     "core_qk_features: requires topk_qk >= group size - 1 (fused_qk.py:19-21)");
+  if (n_recent_queries <= 0) return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: n_recent <= 0");
+  if (feature_stride < 6) return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: feature_stride < 6");
+  QKPlan plan;
+  plan_qk(d, topk_qk, n_recent_queries, &plan);
+  Params& p = plan.p;
+  if (p.nq > kMaxSlowNq)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_qk_features: n_queries must be <= 2048");
+  Carver c(workspace, workspace_bytes);
+  p.part = c.take<float2>(plan.part_elems);
+  float* lse_buf = c.take<float>((size_t)p.B * p.Hq * p.nq);
+  p.rec = c.take<uint32_t>(plan.rec_words);
+  if (c.overflow)
+    return set_error(CORE_ERR_WORKSPACE, "core_qk_features: workspace too small");
+  p.status = device_status();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (lse_in != nullptr) {
+    e = cudaMemcpyAsync(lse_buf, lse_in, sizeof(float) * (size_t)p.B * p.Hq * p.nq,
+                        cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_error(e, "core_qk_features lse copy");
+  }
+  p.lse = lse_buf;
+
+  // Tensor maps: Q as (B*Hq, nq, 128) and K as (B*Hkv, L, 128), bf16, 128 B swizzle.
+  CUtensorMap tmQ_lse, tmQ_rel, tmK;
+  {
+    uint64_t dims[3] = {128, (uint64_t)p.nq, (uint64_t)p.B * p.Hq};
+    uint64_t str[2] = {256, (uint64_t)p.nq * 256};
+    uint32_t box_lse[3] = {64, 128, 1};
+    uint32_t box_rel[3] = {64, 64, 1};
+    if ((rc = make_tmap_bf16(&tmQ_lse, q, 3, dims, str, box_lse, true)) != CORE_OK) return rc;
+    if ((rc = make_tmap_bf16(&tmQ_rel, q, 3, dims, str, box_rel, true)) != CORE_OK) return rc;
+  }
+  {
+    uint64_t dims[3] = {128, (uint64_t)p.L, (uint64_t)p.B * p.Hkv};
+    uint64_t str[2] = {256, (uint64_t)p.L * 256};
+    uint32_t box[3] = {64, 128, 1};
+    if ((rc = make_tmap_bf16(&tmK, k, 3, dims, str, box, true)) != CORE_OK) return rc;
+  }
+  const bool run_lse = (lse_in == nullptr);
+  switch (p.G) {
+    case 1: rc = launch_qk<1>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s); break;
+    case 2: rc = launch_qk<2>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s); break;
+    case 4: rc = launch_qk<4>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s); break;
+    default: return set_error(CORE_ERR_UNSUPPORTED, "core_qk_features: group size");
+  }
+  if (rc != CORE_OK) return rc;
+
+  MergeParams mp{};
+  mp.B = p.B; mp.Hq = p.Hq; mp.Hkv = p.Hkv; mp.G = p.G; mp.nq = p.nq; mp.L = p.L;
+  mp.q_start = p.q_start; mp.n_qb = p.n_qb; mp.topk = topk_qk; mp.n_recent = p.n_recent;
+  mp.head_topk = p.head_topk; mp.scale = p.scale; mp.rec = p.rec;
+  mp.q = static_cast<const __nv_bfloat16*>(q);
+  mp.k = static_cast<const __nv_bfloat16*>(k);
+  mp.lse = lse_buf; mp.features = features; mp.stride = feature_stride; mp.status = p.status;
+  const long long n = (long long)p.B * p.L;
+  qk_merge_kernel<<<(unsigned)((n + kMergeThreads - 1) / kMergeThreads), kMergeThreads, 0, s>>>(mp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_merge_kernel launch");
+  if (lse_out != nullptr) {
+    e = cudaMemcpyAsync(lse_out, lse_buf, sizeof(float) * (size_t)p.B * p.Hq * p.nq,
+                        cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_error(e, "core_qk_features lse copy out");
+  }
+  return CORE_OK;
+}

@@ -1,0 +1,215 @@
+"""Torch-facing wrappers of the C ABI (one function per entry point).
+
+Each wrapper validates shapes/dtypes/devices, allocates outputs and the
+workspace with torch on the tensors' device, and calls the CUDA library on
+the current torch stream.  There is no CPU path: inputs must be CUDA tensors.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import CoreDims, check
+
+HEAD_DIM = 128
+
+
+def _ptr(t: torch.Tensor | None):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("core_b200 operates on CUDA tensors only (no CPU path)")
+
+
+def _dims(keys: torch.Tensor, n_q_heads: int, n_queries: int) -> CoreDims:
+    b, hkv, L, d = keys.shape
+    if keys.dtype != torch.bfloat16:
+        raise TypeError(f"core_b200 computes in bfloat16; got {keys.dtype}")
+    return CoreDims(b, n_q_heads, hkv, d, n_queries, L, _lib.CORE_DTYPE_BF16)
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def status(device=None) -> None:
+    """Raise if a kernel recorded a device-side error (synchronises the stream)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    check(_lib.load().core_check_device_status(_stream(device)))
+
+
+# ---------------------------------------------------------------------------
+def qk_features(q: torch.Tensor, k: torch.Tensor, *, topk_qk: int = 4,
+                n_recent_queries: int = 16, lse: torch.Tensor | None = None,
+                features: torch.Tensor | None = None):
+    """f1..f6 of every cached key (``strict_causal_qk_features``).
+
+    q: (B, Hq, nq, 128) bf16, k: (B, Hkv, L, 128) bf16.  Returns
+    (features (B, L, 6) or the given (B, L, F>=6) buffer, lse (B, Hq, nq)).
+    """
+    _require_cuda(q, k, lse)
+    q = q.contiguous()
+    k = k.contiguous()
+    B, Hq, nq, d = q.shape
+    dims = _dims(k, Hq, nq)
+    if q.dtype != torch.bfloat16 or d != HEAD_DIM:
+        raise TypeError("q must be bfloat16 with head_dim 128")
+    lib = _lib.load()
+    if features is None:
+        features = torch.empty(B, k.shape[2], 6, dtype=torch.float32, device=k.device)
+    lse_out = torch.empty(B, Hq, nq, dtype=torch.float32, device=k.device)
+    ws = _workspace(lib.core_qk_features_workspace_bytes(ctypes.byref(dims)), k.device)
+    lse_in = None if lse is None else lse.to(torch.float32).contiguous()
+    check(lib.core_qk_features(ctypes.byref(dims), _ptr(q), _ptr(k), topk_qk, n_recent_queries,
+                               _ptr(lse_in), _ptr(lse_out), _ptr(features), features.shape[-1],
+                               _ptr(ws), ws.numel(), _stream(k.device)))
+    return features, lse_out
+
+
+def split_bf16(w: torch.Tensor, terms: int) -> torch.Tensor:
+    """f32 -> (terms, *w.shape) bf16 whose sum reproduces w (hi, mid, lo)."""
+    _require_cuda(w)
+    w = w.to(torch.float32).contiguous()
+    out = torch.empty((terms, *w.shape), dtype=torch.bfloat16, device=w.device)
+    check(_lib.load().core_split_bf16(_ptr(w), w.numel(), terms, _ptr(out), _stream(w.device)))
+    return out
+
+
+def coverage_features(k: torch.Tensor, geometry_split: torch.Tensor, prototypes: torch.Tensor,
+                      hadamard: torch.Tensor, *, shrinkage_rho: float = 0.1,
+                      features: torch.Tensor | None = None, col0: int = 0):
+    """o, d_proto, delta_proto, g (``compute_coverage_features``)."""
+    _require_cuda(k, geometry_split, prototypes, hadamard)
+    k = k.contiguous()
+    B, hkv, L, d = k.shape
+    dims = _dims(k, hkv, 0)
+    if tuple(geometry_split.shape) != (3, 64, hkv * d):
+        raise ValueError("geometry_split must be (3, 64, Hkv*d)")
+    lib = _lib.load()
+    if features is None:
+        features = torch.empty(B, L, 4, dtype=torch.float32, device=k.device)
+        col0 = 0
+    ws = _workspace(lib.core_coverage_workspace_bytes(ctypes.byref(dims)), k.device)
+    check(lib.core_coverage_features(
+        ctypes.byref(dims), _ptr(k), _ptr(geometry_split.contiguous()),
+        _ptr(prototypes.float().contiguous()), _ptr(hadamard.float().contiguous()),
+        float(shrinkage_rho), _ptr(features), features.shape[-1], col0, _ptr(ws), ws.numel(),
+        _stream(k.device)))
+    return features
+
+
+def pack_mlp(mlp_params) -> torch.Tensor:
+    """[w1 (128,14) | b1 | w2 (128,128) | b2 | w3 (128) | b3] as one f32 vector."""
+    w1, b1, w2, b2, w3, b3 = mlp_params
+    return torch.cat([w1.reshape(-1), b1.reshape(-1), w2.reshape(-1), b2.reshape(-1),
+                      w3.reshape(-1), b3.reshape(-1)]).to(torch.float32).contiguous()
+
+
+def indexer_scores(v: torch.Tensor, positions: torch.Tensor, features: torch.Tensor,
+                   mlp_packed: torch.Tensor, *, original_length: int, is_prefill: bool,
+                   n_sink: int = 4, special: torch.Tensor | None = None) -> torch.Tensor:
+    """Auxiliary features into columns 10..13 of ``features`` (B, L, 14) and the
+    indexer MLP scores (B, L)."""
+    _require_cuda(v, positions, features, mlp_packed, special)
+    v = v.contiguous()
+    B, hkv, L, d = v.shape
+    dims = _dims(v, hkv, 0)
+    if features.shape != (B, L, 14) or not features.is_contiguous():
+        raise ValueError("features must be a contiguous (B, L, 14) float32 tensor")
+    pos = positions.to(torch.int64).reshape(B, L).contiguous()
+    sp = None if special is None else special.to(torch.uint8).reshape(B, L).contiguous()
+    scores = torch.empty(B, L, dtype=torch.float32, device=v.device)
+    check(_lib.load().core_indexer_scores(
+        ctypes.byref(dims), _ptr(v), _ptr(pos), _ptr(sp), int(original_length), int(is_prefill),
+        int(n_sink), _ptr(features), _ptr(mlp_packed), _ptr(scores), _stream(v.device)))
+    return scores
+
+
+def topb_select(scores: torch.Tensor, n_kept: int, n_sink: int):
+    """(keep (B, n_kept), evict (B, L - n_kept)) int32, both ascending."""
+    _require_cuda(scores)
+    scores = scores.to(torch.float32).contiguous()
+    B, L = scores.shape
+    keep = torch.empty(B, n_kept, dtype=torch.int32, device=scores.device)
+    evict = torch.empty(B, max(L - n_kept, 1), dtype=torch.int32, device=scores.device)
+    check(_lib.load().core_topb_select(_ptr(scores), B, L, int(n_kept), int(n_sink), _ptr(keep),
+                                       _ptr(evict), _ptr(None), 0, _stream(scores.device)))
+    return keep, evict[:, : L - n_kept]
+
+
+def memory_write(k: torch.Tensor, v: torch.Tensor, scores_cal: torch.Tensor,
+                 evict: torch.Tensor, theta_split: torch.Tensor, M: torch.Tensor,
+                 b_state: torch.Tensor, Z: torch.Tensor, *, gamma: float, eta: float,
+                 student_temp: float) -> None:
+    """Update (M, b, Z) in place with the evicted tokens (``compress`` memory write)."""
+    _require_cuda(k, v, scores_cal, evict, theta_split, M, b_state, Z)
+    k = k.contiguous()
+    v = v.contiguous()
+    B, hkv, L, d = k.shape
+    dims = _dims(k, hkv, 0)
+    n_evict = evict.shape[1]
+    d_mem = theta_split.shape[1]
+    for name, t, shape in (("M", M, (B, d_mem, hkv * d)), ("b", b_state, (B, d_mem)), ("Z", Z, (B,))):
+        if tuple(t.shape) != shape or t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous float32 tensor of shape {shape}")
+    lib = _lib.load()
+    ws = _workspace(lib.core_memory_write_workspace_bytes(ctypes.byref(dims), n_evict, d_mem), k.device)
+    check(lib.core_memory_write(
+        ctypes.byref(dims), _ptr(k), _ptr(v), _ptr(scores_cal.float().contiguous()),
+        _ptr(evict.to(torch.int32).contiguous()), n_evict, _ptr(theta_split.contiguous()), d_mem,
+        float(gamma), float(eta), float(student_temp), _ptr(M), _ptr(b_state), _ptr(Z), _ptr(ws),
+        ws.numel(), _stream(k.device)))
+
+
+def compact_kv(k: torch.Tensor, v: torch.Tensor, keep: torch.Tensor):
+    """Gather the kept rows: (B, Hkv, n_kept, d) keys and values."""
+    _require_cuda(k, v, keep)
+    k = k.contiguous()
+    v = v.contiguous()
+    B, hkv, L, d = k.shape
+    n_kept = keep.shape[1]
+    dims = _dims(k, hkv, 0)
+    ok = torch.empty(B, hkv, n_kept, d, dtype=k.dtype, device=k.device)
+    ov = torch.empty_like(ok)
+    check(_lib.load().core_compact_kv(ctypes.byref(dims), _ptr(k), _ptr(v),
+                                      _ptr(keep.to(torch.int32).contiguous()), n_kept, _ptr(ok),
+                                      _ptr(ov), _stream(k.device)))
+    return ok, ov
+
+
+def memory_readout(q: torch.Tensor, theta: torch.Tensor, gate, M: torch.Tensor,
+                   b_state: torch.Tensor, o_fold: torch.Tensor, attn_out: torch.Tensor,
+                   *, n_kv_heads: int, gate_override: float | None = None) -> torch.Tensor:
+    """attn_out (B, q_len, hidden) bf16 += o_fold(g(q) m(q)); updated in place and returned.
+
+    gate = (w1 (gh, Hq*d), b1 (gh), w2 (gh), b2 (1)) f32 tensors.
+    """
+    _require_cuda(q, theta, M, b_state, o_fold, attn_out)
+    q = q.to(torch.bfloat16).contiguous()
+    B, Hq, q_len, d = q.shape
+    dims = CoreDims(B, Hq, n_kv_heads, d, q_len, max(q_len, 1), _lib.CORE_DTYPE_BF16)
+    d_mem = theta.shape[0]
+    hidden = o_fold.shape[0]
+    w1, b1, w2, b2 = gate
+    gh = w1.shape[0]
+    if not attn_out.is_contiguous() or attn_out.dtype != torch.bfloat16:
+        raise ValueError("attn_out must be a contiguous bfloat16 tensor")
+    lib = _lib.load()
+    ws = _workspace(lib.core_memory_readout_workspace_bytes(ctypes.byref(dims), q_len, d_mem, gh),
+                    q.device)
+    go = -1.0 if gate_override is None else float(gate_override)
+    check(lib.core_memory_readout(
+        ctypes.byref(dims), q_len, _ptr(q), _ptr(theta), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2),
+        d_mem, gh, go, _ptr(M), _ptr(b_state), _ptr(o_fold), hidden, _ptr(attn_out), _ptr(ws),
+        ws.numel(), _stream(q.device)))
+    return attn_out

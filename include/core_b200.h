@@ -1,0 +1,201 @@
+/*
+ * core_b200.h -- C ABI of the B200 (sm_100a) implementation of CORE's
+ * KV-compression step (the `core_full` press) and its latent-memory readout.
+ *
+ * Every entry point:
+ *   - takes plain device pointers, sizes and a cudaStream_t (passed as void*);
+ *   - is asynchronous on that stream and allocates nothing: scratch memory is
+ *     a caller-provided workspace whose size the matching *_workspace_bytes
+ *     query returns;
+ *   - returns an int status (CORE_OK = 0, negative on error).  A readable
+ *     message for the last error of the calling thread is available from
+ *     core_last_error().  Device-side failures (a bounded wait that gave up, a
+ *     non-finite feature) are recorded in a device status word that
+ *     core_check_device_status() reads back (it synchronises the stream).
+ *
+ * Tensor layouts are those of the reference press (HF DynamicCache layers):
+ *   Q  : (B, Hq, nq, d)    post-RoPE queries of the query buffer
+ *   K,V: (B, Hkv, L, d)    cached keys / values
+ * with d = 128 and Hq = G * Hkv, G <= 4.  bf16 (CORE_DTYPE_BF16) is the
+ * supported compute type of the CUDA path.
+ *
+ * The reference is pure Python; each entry point below names the reference
+ * function (file:line in the reference project) whose behaviour it replaces.
+ */
+#ifndef CORE_B200_H_
+#define CORE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define CORE_OK 0
+#define CORE_ERR_INVALID_ARG (-1)
+#define CORE_ERR_UNSUPPORTED (-2)
+#define CORE_ERR_NONFINITE (-3)
+#define CORE_ERR_TIMEOUT (-4)
+#define CORE_ERR_CUDA (-5)
+#define CORE_ERR_WORKSPACE (-6)
+
+/* ---- dtypes ---- */
+#define CORE_DTYPE_BF16 1
+#define CORE_DTYPE_F32 2
+
+typedef struct core_dims {
+  int32_t batch;      /* B   */
+  int32_t n_q_heads;  /* Hq  */
+  int32_t n_kv_heads; /* Hkv */
+  int32_t head_dim;   /* d (must be 128) */
+  int32_t n_queries;  /* nq: buffered queries, the last nq cache positions */
+  int32_t seq_len;    /* L: cached tokens */
+  int32_t dtype;      /* CORE_DTYPE_* of Q, K, V */
+} core_dims_t;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int core_version(void);
+
+/* Copies the last error message of the calling host thread into buf. */
+int core_last_error(char* buf, size_t buf_len);
+
+/* Reads and clears the device status word written by the kernels; returns
+ * CORE_OK or the first recorded CORE_ERR_* code.  Synchronises `stream`. */
+int core_check_device_status(void* stream);
+
+/* ---------------------------------------------------------------------------
+ * QK relation features f1..f6 and causal row LSE.
+ * Replaces strict_causal_qk_features (core/fused_qk.py:373-587) including its
+ * kernels _causal_row_lse_kernel (:26-107), _grouped_relation_tile_kernel
+ * (:110-230), _basic_relation_stats_kernel (:233-292) and the top-k
+ * reductions (:527-582).
+ *   q          : (B, Hq, nq, d)
+ *   k          : (B, Hkv, L, d)
+ *   lse_in     : optional (B, Hq, nq) f32 external row LSE (FlashAttention's
+ *                softmax_lse); when non-NULL the LSE pass is skipped (:444-456)
+ *   lse_out    : optional (B, Hq, nq) f32
+ *   features   : (B, L, feature_stride) f32, columns 0..5 receive f1..f6
+ * ------------------------------------------------------------------------- */
+size_t core_qk_features_workspace_bytes(const core_dims_t* dims);
+int core_qk_features(const core_dims_t* dims, const void* q, const void* k,
+                     int32_t topk_qk, int32_t n_recent_queries, const float* lse_in,
+                     float* lse_out, float* features, int32_t feature_stride,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Coverage features o, d_proto, delta_proto, g.
+ * Replaces COREFeatureExtractor.compute_coverage_features
+ * (core/features.py:790-858) with LayerwiseKeyGeometryProjector.forward
+ * (:53-77), PrototypeBank.get_coverage_features (:146-213) and
+ * HadamardProjector.rotate (:259-261).
+ *   geometry_split : (3, P, Hkv*d) bf16, the layer's fp32 Gaussian projection
+ *                    split into hi/mid/lo bf16 terms by core_split_bf16
+ *   prototypes     : (64, P) f32 unit rows;  hadamard : (P, P) f32
+ *   features       : (B, L, feature_stride) f32, columns col0..col0+3
+ * P (proto_dim) must be 64 and the prototype count 64.
+ * ------------------------------------------------------------------------- */
+size_t core_coverage_workspace_bytes(const core_dims_t* dims);
+int core_coverage_features(const core_dims_t* dims, const void* k, const void* geometry_split,
+                           const float* prototypes, const float* hadamard, float shrinkage_rho,
+                           float* features, int32_t feature_stride, int32_t col0,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Auxiliary features + indexer MLP -> per-token scores.
+ * Replaces compute_auxiliary_features (core/features.py:861-921), the
+ * feature concatenation (core/kvpress_adapter.py:536) and COREIndexerMLP
+ * (core/indexer.py:88-108, 14 -> 128 -> 128 -> 1, exact GELU).
+ *   v          : (B, Hkv, L, d)
+ *   positions  : (B, L) int64 original token positions of the cache slots
+ *   special    : optional (B, L) uint8, 1 where the token id is a special id
+ *   features   : (B, L, 14) f32; columns 0..9 already hold f1..f6 and the
+ *                coverage features; columns 10..13 are written here
+ *   mlp        : packed f32 [w1 (128,14) | b1 (128) | w2 (128,128) | b2 (128) |
+ *                w3 (128) | b3 (1)]
+ *   scores     : (B, L) f32
+ * ------------------------------------------------------------------------- */
+int core_indexer_scores(const core_dims_t* dims, const void* v, const int64_t* positions,
+                        const uint8_t* special, int32_t original_length, int32_t is_prefill,
+                        int32_t n_sink, float* features, const float* mlp, float* scores,
+                        void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Top-B selection with sink protection.
+ * Replaces the sink saturation of COREScorerPress.score
+ * (core/kvpress_adapter.py:773-778) and the pooled stable descending argsort,
+ * truncation and chronological re-sort of COREMemoryPress.compress (:1017-1025).
+ *   scores    : (B, L) f32 calibrated scores
+ *   keep_idx  : (B, n_kept) int32, ascending
+ *   evict_idx : (B, L - n_kept) int32, ascending
+ * Ties are broken toward the lower index (stable sort).
+ * ------------------------------------------------------------------------- */
+size_t core_topb_workspace_bytes(int32_t batch, int32_t seq_len);
+int core_topb_select(const float* scores, int32_t batch, int32_t seq_len, int32_t n_kept,
+                     int32_t n_sink, int32_t* keep_idx, int32_t* evict_idx, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Latent-memory write and decayed recurrence (pre_o_proj value space).
+ * Replaces core/kvpress_adapter.py:1041-1202 (student_distribution,
+ * conditional_evicted_weights, phi = K Theta_f^T, M_bar, b_bar, and the
+ * Z/M/b recurrence).
+ *   scores_cal  : (B, L) f32 calibrated (unsaturated) scores
+ *   evict_idx   : (B, n_evict) int32 from core_topb_select
+ *   theta_split : (2, d_mem, Hkv*d) bf16 hi/lo of the group-folded Theta
+ *   M           : (B, d_mem, Hkv*d) f32, updated in place
+ *   b_state     : (B, d_mem) f32, updated in place
+ *   Z           : (B,) f32, updated in place (0 for a fresh layer)
+ * d_mem must be a multiple of 128 (<= 512).
+ * ------------------------------------------------------------------------- */
+size_t core_memory_write_workspace_bytes(const core_dims_t* dims, int32_t n_evict, int32_t d_mem);
+int core_memory_write(const core_dims_t* dims, const void* k, const void* v,
+                      const float* scores_cal, const int32_t* evict_idx, int32_t n_evict,
+                      const void* theta_split, int32_t d_mem, float gamma, float eta,
+                      float student_temp, float* M, float* b_state, float* Z, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Retained-KV gather.  Replaces keys.gather / values.gather
+ * (core/kvpress_adapter.py:1204-1210).  out_k / out_v: (B, Hkv, n_kept, d).
+ * ------------------------------------------------------------------------- */
+int core_compact_kv(const core_dims_t* dims, const void* k, const void* v,
+                    const int32_t* keep_idx, int32_t n_kept, void* out_k, void* out_v,
+                    void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Gated latent-memory readout added to the attention output.
+ * Replaces MemoryModule.readout (core/indexer.py:165-207) and the folded
+ * o_proj projection of COREMemoryPress.apply_memory_readout
+ * (core/kvpress_adapter.py:1302-1352).
+ *   q        : (B, Hq, q_len, d) post-RoPE queries (bf16)
+ *   theta    : (d_mem, Hq*d) f32;  gate_w1 : (gh, Hq*d) f32; gate_b1 : (gh)
+ *   gate_w2  : (gh) f32; gate_b2 : scalar f32 (pointer)
+ *   M, b     : layer fast state (B, d_mem, Hkv*d), (B, d_mem) f32
+ *   o_fold   : (hidden, Hkv*d) f32 group-folded o_proj
+ *   attn_out : (B, q_len, hidden) bf16, updated in place
+ * gate_override < 0 uses the learned gate, otherwise the constant gate.
+ * ------------------------------------------------------------------------- */
+size_t core_memory_readout_workspace_bytes(const core_dims_t* dims, int32_t q_len,
+                                           int32_t d_mem, int32_t gate_hidden);
+int core_memory_readout(const core_dims_t* dims, int32_t q_len, const void* q, const float* theta,
+                        const float* gate_w1, const float* gate_b1, const float* gate_w2,
+                        const float* gate_b2, int32_t d_mem, int32_t gate_hidden,
+                        float gate_override, const float* M, const float* b_state,
+                        const float* o_fold, int32_t hidden, void* attn_out, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Weight preparation: split an f32 array into `terms` (2 or 3) bf16 arrays
+ * whose sum reproduces it (hi = bf16(x), mid = bf16(x - hi), lo = ...).
+ * Used once per layer for the geometry projection and the folded Theta.
+ * No reference counterpart (the reference multiplies in f32 directly).
+ * ------------------------------------------------------------------------- */
+int core_split_bf16(const float* src, int64_t n, int32_t terms, void* dst, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CORE_B200_H_ */
