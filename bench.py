@@ -1,0 +1,377 @@
+"""Benchmark: CORE KV-compression step on B200.
+
+Workload (the headline configuration): a 32-layer Llama-3.1-8B-shaped KV cache
+(8 KV heads, 32 query heads, d = 128), bf16, batch 1, 16384 cached tokens per
+layer, a 128-query scoring window, compression_ratio 0.75 (4096 kept, 4 sinks),
+latent-memory write with d_mem 512.  One step = compressing all 32 layers.
+Inputs are seeded synthetic Gaussian-with-outlier caches and random-init
+indexer / memory weights (no checkpoints or datasets are available).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Under torchrun every rank compresses its own sequence (batch sharding, no
+collective on the data path); ``value`` is the whole-job rate over the slowest
+rank.  ``--impl reference`` times the CPU restatement of the reference
+algorithm (oracle/core_oracle.py) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "KV tokens compressed/sec per B200 (16K ctx, 32 layers); % tensor/HBM roofline"
+UNIT = "tokens/s"
+KERNELS_PER_LAYER = 15  # LSE, combine, relation, merge, 4 coverage, scores, Top-B, 4 memory, gather
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--seq-len", type=int, default=16384)
+    p.add_argument("--n-queries", type=int, default=128)
+    p.add_argument("--ratio", type=float, default=0.75)
+    p.add_argument("--d-mem", type=int, default=512)
+    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def config_dict(a, n):
+    return {"workload": f"core_full compression step, {a.layers} layers x 1 sequence x "
+                        f"{a.seq_len} tokens per rank",
+            "layers": a.layers, "batch_per_rank": 1, "seq_len": a.seq_len,
+            "n_kv_heads": 8, "n_q_heads": 32, "head_dim": 128, "query_buffer": a.n_queries,
+            "compression_ratio": a.ratio, "n_kept": int(a.seq_len * (1 - a.ratio)),
+            "d_mem": a.d_mem, "parallelism": f"batch-sharded x{n}",
+            "l2": "inputs larger than L2 (32 layers x 64 MiB of K/V per step)"}
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the oracle port on a bounded sample
+# ---------------------------------------------------------------------------
+def cpu_layer_sample(a, seed=0):
+    """Time the oracle's compress_layer on one layer of the workload."""
+    from core_b200 import checkpoint as C
+    from oracle import core_oracle as O
+    rng = np.random.default_rng(seed)
+    L, nq = a.seq_len, a.n_queries
+    out_idx = np.stack([rng.choice(128, 4, replace=False) for _ in range(8)])
+
+    def go(h, n, idx):
+        x = rng.standard_normal((h, n, 128), dtype=np.float32) / np.float32(np.sqrt(128))
+        for i in range(h):
+            x[i, :, idx[i]] *= 8
+        return O.bf16_round(x)
+    k = go(8, L, out_idx)
+    q = go(32, nq, np.repeat(out_idx, 4, axis=0))
+    v = O.bf16_round(rng.standard_normal((8, L, 128), dtype=np.float32))
+    parts = C.random_checkpoint_parts(seed=seed, n_layers=1, n_kv_heads=8, n_q_heads=32, d_mem=a.d_mem)
+    mlp = tuple(t.numpy() for t in parts["indexer"].modules[0])
+    geo = parts["geometry"]
+    w = O.LayerWeights(mlp=mlp, geometry=geo.weight[0].numpy(), prototypes=geo.prototypes.numpy(),
+                       hadamard=geo.hadamard.numpy(), theta=parts["memory"].modules[0][0].numpy())
+    t0 = time.perf_counter()
+    O.compress_layer(q, k, v, w, compression_ratio=a.ratio, is_prefill=True, round_bf16=True)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(a):
+    t = cpu_layer_sample(a)
+    return {"value": a.seq_len / (t * a.layers), "unit": UNIT, "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": f"1 of {a.layers} layers (L={a.seq_len}, nq={a.n_queries}, bf16-rounded "
+                      f"inputs) through oracle.core_oracle.compress_layer in {t:.2f} s, "
+                      f"scaled by 1/{a.layers}; numpy/BLAS threads = host cores"}
+
+
+def run_reference(a, rank):
+    if rank != 0:
+        return
+    steps = max(1, min(a.steps, 3))
+    warm = min(a.warmup, 1)
+    for _ in range(warm):
+        cpu_layer_sample(a, seed=1)
+    times = [cpu_layer_sample(a, seed=2 + i) for i in range(steps)]
+    t = statistics.median(times)
+    value = a.seq_len / (t * a.layers)
+    sample = (f"{steps} timed samples (+{warm} warm-up) of 1 of {a.layers} layers each "
+              f"(L={a.seq_len}, nq={a.n_queries}) through oracle.core_oracle.compress_layer, "
+              f"median {t:.2f} s per layer, scaled by 1/{a.layers}")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": a.gpus,
+            "steps": steps, "warmup": warm, "ms_per_step": t * a.layers * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": config_dict(a, 1),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU
+# ---------------------------------------------------------------------------
+def build_layers(a, dev, seed_base=1000):
+    from core_b200 import checkpoint as C
+    from core_b200 import engine, synthetic
+    parts = C.random_checkpoint_parts(seed=seed_base, n_layers=a.layers, n_kv_heads=8, n_q_heads=32,
+                                      d_mem=a.d_mem)
+    geo = parts["geometry"]
+    layers = []
+    for l in range(a.layers):
+        q, k, v = synthetic.make_layer_inputs(seed=seed_base + 7 * l, batch=1, n_kv_heads=8,
+                                              n_q_heads=32, seq_len=a.seq_len,
+                                              n_queries=a.n_queries, device=dev)
+        lw = engine.LayerWeights.prepare(
+            geometry=geo.weight[l], prototypes=geo.prototypes, hadamard=geo.hadamard,
+            mlp_params=parts["indexer"].modules[l], theta=parts["memory"].modules[l][0],
+            n_kv_heads=8, n_q_heads=32, device=dev)
+        mem = engine.MemoryState.zeros(1, a.d_mem, 8 * 128, dev)
+        layers.append((q, k, v, lw, mem))
+    return parts, layers
+
+
+def main():
+    a = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n = world
+    from core_b200 import engine, ops
+
+    parts, layers = build_layers(a, dev)
+    L = a.seq_len
+    n_kept = engine.n_kept_for(L, a.ratio, 4)
+    pos = torch.arange(L, device=dev)[None]
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+    # one (start, end) pair per layer and timed step, around the QK relation kernel
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(a.layers)] for _ in range(a.steps)]
+    for pairs in ev:  # materialise the event handles before the timed region
+        for e0, e1 in pairs:
+            e0.record()
+            e1.record()
+    torch.cuda.synchronize()
+
+    def step(pairs):
+        for l, (q, k, v, lw, mem) in enumerate(layers):
+            engine.compress_layer(q, k, v, lw, n_kept=n_kept, positions=pos, original_length=L,
+                                  is_prefill=True, memory=mem, workspace=ws,
+                                  timing_events=None if pairs is None else pairs[l])
+
+    for _ in range(a.warmup):
+        step(None)
+    torch.cuda.synchronize()
+    ops.status(dev)
+
+    # ---- timed region: device-resident inputs ----
+    with ClockSampler(local) as clocks:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(a.steps):
+            step(ev[i])
+        t1.record()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+    ms = t0.elapsed_time(t1) / a.steps
+    relation_ms = [e0.elapsed_time(e1) for pairs in ev for e0, e1 in pairs]
+    ops.status(dev)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = n * L / (ms / 1e3)
+
+    # ---- roofline of the dominant kernel (QK relation pass) ----
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, peak_src = 1590.0, "fallback"
+    if os.path.exists(peaks_path):
+        pk = json.load(open(peaks_path))
+        peak, peak_src = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))), "measured"
+    flops = 2.0 * 32 * a.n_queries * L * 128
+    rel_ms = statistics.mean(relation_ms)
+    achieved = flops / (rel_ms / 1e3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "qk_relation_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            tr = json.load(open(tpath))
+            if int(tr.get("seq_len", 0)) == L:
+                traffic = tr.get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    roofline = {"kernel": "qk_relation_kernel (QK pass 2: relation + per-key statistics)",
+                "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "peak_source": f"{peak_src} bf16_tflops_sustained",
+                "traffic": traffic, "avg_launch_ms": rel_ms,
+                "algorithmic": f"2*Hq*nq*L*d = {flops / 1e9:.2f} GFLOP per launch"}
+
+    # ---- end to end through the press API with host buffers ----
+    e2e = run_e2e(a, dev, parts, layers, dist)
+
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": config_dict(a, n), "roofline": roofline, "e2e": e2e,
+            "gpu_launches": KERNELS_PER_LAYER * a.layers * a.steps,
+            "clocks": clocks.summary()}
+    if rank == 0 and n == 1 and not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(a)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+class _FakeAttn:
+    """Minimal attention module for the press API: layer index, config and the
+    post-RoPE queries the CORE attention adapter stashes."""
+
+    def __init__(self, layer_idx):
+        self.layer_idx = layer_idx
+        self.q_proj = True
+
+
+def run_e2e(a, dev, parts, layers, dist):
+    """Per step: pinned H2D of every layer's K, V and scoring queries, the
+    press's compress() for every layer, D2H of retained positions and Z."""
+    from core_b200 import press as P
+    L, nq = a.seq_len, a.n_queries
+    cfg = parts["config"]
+    cfg.prefill_qk_scope = "question"
+    base = P.COREScorerPress(indexer=parts["indexer"].to(dev), feature_extractor=parts["geometry"].to(dev),
+                             compression_ratio=a.ratio, use_indexer_stack=True, scoring_layer_idx=-1,
+                             n_sink_protect=4, prefill_qk_scope="question")
+    press = P.COREMemoryPress(base_press=base, memory_module=parts["memory"].to(dev))
+    host = []
+    for (q, k, v, _, _) in layers:
+        host.append((q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()))
+    full_q = torch.zeros(1, 32, L, 128, dtype=torch.bfloat16, device=dev)
+    hs = torch.zeros(1, L, 1, device=dev)
+    mods = [_FakeAttn(l) for l in range(a.layers)]
+    h2d = sum(t.numel() * t.element_size() for h in host for t in h)
+    d2h_per_step = [0]
+
+    def step():
+        press.reset_cache()
+        base.set_query_boundary(L - nq)
+        results = []
+        for l, (hq, hk, hv) in enumerate(host):
+            k = hk.to(dev, non_blocking=True)
+            v = hv.to(dev, non_blocking=True)
+            full_q[:, :, L - nq:].copy_(hq, non_blocking=True)
+            mods[l]._core_cached_query_states = full_q
+            press.compress(mods[l], hs, k, v, None, {})
+            results.append(base.cache_metadata.positions[l])
+            results.append(press._Z[l])
+        out = [r.to("cpu", non_blocking=True) for r in results]
+        torch.cuda.current_stream().synchronize()
+        d2h_per_step[0] = sum(o.numel() * o.element_size() for o in out)
+        return out
+
+    step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(a.e2e_steps):
+        step()
+    torch.cuda.synchronize()
+    dt = (time.perf_counter() - t0) / a.e2e_steps
+    if dist is not None:
+        t = torch.tensor([dt], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    n = dist.get_world_size() if dist is not None else 1
+    return {"value": n * L / dt, "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h_per_step[0], "ms_per_step": dt * 1e3,
+            "steps": a.e2e_steps,
+            "path": "core_b200.press.COREMemoryPress.compress per layer, inputs from pinned host memory"}
+
+
+if __name__ == "__main__":
+    main()

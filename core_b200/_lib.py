@@ -38,6 +38,32 @@ class CoreDims(ctypes.Structure):
     ]
 
 
+class CoreLayerWeights(ctypes.Structure):
+    _fields_ = [
+        ("geometry_split", ctypes.c_void_p),
+        ("prototypes", ctypes.c_void_p),
+        ("hadamard", ctypes.c_void_p),
+        ("mlp", ctypes.c_void_p),
+        ("theta_split", ctypes.c_void_p),
+        ("d_mem", ctypes.c_int32),
+    ]
+
+
+class CoreCompressArgs(ctypes.Structure):
+    _fields_ = [
+        ("n_kept", ctypes.c_int32),
+        ("n_sink", ctypes.c_int32),
+        ("topk_qk", ctypes.c_int32),
+        ("n_recent_queries", ctypes.c_int32),
+        ("shrinkage_rho", ctypes.c_float),
+        ("original_length", ctypes.c_int32),
+        ("is_prefill", ctypes.c_int32),
+        ("gamma", ctypes.c_float),
+        ("eta", ctypes.c_float),
+        ("student_temp", ctypes.c_float),
+    ]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 _F = ctypes.c_float
@@ -64,6 +90,11 @@ SIGNATURES = {
     "core_memory_readout": (ctypes.c_int, [_D, _I, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P, _P, _P,
                                            _I, _P, _P, _S, _P]),
     "core_split_bf16": (ctypes.c_int, [_P, ctypes.c_int64, _I, _P, _P]),
+    "core_compress_layer_workspace_bytes": (_S, [_D, _I, _I]),
+    "core_compress_layer": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P,
+                                           ctypes.POINTER(CoreLayerWeights),
+                                           ctypes.POINTER(CoreCompressArgs), _P, _P, _P, _P, _P,
+                                           _P, _P, _P, _P, _P, _S, _P, _P, _P]),
 }
 
 

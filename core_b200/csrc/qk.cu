@@ -888,7 +888,8 @@ int plan_qk(const core_dims_t* d, int topk, int n_recent, QKPlan* out) {
 
 template <int G>
 int launch_qk(const QKPlan& plan, const CUtensorMap& tmQ_lse, const CUtensorMap& tmQ_rel,
-              const CUtensorMap& tmK, bool run_lse, float* lse_buf, cudaStream_t s) {
+              const CUtensorMap& tmK, bool run_lse, float* lse_buf, cudaStream_t s,
+              cudaEvent_t ev0, cudaEvent_t ev1) {
   const Params& p = plan.p;
   cudaError_t e;
   if (run_lse) {
@@ -904,8 +905,10 @@ int launch_qk(const QKPlan& plan, const CUtensorMap& tmQ_lse, const CUtensorMap&
   const uint32_t smem = RelSmem<G>::kTotal + 1024;
   e = cudaFuncSetAttribute(qk_relation_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_error(e, "qk_relation_kernel attribute");
+  if (ev0 != nullptr) cudaEventRecord(ev0, s);
   qk_relation_kernel<G><<<plan.grid, kThreads, smem, s>>>(tmQ_rel, tmK, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_relation_kernel launch");
+  if (ev1 != nullptr) cudaEventRecord(ev1, s);
   return CORE_OK;
 }
 
@@ -922,10 +925,27 @@ extern "C" size_t core_qk_features_workspace_bytes(const core_dims_t* d) {
   return z.used;
 }
 
+namespace core {
+int qk_features_impl(const core_dims_t* d, const void* q, const void* k, int32_t topk_qk,
+                     int32_t n_recent_queries, const float* lse_in, float* lse_out,
+                     float* features, int32_t feature_stride, void* workspace,
+                     size_t workspace_bytes, void* stream, void* ev0, void* ev1);
+}
+
 extern "C" int core_qk_features(const core_dims_t* d, const void* q, const void* k,
                                 int32_t topk_qk, int32_t n_recent_queries, const float* lse_in,
                                 float* lse_out, float* features, int32_t feature_stride,
                                 void* workspace, size_t workspace_bytes, void* stream) {
+  return core::qk_features_impl(d, q, k, topk_qk, n_recent_queries, lse_in, lse_out, features,
+                                feature_stride, workspace, workspace_bytes, stream, nullptr,
+                                nullptr);
+}
+
+int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, int32_t topk_qk,
+                           int32_t n_recent_queries, const float* lse_in, float* lse_out,
+                           float* features, int32_t feature_stride, void* workspace,
+                           size_t workspace_bytes, void* stream, void* ev0_, void* ev1_) {
+  cudaEvent_t ev0 = static_cast<cudaEvent_t>(ev0_), ev1 = static_cast<cudaEvent_t>(ev1_);
   int rc = check_dims(d, "core_qk_features");
   if (rc != CORE_OK) return rc;
   if (q == nullptr || k == nullptr || features == nullptr)
@@ -978,9 +998,9 @@ extern "C" int core_qk_features(const core_dims_t* d, const void* q, const void*
   }
   const bool run_lse = (lse_in == nullptr);
   switch (p.G) {
-    case 1: rc = launch_qk<1>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s); break;
-    case 2: rc = launch_qk<2>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s); break;
-    case 4: rc = launch_qk<4>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s); break;
+    case 1: rc = launch_qk<1>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s, ev0, ev1); break;
+    case 2: rc = launch_qk<2>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s, ev0, ev1); break;
+    case 4: rc = launch_qk<4>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s, ev0, ev1); break;
     default: return set_error(CORE_ERR_UNSUPPORTED, "core_qk_features: group size");
   }
   if (rc != CORE_OK) return rc;

@@ -90,34 +90,63 @@ def compress_layer(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
                    n_recent_queries: int = 16, shrinkage_rho: float = 0.1,
                    memory: MemoryState | None = None, gamma: float = 0.9, eta: float = 1.0,
                    student_temp: float = 1.0, special: torch.Tensor | None = None,
-                   lse: torch.Tensor | None = None, score_hook=None) -> dict:
-    """Score, select, write memory and gather for one layer (all batch rows).
+                   lse: torch.Tensor | None = None, timing_events=None,
+                   workspace: torch.Tensor | None = None) -> dict:
+    """Score, select, write memory and gather for one layer (all batch rows)
+    with a single call of ``core_compress_layer``.
 
     q: (B, Hq, nq, 128) bf16 post-RoPE queries of the scoring window;
     keys/values: (B, Hkv, L, 128) bf16.  ``memory`` is updated in place.
-    ``score_hook(scores) -> scores`` may adjust the calibrated scores before
-    selection (recency bonus).  Returns dict(keys, values, keep, evict,
-    scores, features).
+    ``timing_events``: optional (start, end) torch.cuda.Event pair recorded
+    around the QK relation kernel.  Returns dict(keys, values, keep, evict,
+    scores, features); keep/evict are None and keys/values the inputs when
+    n_kept >= L.
     """
-    B, hkv, L, d = keys.shape
-    feats = torch.empty(B, L, 14, dtype=torch.float32, device=keys.device)
-    ops.qk_features(q, keys, topk_qk=topk_qk, n_recent_queries=n_recent_queries, lse=lse,
-                    features=feats)
-    ops.coverage_features(keys, weights.geometry_split, weights.prototypes, weights.hadamard,
-                          shrinkage_rho=shrinkage_rho, features=feats, col0=6)
-    scores = ops.indexer_scores(values, positions, feats, weights.mlp,
-                                original_length=original_length, is_prefill=is_prefill,
-                                n_sink=n_sink, special=special)
-    if score_hook is not None:
-        scores = score_hook(scores)
-    out = dict(scores=scores, features=feats)
-    if n_kept >= L:
-        out.update(keys=keys, values=values, keep=None, evict=None)
-        return out
-    keep, evict = ops.topb_select(scores, n_kept, n_sink)
-    if memory is not None and weights.theta_split is not None and evict.shape[1] > 0:
-        ops.memory_write(keys, values, scores, evict, weights.theta_split, memory.M, memory.b,
-                         memory.Z, gamma=gamma, eta=eta, student_temp=student_temp)
-    ok, ov = ops.compact_kv(keys, values, keep)
-    out.update(keys=ok, values=ov, keep=keep, evict=evict)
-    return out
+    import ctypes
+
+    from . import _lib
+    ops._require_cuda(q, keys, values, positions)
+    q = q.to(torch.bfloat16).contiguous()
+    k = keys.to(torch.bfloat16).contiguous()
+    v = values.to(torch.bfloat16).contiguous()
+    B, hkv, L, d = k.shape
+    Hq, nq = q.shape[1], q.shape[2]
+    dev = k.device
+    dims = _lib.CoreDims(B, Hq, hkv, d, nq, L, _lib.CORE_DTYPE_BF16)
+    write = memory is not None and weights.theta_split is not None
+    d_mem = weights.theta_split.shape[1] if write else 0
+    feats = torch.empty(B, L, 14, dtype=torch.float32, device=dev)
+    scores = torch.empty(B, L, dtype=torch.float32, device=dev)
+    n_ev = max(L - n_kept, 0)
+    keep = torch.empty(B, max(n_kept, 1), dtype=torch.int32, device=dev)
+    evict = torch.empty(B, max(n_ev, 1), dtype=torch.int32, device=dev)
+    compact = n_kept < L
+    ok = torch.empty(B, hkv, n_kept, d, dtype=torch.bfloat16, device=dev) if compact else k
+    ov = torch.empty_like(ok) if compact else v
+    lib = _lib.load()
+    need = lib.core_compress_layer_workspace_bytes(ctypes.byref(dims), int(n_kept), int(d_mem))
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(int(need), 256), dtype=torch.uint8, device=dev)
+    w = _lib.CoreLayerWeights(weights.geometry_split.data_ptr(), weights.prototypes.data_ptr(),
+                              weights.hadamard.data_ptr(), weights.mlp.data_ptr(),
+                              weights.theta_split.data_ptr() if write else 0, int(d_mem))
+    a = _lib.CoreCompressArgs(int(n_kept), int(n_sink), int(topk_qk), int(n_recent_queries),
+                              float(shrinkage_rho), int(original_length), int(bool(is_prefill)),
+                              float(gamma), float(eta), float(student_temp))
+    pos = positions.to(torch.int64).reshape(B, L).contiguous()
+    sp = None if special is None else special.to(torch.uint8).reshape(B, L).contiguous()
+    lse_in = None if lse is None else lse.to(torch.float32).contiguous()
+    ev0 = ev1 = None
+    if timing_events is not None:
+        ev0, ev1 = (ctypes.c_void_p(e.cuda_event) for e in timing_events)
+    P = ops._ptr
+    _lib.check(lib.core_compress_layer(
+        ctypes.byref(dims), P(q), P(k), P(v), P(pos), P(sp), P(lse_in), ctypes.byref(w),
+        ctypes.byref(a), P(feats), P(scores), P(keep), P(evict),
+        P(memory.M if write else None), P(memory.b if write else None),
+        P(memory.Z if write else None), P(ok), P(ov), P(workspace), workspace.numel(),
+        ops._stream(dev), ev0, ev1))
+    if not compact:
+        return dict(keys=keys, values=values, keep=None, evict=None, scores=scores, features=feats)
+    return dict(keys=ok, values=ov, keep=keep, evict=evict[:, :n_ev], scores=scores,
+                features=feats)

@@ -187,6 +187,49 @@ int core_memory_readout(const core_dims_t* dims, int32_t q_len, const void* q, c
                         size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * One layer's complete compression step.
+ * Replaces COREMemoryPress.compress (core/kvpress_adapter.py:968-1210) with
+ * the scores of COREScorerPress.score (:690-797): the QK, coverage and
+ * auxiliary features, the indexer MLP, Top-B with sinks, the memory write
+ * (when theta_split and M are non-NULL) and the retained-KV gather.
+ *   features  : (B, L, 14) f32 out;  scores : (B, L) f32 out (calibrated)
+ *   keep_idx  : (B, n_kept) int32 out;  evict_idx : (B, L - n_kept) int32 out
+ *   out_k/v   : (B, Hkv, n_kept, d) out
+ * When n_kept >= L only features and scores are produced.  ev_begin/ev_end,
+ * when non-NULL, are cudaEvent_t recorded around the QK relation kernel.
+ * ------------------------------------------------------------------------- */
+typedef struct core_layer_weights {
+  const void* geometry_split; /* (3, 64, Hkv*d) bf16 */
+  const float* prototypes;    /* (64, 64) f32 */
+  const float* hadamard;      /* (64, 64) f32 */
+  const float* mlp;           /* packed indexer MLP (see core_indexer_scores) */
+  const void* theta_split;    /* (2, d_mem, Hkv*d) bf16, or NULL: no memory write */
+  int32_t d_mem;
+} core_layer_weights_t;
+
+typedef struct core_compress_args {
+  int32_t n_kept;
+  int32_t n_sink;
+  int32_t topk_qk;
+  int32_t n_recent_queries;
+  float shrinkage_rho;
+  int32_t original_length;
+  int32_t is_prefill;
+  float gamma;
+  float eta;
+  float student_temp;
+} core_compress_args_t;
+
+size_t core_compress_layer_workspace_bytes(const core_dims_t* dims, int32_t n_kept, int32_t d_mem);
+int core_compress_layer(const core_dims_t* dims, const void* q, const void* k, const void* v,
+                        const int64_t* positions, const uint8_t* special, const float* lse_in,
+                        const core_layer_weights_t* weights, const core_compress_args_t* args,
+                        float* features, float* scores, int32_t* keep_idx, int32_t* evict_idx,
+                        float* M, float* b_state, float* Z, void* out_k, void* out_v,
+                        void* workspace, size_t workspace_bytes, void* stream, void* ev_begin,
+                        void* ev_end);
+
+/* ---------------------------------------------------------------------------
  * Weight preparation: split an f32 array into `terms` (2 or 3) bf16 arrays
  * whose sum reproduces it (hi = bf16(x), mid = bf16(x - hi), lo = ...).
  * Used once per layer for the geometry projection and the folded Theta.

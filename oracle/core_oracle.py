@@ -23,6 +23,8 @@ Where the reference rounds to bfloat16 (QK logits, ``fused_qk.py:83-87``;
 from __future__ import annotations
 
 import math
+import os
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass
 
 import numpy as np
@@ -64,6 +66,28 @@ def _f32(x):
 # QK relation features f1..f6
 # ----------------------------------------------------------------------------
 
+def _logits(qh: np.ndarray, kh: np.ndarray, round_bf16: bool) -> np.ndarray:
+    """float32 dot products (BLAS), rounded to bf16 when the inputs are bf16
+    (``fused_qk.py:82-87``)."""
+    x = np.matmul(qh.astype(np.float32), kh.astype(np.float32).T)
+    return bf16_round(x) if round_bf16 else x
+
+
+def _causal_setup(seq_q: int, seq_k: int):
+    q_start = max(0, seq_k - seq_q)
+    key_pos = np.arange(seq_k)
+    q_pos = q_start + np.arange(seq_q)
+    return q_start, key_pos, q_pos, key_pos[None, :] <= q_pos[:, None]
+
+
+def _lse_rows(x: np.ndarray, visible: np.ndarray) -> np.ndarray:
+    """Row log-sum-exp over the visible entries, accumulated in float64."""
+    xm = np.where(visible, x, -np.inf)
+    m = xm.max(axis=1)
+    s = np.exp((xm - m[:, None]).astype(np.float64)).sum(axis=1)
+    return (m + np.log(s)).astype(np.float32)
+
+
 def causal_lse(q: np.ndarray, k: np.ndarray, *, groups: int, round_bf16: bool) -> np.ndarray:
     """Causal row log-sum-exp of ``scale * round(q . k)``.
 
@@ -74,26 +98,12 @@ def causal_lse(q: np.ndarray, k: np.ndarray, *, groups: int, round_bf16: bool) -
     Returns (Hq, Q) float32.
     """
     nq, seq_q, d = q.shape
-    seq_k = k.shape[1]
-    q_start = max(0, seq_k - seq_q)
+    _, _, _, visible = _causal_setup(seq_q, k.shape[1])
     scale = np.float32(d ** -0.5)
-    key_pos = np.arange(seq_k)
-    q_pos = q_start + np.arange(seq_q)
-    visible = key_pos[None, :] <= q_pos[:, None]
     out = np.empty((nq, seq_q), np.float32)
     for h in range(nq):
-        x = _logits(q[h], k[h // groups], round_bf16) * scale
-        x = np.where(visible, x.astype(np.float64), -np.inf)
-        m = x.max(axis=1)
-        s = np.exp(x - m[:, None]).sum(axis=1)
-        out[h] = (m + np.log(s)).astype(np.float32)
+        out[h] = _lse_rows(_logits(q[h], k[h // groups], round_bf16) * scale, visible)
     return out
-
-
-def _logits(qh: np.ndarray, kh: np.ndarray, round_bf16: bool) -> np.ndarray:
-    """Exact dot products (float64), rounded to float32, then to bf16 if asked."""
-    x = (qh.astype(np.float64) @ kh.astype(np.float64).T).astype(np.float32)
-    return bf16_round(x) if round_bf16 else x
 
 
 def grouped_relation(q, k, lse, *, groups: int, topk_qk: int, round_bf16: bool) -> np.ndarray:
@@ -106,37 +116,46 @@ def grouped_relation(q, k, lse, *, groups: int, topk_qk: int, round_bf16: bool) 
     (``:206-210``), invisible entries at the floor (``:465-470``), the group
     sum accumulated head by head in order (``:168-213``), minus the group
     minimum for leave-one-out TopMean (``:217-218``), divided by
-    ``min(topk_qk, groups)`` (``:219``, ``:496``).
+    ``min(topk_qk, groups)`` (``:219``, ``:496``).  When ``lse`` is None it is
+    computed from the same logits (``causal_lse``).  Returns (R, lse).
     """
     nq, seq_q, d = q.shape
     nkv, seq_k, _ = k.shape
-    q_start = max(0, seq_k - seq_q)
+    _, key_pos, q_pos, visible = _causal_setup(seq_q, seq_k)
     scale = np.float32(d ** -0.5)
     head_topk = min(topk_qk, groups)
-    key_pos = np.arange(seq_k)
-    q_pos = q_start + np.arange(seq_q)
-    visible = key_pos[None, :] <= q_pos[:, None]
     cc = np.minimum(q_pos + 1, seq_k).astype(np.float32)
     log_cc = np.log(cc).astype(np.float32)
     single = (cc == 1)[:, None] & visible
     single_val = np.float32(np.log1p(np.exp(np.float64(LOG_FLOOR))))
+    own_lse = lse is None
+    if own_lse:
+        lse = np.empty((nq, seq_q), np.float32)
     R = np.empty((nkv, seq_q, seq_k), np.float32)
-    for h in range(nkv):
+
+    def head(h):
         acc = np.zeros((seq_q, seq_k), np.float32)
-        mn = np.full((seq_q, seq_k), np.inf, np.float32)
+        mn = np.full((seq_q, seq_k), np.inf, np.float32) if head_topk < groups else None
         for g in range(groups):
             qh = h * groups + g
-            x = _logits(q[qh], k[h], round_bf16)
-            r = (x * scale - lse[qh][:, None]) + log_cc[:, None]
+            x = _logits(q[qh], k[h], round_bf16) * scale
+            if own_lse:
+                lse[qh] = _lse_rows(x, visible)
+            r = (x - lse[qh][:, None]) + log_cc[:, None]
             rel = np.maximum(r, LOG_FLOOR) + np.log1p(np.exp(-np.abs(r - LOG_FLOOR)))
-            rel = np.where(visible, rel, LOG_FLOOR).astype(np.float32)
+            rel = np.where(visible, rel, LOG_FLOOR)
             rel = np.where(single, single_val, rel).astype(np.float32)
-            acc = (acc + rel).astype(np.float32)
-            mn = np.minimum(mn, rel)
-        if head_topk < groups:
-            acc = (acc - mn).astype(np.float32)
-        R[h] = (acc / np.float32(head_topk)).astype(np.float32)
-    return R
+            acc += rel
+            if mn is not None:
+                np.minimum(mn, rel, out=mn)
+        if mn is not None:
+            acc -= mn
+        R[h] = acc / np.float32(head_topk)
+
+    # KV heads are independent; numpy releases the GIL inside these array ops
+    with ThreadPoolExecutor(max_workers=min(nkv, os.cpu_count() or 1)) as pool:
+        list(pool.map(head, range(nkv)))
+    return R, lse
 
 
 def _topk_mean(vals: np.ndarray, k_per: np.ndarray, k_max: int) -> np.ndarray:
@@ -198,9 +217,7 @@ def qk_features(q, k, *, groups: int, topk_qk: int = 4, n_recent_queries: int = 
     """
     q = _f32(q)
     k = _f32(k)
-    if lse is None:
-        lse = causal_lse(q, k, groups=groups, round_bf16=round_bf16)
-    R = grouped_relation(q, k, lse, groups=groups, topk_qk=topk_qk, round_bf16=round_bf16)
+    R, lse = grouped_relation(q, k, lse, groups=groups, topk_qk=topk_qk, round_bf16=round_bf16)
     feats = qk_features_from_relation(R, seq_k=k.shape[1], topk_qk=topk_qk,
                                       n_recent_queries=n_recent_queries)
     return feats, lse, R

@@ -257,6 +257,27 @@ def run_two_step_case(ref, name, *, seed, hkv=2, hq=8, d=128, L0=384, nq=64,
     return res, meta
 
 
+def save_reference_checkpoint(ref, *, seed, out, hkv=2, hq=8, d=128, d_mem=64, gate_hidden=64,
+                              hidden=128):
+    """The two-step case's stacks written by the reference's own save_indexer_stack
+    (core/train.py:2982-3047), for the checkpoint-format tests."""
+    import shutil
+    import torch
+    from core.train import save_indexer_stack
+    press, scorer, indexer, memory, fe, o_proj, q_proj, cap = build_press(
+        ref, seed=seed, n_layers=2, hkv=hkv, hq=hq, d=d, d_mem=d_mem, gate_hidden=gate_hidden,
+        hidden=hidden, ratio=0.5, dtype="bfloat16", scope="question")
+    cfg = fe.config
+    cfg.n_sink_protect = 4
+    cfg.compression_ratio = 0.5
+    cfg.prefill_qk_scope = "question"
+    cfg.span_selection_mode = "tokenwise"
+    tmp = Path(tempfile.mkdtemp(prefix="core_ckpt_"))
+    cfg.output_dir = str(tmp)
+    save_indexer_stack(indexer, cfg, history=[], feature_extractor=fe, memory_module=memory)
+    shutil.copy(tmp / "indexer" / "core_indexer.pt", out)
+
+
 CASES = [
     ("fp32_decode_L512_Q64", dict(seed=0, hkv=2, hq=8, d=128, L=512, nq=64,
                                   ratio=0.75, dtype="float32", scope="decode")),
@@ -302,6 +323,7 @@ def main():
         print("wrote", name, {k: getattr(v, "shape", None) for k, v in res.items()
                               if k in ("features", "keep", "M")})
     res, meta = run_two_step_case(ref, "bf16_two_step_L384_Q64", seed=6)
+    save_reference_checkpoint(ref, seed=6, out=HERE / "core_indexer_two_step.pt")
     np.savez_compressed(HERE / "bf16_two_step_L384_Q64.npz", meta=np.array(repr(meta)),
                         **pack(res, meta, readout=True))
     print("wrote two-step", res["keep1"].shape, res["keep2"].shape)
