@@ -35,7 +35,8 @@ if ROOT not in sys.path:
 
 METRIC = "KV tokens compressed/sec per B200 (16K ctx, 32 layers); % tensor/HBM roofline"
 UNIT = "tokens/s"
-KERNELS_PER_LAYER = 15  # LSE, combine, relation, merge, 4 coverage, scores, Top-B, 4 memory, gather
+# LSE, combine, relation, merge, f6 resolve, 4 coverage, scores, Top-B, 4 memory write, gather
+KERNELS_PER_LAYER = 16
 
 
 def parse():

@@ -40,9 +40,8 @@ class CoreDims(ctypes.Structure):
 
 class CoreLayerWeights(ctypes.Structure):
     _fields_ = [
-        ("geometry_split", ctypes.c_void_p),
+        ("geometry_ext", ctypes.c_void_p),
         ("prototypes", ctypes.c_void_p),
-        ("hadamard", ctypes.c_void_p),
         ("mlp", ctypes.c_void_p),
         ("theta_split", ctypes.c_void_p),
         ("d_mem", ctypes.c_int32),
@@ -78,7 +77,8 @@ SIGNATURES = {
     "core_qk_features_workspace_bytes": (_S, [_D]),
     "core_qk_features": (ctypes.c_int, [_D, _P, _P, _I, _I, _P, _P, _P, _I, _P, _S, _P]),
     "core_coverage_workspace_bytes": (_S, [_D]),
-    "core_coverage_features": (ctypes.c_int, [_D, _P, _P, _P, _P, _F, _P, _I, _I, _P, _S, _P]),
+    "core_coverage_features": (ctypes.c_int, [_D, _P, _P, _P, _F, _P, _I, _I, _P, _S, _P]),
+    "core_prepare_geometry": (ctypes.c_int, [_P, _P, _I, _P, _P]),
     "core_indexer_scores": (ctypes.c_int, [_D, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P]),
     "core_topb_workspace_bytes": (_S, [_I, _I]),
     "core_topb_select": (ctypes.c_int, [_P, _I, _I, _I, _I, _P, _P, _P, _S, _P]),

@@ -54,9 +54,8 @@ extern "C" int core_compress_layer(const core_dims_t* d, const void* q, const vo
   if ((rc = qk_features_impl(d, q, k, a->topk_qk, a->n_recent_queries, lse_in, nullptr, features,
                              14, workspace, workspace_bytes, stream, ev_begin, ev_end)) != CORE_OK)
     return rc;
-  if ((rc = core_coverage_features(&e, k, w->geometry_split, w->prototypes, w->hadamard,
-                                   a->shrinkage_rho, features, 14, 6, workspace, workspace_bytes,
-                                   stream)) != CORE_OK)
+  if ((rc = core_coverage_features(&e, k, w->geometry_ext, w->prototypes, a->shrinkage_rho,
+                                   features, 14, 6, workspace, workspace_bytes, stream)) != CORE_OK)
     return rc;
   if ((rc = core_indexer_scores(&e, v, positions, special, a->original_length, a->is_prefill,
                                 a->n_sink, features, w->mlp, scores, stream)) != CORE_OK)

@@ -17,8 +17,25 @@ namespace idx {
 
 constexpr int kIn = 14;
 constexpr int kHid = 128;
-constexpr int kThreads = 128;
+constexpr int kThreads = 128;          // 32 tokens x 4 threads
+constexpr int kTok = kThreads / 4;
 constexpr int kMlpFloats = kHid * kIn + kHid + kHid * kHid + kHid + kHid + 1;
+// shared-memory layout (floats): padded rows keep the four threads of a token
+// on distinct banks
+constexpr int kW1Stride = 16;
+constexpr int kW2Stride = 132;
+constexpr int kH1Stride = 132;
+constexpr int kOffW1 = 0;
+constexpr int kOffB1 = kOffW1 + kHid * kW1Stride;
+constexpr int kOffW2 = kOffB1 + kHid;
+constexpr int kOffB2 = kOffW2 + kHid * kW2Stride;
+constexpr int kOffW3 = kOffB2 + kHid;
+constexpr int kOffB3 = kOffW3 + kHid;
+constexpr int kOffH1 = kOffB3 + 4;
+constexpr int kOffX = kOffH1 + kTok * kH1Stride;
+constexpr int kOffHs = kOffX + kTok * 16;
+constexpr int kMaxHkv = 16;
+constexpr int kSmemFloats = kOffHs + kTok * kMaxHkv;
 
 __device__ __forceinline__ float gelu(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
@@ -37,87 +54,125 @@ struct Params {
 
 __global__ void __launch_bounds__(kThreads)
     indexer_scores_kernel(const Params p) {
-  extern __shared__ float sw[];
-  for (int i = threadIdx.x; i < kMlpFloats; i += blockDim.x) sw[i] = p.mlp[i];
-  __syncthreads();
-  const float* w1 = sw;
-  const float* b1 = w1 + kHid * kIn;
-  const float* w2 = b1 + kHid;
-  const float* b2 = w2 + kHid * kHid;
-  const float* w3 = b2 + kHid;
-  const float b3 = w3[kHid];
-
-  const long long gi = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (gi >= (long long)p.B * p.L) return;
-  const int b = (int)(gi / p.L);
-  const int i = (int)(gi % p.L);
-  float* f = p.features + gi * kIn;
-
-  // ---- auxiliary features (features.py:886-921) ----
-  const long long pos = p.positions[gi];
-  const int T = p.original_length;
-  if (pos < 0 || pos >= T) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
-  const float age_den = log1pf((float)(T - 1 > 1 ? T - 1 : 1));
-  const float a_age = log1pf((float)(T - 1 - pos)) / age_den;
-  bool sink = pos < p.n_sink;
-  if (p.special != nullptr && p.special[gi]) sink = true;
-  // a_value = log1p(mean_h |v_h|^2 / d) with bf16 rounding at each torch op
-  float hsum = 0.f;
-  for (int h = 0; h < p.Hkv; ++h) {
-    const uint4* row = reinterpret_cast<const uint4*>(p.v + (((long long)b * p.Hkv + h) * p.L + i) * 128);
-    float s = 0.f;
-#pragma unroll 4
-    for (int c = 0; c < 16; ++c) {
-      const uint4 w = row[c];
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 x = __bfloat1622float2(h2[e]);
-        s += bf16_round(x.x * x.x);
-        s += bf16_round(x.y * x.y);
-      }
+  extern __shared__ float sm[];
+  {
+    const float* w1 = p.mlp;
+    const float* b1 = w1 + kHid * kIn;
+    const float* w2 = b1 + kHid;
+    const float* b2 = w2 + kHid * kHid;
+    const float* w3 = b2 + kHid;
+    for (int i = threadIdx.x; i < kHid * kIn; i += blockDim.x)
+      sm[kOffW1 + (i / kIn) * kW1Stride + (i % kIn)] = w1[i];
+    for (int i = threadIdx.x; i < kHid * kHid; i += blockDim.x)
+      sm[kOffW2 + (i / kHid) * kW2Stride + (i % kHid)] = w2[i];
+    for (int i = threadIdx.x; i < kHid; i += blockDim.x) {
+      sm[kOffB1 + i] = b1[i];
+      sm[kOffB2 + i] = b2[i];
+      sm[kOffW3 + i] = w3[i];
     }
-    hsum += bf16_round(s);
+    if (threadIdx.x == 0) sm[kOffB3] = w3[kHid];
   }
-  const float vmean = bf16_round(hsum / (float)p.Hkv);
-  const float a_value = bf16_round(log1pf(bf16_round(vmean / 128.0f)));
-  f[10] = a_age;
-  f[11] = sink ? 1.0f : 0.0f;
-  f[12] = a_value;
-  f[13] = p.is_prefill ? 0.0f : 1.0f;
+  __syncthreads();
+  const int tl = threadIdx.x >> 2;  // token within the group
+  const int part = threadIdx.x & 3;
+  const long long ngroups = ((long long)p.B * p.L + kTok - 1) / kTok;
+  for (long long grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
+  const long long gi = grp * kTok + tl;
+  const bool active = gi < (long long)p.B * p.L;
+  const int b = active ? (int)(gi / p.L) : 0;
+  const int i = active ? (int)(gi % p.L) : 0;
+  float* hs = sm + kOffHs + tl * kMaxHkv;
+  float* xs = sm + kOffX + tl * 16;
 
+  // ---- a_value: bf16-rounded |v_h|^2 per head, heads split over the 4 threads ----
+  if (active) {
+    for (int h = part; h < p.Hkv; h += 4) {
+      const uint4* row = reinterpret_cast<const uint4*>(p.v + (((long long)b * p.Hkv + h) * p.L + i) * 128);
+      float s = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < 16; ++c) {
+        const uint4 w = row[c];
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 x = __bfloat1622float2(h2[e]);
+          s += bf16_round(x.x * x.x);
+          s += bf16_round(x.y * x.y);
+        }
+      }
+      hs[h] = bf16_round(s);
+    }
+  }
+  __syncwarp();
+  if (active && part == 0) {
+    // auxiliary features (features.py:886-921), heads summed in order
+    const long long pos = p.positions[gi];
+    const int T = p.original_length;
+    if (pos < 0 || pos >= T) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
+    const float age_den = log1pf((float)(T - 1 > 1 ? T - 1 : 1));
+    const float a_age = log1pf((float)(T - 1 - pos)) / age_den;
+    bool sink = pos < p.n_sink;
+    if (p.special != nullptr && p.special[gi]) sink = true;
+    float hsum = 0.f;
+    for (int h = 0; h < p.Hkv; ++h) hsum += hs[h];
+    const float vmean = bf16_round(hsum / (float)p.Hkv);
+    const float a_value = bf16_round(log1pf(bf16_round(vmean / 128.0f)));
+    float* f = p.features + gi * kIn;
+    f[10] = a_age;
+    f[11] = sink ? 1.0f : 0.0f;
+    f[12] = a_value;
+    f[13] = p.is_prefill ? 0.0f : 1.0f;
+    bool finite = true;
+    for (int k = 0; k < kIn; ++k) {
+      xs[k] = f[k];
+      finite &= isfinite(xs[k]);
+    }
+    if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 602, i);
+  }
+  __syncwarp();
+  // ---- layer 1: this thread's hidden units o = 4 j + part ----
   float x[kIn];
 #pragma unroll
-  for (int k = 0; k < kIn; ++k) x[k] = f[k];
-  bool finite = true;
-#pragma unroll
-  for (int k = 0; k < kIn; ++k) finite &= isfinite(x[k]);
-  if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 602, i);
-
-  // ---- MLP 14 -> 128 -> 128 -> 1 ----
-  float h1[kHid];
-#pragma unroll
-  for (int o = 0; o < kHid; ++o) {
+  for (int k = 0; k < kIn; ++k) x[k] = xs[k];
+  float* h1 = sm + kOffH1 + tl * kH1Stride;
+  for (int j = 0; j < kHid / 4; ++j) {
+    const int o = 4 * j + part;
+    const float* w = sm + kOffW1 + o * kW1Stride;
     float acc = 0.f;
 #pragma unroll
-    for (int k = 0; k < kIn; ++k) acc = fmaf(w1[o * kIn + k], x[k], acc);
-    h1[o] = gelu(acc + b1[o]);
+    for (int k = 0; k < kIn; ++k) acc = fmaf(w[k], x[k], acc);
+    h1[o] = gelu(acc + sm[kOffB1 + o]);
   }
+  __syncwarp();
+  // ---- layer 2 (four outputs at a time) and the output unit ----
   float out = 0.f;
-  for (int o = 0; o < kHid; ++o) {
-    const float4* wr = reinterpret_cast<const float4*>(w2 + o * kHid);
-    float acc = 0.f;
-#pragma unroll
+  const float4* h4 = reinterpret_cast<const float4*>(h1);
+  for (int j = 0; j < kHid / 4; j += 4) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
     for (int k = 0; k < kHid / 4; ++k) {
-      const float4 w = wr[k];
-      acc = fmaf(w.x, h1[4 * k], acc);
-      acc = fmaf(w.y, h1[4 * k + 1], acc);
-      acc = fmaf(w.z, h1[4 * k + 2], acc);
-      acc = fmaf(w.w, h1[4 * k + 3], acc);
+      const float4 hv = h4[k];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int o = 4 * (j + u) + part;
+        const float4 w = reinterpret_cast<const float4*>(sm + kOffW2 + o * kW2Stride)[k];
+        acc[u] = fmaf(w.x, hv.x, acc[u]);
+        acc[u] = fmaf(w.y, hv.y, acc[u]);
+        acc[u] = fmaf(w.z, hv.z, acc[u]);
+        acc[u] = fmaf(w.w, hv.w, acc[u]);
+      }
     }
-    out = fmaf(w3[o], gelu(acc + b2[o]), out);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int o = 4 * (j + u) + part;
+      out = fmaf(sm[kOffW3 + o], gelu(acc[u] + sm[kOffB2 + o]), out);
+    }
   }
-  p.scores[gi] = out + b3;
+  out += __shfl_xor_sync(0xffffffffu, out, 1);
+  out += __shfl_xor_sync(0xffffffffu, out, 2);
+  if (active && part == 0) p.scores[gi] = out + sm[kOffB3];
+  __syncwarp();
+  }
 }
 
 }  // namespace idx
@@ -137,6 +192,8 @@ extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const in
     return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores: NULL tensor");
   if (original_length < d->seq_len)
     return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores: original_length < seq_len");
+  if (d->n_kv_heads > kMaxHkv)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_indexer_scores: at most 16 KV heads");
   Params p{};
   p.B = d->batch;
   p.Hkv = d->n_kv_heads;
@@ -152,12 +209,14 @@ extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const in
   p.scores = scores;
   p.status = device_status();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t smem = sizeof(float) * kMlpFloats;
+  const size_t smem = sizeof(float) * kSmemFloats;
   cudaError_t e =
       cudaFuncSetAttribute(indexer_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_error(e, "indexer_scores_kernel attribute");
   const long long n = (long long)p.B * p.L;
-  indexer_scores_kernel<<<(unsigned)((n + kThreads - 1) / kThreads), kThreads, smem, s>>>(p);
+  long long blocks = (n + kTok - 1) / kTok;
+  if (blocks > 2LL * sm_count()) blocks = 2LL * sm_count();
+  indexer_scores_kernel<<<(unsigned)blocks, kThreads, smem, s>>>(p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "indexer_scores_kernel launch");
   return CORE_OK;
 }

@@ -268,8 +268,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * G * 64 + g * 64 + team * 32), v);
           float cmax = -INFINITY;
 #pragma unroll
+          for (int j = 0; j < 32; j += 2) bf16_round2(v[j], v[j + 1]);
+#pragma unroll
           for (int j = 0; j < 32; ++j) {
-            float x = bf16_round(v[j]) * p.scale_log2;
+            float x = v[j] * p.scale_log2;
             if (need_mask) {
               const int kk = k0 + j;
               if (kk > qpos || kk >= p.L) x = -INFINITY;
@@ -341,8 +343,8 @@ struct RelSmem {
   static constexpr uint32_t kQBytes = 2u * 2u * G * 64u * 128u;  // [katom][half][g][64][128 B]
   static constexpr uint32_t kQOff = 0;
   static constexpr uint32_t kKOff = kQOff + kQBytes;
-  static constexpr uint32_t kLseOff = kKOff + kKStages * kKTileBytes;  // float [G][128]
-  static constexpr uint32_t kCcOff = kLseOff + G * kTile * 4;          // float [128]
+  static constexpr uint32_t kLseOff = kKOff + kKStages * kKTileBytes;  // float2 [G][128]: (-lse, log|C|)
+  static constexpr uint32_t kCcOff = kLseOff + G * kTile * 8;          // unused
   static constexpr uint32_t kXchOff = kCcOff + kTile * 4;              // uint32 [128][16]
   static constexpr uint32_t kBarOff = kXchOff + kTile * 16 * 4;
   static constexpr uint32_t kTotal = kBarOff + 256;
@@ -363,7 +365,7 @@ struct KeyStats {
   }
 };
 
-template <int G>
+template <int G, bool kLoo>
 __global__ void __launch_bounds__(kThreads, 1)
     qk_relation_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK, const Params p) {
@@ -373,8 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
   const uint32_t sQ = sbase + S::kQOff;
   const uint32_t sK = sbase + S::kKOff;
-  float* s_nlse = reinterpret_cast<float*>(sgen + S::kLseOff);
-  float* s_lcc = reinterpret_cast<float*>(sgen + S::kCcOff);
+  float2* s_rc = reinterpret_cast<float2*>(sgen + S::kLseOff);
   uint32_t* s_xch = reinterpret_cast<uint32_t*>(sgen + S::kXchOff);
   const uint32_t bar = sbase + S::kBarOff;
   const uint32_t bar_q_full = bar + 0, bar_q_empty = bar + 8;
@@ -505,18 +506,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (long long u = u0; u < u1 && ok; ++u) {
       Unit t = decode(u, p);
       if (t.grp != cur) {
-        // (re)load -lse and log|C_t| of this query block
+        // (re)load (-lse, log|C_t|) of this query block
         named_barrier(1, kEpiThreads);
         const int tid = threadIdx.x - 64;
         for (int i = tid; i < G * kTile; i += kEpiThreads) {
           const int g = i / kTile, tq = i % kTile;
           const int tt = t.qb * kTile + tq;
-          s_nlse[i] = (tt < p.nq) ? -p.lse[(long long)(t.b * p.Hq + t.h * G + g) * p.nq + tt] : 0.f;
-        }
-        for (int i = tid; i < kTile; i += kEpiThreads) {
-          const long long qpos = (long long)p.q_start + t.qb * kTile + i;
+          const long long qpos = (long long)p.q_start + tt;
           const long long cc = (qpos + 1 < p.L) ? qpos + 1 : p.L;
-          s_lcc[i] = logf((float)cc);
+          const float nl = (tt < p.nq) ? -p.lse[(long long)(t.b * p.Hq + t.h * G + g) * p.nq + tt] : 0.f;
+          s_rc[i] = make_float2(nl, logf((float)cc));
         }
         named_barrier(1, kEpiThreads);
         cur = t.grp;
@@ -534,58 +533,85 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tl0 = hf * 64 + team * 32;  // query index within the block of j = 0
         const bool full = (t.kt * kTile + kTile - 1 <= qb_first_pos) &&
                           (t.kt * kTile + kTile <= p.L) && (tl0 + 32 <= qb_valid);
-        float acc[32];
-        float mn[32];
-        for (int g = 0; g < G; ++g) {
-          float v[32];
-          tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * kN + g * 64 + team * 32), v);
-          const float* nl = s_nlse + g * kTile + tl0;
-          const float* lc = s_lcc + tl0;
+        // 32 queries per thread, processed as two chunks of 16 to bound registers
+        uint32_t msk = 0;
+#pragma unroll 1
+        for (int ch = 0; ch < 2; ++ch) {
+          const int c0 = tl0 + ch * 16;  // query index within the block of element 0
+          float acc[16];
+          float mn[kLoo ? 16 : 1];
+#pragma unroll 1
+          for (int g = 0; g < G; ++g) {
+            float v[16];
+            tmem_ld16(tmem + ((uint32_t)(wq * 32) << 16) +
+                          (uint32_t)(buf * kN + g * 64 + team * 32 + ch * 16), v);
+            const float2* rc = s_rc + g * kTile + c0;
+            float rel[16];
+            float amin = INFINITY;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = bf16_round(v[j]);
-            const float r = fmaf(x, p.scale, nl[j]) + lc[j];
-            float rel = logaddexp_floor(r);
+            for (int j = 0; j < 16; j += 2) bf16_round2(v[j], v[j + 1]);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float2 c = rc[j];
+              const float r = fmaf(v[j], p.scale, c.x) + c.y;
+              const float a = fabsf(r - kLogFloor);
+              amin = fminf(amin, a);
+              // exp(-a) < 1.2e-7 for a >= 16: log1p(x) equals x to within half an ulp of x
+              rel[j] = fmaxf(r, kLogFloor) + ex2_approx(-a * kLog2e);
+              v[j] = r;
+            }
+            if (__any_sync(0xffffffffu, amin < 16.0f)) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float a = fabsf(v[j] - kLogFloor);
+                if (a < 16.0f) rel[j] = fmaxf(v[j], kLogFloor) + log1pf(expf(-a));
+              }
+            }
             if (!full) {
-              const int qpos = qb_first_pos + tl0 + j;
-              if (key > qpos) rel = kLogFloor;
-              else if (qpos == 0) rel = single_val;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int qpos = qb_first_pos + c0 + j;
+                if (key > qpos) rel[j] = kLogFloor;
+                else if (qpos == 0) rel[j] = single_val;
+              }
             }
-            if (g == 0) {
-              acc[j] = rel;
-              mn[j] = rel;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if (g == 0) {
+                acc[j] = rel[j];
+                if (kLoo) mn[kLoo ? j : 0] = rel[j];
+              } else {
+                acc[j] += rel[j];
+                if (kLoo) mn[kLoo ? j : 0] = fminf(mn[kLoo ? j : 0], rel[j]);
+              }
+            }
+          }
+          const int tabs0 = t.qb * kTile + c0;  // absolute query index of element 0
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float R;
+            if (kLoo) {
+              R = __fdiv_rn(acc[j] - mn[kLoo ? j : 0], (float)p.head_topk);
             } else {
-              acc[j] += rel;
-              mn[j] = fminf(mn[j], rel);
+              R = exact_div ? __fdiv_rn(acc[j], (float)p.head_topk) : acc[j] * inv_ht;
             }
+            if (!full) {
+              const int qpos = qb_first_pos + c0 + j;
+              if (c0 + j >= qb_valid || key > qpos) R = -INFINITY;
+            }
+            top4_insert(st.top, R);
+            if (tabs0 + j >= p.nq - p.n_recent) top4_insert(st.rtop, R);
+            const bool pz = R > 0.f;
+            st.psum += pz ? R : 0.f;
+            st.pcnt += pz ? 1u : 0u;
+            msk |= (pz ? 1u : 0u) << (ch * 16 + j);
+            st.mxnp = fmaxf(st.mxnp, pz ? -INFINITY : R);
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_t_empty(buf));
         ++sub;
-        uint32_t msk = 0;
-        const int tabs0 = t.qb * kTile + tl0;  // absolute query index of j = 0
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float R;
-          if (p.head_topk < G) {
-            R = __fdiv_rn(acc[j] - mn[j], (float)p.head_topk);
-          } else {
-            R = exact_div ? __fdiv_rn(acc[j], (float)p.head_topk) : acc[j] * inv_ht;
-          }
-          if (!full) {
-            const int qpos = qb_first_pos + tl0 + j;
-            if (tl0 + j >= qb_valid || key > qpos) R = -INFINITY;
-          }
-          top4_insert(st.top, R);
-          if (tabs0 + j >= p.nq - p.n_recent) top4_insert(st.rtop, R);
-          const bool pz = R > 0.f;
-          st.psum += pz ? R : 0.f;
-          st.pcnt += pz ? 1u : 0u;
-          msk |= (pz ? 1u : 0u) << j;
-          st.mxnp = fmaxf(st.mxnp, pz ? -INFINITY : R);
-        }
         st.mask[hf] = msk;
       }
       if (!ok) break;
@@ -647,12 +673,14 @@ struct MergeParams {
   const float* lse;        // (B, Hq, nq)
   float* features;
   int stride;
+  int* queue_count;      // undecided f6 (key, head) pairs, resolved by qk_f6_resolve_kernel
+  int2* queue;
+  int queue_cap;
   DeviceStatus* status;
 };
 
 constexpr int kMergeThreads = 256;
 constexpr int kMaxSlowNq = 2048;
-constexpr int kSlowCap = 1024;  // undecided (key, head) pairs per merge block
 
 __device__ __forceinline__ float sum_top_desc(const float (&t)[4], int k) {
   // cumsum of the descending values, read at k-1 (fused_qk.py:541-543)
@@ -689,118 +717,114 @@ __device__ float relation_exact(const MergeParams& p, int b, int h, int key, int
 
 __global__ void __launch_bounds__(kMergeThreads)
     qk_merge_kernel(const MergeParams p) {
-  __shared__ int s_nslow;
-  __shared__ int s_slow[kSlowCap * 2];  // (local key, head) pairs
-  __shared__ int s_f6[kMergeThreads];
-  __shared__ float s_vals[kMaxSlowNq];
-  if (threadIdx.x == 0) s_nslow = 0;
-  s_f6[threadIdx.x] = 0;
-  __syncthreads();
-
   const long long gi = (long long)blockIdx.x * kMergeThreads + threadIdx.x;
-  const bool active = gi < (long long)p.B * p.L;
-  int b = 0, key = 0, valid = 1, kf = 1;
-  float f[6] = {0, 0, 0, 0, 0, 0};
-  if (active) {
-    b = (int)(gi / p.L);
-    key = (int)(gi % p.L);
-    valid = p.nq - max(key - p.q_start, 0);
-    valid = min(max(valid, 1), p.nq);
-    const int k2max = min(p.topk, p.nq * p.Hkv);
-    const int k2 = min(max(valid * p.Hkv, 1), k2max);
-    const int nrec = p.n_recent;
-    const int rstart = p.q_start + p.nq - nrec;
-    int rvalid = p.q_start + p.nq - max(key, rstart);
-    rvalid = min(max(rvalid, 1), nrec);
-    const int k4max = min(p.topk, nrec * p.Hkv);
-    const int k4 = min(max(rvalid * p.Hkv, 1), k4max);
-    kf = max((valid + 3) / 4, 1);
+  if (gi >= (long long)p.B * p.L) return;
+  const int b = (int)(gi / p.L);
+  const int key = (int)(gi % p.L);
+  int valid = p.nq - max(key - p.q_start, 0);
+  valid = min(max(valid, 1), p.nq);
+  const int k2max = min(p.topk, p.nq * p.Hkv);
+  const int k2 = min(max(valid * p.Hkv, 1), k2max);
+  const int nrec = p.n_recent;
+  const int rstart = p.q_start + p.nq - nrec;
+  int rvalid = p.q_start + p.nq - max(key, rstart);
+  rvalid = min(max(rvalid, 1), nrec);
+  const int k4max = min(p.topk, nrec * p.Hkv);
+  const int k4 = min(max(rvalid * p.Hkv, 1), k4max);
+  const int kf = max((valid + 3) / 4, 1);
 
-    float top[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    float rtop[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    float psum = 0.f;
-    unsigned long long pcnt = 0;
-    int f5cnt = 0;
-    int f6pos = 0;
-    const uint32_t* base = p.rec + ((long long)b * p.L + key) * p.Hkv * p.n_qb * kRecWords;
-    // f5: OR over heads of the per-query positive bits, per query block
-    for (int qb = 0; qb < p.n_qb; ++qb) {
-      uint32_t w[4] = {0, 0, 0, 0};
-      for (int h = 0; h < p.Hkv; ++h) {
-        const uint4 r2 = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords)[2];
-        const uint4 r3 = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords)[3];
-        w[0] |= r2.z;
-        w[1] |= r2.w;
-        w[2] |= r3.x;
-        w[3] |= r3.y;
-      }
-      f5cnt += __popc(w[0]) + __popc(w[1]) + __popc(w[2]) + __popc(w[3]);
-    }
+  float top[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  float rtop[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  float psum = 0.f;
+  unsigned long long pcnt = 0;
+  int f5cnt = 0;
+  int f6pos = 0;
+  const uint32_t* base = p.rec + ((long long)b * p.L + key) * p.Hkv * p.n_qb * kRecWords;
+  // f5: OR over heads of the per-query positive bits, per query block
+  for (int qb = 0; qb < p.n_qb; ++qb) {
+    uint32_t w[4] = {0, 0, 0, 0};
     for (int h = 0; h < p.Hkv; ++h) {
-      float hs = 0.f, mx = -INFINITY;
-      unsigned int hc = 0;
-      for (int qb = 0; qb < p.n_qb; ++qb) {
-        const uint4* r = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords);
-        const uint4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
-        top4_insert(top, __uint_as_float(r0.x));
-        top4_insert(top, __uint_as_float(r0.y));
-        top4_insert(top, __uint_as_float(r0.z));
-        top4_insert(top, __uint_as_float(r0.w));
-        top4_insert(rtop, __uint_as_float(r1.x));
-        top4_insert(rtop, __uint_as_float(r1.y));
-        top4_insert(rtop, __uint_as_float(r1.z));
-        top4_insert(rtop, __uint_as_float(r1.w));
-        hs += __uint_as_float(r2.x);
-        hc += r2.y;
-        mx = fmaxf(mx, __uint_as_float(r3.z));
-      }
-      psum += hs;
-      pcnt += hc;
-      // f6 for head h: sign of the mean of the top-kf relations over queries
-      if ((int)hc >= kf) {
+      const uint4* r = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords);
+      const uint4 r2 = r[2], r3 = r[3];
+      w[0] |= r2.z;
+      w[1] |= r2.w;
+      w[2] |= r3.x;
+      w[3] |= r3.y;
+    }
+    f5cnt += __popc(w[0]) + __popc(w[1]) + __popc(w[2]) + __popc(w[3]);
+  }
+  for (int h = 0; h < p.Hkv; ++h) {
+    float hs = 0.f, mx = -INFINITY;
+    unsigned int hc = 0;
+    for (int qb = 0; qb < p.n_qb; ++qb) {
+      const uint4* r = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords);
+      const uint4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
+      top4_insert(top, __uint_as_float(r0.x));
+      top4_insert(top, __uint_as_float(r0.y));
+      top4_insert(top, __uint_as_float(r0.z));
+      top4_insert(top, __uint_as_float(r0.w));
+      top4_insert(rtop, __uint_as_float(r1.x));
+      top4_insert(rtop, __uint_as_float(r1.y));
+      top4_insert(rtop, __uint_as_float(r1.z));
+      top4_insert(rtop, __uint_as_float(r1.w));
+      hs += __uint_as_float(r2.x);
+      hc += r2.y;
+      mx = fmaxf(mx, __uint_as_float(r3.z));
+    }
+    psum += hs;
+    pcnt += hc;
+    // f6 for head h: sign of the mean of the top-kf relations over queries
+    if ((int)hc >= kf) {
+      ++f6pos;
+    } else if (hc > 0) {
+      const float rem = (float)(kf - (int)hc);
+      const float hi = hs + rem * mx;                       // remaining values <= mx
+      const float lo = hs + rem * (kLogFloor * 1.0001f);    // and >= the floor
+      const float tol = 1e-5f * (fabsf(hs) + rem * fabsf(kLogFloor));
+      if (hi < -tol) {
+        // definitely not positive
+      } else if (lo > tol) {
         ++f6pos;
-      } else if (hc > 0) {
-        const float rem = (float)(kf - (int)hc);
-        const float hi = hs + rem * mx;                       // remaining values <= mx
-        const float lo = hs + rem * (kLogFloor * 1.0001f);    // and >= the floor
-        const float tol = 1e-5f * (fabsf(hs) + rem * fabsf(kLogFloor));
-        if (hi < -tol) {
-          // definitely not positive
-        } else if (lo > tol) {
-          ++f6pos;
-        } else {
-          const int slot = atomicAdd(&s_nslow, 1);
-          if (slot < kSlowCap) {
-            s_slow[slot * 2] = threadIdx.x;
-            s_slow[slot * 2 + 1] = h;
-          } else {
-            record_error(p.status, CORE_ERR_UNSUPPORTED, 401, key);
-          }
-        }
+      } else {
+        const int slot = atomicAdd(p.queue_count, 1);
+        if (slot < p.queue_cap) p.queue[slot] = make_int2((int)gi, h);
+        else record_error(p.status, CORE_ERR_UNSUPPORTED, 401, key);
       }
     }
-    f[0] = top[0];
-    f[1] = sum_top_desc(top, k2) / (float)k2;
-    f[2] = psum / (float)(pcnt > 0 ? pcnt : 1);
-    f[3] = sum_top_desc(rtop, k4) / (float)k4;
-    f[4] = (float)f5cnt / (float)p.nq;
-    s_f6[threadIdx.x] = f6pos;
   }
-  __syncthreads();
-  // Cooperative exact resolution of undecided f6 heads: recompute the
-  // relation values of one (key, head) over all queries, sort descending and
-  // test the mean of the top ceil(valid / 4).
-  const int nslow = min(s_nslow, kSlowCap);
-  for (int it = 0; it < nslow; ++it) {
-    const int lk = s_slow[it * 2], h = s_slow[it * 2 + 1];
-    const long long gk = (long long)blockIdx.x * kMergeThreads + lk;
-    const int bb = (int)(gk / p.L), kk = (int)(gk % p.L);
-    int n2 = 1;
-    while (n2 < p.nq) n2 <<= 1;
+  float f[6];
+  f[0] = top[0];
+  f[1] = sum_top_desc(top, k2) / (float)k2;
+  f[2] = psum / (float)(pcnt > 0 ? pcnt : 1);
+  f[3] = sum_top_desc(rtop, k4) / (float)k4;
+  f[4] = (float)f5cnt / (float)p.nq;
+  f[5] = (float)f6pos / (float)p.Hkv;  // undecided heads are added by qk_f6_resolve_kernel
+  float* out = p.features + gi * p.stride;
+  bool finite = true;
+  for (int i = 0; i < 6; ++i) {
+    out[i] = f[i];
+    finite &= isfinite(f[i]);
+  }
+  if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 402, key);
+}
+
+// Exact resolution of the f6 heads the running statistics could not decide:
+// one block per queued (key, head) pair recomputes its relation values over
+// all queries, sorts them in descending order and tests the mean of the top
+// ceil(valid / 4) (fused_qk.py:571-578).  A positive head adds 1/Hkv to f6;
+// Hkv is a power of two here, so the additions are exact in any order.
+__global__ void __launch_bounds__(kMergeThreads)
+    qk_f6_resolve_kernel(const MergeParams p) {
+  __shared__ float s_vals[kMaxSlowNq];
+  const int count = min(*p.queue_count, p.queue_cap);
+  int n2 = 1;
+  while (n2 < p.nq) n2 <<= 1;
+  for (int it = blockIdx.x; it < count; it += gridDim.x) {
+    const int2 item = p.queue[it];
+    const int bb = (int)(item.x / p.L), kk = (int)(item.x % p.L), h = item.y;
     for (int t = threadIdx.x; t < n2; t += kMergeThreads)
       s_vals[t] = (t < p.nq) ? relation_exact(p, bb, h, kk, t) : -INFINITY;
     __syncthreads();
-    // bitonic sort, descending
     for (int size = 2; size <= n2; size <<= 1) {
       for (int stride = size >> 1; stride > 0; stride >>= 1) {
         for (int i = threadIdx.x; i < n2; i += kMergeThreads) {
@@ -823,19 +847,9 @@ __global__ void __launch_bounds__(kMergeThreads)
       const int kfr = max((vld + 3) / 4, 1);
       float s = 0.f;
       for (int i = 0; i < kfr; ++i) s += s_vals[i];
-      if (s / (float)kfr > 0.f) s_f6[lk] += 1;
+      if (s / (float)kfr > 0.f) atomicAdd(p.features + (long long)item.x * p.stride + 5, 1.0f / (float)p.Hkv);
     }
     __syncthreads();
-  }
-  if (active) {
-    f[5] = (float)s_f6[threadIdx.x] / (float)p.Hkv;
-    float* out = p.features + ((long long)b * p.L + key) * p.stride;
-    bool finite = true;
-    for (int i = 0; i < 6; ++i) {
-      out[i] = f[i];
-      finite &= isfinite(f[i]);
-    }
-    if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 402, key);
   }
 }
 
@@ -903,16 +917,23 @@ int launch_qk(const QKPlan& plan, const CUtensorMap& tmQ_lse, const CUtensorMap&
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "lse_combine launch");
   }
   const uint32_t smem = RelSmem<G>::kTotal + 1024;
-  e = cudaFuncSetAttribute(qk_relation_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const bool loo = p.head_topk < G;
+  auto kern = loo ? qk_relation_kernel<G, (G > 1)> : qk_relation_kernel<G, false>;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_error(e, "qk_relation_kernel attribute");
   if (ev0 != nullptr) cudaEventRecord(ev0, s);
-  qk_relation_kernel<G><<<plan.grid, kThreads, smem, s>>>(tmQ_rel, tmK, p);
+  kern<<<plan.grid, kThreads, smem, s>>>(tmQ_rel, tmK, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_relation_kernel launch");
   if (ev1 != nullptr) cudaEventRecord(ev1, s);
   return CORE_OK;
 }
 
 }  // namespace
+
+static size_t queue_cap_for(const core_dims_t* d) {
+  // undecided f6 heads: bounded by every (key, head) pair of the cache
+  return (size_t)d->batch * d->seq_len * d->n_kv_heads;
+}
 
 extern "C" size_t core_qk_features_workspace_bytes(const core_dims_t* d) {
   if (check_dims(d, "core_qk_features_workspace_bytes") != CORE_OK) return 0;
@@ -922,6 +943,8 @@ extern "C" size_t core_qk_features_workspace_bytes(const core_dims_t* d) {
   z.take<float2>(plan.part_elems);
   z.take<float>((size_t)d->batch * d->n_q_heads * d->n_queries);
   z.take<uint32_t>(plan.rec_words);
+  z.take<int>(1);
+  z.take<int2>(queue_cap_for(d));
   return z.used;
 }
 
@@ -968,6 +991,8 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
   p.part = c.take<float2>(plan.part_elems);
   float* lse_buf = c.take<float>((size_t)p.B * p.Hq * p.nq);
   p.rec = c.take<uint32_t>(plan.rec_words);
+  int* queue_count = c.take<int>(1);
+  int2* queue = c.take<int2>(queue_cap_for(d));
   if (c.overflow)
     return set_error(CORE_ERR_WORKSPACE, "core_qk_features: workspace too small");
   p.status = device_status();
@@ -1012,9 +1037,16 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
   mp.q = static_cast<const __nv_bfloat16*>(q);
   mp.k = static_cast<const __nv_bfloat16*>(k);
   mp.lse = lse_buf; mp.features = features; mp.stride = feature_stride; mp.status = p.status;
+  mp.queue_count = queue_count; mp.queue = queue; mp.queue_cap = (int)queue_cap_for(d);
+  if ((p.Hkv & (p.Hkv - 1)) != 0)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_qk_features: n_kv_heads must be a power of two");
+  e = cudaMemsetAsync(queue_count, 0, sizeof(int), s);
+  if (e != cudaSuccess) return cuda_error(e, "core_qk_features queue clear");
   const long long n = (long long)p.B * p.L;
   qk_merge_kernel<<<(unsigned)((n + kMergeThreads - 1) / kMergeThreads), kMergeThreads, 0, s>>>(mp);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_merge_kernel launch");
+  qk_f6_resolve_kernel<<<sm_count(), kMergeThreads, 0, s>>>(mp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_f6_resolve_kernel launch");
   if (lse_out != nullptr) {
     e = cudaMemcpyAsync(lse_out, lse_buf, sizeof(float) * (size_t)p.B * p.Hq * p.nq,
                         cudaMemcpyDeviceToDevice, s);

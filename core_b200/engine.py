@@ -33,17 +33,16 @@ def fold_groups(w: torch.Tensor, n_kv_heads: int, groups: int, head_dim: int) ->
 class LayerWeights:
     """Per-layer slow weights on the device.
 
-    geometry_split : (3, 64, Hkv*d) bf16 terms of the fixed Gaussian projection
-    prototypes     : (64, 64) f32;  hadamard : (64, 64) f32
+    geometry_ext   : (3, 128, Hkv*d) bf16 terms of [W ; R W] (projection, rotation)
+    prototypes     : (64, 64) f32
     mlp            : packed f32 indexer MLP (see ops.pack_mlp)
     theta          : (d_mem, Hq*d) f32 memory projection (readout side)
     theta_split    : (2, d_mem, Hkv*d) bf16 terms of the group-folded projection
     gate           : (w1 (gh, Hq*d), b1 (gh), w2 (gh), b2 (1)) f32
     """
 
-    geometry_split: torch.Tensor
+    geometry_ext: torch.Tensor
     prototypes: torch.Tensor
-    hadamard: torch.Tensor
     mlp: torch.Tensor
     theta: torch.Tensor | None = None
     theta_split: torch.Tensor | None = None
@@ -53,8 +52,7 @@ class LayerWeights:
     def prepare(cls, *, geometry, prototypes, hadamard, mlp_params, theta=None, gate=None,
                 n_kv_heads: int, n_q_heads: int, head_dim: int = 128, device="cuda"):
         dev = torch.device(device)
-        geometry = geometry.to(dev, torch.float32).contiguous()
-        geo = ops.split_bf16(geometry, 3)
+        geo = ops.prepare_geometry(geometry.to(dev, torch.float32), hadamard.to(dev, torch.float32))
         groups = n_q_heads // n_kv_heads
         th = ths = g = None
         if theta is not None:
@@ -64,9 +62,8 @@ class LayerWeights:
             g = tuple(x.to(dev, torch.float32).reshape(-1).contiguous() if i else
                       x.to(dev, torch.float32).contiguous() for i, x in enumerate(gate))
         return cls(
-            geometry_split=geo,
+            geometry_ext=geo,
             prototypes=prototypes.to(dev, torch.float32).contiguous(),
-            hadamard=hadamard.to(dev, torch.float32).contiguous(),
             mlp=ops.pack_mlp([t.to(dev) for t in mlp_params]),
             theta=th, theta_split=ths, gate=g)
 
@@ -127,8 +124,8 @@ def compress_layer(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
     need = lib.core_compress_layer_workspace_bytes(ctypes.byref(dims), int(n_kept), int(d_mem))
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(max(int(need), 256), dtype=torch.uint8, device=dev)
-    w = _lib.CoreLayerWeights(weights.geometry_split.data_ptr(), weights.prototypes.data_ptr(),
-                              weights.hadamard.data_ptr(), weights.mlp.data_ptr(),
+    w = _lib.CoreLayerWeights(weights.geometry_ext.data_ptr(), weights.prototypes.data_ptr(),
+                              weights.mlp.data_ptr(),
                               weights.theta_split.data_ptr() if write else 0, int(d_mem))
     a = _lib.CoreCompressArgs(int(n_kept), int(n_sink), int(topk_qk), int(n_recent_queries),
                               float(shrinkage_rho), int(original_length), int(bool(is_prefill)),

@@ -85,26 +85,37 @@ def split_bf16(w: torch.Tensor, terms: int) -> torch.Tensor:
     return out
 
 
-def coverage_features(k: torch.Tensor, geometry_split: torch.Tensor, prototypes: torch.Tensor,
-                      hadamard: torch.Tensor, *, shrinkage_rho: float = 0.1,
-                      features: torch.Tensor | None = None, col0: int = 0):
+def prepare_geometry(geometry: torch.Tensor, hadamard: torch.Tensor) -> torch.Tensor:
+    """(3, 128, Hkv*d) bf16 terms of [W ; R W] for ``coverage_features``."""
+    _require_cuda(geometry, hadamard)
+    g = geometry.to(torch.float32).contiguous()
+    r = hadamard.to(torch.float32).contiguous()
+    if g.shape[0] != 64 or tuple(r.shape) != (64, 64):
+        raise ValueError("geometry must be (64, Hkv*d) and hadamard (64, 64)")
+    out = torch.empty(3, 128, g.shape[1], dtype=torch.bfloat16, device=g.device)
+    check(_lib.load().core_prepare_geometry(_ptr(g), _ptr(r), g.shape[1], _ptr(out), _stream(g.device)))
+    return out
+
+
+def coverage_features(k: torch.Tensor, geometry_ext: torch.Tensor, prototypes: torch.Tensor, *,
+                      shrinkage_rho: float = 0.1, features: torch.Tensor | None = None,
+                      col0: int = 0):
     """o, d_proto, delta_proto, g (``compute_coverage_features``)."""
-    _require_cuda(k, geometry_split, prototypes, hadamard)
+    _require_cuda(k, geometry_ext, prototypes)
     k = k.contiguous()
     B, hkv, L, d = k.shape
     dims = _dims(k, hkv, 0)
-    if tuple(geometry_split.shape) != (3, 64, hkv * d):
-        raise ValueError("geometry_split must be (3, 64, Hkv*d)")
+    if tuple(geometry_ext.shape) != (3, 128, hkv * d):
+        raise ValueError("geometry_ext must be (3, 128, Hkv*d) (see prepare_geometry)")
     lib = _lib.load()
     if features is None:
         features = torch.empty(B, L, 4, dtype=torch.float32, device=k.device)
         col0 = 0
     ws = _workspace(lib.core_coverage_workspace_bytes(ctypes.byref(dims)), k.device)
     check(lib.core_coverage_features(
-        ctypes.byref(dims), _ptr(k), _ptr(geometry_split.contiguous()),
-        _ptr(prototypes.float().contiguous()), _ptr(hadamard.float().contiguous()),
-        float(shrinkage_rho), _ptr(features), features.shape[-1], col0, _ptr(ws), ws.numel(),
-        _stream(k.device)))
+        ctypes.byref(dims), _ptr(k), _ptr(geometry_ext.contiguous()),
+        _ptr(prototypes.float().contiguous()), float(shrinkage_rho), _ptr(features),
+        features.shape[-1], col0, _ptr(ws), ws.numel(), _stream(k.device)))
     return features
 
 

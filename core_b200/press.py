@@ -561,7 +561,7 @@ class COREScorerPress(ScorerPress):
         feats = torch.empty(B, L, 14, dtype=torch.float32, device=keys.device)
         ops.qk_features(q, k, topk_qk=int(cfg.topk_qk), n_recent_queries=int(cfg.n_recent_queries),
                         lse=lse, features=feats)
-        ops.coverage_features(k, lw.geometry_split, lw.prototypes, lw.hadamard,
+        ops.coverage_features(k, lw.geometry_ext, lw.prototypes,
                               shrinkage_rho=float(cfg.shrinkage_rho), features=feats, col0=6)
         scores = ops.indexer_scores(v, positions, feats, lw.mlp, original_length=int(original_length),
                                     is_prefill=is_prefill, n_sink=int(cfg.n_sink),

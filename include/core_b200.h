@@ -90,17 +90,24 @@ int core_qk_features(const core_dims_t* dims, const void* q, const void* k,
  * (core/features.py:790-858) with LayerwiseKeyGeometryProjector.forward
  * (:53-77), PrototypeBank.get_coverage_features (:146-213) and
  * HadamardProjector.rotate (:259-261).
- *   geometry_split : (3, P, Hkv*d) bf16, the layer's fp32 Gaussian projection
- *                    split into hi/mid/lo bf16 terms by core_split_bf16
- *   prototypes     : (64, P) f32 unit rows;  hadamard : (P, P) f32
- *   features       : (B, L, feature_stride) f32, columns col0..col0+3
+ *   geometry_ext : (3, 128, Hkv*d) bf16 from core_prepare_geometry
+ *   prototypes   : (64, P) f32 unit rows
+ *   features     : (B, L, feature_stride) f32, columns col0..col0+3
  * P (proto_dim) must be 64 and the prototype count 64.
  * ------------------------------------------------------------------------- */
 size_t core_coverage_workspace_bytes(const core_dims_t* dims);
-int core_coverage_features(const core_dims_t* dims, const void* k, const void* geometry_split,
-                           const float* prototypes, const float* hadamard, float shrinkage_rho,
-                           float* features, int32_t feature_stride, int32_t col0,
-                           void* workspace, size_t workspace_bytes, void* stream);
+int core_coverage_features(const core_dims_t* dims, const void* k, const void* geometry_ext,
+                           const float* prototypes, float shrinkage_rho, float* features,
+                           int32_t feature_stride, int32_t col0, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Once per layer: geometry_ext = three bf16 terms of [W ; R W], where W is the
+ * layer's (64, in_dim) f32 Gaussian projection (core/features.py:29-50) and R
+ * the (64, 64) Hadamard rotation (:216-236), so that one tensor-core pass
+ * yields both the projected key and its rotation.  No reference counterpart
+ * (the reference multiplies by W and R separately in f32). */
+int core_prepare_geometry(const float* geometry, const float* hadamard, int32_t in_dim,
+                          void* geometry_ext, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Auxiliary features + indexer MLP -> per-token scores.
@@ -199,9 +206,8 @@ int core_memory_readout(const core_dims_t* dims, int32_t q_len, const void* q, c
  * when non-NULL, are cudaEvent_t recorded around the QK relation kernel.
  * ------------------------------------------------------------------------- */
 typedef struct core_layer_weights {
-  const void* geometry_split; /* (3, 64, Hkv*d) bf16 */
+  const void* geometry_ext;   /* (3, 128, Hkv*d) bf16 from core_prepare_geometry */
   const float* prototypes;    /* (64, 64) f32 */
-  const float* hadamard;      /* (64, 64) f32 */
   const float* mlp;           /* packed indexer MLP (see core_indexer_scores) */
   const void* theta_split;    /* (2, d_mem, Hkv*d) bf16, or NULL: no memory write */
   int32_t d_mem;

@@ -100,8 +100,8 @@ def test_coverage_matches_oracle(name):
     dev = _dev()
     d, m = load_case(name)
     k = _bf16(d["k"], dev)[None]
-    geo = ops.split_bf16(_f32(d["geometry"], dev), 3)
-    cov = ops.coverage_features(k, geo, _f32(d["prototypes"], dev), _f32(d["hadamard"], dev))
+    geo = ops.prepare_geometry(_f32(d["geometry"], dev), _f32(d["hadamard"], dev))
+    cov = ops.coverage_features(k, geo, _f32(d["prototypes"], dev))
     ops.status()
     got = cov[0].cpu().numpy()
     ref = O.coverage_features(d["k"], d["geometry"], d["prototypes"], d["hadamard"])
