@@ -256,6 +256,28 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, int a_mn_major, 
 }
 
 // ---------------------------------------------------------------------------
+// cp.async (16-byte global -> shared copies, L1 bypass)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Copy n16 16-byte chunks global -> shared with all threads of the block
+// (both addresses 16-byte aligned); completes with cp_async_wait_all().
+__device__ __forceinline__ void cp_async_block(void* dst, const void* src, int n16) {
+  const uint32_t d = smem_u32(dst);
+  const char* s = static_cast<const char*>(src);
+  for (int i = threadIdx.x; i < n16; i += blockDim.x) cp_async16(d + 16u * i, s + 16ll * i);
+  cp_async_commit();
+}
+
+// ---------------------------------------------------------------------------
 // Numerics helpers
 // ---------------------------------------------------------------------------
 // Round an f32 to bfloat16 precision (nearest-even) and widen back.

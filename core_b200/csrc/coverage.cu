@@ -299,7 +299,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Per batch row: the column sums over the CTAs that covered the row (double),
 // then mean z, mu and sigma2_eff (features.py:812, :830-845) as floats:
 // stats[b] = [mean z (64) | mu (64) | sigma2_eff (64)].
-__global__ void __launch_bounds__(512)
+constexpr int kStatsThreads = 1024;
+constexpr int kMaxPartCtas = 256;  // per-lane unrolled loads cover 8 x 32 CTAs per pass
+
+__global__ void __launch_bounds__(kStatsThreads)
     cov_stats_kernel(const double* __restrict__ part, int grid_ctas, int B, int n_tiles, int L,
                      float rho, float* __restrict__ stats) {
   __shared__ double s[kNStats];
@@ -308,12 +311,22 @@ __global__ void __launch_bounds__(512)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long U = (long long)B * n_tiles;
   const long long lo = (long long)b * n_tiles, hi = lo + n_tiles;
-  for (int i = warp; i < kNStats; i += blockDim.x / 32) {
+  // which of this lane's CTAs covered row b (contiguous static partition of the tiles)
+  unsigned covered = 0;
+#pragma unroll
+  for (int j = 0; j < kMaxPartCtas / 32; ++j) {
+    const int c = lane + 32 * j;
+    const long long a = (long long)c * U / grid_ctas, e = (long long)(c + 1) * U / grid_ctas;
+    if (c < grid_ctas && a < hi && e > lo) covered |= 1u << j;
+  }
+  for (int i = warp; i < kNStats; i += kStatsThreads / 32) {
+    double v[kMaxPartCtas / 32];
+#pragma unroll
+    for (int j = 0; j < kMaxPartCtas / 32; ++j)
+      v[j] = (covered >> j & 1u) ? part[((long long)(lane + 32 * j) * B + b) * kNStats + i] : 0.0;
     double acc = 0.0;
-    for (int c = lane; c < grid_ctas; c += 32) {
-      const long long a = (long long)c * U / grid_ctas, e = (long long)(c + 1) * U / grid_ctas;
-      if (a < hi && e > lo) acc += part[((long long)c * B + b) * kNStats + i];
-    }
+#pragma unroll
+    for (int j = 0; j < kMaxPartCtas / 32; ++j) acc += v[j];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) s[i] = acc;
@@ -338,16 +351,28 @@ __global__ void __launch_bounds__(512)
 }
 
 constexpr int kAssignThreads = 128;  // 32 tokens x 4 threads
+constexpr int kProtoStride = 68;     // padded prototype rows: the 4 threads of a token hit distinct banks
 
+// Prototype assignment and g.  Thread `part` of a token scores prototypes
+// m = 4 mm + part (mm ascending); ties resolve to the lowest index, as the
+// first maximum of argmax does (features.py:177).
 __global__ void __launch_bounds__(kAssignThreads)
     cov_assign_kernel(const float* __restrict__ z, const float* __restrict__ zt,
                       const float* __restrict__ stats, const float* __restrict__ protos,
                       int B, int L, int* __restrict__ assign, int* __restrict__ hist,
                       float* __restrict__ features, int stride, int col0, DeviceStatus* status) {
-  __shared__ float sP[kNP * kP];
+  __shared__ __align__(16) float sP[kNP * kProtoStride];
   __shared__ int sh[kNP];
   const int tid = threadIdx.x;
-  for (int i = tid; i < kNP * kP; i += blockDim.x) sP[i] = protos[i];
+  {
+    const uint32_t d = smem_u32(sP);
+    for (int i = tid; i < kNP * kP / 4; i += blockDim.x) {
+      const int m = i / (kP / 4), c = i % (kP / 4);
+      cp_async16(d + (uint32_t)(m * kProtoStride + 4 * c) * 4u, protos + 4 * i);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+  }
   const long long n = (long long)B * L;
   const long long ngroups = (n + kAssignThreads / 4 - 1) / (kAssignThreads / 4);
   for (long long grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
@@ -356,7 +381,7 @@ __global__ void __launch_bounds__(kAssignThreads)
     const long long tok0 = grp * (kAssignThreads / 4);
     const int row0 = (int)(tok0 / L);
     const long long gi = tok0 + (tid >> 2);
-    const int part = tid & 3;  // prototypes [16 part, 16 part + 16), zt dims likewise
+    const int part = tid & 3;  // prototypes 4 mm + part; zt dims [16 part, 16 part + 16)
     const bool active = gi < n;
     const int b = active ? (int)(gi / L) : row0;
     const float* st = stats + (long long)b * kNStats;
@@ -385,12 +410,19 @@ __global__ void __launch_bounds__(kAssignThreads)
     for (int j = 0; j < kP; ++j) zc[j] *= inv;
     // top-2 of this thread's 16 prototypes, ascending index (first maximum wins)
     float c1 = -INFINITY, c2 = -INFINITY;
-    int m1 = part * 16;
-    for (int mm = 0; mm < 16; ++mm) {
-      const int m = part * 16 + mm;
+    int m1 = part;
+    for (int mm = 0; mm < kNP / 4; ++mm) {
+      const int m = 4 * mm + part;
+      const float4* pr = reinterpret_cast<const float4*>(sP + m * kProtoStride);
       float c = 0.f;
 #pragma unroll
-      for (int j = 0; j < kP; ++j) c = fmaf(zc[j], sP[m * kP + j], c);
+      for (int j = 0; j < kP / 4; ++j) {
+        const float4 w = pr[j];
+        c = fmaf(zc[4 * j], w.x, c);
+        c = fmaf(zc[4 * j + 1], w.y, c);
+        c = fmaf(zc[4 * j + 2], w.z, c);
+        c = fmaf(zc[4 * j + 3], w.w, c);
+      }
       if (c > c1) {
         c2 = c1;
         c1 = c;
@@ -399,24 +431,18 @@ __global__ void __launch_bounds__(kAssignThreads)
         c2 = c;
       }
     }
-    // merge with the neighbouring ranges; the lower index range wins ties
+    // merge across the 4 threads of the token; equal cosines go to the lower index
 #pragma unroll
     for (int off = 1; off < 4; off <<= 1) {
       const float oc1 = __shfl_xor_sync(0xffffffffu, c1, off);
       const float oc2 = __shfl_xor_sync(0xffffffffu, c2, off);
       const int om1 = __shfl_xor_sync(0xffffffffu, m1, off);
-      const bool lower = (part & off) == 0;
-      const float ac1 = lower ? c1 : oc1, ac2 = lower ? c2 : oc2;
-      const float bc1 = lower ? oc1 : c1, bc2 = lower ? oc2 : c2;
-      const int am1 = lower ? m1 : om1, bm1 = lower ? om1 : m1;
-      if (bc1 > ac1) {
-        c1 = bc1;
-        m1 = bm1;
-        c2 = fmaxf(ac1, bc2);
+      if (oc1 > c1 || (oc1 == c1 && om1 < m1)) {
+        c2 = fmaxf(c1, oc2);
+        c1 = oc1;
+        m1 = om1;
       } else {
-        c1 = ac1;
-        m1 = am1;
-        c2 = fmaxf(ac2, bc1);
+        c2 = fmaxf(c2, oc1);
       }
     }
     // g over this thread's 16 rotated dims, then summed across the 4 threads
@@ -505,7 +531,7 @@ void plan_cov(const core_dims_t* d, CovPlan* c) {
   c->p.L = d->seq_len;
   c->p.n_tiles = (d->seq_len + kTile - 1) / kTile;
   c->p.U = (long long)c->p.B * c->p.n_tiles;
-  const int sms = sm_count();
+  const int sms = sm_count() < kMaxPartCtas ? sm_count() : kMaxPartCtas;
   c->grid = (int)(c->p.U < sms ? c->p.U : sms);
 }
 }  // namespace
@@ -547,6 +573,8 @@ extern "C" int core_coverage_features(const core_dims_t* d, const void* k,
     return set_error(CORE_ERR_INVALID_ARG, "core_coverage_features: NULL tensor");
   if (col0 < 0 || col0 + 4 > feature_stride)
     return set_error(CORE_ERR_INVALID_ARG, "core_coverage_features: bad feature columns");
+  if (reinterpret_cast<uintptr_t>(prototypes) % 16 != 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_coverage_features: prototypes must be 16-byte aligned");
   CovPlan c;
   plan_cov(d, &c);
   Params& p = c.p;
@@ -582,7 +610,7 @@ extern "C" int core_coverage_features(const core_dims_t* d, const void* k,
   if (e != cudaSuccess) return cuda_error(e, "cov_project_kernel attribute");
   cov_project_kernel<<<c.grid, kThreads, smem, s>>>(tmK, tmW, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "cov_project_kernel launch");
-  cov_stats_kernel<<<p.B, 512, 0, s>>>(p.part, c.grid, p.B, p.n_tiles, p.L, shrinkage_rho, stats);
+  cov_stats_kernel<<<p.B, kStatsThreads, 0, s>>>(p.part, c.grid, p.B, p.n_tiles, p.L, shrinkage_rho, stats);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "cov_stats_kernel launch");
   const long long n = (long long)p.B * p.L;
   long long ablocks = (n + kAssignThreads / 4 - 1) / (kAssignThreads / 4);

@@ -2,11 +2,14 @@
 // the feature concatenation at core/kvpress_adapter.py:536 and
 // COREIndexerMLP, core/indexer.py:88-108).
 //
-// One thread per cached token.  The auxiliary features follow the
-// reference's dtype: for bf16 caches a_value is computed with the same
-// bf16 roundings as the reference's torch ops (squares, per-head sums, the
-// head mean, /d and log1p each round to bf16).  The MLP runs in f32 with its
-// weights in shared memory (exact erf GELU).
+// One thread per cached token, persistent blocks.  The auxiliary features
+// follow the reference's dtype: for bf16 caches a_value is computed with the
+// same bf16 roundings as the reference's torch ops (squares, per-head sums,
+// the head mean, /d and log1p each round to bf16).  The MLP runs in f32 with
+// its weights staged once per block into shared memory (cp.async) and read as
+// warp-wide broadcasts: hidden unit k of layer 1 is computed, GELU'd, and
+// immediately accumulated into all 128 layer-2 outputs held in registers
+// (an outer-product form, so layer-2 sums run over k in ascending order).
 #include <cmath>
 
 #include "common.cuh"
@@ -17,25 +20,23 @@ namespace idx {
 
 constexpr int kIn = 14;
 constexpr int kHid = 128;
-constexpr int kThreads = 128;          // 32 tokens x 4 threads
-constexpr int kTok = kThreads / 4;
-constexpr int kMlpFloats = kHid * kIn + kHid + kHid * kHid + kHid + kHid + 1;
-// shared-memory layout (floats): padded rows keep the four threads of a token
-// on distinct banks
+constexpr int kThreads = 128;  // one token per thread
+// packed global layout (floats): [w1 (128,14) | b1 | w2^T (in 128, out 128) | b2 | w3 | b3]
+constexpr int kGW1 = 0;
+constexpr int kGB1 = kGW1 + kHid * kIn;    // 1792
+constexpr int kGW2T = kGB1 + kHid;         // 1920 (16-byte aligned)
+constexpr int kGB3 = kGW2T + kHid * kHid + 2 * kHid;
+// shared layout (floats): w1 rows padded to 16 | b1 | w2^T | b2 | w3 | b3
 constexpr int kW1Stride = 16;
-constexpr int kW2Stride = 132;
-constexpr int kH1Stride = 132;
 constexpr int kOffW1 = 0;
-constexpr int kOffB1 = kOffW1 + kHid * kW1Stride;
-constexpr int kOffW2 = kOffB1 + kHid;
-constexpr int kOffB2 = kOffW2 + kHid * kW2Stride;
+constexpr int kOffB1 = kOffW1 + kHid * kW1Stride;  // 2048
+constexpr int kOffW2T = kOffB1 + kHid;             // 2176 (16-byte aligned)
+constexpr int kOffB2 = kOffW2T + kHid * kHid;
 constexpr int kOffW3 = kOffB2 + kHid;
 constexpr int kOffB3 = kOffW3 + kHid;
-constexpr int kOffH1 = kOffB3 + 4;
-constexpr int kOffX = kOffH1 + kTok * kH1Stride;
-constexpr int kOffHs = kOffX + kTok * 16;
+constexpr int kSmemFloats = kOffB3 + 4;
 constexpr int kMaxHkv = 16;
-constexpr int kSmemFloats = kOffHs + kTok * kMaxHkv;
+static_assert(kGW2T % 4 == 0 && kOffW2T % 4 == 0, "cp.async chunks need 16-byte alignment");
 
 __device__ __forceinline__ float gelu(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
@@ -52,126 +53,119 @@ struct Params {
   DeviceStatus* status;
 };
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
     indexer_scores_kernel(const Params p) {
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
+  // w2^T | b2 | w3 are contiguous in both layouts: one asynchronous copy
+  cp_async_block(sm + kOffW2T, p.mlp + kGW2T, (kHid * kHid + 2 * kHid) / 4);
   {
-    const float* w1 = p.mlp;
-    const float* b1 = w1 + kHid * kIn;
-    const float* w2 = b1 + kHid;
-    const float* b2 = w2 + kHid * kHid;
-    const float* w3 = b2 + kHid;
-    for (int i = threadIdx.x; i < kHid * kIn; i += blockDim.x)
-      sm[kOffW1 + (i / kIn) * kW1Stride + (i % kIn)] = w1[i];
-    for (int i = threadIdx.x; i < kHid * kHid; i += blockDim.x)
-      sm[kOffW2 + (i / kHid) * kW2Stride + (i % kHid)] = w2[i];
-    for (int i = threadIdx.x; i < kHid; i += blockDim.x) {
-      sm[kOffB1 + i] = b1[i];
-      sm[kOffB2 + i] = b2[i];
-      sm[kOffW3 + i] = w3[i];
+    float r[kHid * kIn / kThreads + 1];
+#pragma unroll
+    for (int j = 0; j < kHid * kIn / kThreads; ++j) r[j] = p.mlp[kGW1 + threadIdx.x + j * kThreads];
+    r[kHid * kIn / kThreads] = p.mlp[kGB1 + threadIdx.x];
+#pragma unroll
+    for (int j = 0; j < kHid * kIn / kThreads; ++j) {
+      const int i = threadIdx.x + j * kThreads;
+      sm[kOffW1 + (i / kIn) * kW1Stride + (i % kIn)] = r[j];
     }
-    if (threadIdx.x == 0) sm[kOffB3] = w3[kHid];
+    sm[kOffB1 + threadIdx.x] = r[kHid * kIn / kThreads];
+    if (threadIdx.x == 0) sm[kOffB3] = p.mlp[kGB3];
   }
+  cp_async_wait_all();
   __syncthreads();
-  const int tl = threadIdx.x >> 2;  // token within the group
-  const int part = threadIdx.x & 3;
-  const long long ngroups = ((long long)p.B * p.L + kTok - 1) / kTok;
-  for (long long grp = blockIdx.x; grp < ngroups; grp += gridDim.x) {
-  const long long gi = grp * kTok + tl;
-  const bool active = gi < (long long)p.B * p.L;
-  const int b = active ? (int)(gi / p.L) : 0;
-  const int i = active ? (int)(gi % p.L) : 0;
-  float* hs = sm + kOffHs + tl * kMaxHkv;
-  float* xs = sm + kOffX + tl * 16;
 
-  // ---- a_value: bf16-rounded |v_h|^2 per head, heads split over the 4 threads ----
-  if (active) {
-    for (int h = part; h < p.Hkv; h += 4) {
-      const uint4* row = reinterpret_cast<const uint4*>(p.v + (((long long)b * p.Hkv + h) * p.L + i) * 128);
-      float s = 0.f;
+  const long long n = (long long)p.B * p.L;
+  const float age_den = log1pf((float)(p.original_length - 1 > 1 ? p.original_length - 1 : 1));
+  for (long long gi = (long long)blockIdx.x * kThreads + threadIdx.x; gi - threadIdx.x < n;
+       gi += (long long)gridDim.x * kThreads) {
+    const bool active = gi < n;
+    float x[kIn];
+    if (active) {
+      const int b = (int)(gi / p.L);
+      const int i = (int)(gi % p.L);
+      // ---- a_value: bf16-rounded |v_h|^2 per head, heads summed in order ----
+      float hsum = 0.f;
+      for (int h = 0; h < p.Hkv; ++h) {
+        const uint4* row =
+            reinterpret_cast<const uint4*>(p.v + (((long long)b * p.Hkv + h) * p.L + i) * 128);
+        float s = 0.f;
 #pragma unroll 4
-      for (int c = 0; c < 16; ++c) {
-        const uint4 w = row[c];
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+        for (int c = 0; c < 16; ++c) {
+          const uint4 w = __ldg(row + c);
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 x = __bfloat1622float2(h2[e]);
-          s += bf16_round(x.x * x.x);
-          s += bf16_round(x.y * x.y);
+          for (int e = 0; e < 4; ++e) {
+            const float2 t = __bfloat1622float2(h2[e]);
+            s += bf16_round(t.x * t.x);
+            s += bf16_round(t.y * t.y);
+          }
         }
+        hsum += bf16_round(s);
       }
-      hs[h] = bf16_round(s);
+      // ---- auxiliary features (features.py:886-921) ----
+      const long long pos = p.positions[gi];
+      const int T = p.original_length;
+      if (pos < 0 || pos >= T) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
+      const float a_age = log1pf((float)(T - 1 - pos)) / age_den;
+      bool sink = pos < p.n_sink;
+      if (p.special != nullptr && p.special[gi]) sink = true;
+      const float vmean = bf16_round(hsum / (float)p.Hkv);
+      const float a_value = bf16_round(log1pf(bf16_round(vmean / 128.0f)));
+      float* f = p.features + gi * kIn;
+#pragma unroll
+      for (int k = 0; k < 10; ++k) x[k] = f[k];
+      x[10] = a_age;
+      x[11] = sink ? 1.0f : 0.0f;
+      x[12] = a_value;
+      x[13] = p.is_prefill ? 0.0f : 1.0f;
+#pragma unroll
+      for (int k = 10; k < kIn; ++k) f[k] = x[k];
+      bool finite = true;
+#pragma unroll
+      for (int k = 0; k < kIn; ++k) finite &= isfinite(x[k]);
+      if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 602, i);
+    } else {
+#pragma unroll
+      for (int k = 0; k < kIn; ++k) x[k] = 0.f;
     }
-  }
-  __syncwarp();
-  if (active && part == 0) {
-    // auxiliary features (features.py:886-921), heads summed in order
-    const long long pos = p.positions[gi];
-    const int T = p.original_length;
-    if (pos < 0 || pos >= T) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
-    const float age_den = log1pf((float)(T - 1 > 1 ? T - 1 : 1));
-    const float a_age = log1pf((float)(T - 1 - pos)) / age_den;
-    bool sink = pos < p.n_sink;
-    if (p.special != nullptr && p.special[gi]) sink = true;
-    float hsum = 0.f;
-    for (int h = 0; h < p.Hkv; ++h) hsum += hs[h];
-    const float vmean = bf16_round(hsum / (float)p.Hkv);
-    const float a_value = bf16_round(log1pf(bf16_round(vmean / 128.0f)));
-    float* f = p.features + gi * kIn;
-    f[10] = a_age;
-    f[11] = sink ? 1.0f : 0.0f;
-    f[12] = a_value;
-    f[13] = p.is_prefill ? 0.0f : 1.0f;
-    bool finite = true;
-    for (int k = 0; k < kIn; ++k) {
-      xs[k] = f[k];
-      finite &= isfinite(xs[k]);
-    }
-    if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 602, i);
-  }
-  __syncwarp();
-  // ---- layer 1: this thread's hidden units o = 4 j + part ----
-  float x[kIn];
+    // ---- MLP: layer-1 unit k, then its rank-1 update of the 128 layer-2 sums ----
+    float acc[kHid];
 #pragma unroll
-  for (int k = 0; k < kIn; ++k) x[k] = xs[k];
-  float* h1 = sm + kOffH1 + tl * kH1Stride;
-  for (int j = 0; j < kHid / 4; ++j) {
-    const int o = 4 * j + part;
-    const float* w = sm + kOffW1 + o * kW1Stride;
-    float acc = 0.f;
+    for (int o = 0; o < kHid; ++o) acc[o] = 0.f;
+#pragma unroll 1
+    for (int k = 0; k < kHid; ++k) {
+      const float4* w1 = reinterpret_cast<const float4*>(sm + kOffW1 + k * kW1Stride);
+      const float4 a0 = w1[0], a1 = w1[1], a2 = w1[2], a3 = w1[3];
+      float t = 0.f;
+      t = fmaf(a0.x, x[0], t);
+      t = fmaf(a0.y, x[1], t);
+      t = fmaf(a0.z, x[2], t);
+      t = fmaf(a0.w, x[3], t);
+      t = fmaf(a1.x, x[4], t);
+      t = fmaf(a1.y, x[5], t);
+      t = fmaf(a1.z, x[6], t);
+      t = fmaf(a1.w, x[7], t);
+      t = fmaf(a2.x, x[8], t);
+      t = fmaf(a2.y, x[9], t);
+      t = fmaf(a2.z, x[10], t);
+      t = fmaf(a2.w, x[11], t);
+      t = fmaf(a3.x, x[12], t);
+      t = fmaf(a3.y, x[13], t);
+      const float hk = gelu(t + sm[kOffB1 + k]);
+      const float4* w2 = reinterpret_cast<const float4*>(sm + kOffW2T + k * kHid);
 #pragma unroll
-    for (int k = 0; k < kIn; ++k) acc = fmaf(w[k], x[k], acc);
-    h1[o] = gelu(acc + sm[kOffB1 + o]);
-  }
-  __syncwarp();
-  // ---- layer 2 (four outputs at a time) and the output unit ----
-  float out = 0.f;
-  const float4* h4 = reinterpret_cast<const float4*>(h1);
-  for (int j = 0; j < kHid / 4; j += 4) {
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-    for (int k = 0; k < kHid / 4; ++k) {
-      const float4 hv = h4[k];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int o = 4 * (j + u) + part;
-        const float4 w = reinterpret_cast<const float4*>(sm + kOffW2 + o * kW2Stride)[k];
-        acc[u] = fmaf(w.x, hv.x, acc[u]);
-        acc[u] = fmaf(w.y, hv.y, acc[u]);
-        acc[u] = fmaf(w.z, hv.z, acc[u]);
-        acc[u] = fmaf(w.w, hv.w, acc[u]);
+      for (int o4 = 0; o4 < kHid / 4; ++o4) {
+        const float4 w = w2[o4];
+        acc[4 * o4] = fmaf(w.x, hk, acc[4 * o4]);
+        acc[4 * o4 + 1] = fmaf(w.y, hk, acc[4 * o4 + 1]);
+        acc[4 * o4 + 2] = fmaf(w.z, hk, acc[4 * o4 + 2]);
+        acc[4 * o4 + 3] = fmaf(w.w, hk, acc[4 * o4 + 3]);
       }
     }
+    float out = 0.f;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int o = 4 * (j + u) + part;
-      out = fmaf(sm[kOffW3 + o], gelu(acc[u] + sm[kOffB2 + o]), out);
-    }
-  }
-  out += __shfl_xor_sync(0xffffffffu, out, 1);
-  out += __shfl_xor_sync(0xffffffffu, out, 2);
-  if (active && part == 0) p.scores[gi] = out + sm[kOffB3];
-  __syncwarp();
+    for (int o = 0; o < kHid; ++o) out = fmaf(sm[kOffW3 + o], gelu(acc[o] + sm[kOffB2 + o]), out);
+    if (active) p.scores[gi] = out + sm[kOffB3];
   }
 }
 
@@ -190,6 +184,8 @@ extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const in
   if (v == nullptr || positions == nullptr || features == nullptr || mlp == nullptr ||
       scores == nullptr)
     return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores: NULL tensor");
+  if (reinterpret_cast<uintptr_t>(mlp) % 16 != 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores: mlp must be 16-byte aligned");
   if (original_length < d->seq_len)
     return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores: original_length < seq_len");
   if (d->n_kv_heads > kMaxHkv)
@@ -214,7 +210,7 @@ extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const in
       cudaFuncSetAttribute(indexer_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_error(e, "indexer_scores_kernel attribute");
   const long long n = (long long)p.B * p.L;
-  long long blocks = (n + kTok - 1) / kTok;
+  long long blocks = (n + kThreads - 1) / kThreads;
   if (blocks > 2LL * sm_count()) blocks = 2LL * sm_count();
   indexer_scores_kernel<<<(unsigned)blocks, kThreads, smem, s>>>(p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "indexer_scores_kernel launch");

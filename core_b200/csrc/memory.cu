@@ -27,11 +27,6 @@ constexpr int kNCols = 256;       // d_mem columns per phi unit (MMA N)
 constexpr int kProdThreads = 128; // 4 gathering warps
 constexpr int kMbarChunk = 64;    // tokens per M_bar K chunk
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void st_shared_zero16(uint32_t dst) {
   asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
 }
@@ -53,6 +48,7 @@ __global__ void __launch_bounds__(1024)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   (void)inv_tau_num;
   float m = -INFINITY;
+#pragma unroll 8
   for (int i = threadIdx.x; i < L; i += blockDim.x) m = fmaxf(m, s[i] / tau);
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) red[warp] = m;
@@ -65,6 +61,7 @@ __global__ void __launch_bounds__(1024)
   __syncthreads();
   const float mx = s_max;
   double sum = 0.0;
+#pragma unroll 8
   for (int i = threadIdx.x; i < L; i += blockDim.x) sum += (double)expf(s[i] / tau - mx);
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) redd[warp] = sum;
@@ -78,6 +75,7 @@ __global__ void __launch_bounds__(1024)
   const float tot = s_sum;
   const int* ev = evict + (long long)b * n_evict;
   double pe = 0.0;
+#pragma unroll 8
   for (int k = threadIdx.x; k < n_evict; k += blockDim.x) {
     const float p = expf(s[ev[k]] / tau - mx) / tot;
     pe += (double)p;
@@ -94,6 +92,7 @@ __global__ void __launch_bounds__(1024)
   const float pie = (float)s_pie;
   const float mass = pie > 0.f ? pie : 1.0f;
   float* pb = pbar + (long long)b * n_ev_pad;
+#pragma unroll 8
   for (int k = threadIdx.x; k < n_ev_pad; k += blockDim.x) {
     float v = 0.f;
     if (k < n_evict) v = (expf(s[ev[k]] / tau - mx) / tot) / mass;
@@ -209,12 +208,19 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
           }
         }
         cp_async_commit();
-        cp_async_wait_all();
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_full(st));
+        // one gather group stays in flight: publish the stage issued before this one
+        if (it >= 1) {
+          cp_async_wait_group<1>();
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_full((it - 1) % kPhiStages));
+        }
       }
     }
+    cp_async_wait_all();
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (ok && it >= 1 && lane == 0) mbar_arrive(bar_full((it - 1) % kPhiStages));
   } else if (warp == 4) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(128, kNCols, 0, 0);
@@ -326,6 +332,7 @@ constexpr uint32_t kMbA = 2u * 128 * 128;           // two terms x 128 rows x 64
 constexpr uint32_t kMbBMax = 4u * kMbarChunk * 128; // up to 4 MN atoms x 64 token rows x 128 B
 constexpr uint32_t kMbStage = kMbA + kMbBMax;       // 64 KB
 constexpr int kMbStages = 3;
+constexpr int kMbLag = kMbStages - 1;  // gather groups in flight per producer thread
 constexpr int kMbThreads = 384;  // warps 0-3 gather, 4 MMA, 8-11 epilogue
 
 // CT = value columns per output tile (256, or 128 when Hkv*d is an odd
@@ -379,6 +386,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
   if (warp < 4) {
     const int tid = threadIdx.x;
     bool ok = true;
+    int last = 0;  // stages issued
     for (int kc = kc0, it = 0; kc < kc1 && ok; ++kc, ++it) {
       const int st = it % kMbStages;
       if (it >= kMbStages && !(ok = wait(bar_empty(st), ((it / kMbStages) - 1) & 1, 911))) break;
@@ -405,11 +413,20 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         }
       }
       cp_async_commit();
-      cp_async_wait_all();
-      fence_proxy_async_shared();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_full(st));
+      // kMbStages - 1 gather groups stay in flight: publish the oldest one
+      if (it >= kMbLag) {
+        cp_async_wait_group<kMbLag>();
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_full((it - kMbLag) % kMbStages));
+      }
+      last = it + 1;
     }
+    cp_async_wait_all();
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (ok && lane == 0)
+      for (int j = last > kMbLag ? last - kMbLag : 0; j < last; ++j) mbar_arrive(bar_full(j % kMbStages));
   } else if (warp == 4) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(128, CT, 0, 1);

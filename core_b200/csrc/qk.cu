@@ -691,25 +691,52 @@ __device__ __forceinline__ float sum_top_desc(const float (&t)[4], int k) {
   return s;
 }
 
-// Exact relation value R[h, t, key] (one query), as the relation kernel computes it.
-__device__ float relation_exact(const MergeParams& p, int b, int h, int key, int t) {
+// Exact relation value R[h, t, key] (one query), as the relation kernel
+// computes it; the key row is in shared memory as f32, the G query rows are
+// read 8 bf16 at a time and the dot products run over d in ascending order.
+__device__ float relation_exact(const MergeParams& p, int b, int h, int key, int t,
+                                const float* __restrict__ s_k) {
   const long long qpos = (long long)p.q_start + t;
   if (key > qpos) return kLogFloor;
-  const __nv_bfloat16* kr = p.k + (((long long)b * p.Hkv + h) * p.L + key) * kD;
   const long long cc = (qpos + 1 < p.L) ? qpos + 1 : p.L;
   const float lcc = logf((float)cc);
+  float dot[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint4* qr[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+    qr[g] = reinterpret_cast<const uint4*>(
+        p.q + (((long long)b * p.Hq + h * p.G + (g < p.G ? g : 0)) * p.nq + t) * kD);
+#pragma unroll 4
+  for (int c = 0; c < kD / 8; ++c) {
+    const float4 k0 = reinterpret_cast<const float4*>(s_k)[2 * c];
+    const float4 k1 = reinterpret_cast<const float4*>(s_k)[2 * c + 1];
+    const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (g < p.G) {
+        const uint4 w = __ldg(qr[g] + c);
+        const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 qf = __bfloat1622float2(q2[e]);
+          dot[g] = fmaf(qf.x, kv[2 * e], dot[g]);
+          dot[g] = fmaf(qf.y, kv[2 * e + 1], dot[g]);
+        }
+      }
+    }
+  }
   float acc = 0.f, mn = INFINITY;
-  for (int g = 0; g < p.G; ++g) {
-    const int qh = h * p.G + g;
-    const __nv_bfloat16* qr = p.q + (((long long)b * p.Hq + qh) * p.nq + t) * kD;
-    float dot = 0.f;
-    for (int e = 0; e < kD; ++e) dot = fmaf(__bfloat162float(qr[e]), __bfloat162float(kr[e]), dot);
-    const float x = bf16_round(dot);
-    const float r = fmaf(x, p.scale, -p.lse[((long long)b * p.Hq + qh) * p.nq + t]) + lcc;
-    float rel = logaddexp_floor(r);
-    if (qpos == 0) rel = log1pf(expf(kLogFloor));
-    acc = (g == 0) ? rel : acc + rel;
-    mn = fminf(mn, rel);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    if (g < p.G) {
+      const int qh = h * p.G + g;
+      const float x = bf16_round(dot[g]);
+      const float r = fmaf(x, p.scale, -p.lse[((long long)b * p.Hq + qh) * p.nq + t]) + lcc;
+      float rel = logaddexp_floor(r);
+      if (qpos == 0) rel = log1pf(expf(kLogFloor));
+      acc = (g == 0) ? rel : acc + rel;
+      mn = fminf(mn, rel);
+    }
   }
   if (p.head_topk < p.G) return __fdiv_rn(acc - mn, (float)p.head_topk);
   return __fdiv_rn(acc, (float)p.head_topk);
@@ -810,44 +837,45 @@ __global__ void __launch_bounds__(kMergeThreads)
 
 // Exact resolution of the f6 heads the running statistics could not decide:
 // one block per queued (key, head) pair recomputes its relation values over
-// all queries, sorts them in descending order and tests the mean of the top
-// ceil(valid / 4) (fused_qk.py:571-578).  A positive head adds 1/Hkv to f6;
-// Hkv is a power of two here, so the additions are exact in any order.
-__global__ void __launch_bounds__(kMergeThreads)
+// all queries, ranks them (descending, ties by query index, i.e. the order of
+// a stable descending sort) and tests the mean of the top ceil(valid / 4)
+// summed in that order (fused_qk.py:571-578).  A positive head adds 1/Hkv to
+// f6; Hkv is a power of two here, so the additions are exact in any order.
+constexpr int kResolveThreads = 128;
+
+__global__ void __launch_bounds__(kResolveThreads)
     qk_f6_resolve_kernel(const MergeParams p) {
-  __shared__ float s_vals[kMaxSlowNq];
+  __shared__ __align__(16) float s_k[kD];
+  __shared__ float s_rel[kMaxSlowNq];
+  __shared__ float s_sorted[kMaxSlowNq];
   const int count = min(*p.queue_count, p.queue_cap);
-  int n2 = 1;
-  while (n2 < p.nq) n2 <<= 1;
   for (int it = blockIdx.x; it < count; it += gridDim.x) {
     const int2 item = p.queue[it];
     const int bb = (int)(item.x / p.L), kk = (int)(item.x % p.L), h = item.y;
-    for (int t = threadIdx.x; t < n2; t += kMergeThreads)
-      s_vals[t] = (t < p.nq) ? relation_exact(p, bb, h, kk, t) : -INFINITY;
+    const __nv_bfloat16* kr = p.k + (((long long)bb * p.Hkv + h) * p.L + kk) * kD;
+    for (int e = threadIdx.x; e < kD; e += kResolveThreads) s_k[e] = __bfloat162float(kr[e]);
     __syncthreads();
-    for (int size = 2; size <= n2; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int i = threadIdx.x; i < n2; i += kMergeThreads) {
-          const int j = i ^ stride;
-          if (j > i) {
-            const bool desc = ((i & size) == 0);
-            const float a = s_vals[i], c = s_vals[j];
-            if (desc ? (a < c) : (a > c)) {
-              s_vals[i] = c;
-              s_vals[j] = a;
-            }
-          }
-        }
-        __syncthreads();
+    for (int t = threadIdx.x; t < p.nq; t += kResolveThreads)
+      s_rel[t] = relation_exact(p, bb, h, kk, t, s_k);
+    __syncthreads();
+    for (int t = threadIdx.x; t < p.nq; t += kResolveThreads) {
+      const float v = s_rel[t];
+      int r = 0;
+      for (int j = 0; j < p.nq; ++j) {
+        const float u = s_rel[j];
+        r += (u > v || (u == v && j < t)) ? 1 : 0;
       }
+      s_sorted[r] = v;
     }
+    __syncthreads();
     if (threadIdx.x == 0) {
       int vld = p.nq - max(kk - p.q_start, 0);
       vld = min(max(vld, 1), p.nq);
       const int kfr = max((vld + 3) / 4, 1);
-      float s = 0.f;
-      for (int i = 0; i < kfr; ++i) s += s_vals[i];
-      if (s / (float)kfr > 0.f) atomicAdd(p.features + (long long)item.x * p.stride + 5, 1.0f / (float)p.Hkv);
+      float sum = 0.f;
+      for (int i = 0; i < kfr; ++i) sum += s_sorted[i];
+      if (sum / (float)kfr > 0.f)
+        atomicAdd(p.features + (long long)item.x * p.stride + 5, 1.0f / (float)p.Hkv);
     }
     __syncthreads();
   }
@@ -1045,7 +1073,7 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
   const long long n = (long long)p.B * p.L;
   qk_merge_kernel<<<(unsigned)((n + kMergeThreads - 1) / kMergeThreads), kMergeThreads, 0, s>>>(mp);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_merge_kernel launch");
-  qk_f6_resolve_kernel<<<sm_count(), kMergeThreads, 0, s>>>(mp);
+  qk_f6_resolve_kernel<<<4 * sm_count(), kResolveThreads, 0, s>>>(mp);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_f6_resolve_kernel launch");
   if (lse_out != nullptr) {
     e = cudaMemcpyAsync(lse_out, lse_buf, sizeof(float) * (size_t)p.B * p.Hq * p.nq,

@@ -9,8 +9,12 @@
 //
 // One CTA per batch row: an MSB-first 8-bit radix select over order-preserving
 // uint32 keys of the scores finds the threshold key and how many of the tied
-// tokens at the threshold to keep (lowest indices first), then a block-wide
-// prefix scan writes the kept and evicted indices in ascending order.
+// tokens at the threshold to keep (lowest indices first); histograms are
+// warp-aggregated (__match_any_sync) and the digit is picked by one warp's
+// suffix scan.  Then every thread takes a contiguous run of tokens, one
+// block-wide scan of packed (ties, definite keeps) counts gives each run its
+// output offsets, and the kept and evicted indices are written in ascending
+// order.
 #include <cmath>
 
 #include "common.cuh"
@@ -28,32 +32,29 @@ __device__ __forceinline__ uint32_t order_key(float x) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Block-wide exclusive scan of one int per thread; returns the exclusive
-// prefix and writes the block total to *total.
-__device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* total) {
+// Block-wide exclusive scan of one 64-bit value per thread.
+__device__ __forceinline__ unsigned long long block_exclusive_scan64(unsigned long long v,
+                                                                     unsigned long long* s_warp) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = v;
+  unsigned long long x = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    const unsigned long long y = __shfl_up_sync(0xffffffffu, x, o);
     if (lane >= o) x += y;
   }
   if (lane == 31) s_warp[warp] = x;
   __syncthreads();
   if (warp == 0) {
-    int w = (lane < kWarps) ? s_warp[lane] : 0;
+    unsigned long long w = (lane < kWarps) ? s_warp[lane] : 0ull;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      const unsigned long long y = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += y;
     }
     s_warp[lane] = w;  // inclusive warp prefix
   }
   __syncthreads();
-  const int before = (warp > 0 ? s_warp[warp - 1] : 0) + x - v;
-  *total = s_warp[kWarps - 1];
-  __syncthreads();
-  return before;
+  return (warp > 0 ? s_warp[warp - 1] : 0ull) + x - v;
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -63,8 +64,9 @@ __global__ void __launch_bounds__(kThreads)
   const float* s = scores + (long long)b * L;
   const int sinks = (n_sink > 0 && n_sink < L) ? n_sink : 0;
   const int need = n_kept - sinks;  // non-sink tokens to keep (>= 0)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __shared__ int hist[256];
-  __shared__ int s_warp[32];
+  __shared__ unsigned long long s_warp[32];
   __shared__ uint32_t s_prefix, s_mask;
   __shared__ int s_need, s_bad;
 
@@ -76,67 +78,97 @@ __global__ void __launch_bounds__(kThreads)
   }
   __syncthreads();
   // ---- radix select: find key T such that #(key > T) < need <= #(key >= T) ----
+  bool bad = false;
   for (int shift = 24; shift >= 0 && need > 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += kThreads) hist[i] = 0;
     __syncthreads();
     const uint32_t prefix = s_prefix, mask = s_mask;
-    for (int i = sinks + threadIdx.x; i < L; i += kThreads) {
-      const float x = s[i];
-      if (isnan(x)) s_bad = 1;
-      const uint32_t k = order_key(x);
-      if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1);
+#pragma unroll 4
+    for (int i0 = sinks; i0 < L; i0 += kThreads) {
+      const int i = i0 + threadIdx.x;
+      int bin = -1;
+      if (i < L) {
+        const float x = s[i];
+        bad |= isnan(x);
+        const uint32_t k = order_key(x);
+        if ((k & mask) == prefix) bin = (int)((k >> shift) & 255u);
+      }
+      const unsigned grp = __match_any_sync(0xffffffffu, bin);
+      if (bin >= 0 && lane == __ffs(grp) - 1) atomicAdd(&hist[bin], __popc(grp));
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int rem = s_need;
-      int d = 255;
-      for (; d > 0; --d) {
-        if (hist[d] >= rem) break;
-        rem -= hist[d];
+    if (warp == 0) {
+      // lane l owns bins [8 l, 8 l + 8); inclusive suffix sums over lanes
+      int own = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) own += hist[8 * lane + j];
+      int suf = own;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_down_sync(0xffffffffu, suf, o);
+        if (lane + o < 32) suf += y;
       }
-      s_prefix = prefix | ((uint32_t)d << shift);
-      s_mask = mask | (255u << shift);
-      s_need = rem;
+      const int rem0 = s_need;
+      const int above = suf - own;
+      if (above < rem0 && rem0 <= suf) {
+        int rem = rem0 - above;
+        int d = 8 * lane + 7;
+        for (; d > 8 * lane; --d) {
+          if (hist[d] >= rem) break;
+          rem -= hist[d];
+        }
+        s_prefix = prefix | ((uint32_t)d << shift);
+        s_mask = mask | (255u << shift);
+        s_need = rem;
+      }
     }
     __syncthreads();
   }
+  if (bad) s_bad = 1;
+  __syncthreads();
   if (s_bad && threadIdx.x == 0) record_error(status, CORE_ERR_NONFINITE, 701, b);
   const uint32_t T = s_prefix;
   const int ties_keep = s_need;  // tokens equal to T to keep, lowest index first
-  // ---- ascending compaction ----
-  int kept_base = 0, ev_base = 0, tie_base = 0;
+  // ---- ascending compaction over contiguous runs ----
+  const int per = (L + kThreads - 1) / kThreads;
+  const int r0 = min(L, threadIdx.x * per), r1 = min(L, r0 + per);
+  int n_def = 0, n_tie = 0;
+  for (int i = r0; i < r1; ++i) {
+    if (i < sinks) {
+      ++n_def;
+    } else if (need > 0) {
+      const uint32_t k = order_key(s[i]);
+      n_def += (k > T);
+      n_tie += (k == T);
+    }
+  }
+  const unsigned long long pre =
+      block_exclusive_scan64(((unsigned long long)n_tie << 32) | (unsigned)n_def, s_warp);
+  int tie_before = (int)(pre >> 32);
+  int kept_before = (int)(pre & 0xFFFFFFFFull) + min(tie_before, ties_keep);
   int* kout = keep_idx + (long long)b * n_kept;
   int* eout = evict_idx + (long long)b * (L - n_kept);
-  for (int c0 = 0; c0 < L; c0 += kThreads) {
-    const int i = c0 + threadIdx.x;
-    int is_tie = 0, keep = 0;
-    if (i < L) {
-      if (i < sinks) {
-        keep = 1;
-      } else if (need > 0) {
-        const uint32_t k = order_key(s[i]);
-        if (k > T) keep = 1;
-        else if (k == T) is_tie = 1;
-      }
+  for (int i = r0; i < r1; ++i) {
+    bool keep;
+    if (i < sinks) {
+      keep = true;
+    } else if (need > 0) {
+      const uint32_t k = order_key(s[i]);
+      keep = k > T;
+      if (k == T) keep = tie_before++ < ties_keep;
+    } else {
+      keep = false;
     }
-    int tie_total;
-    const int tie_rank = tie_base + block_exclusive_scan(is_tie, s_warp, &tie_total);
-    if (is_tie && tie_rank < ties_keep) keep = 1;
-    int keep_total;
-    const int kpos = kept_base + block_exclusive_scan(keep, s_warp, &keep_total);
-    if (i < L) {
-      if (keep) {
-        if (kpos < n_kept) kout[kpos] = i;
-      } else {
-        const int epos = i - kpos;  // evicted tokens before i
-        if (epos < L - n_kept) eout[epos] = i;
-      }
+    if (keep) {
+      if (kept_before < n_kept) kout[kept_before] = i;
+      ++kept_before;
+    } else {
+      const int epos = i - kept_before;  // evicted tokens before i
+      if (epos < L - n_kept) eout[epos] = i;
     }
-    kept_base += keep_total;
-    tie_base += tie_total;
-    ev_base += (min(kThreads, L - c0) - keep_total);
   }
-  if (threadIdx.x == 0 && kept_base != n_kept) record_error(status, CORE_ERR_INVALID_ARG, 702, b);
+  if (threadIdx.x == kThreads - 1 && kept_before != n_kept)
+    record_error(status, CORE_ERR_INVALID_ARG, 702, b);
 }
 
 }  // namespace topb

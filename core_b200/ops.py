@@ -120,9 +120,10 @@ def coverage_features(k: torch.Tensor, geometry_ext: torch.Tensor, prototypes: t
 
 
 def pack_mlp(mlp_params) -> torch.Tensor:
-    """[w1 (128,14) | b1 | w2 (128,128) | b2 | w3 (128) | b3] as one f32 vector."""
+    """[w1 (128,14) | b1 | w2^T (in 128, out 128) | b2 | w3 (128) | b3] as one f32
+    vector (nn.Linear weights are (out, in); layer 2 is stored transposed)."""
     w1, b1, w2, b2, w3, b3 = mlp_params
-    return torch.cat([w1.reshape(-1), b1.reshape(-1), w2.reshape(-1), b2.reshape(-1),
+    return torch.cat([w1.reshape(-1), b1.reshape(-1), w2.t().reshape(-1), b2.reshape(-1),
                       w3.reshape(-1), b3.reshape(-1)]).to(torch.float32).contiguous()
 
 

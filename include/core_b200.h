@@ -91,7 +91,7 @@ int core_qk_features(const core_dims_t* dims, const void* q, const void* k,
  * (:53-77), PrototypeBank.get_coverage_features (:146-213) and
  * HadamardProjector.rotate (:259-261).
  *   geometry_ext : (3, 128, Hkv*d) bf16 from core_prepare_geometry
- *   prototypes   : (64, P) f32 unit rows
+ *   prototypes   : (64, P) f32 unit rows, 16-byte aligned
  *   features     : (B, L, feature_stride) f32, columns col0..col0+3
  * P (proto_dim) must be 64 and the prototype count 64.
  * ------------------------------------------------------------------------- */
@@ -119,8 +119,8 @@ int core_prepare_geometry(const float* geometry, const float* hadamard, int32_t 
  *   special    : optional (B, L) uint8, 1 where the token id is a special id
  *   features   : (B, L, 14) f32; columns 0..9 already hold f1..f6 and the
  *                coverage features; columns 10..13 are written here
- *   mlp        : packed f32 [w1 (128,14) | b1 (128) | w2 (128,128) | b2 (128) |
- *                w3 (128) | b3 (1)]
+ *   mlp        : packed f32, 16-byte aligned: [w1 (128 out,14 in) | b1 (128) |
+ *                w2 transposed (128 in,128 out) | b2 (128) | w3 (128) | b3 (1)]
  *   scores     : (B, L) f32
  * ------------------------------------------------------------------------- */
 int core_indexer_scores(const core_dims_t* dims, const void* v, const int64_t* positions,
