@@ -337,20 +337,45 @@ def run_e2e(a, dev, parts, layers, dist):
     h2d = sum(t.numel() * t.element_size() for h in host for t in h)
     d2h_per_step = [0]
 
+    # Double-buffered device slots: the copy stream uploads layer l + 2 while
+    # the compute stream compresses layer l + 1 (PCIe and SMs run concurrently).
+    nbuf = 2
+    copy_stream = torch.cuda.Stream(dev)
+    slots = [tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in host[0])
+             for _ in range(nbuf)]
+    copied = [torch.cuda.Event() for _ in range(nbuf)]
+    consumed = [torch.cuda.Event() for _ in range(nbuf)]
+
+    def upload(l):
+        j = l % nbuf
+        with torch.cuda.stream(copy_stream):
+            if l >= nbuf:
+                copy_stream.wait_event(consumed[j])
+            for dst, src in zip(slots[j], host[l]):
+                dst.copy_(src, non_blocking=True)
+            copied[j].record(copy_stream)
+
     def step():
         press.reset_cache()
         base.set_query_boundary(L - nq)
+        comp = torch.cuda.current_stream()
         results = []
-        for l, (hq, hk, hv) in enumerate(host):
-            k = hk.to(dev, non_blocking=True)
-            v = hv.to(dev, non_blocking=True)
-            full_q[:, :, L - nq:].copy_(hq, non_blocking=True)
+        for l in range(min(nbuf, len(host))):
+            upload(l)
+        for l in range(len(host)):
+            j = l % nbuf
+            comp.wait_event(copied[j])
+            q, k, v = slots[j]
+            full_q[:, :, L - nq:].copy_(q)
             mods[l]._core_cached_query_states = full_q
             press.compress(mods[l], hs, k, v, None, {})
+            consumed[j].record(comp)
+            if l + nbuf < len(host):
+                upload(l + nbuf)
             results.append(base.cache_metadata.positions[l])
             results.append(press._Z[l])
         out = [r.to("cpu", non_blocking=True) for r in results]
-        torch.cuda.current_stream().synchronize()
+        comp.synchronize()
         d2h_per_step[0] = sum(o.numel() * o.element_size() for o in out)
         return out
 
@@ -371,7 +396,8 @@ def run_e2e(a, dev, parts, layers, dist):
     return {"value": n * L / dt, "unit": UNIT, "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h_per_step[0], "ms_per_step": dt * 1e3,
             "steps": a.e2e_steps,
-            "path": "core_b200.press.COREMemoryPress.compress per layer, inputs from pinned host memory"}
+            "path": "core_b200.press.COREMemoryPress.compress per layer, inputs from pinned host "
+                    "memory (uploads double-buffered on a copy stream)"}
 
 
 if __name__ == "__main__":

@@ -2,14 +2,14 @@
 // the feature concatenation at core/kvpress_adapter.py:536 and
 // COREIndexerMLP, core/indexer.py:88-108).
 //
-// One thread per cached token, persistent blocks.  The auxiliary features
+// Four threads per cached token, persistent blocks.  The auxiliary features
 // follow the reference's dtype: for bf16 caches a_value is computed with the
 // same bf16 roundings as the reference's torch ops (squares, per-head sums,
 // the head mean, /d and log1p each round to bf16).  The MLP runs in f32 with
 // its weights staged once per block into shared memory (cp.async) and read as
-// warp-wide broadcasts: hidden unit k of layer 1 is computed, GELU'd, and
-// immediately accumulated into all 128 layer-2 outputs held in registers
-// (an outer-product form, so layer-2 sums run over k in ascending order).
+// broadcasts: hidden unit k of layer 1 is computed, GELU'd, and immediately
+// accumulated into the 128 layer-2 outputs held in registers, a quarter per
+// thread (an outer-product form, so layer-2 sums run over k in ascending order).
 #include <cmath>
 
 #include "common.cuh"
@@ -20,7 +20,7 @@ namespace idx {
 
 constexpr int kIn = 14;
 constexpr int kHid = 128;
-constexpr int kThreads = 128;  // one token per thread
+constexpr int kThreads = 256;  // 64 tokens x 4 threads
 // packed global layout (floats): [w1 (128,14) | b1 | w2^T (in 128, out 128) | b2 | w3 | b3]
 constexpr int kGW1 = 0;
 constexpr int kGB1 = kGW1 + kHid * kIn;    // 1792
@@ -59,16 +59,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   // w2^T | b2 | w3 are contiguous in both layouts: one asynchronous copy
   cp_async_block(sm + kOffW2T, p.mlp + kGW2T, (kHid * kHid + 2 * kHid) / 4);
   {
+    static_assert(kHid * kIn % kThreads == 0 && kHid <= kThreads, "staging layout");
     float r[kHid * kIn / kThreads + 1];
 #pragma unroll
     for (int j = 0; j < kHid * kIn / kThreads; ++j) r[j] = p.mlp[kGW1 + threadIdx.x + j * kThreads];
-    r[kHid * kIn / kThreads] = p.mlp[kGB1 + threadIdx.x];
+    if (threadIdx.x < kHid) r[kHid * kIn / kThreads] = p.mlp[kGB1 + threadIdx.x];
 #pragma unroll
     for (int j = 0; j < kHid * kIn / kThreads; ++j) {
       const int i = threadIdx.x + j * kThreads;
       sm[kOffW1 + (i / kIn) * kW1Stride + (i % kIn)] = r[j];
     }
-    sm[kOffB1 + threadIdx.x] = r[kHid * kIn / kThreads];
+    if (threadIdx.x < kHid) sm[kOffB1 + threadIdx.x] = r[kHid * kIn / kThreads];
     if (threadIdx.x == 0) sm[kOffB3] = p.mlp[kGB3];
   }
   cp_async_wait_all();
@@ -76,16 +77,24 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const long long n = (long long)p.B * p.L;
   const float age_den = log1pf((float)(p.original_length - 1 > 1 ? p.original_length - 1 : 1));
-  for (long long gi = (long long)blockIdx.x * kThreads + threadIdx.x; gi - threadIdx.x < n;
-       gi += (long long)gridDim.x * kThreads) {
+  const int part = threadIdx.x & 3;       // this thread's quarter of the token's work
+  const int lane = threadIdx.x & 31;
+  const int qbase = lane & ~3;            // lane of part 0 of this token
+  for (long long gi = ((long long)blockIdx.x * kThreads + threadIdx.x) >> 2; ;
+       gi += (long long)gridDim.x * (kThreads / 4)) {
+    const long long g0 = gi - (threadIdx.x >> 2);  // first token of this block's group
+    if (g0 >= n) break;
     const bool active = gi < n;
     float x[kIn];
-    if (active) {
-      const int b = (int)(gi / p.L);
-      const int i = (int)(gi % p.L);
-      // ---- a_value: bf16-rounded |v_h|^2 per head, heads summed in order ----
-      float hsum = 0.f;
-      for (int h = 0; h < p.Hkv; ++h) {
+    // ---- a_value: heads part, part + 4, ... summed here, combined in head order ----
+    float hs[kMaxHkv / 4];
+    const int b = active ? (int)(gi / p.L) : 0;
+    const int i = active ? (int)(gi % p.L) : 0;
+#pragma unroll
+    for (int r = 0; r < kMaxHkv / 4; ++r) {
+      hs[r] = 0.f;
+      const int h = 4 * r + part;
+      if (active && h < p.Hkv) {
         const uint4* row =
             reinterpret_cast<const uint4*>(p.v + (((long long)b * p.Hkv + h) * p.L + i) * 128);
         float s = 0.f;
@@ -100,12 +109,23 @@ __global__ void __launch_bounds__(kThreads, 2)
             s += bf16_round(t.y * t.y);
           }
         }
-        hsum += bf16_round(s);
+        hs[r] = bf16_round(s);
       }
+    }
+    float hsum = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxHkv / 4; ++r) {
+#pragma unroll
+      for (int pp = 0; pp < 4; ++pp) {
+        const float t = __shfl_sync(0xffffffffu, hs[r], qbase | pp);
+        if (4 * r + pp < p.Hkv) hsum += t;
+      }
+    }
+    if (active) {
       // ---- auxiliary features (features.py:886-921) ----
       const long long pos = p.positions[gi];
       const int T = p.original_length;
-      if (pos < 0 || pos >= T) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
+      if (part == 0 && (pos < 0 || pos >= T)) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
       const float a_age = log1pf((float)(T - 1 - pos)) / age_den;
       bool sink = pos < p.n_sink;
       if (p.special != nullptr && p.special[gi]) sink = true;
@@ -118,23 +138,28 @@ __global__ void __launch_bounds__(kThreads, 2)
       x[11] = sink ? 1.0f : 0.0f;
       x[12] = a_value;
       x[13] = p.is_prefill ? 0.0f : 1.0f;
+      if (part == 0) {
 #pragma unroll
-      for (int k = 10; k < kIn; ++k) f[k] = x[k];
-      bool finite = true;
+        for (int k = 10; k < kIn; ++k) f[k] = x[k];
+        bool finite = true;
 #pragma unroll
-      for (int k = 0; k < kIn; ++k) finite &= isfinite(x[k]);
-      if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 602, i);
+        for (int k = 0; k < kIn; ++k) finite &= isfinite(x[k]);
+        if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 602, i);
+      }
     } else {
 #pragma unroll
       for (int k = 0; k < kIn; ++k) x[k] = 0.f;
     }
-    // ---- MLP: layer-1 unit k, then its rank-1 update of the 128 layer-2 sums ----
-    float acc[kHid];
+    // ---- MLP.  Hidden unit k = 4 j + pp is computed by part pp and shared by
+    // shuffle; this thread accumulates outputs o = 16 c + 4 part + e (c < 8,
+    // e < 4) over k in ascending order. ----
+    float acc[kHid / 4];
 #pragma unroll
-    for (int o = 0; o < kHid; ++o) acc[o] = 0.f;
+    for (int o = 0; o < kHid / 4; ++o) acc[o] = 0.f;
 #pragma unroll 1
-    for (int k = 0; k < kHid; ++k) {
-      const float4* w1 = reinterpret_cast<const float4*>(sm + kOffW1 + k * kW1Stride);
+    for (int j = 0; j < kHid / 4; ++j) {
+      const int kown = 4 * j + part;
+      const float4* w1 = reinterpret_cast<const float4*>(sm + kOffW1 + kown * kW1Stride);
       const float4 a0 = w1[0], a1 = w1[1], a2 = w1[2], a3 = w1[3];
       float t = 0.f;
       t = fmaf(a0.x, x[0], t);
@@ -151,21 +176,33 @@ __global__ void __launch_bounds__(kThreads, 2)
       t = fmaf(a2.w, x[11], t);
       t = fmaf(a3.x, x[12], t);
       t = fmaf(a3.y, x[13], t);
-      const float hk = gelu(t + sm[kOffB1 + k]);
-      const float4* w2 = reinterpret_cast<const float4*>(sm + kOffW2T + k * kHid);
+      const float hown = gelu(t + sm[kOffB1 + kown]);
 #pragma unroll
-      for (int o4 = 0; o4 < kHid / 4; ++o4) {
-        const float4 w = w2[o4];
-        acc[4 * o4] = fmaf(w.x, hk, acc[4 * o4]);
-        acc[4 * o4 + 1] = fmaf(w.y, hk, acc[4 * o4 + 1]);
-        acc[4 * o4 + 2] = fmaf(w.z, hk, acc[4 * o4 + 2]);
-        acc[4 * o4 + 3] = fmaf(w.w, hk, acc[4 * o4 + 3]);
+      for (int pp = 0; pp < 4; ++pp) {
+        const float hk = __shfl_sync(0xffffffffu, hown, qbase | pp);
+        const float4* w2 = reinterpret_cast<const float4*>(sm + kOffW2T + (4 * j + pp) * kHid) + part;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 w = w2[4 * c];
+          acc[4 * c] = fmaf(w.x, hk, acc[4 * c]);
+          acc[4 * c + 1] = fmaf(w.y, hk, acc[4 * c + 1]);
+          acc[4 * c + 2] = fmaf(w.z, hk, acc[4 * c + 2]);
+          acc[4 * c + 3] = fmaf(w.w, hk, acc[4 * c + 3]);
+        }
       }
     }
     float out = 0.f;
 #pragma unroll
-    for (int o = 0; o < kHid; ++o) out = fmaf(sm[kOffW3 + o], gelu(acc[o] + sm[kOffB2 + o]), out);
-    if (active) p.scores[gi] = out + sm[kOffB3];
+    for (int c = 0; c < 8; ++c) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int o = 16 * c + 4 * part + e;
+        out = fmaf(sm[kOffW3 + o], gelu(acc[4 * c + e] + sm[kOffB2 + o]), out);
+      }
+    }
+    out += __shfl_xor_sync(0xffffffffu, out, 1);
+    out += __shfl_xor_sync(0xffffffffu, out, 2);
+    if (active && part == 0) p.scores[gi] = out + sm[kOffB3];
   }
 }
 
@@ -210,7 +247,7 @@ extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const in
       cudaFuncSetAttribute(indexer_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_error(e, "indexer_scores_kernel attribute");
   const long long n = (long long)p.B * p.L;
-  long long blocks = (n + kThreads - 1) / kThreads;
+  long long blocks = (n + kThreads / 4 - 1) / (kThreads / 4);
   if (blocks > 2LL * sm_count()) blocks = 2LL * sm_count();
   indexer_scores_kernel<<<(unsigned)blocks, kThreads, smem, s>>>(p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "indexer_scores_kernel launch");

@@ -535,7 +535,7 @@ void plan_mw(const core_dims_t* d, int n_evict, int d_mem, MwPlan* m) {
   m->n_ct = m->kvw / m->ct;
   const long long tiles = (long long)m->n_jt * m->n_ct;
   const int n_kc = m->n_ev_pad / kMbarChunk;
-  int splits = (int)((sms + tiles - 1) / tiles);
+  int splits = (int)(sms / tiles);  // one wave: one CTA per SM (the stages fill shared memory)
   if (splits > n_kc) splits = n_kc;
   if (splits < 1) splits = 1;
   m->splits = splits;
