@@ -276,14 +276,11 @@ def main():
     rel_ms = statistics.mean(relation_ms)
     achieved = flops / (rel_ms / 1e3) / 1e12
     traffic = None
-    tpath = os.path.join(ROOT, "profiles", "qk_relation_traffic.json")
+    tpath = os.path.join(ROOT, "profiles", f"qk_relation_L{L}_traffic.txt")
     if os.path.exists(tpath):
-        try:
-            tr = json.load(open(tpath))
-            if int(tr.get("seq_len", 0)) == L:
-                traffic = tr.get("bytes_per_launch")
-        except Exception:
-            traffic = None
+        rec = dict(line.split(None, 1) for line in open(tpath) if line.strip())
+        if int(rec.get("seq_len", 0)) == L:
+            traffic = int(rec["bytes_per_launch"])
     roofline = {"kernel": "qk_relation_kernel (QK pass 2: relation + per-key statistics)",
                 "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "peak_source": f"{peak_src} bf16_tflops_sustained",
