@@ -89,6 +89,8 @@ SIGNATURES = {
     "core_memory_readout_workspace_bytes": (_S, [_D, _I, _I, _I]),
     "core_memory_readout": (ctypes.c_int, [_D, _I, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P, _P, _P,
                                            _I, _P, _P, _S, _P]),
+    "core_memory_readout_noalloc": (ctypes.c_int, [_D, _I, _P, _P, _P, _P, _P, _P, _I, _I, _F,
+                                                   _P, _P, _P, _I, _P, _P]),
     "core_split_bf16": (ctypes.c_int, [_P, ctypes.c_int64, _I, _P, _P]),
     "core_compress_layer_workspace_bytes": (_S, [_D, _I, _I]),
     "core_compress_layer": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P,

@@ -240,3 +240,68 @@ extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const vo
   }
   return CORE_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Readout without a caller workspace: the same three kernels, their scratch in
+// a file-scope device array.  Every scratch element a kernel reads is written
+// earlier in the same call, so nothing has to start at zero.  The array is one
+// per device: overlapping calls on one device race on it.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+constexpr size_t kReadoutScratchFloats = 65536;  // 256 KB
+__device__ __align__(256) float g_readout_scratch[kReadoutScratchFloats];
+
+constexpr int kMaxDevices = 64;
+float* g_readout_scratch_ptr[kMaxDevices] = {};
+std::mutex g_readout_scratch_mu;
+
+// Resolves the scratch address of the current device once (the first call on
+// a device does this set-up; later calls only read the cached pointer).
+int readout_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "core_memory_readout_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_memory_readout_noalloc: device index above 63");
+  std::lock_guard<std::mutex> lock(g_readout_scratch_mu);
+  if (g_readout_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_readout_scratch);
+    if (e != cudaSuccess) return cuda_error(e, "core_memory_readout_noalloc: cudaGetSymbolAddress");
+    g_readout_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_readout_scratch_ptr[dev];
+  return CORE_OK;
+}
+}  // namespace
+
+extern "C" int core_memory_readout_noalloc(const core_dims_t* d, int32_t q_len, const void* q,
+                                           const float* theta, const float* gate_w1,
+                                           const float* gate_b1, const float* gate_w2,
+                                           const float* gate_b2, int32_t d_mem,
+                                           int32_t gate_hidden, float gate_override,
+                                           const float* M, const float* b_state,
+                                           const float* o_fold, int32_t hidden, void* attn_out,
+                                           void* stream) {
+  if (d == nullptr || d->batch <= 0 || d->n_q_heads <= 0 || d->n_kv_heads <= 0 || d->head_dim != kD)
+    return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout_noalloc: bad dims");
+  if (q_len <= 0 || d_mem <= 0 || hidden <= 0 || gate_hidden < 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout_noalloc: bad sizes");
+  // the carves core_memory_readout makes from its workspace, 256-byte aligned
+  Sizer need;
+  need.take<float>((size_t)d->batch * q_len * d_mem);
+  need.take<float>((size_t)d->batch * q_len * (gate_hidden > 0 ? gate_hidden : 1));
+  need.take<float>((size_t)d->batch * q_len * d->n_kv_heads * kD);
+  if (need.used > kReadoutScratchFloats * sizeof(float))
+    return set_error(CORE_ERR_INVALID_ARG,
+                     "core_memory_readout_noalloc: B*q_len*(d_mem + gate_hidden + Hkv*d) floats "
+                     "exceed the 256 KB static scratch; use core_memory_readout");
+  float* scratch = nullptr;
+  int rc = readout_scratch(&scratch);
+  if (rc != CORE_OK) return rc;
+  return core_memory_readout(d, q_len, q, theta, gate_w1, gate_b1, gate_w2, gate_b2, d_mem,
+                             gate_hidden, gate_override, M, b_state, o_fold, hidden, attn_out,
+                             scratch, kReadoutScratchFloats * sizeof(float), stream);
+}

@@ -193,6 +193,23 @@ int core_memory_readout(const core_dims_t* dims, int32_t q_len, const void* q, c
                         const float* o_fold, int32_t hidden, void* attn_out, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* core_memory_readout without a caller workspace: no counterpart in the
+ * reference.  Same arguments and result as core_memory_readout; its scratch is
+ * a 256 KB static device array (no cudaMalloc or other allocation), so
+ * B * q_len * (d_mem + gate_hidden + Hkv*d) floats, each of the three parts
+ * rounded up to 256 bytes, must fit in 256 KB; larger calls return
+ * CORE_ERR_INVALID_ARG.  The first call on a device, with that device current,
+ * resolves the scratch address (cudaGetSymbolAddress) and should precede any
+ * stream capture.  Nothing in the scratch needs to start at zero.  There is one
+ * scratch per device: calls that overlap on one device (other streams or host
+ * threads) race on it and must be serialised by the caller. */
+int core_memory_readout_noalloc(const core_dims_t* dims, int32_t q_len, const void* q,
+                                const float* theta, const float* gate_w1, const float* gate_b1,
+                                const float* gate_w2, const float* gate_b2, int32_t d_mem,
+                                int32_t gate_hidden, float gate_override, const float* M,
+                                const float* b_state, const float* o_fold, int32_t hidden,
+                                void* attn_out, void* stream);
+
 /* ---------------------------------------------------------------------------
  * One layer's complete compression step.
  * Replaces COREMemoryPress.compress (core/kvpress_adapter.py:968-1210) with
