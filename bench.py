@@ -52,6 +52,9 @@ def parse():
     p.add_argument("--d-mem", type=int, default=512)
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--streams", type=int, default=3, help="layers compressed concurrently")
+    p.add_argument("--sm-reserve", type=int, default=2,
+                   help="SMs the persistent grids leave free for the other streams' kernels")
     return p.parse_args()
 
 
@@ -62,7 +65,8 @@ def config_dict(a, n):
             "n_kv_heads": 8, "n_q_heads": 32, "head_dim": 128, "query_buffer": a.n_queries,
             "compression_ratio": a.ratio, "n_kept": int(a.seq_len * (1 - a.ratio)),
             "d_mem": a.d_mem, "parallelism": f"batch-sharded x{n}",
-            "l2": "inputs larger than L2 (32 layers x 64 MiB of K/V per step)"}
+            "l2": "inputs larger than L2 (32 layers x 64 MiB of K/V per step)",
+            "layers_in_flight": a.streams, "sm_reserve": a.sm_reserve if a.streams > 1 else 0}
 
 
 # ---------------------------------------------------------------------------
@@ -222,7 +226,7 @@ def main():
     L = a.seq_len
     n_kept = engine.n_kept_for(L, a.ratio, 4)
     pos = torch.arange(L, device=dev)[None]
-    ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+    ws = [torch.empty(64 << 20, dtype=torch.uint8, device=dev) for _ in range(a.streams)]
     # one (start, end) pair per layer and timed step, around the QK relation kernel
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(a.layers)] for _ in range(a.steps)]
@@ -231,12 +235,15 @@ def main():
             e0.record()
             e1.record()
     torch.cuda.synchronize()
+    n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    budget = ops.sm_budget(max(1, n_sms - a.sm_reserve) if a.streams > 1 else 0)
 
     def step(pairs):
-        for l, (q, k, v, lw, mem) in enumerate(layers):
-            engine.compress_layer(q, k, v, lw, n_kept=n_kept, positions=pos, original_length=L,
-                                  is_prefill=True, memory=mem, workspace=ws,
-                                  timing_events=None if pairs is None else pairs[l])
+        jobs = [dict(q=q, keys=k, values=v, weights=lw, positions=pos, memory=mem,
+                     timing_events=None if pairs is None else pairs[l])
+                for l, (q, k, v, lw, mem) in enumerate(layers)]
+        engine.compress_layers(jobs, n_streams=a.streams, workspaces=ws, n_kept=n_kept,
+                               original_length=L, is_prefill=True)
 
     for _ in range(a.warmup):
         step(None)
@@ -257,6 +264,7 @@ def main():
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
+    budget.__exit__(None, None, None)  # the e2e leg below uses the press on one stream
     ms = t0.elapsed_time(t1) / a.steps
     relation_ms = [e0.elapsed_time(e1) for pairs in ev for e0, e1 in pairs]
     ops.status(dev)

@@ -91,6 +91,7 @@ SIGNATURES = {
                                            _I, _P, _P, _S, _P]),
     "core_memory_readout_noalloc": (ctypes.c_int, [_D, _I, _P, _P, _P, _P, _P, _P, _I, _I, _F,
                                                    _P, _P, _P, _I, _P, _P]),
+    "core_set_sm_budget": (ctypes.c_int, [_I]),
     "core_split_bf16": (ctypes.c_int, [_P, ctypes.c_int64, _I, _P, _P]),
     "core_compress_layer_workspace_bytes": (_S, [_D, _I, _I]),
     "core_compress_layer": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P,

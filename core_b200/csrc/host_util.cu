@@ -10,6 +10,8 @@
 #include "common.cuh"
 #include "host_util.h"
 
+#include <atomic>
+
 namespace core {
 
 static thread_local std::string g_last_error;
@@ -43,6 +45,9 @@ DeviceStatus* device_status() {
   return g_status[dev];
 }
 
+// Process-wide cap on the SMs a launch plans for (0: all of them).
+static std::atomic<int> g_sm_budget{0};
+
 int sm_count() {
   static int cache[kMaxDevices] = {0};
   int dev = 0;
@@ -53,7 +58,8 @@ int sm_count() {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     cache[dev] = n > 0 ? n : 1;
   }
-  return cache[dev];
+  const int budget = g_sm_budget.load(std::memory_order_relaxed);
+  return (budget > 0 && budget < cache[dev]) ? budget : cache[dev];
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -180,4 +186,10 @@ extern "C" int core_split_bf16(const float* src, int64_t n, int32_t terms, void*
                                                          static_cast<__nv_bfloat16*>(dst));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CORE_OK : cuda_error(e, "core_split_bf16 launch");
+}
+
+extern "C" int core_set_sm_budget(int32_t n_sms) {
+  if (n_sms < 0) return set_error(CORE_ERR_INVALID_ARG, "core_set_sm_budget: negative SM count");
+  g_sm_budget.store(n_sms, std::memory_order_relaxed);
+  return CORE_OK;
 }

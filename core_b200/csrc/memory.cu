@@ -34,11 +34,14 @@ __device__ __forceinline__ void st_shared_zero16(uint32_t dst) {
 // ===========================================================================
 // softmax mass
 // ===========================================================================
+constexpr int kMassMaxSmem = 49152;  // exp terms of rows up to this length stay in shared memory
+
+template <bool kSmem>
 __global__ void __launch_bounds__(1024)
     mw_mass_kernel(const float* __restrict__ scores, int L, const int* __restrict__ evict,
-                   int n_evict, int n_ev_pad, float inv_tau_num, float tau, float gamma,
-                   float* __restrict__ Z, float* __restrict__ pbar, float* __restrict__ coef,
-                   DeviceStatus* status) {
+                   int n_evict, int n_ev_pad, float tau, float gamma, float* __restrict__ Z,
+                   float* __restrict__ pbar, float* __restrict__ coef, DeviceStatus* status) {
+  extern __shared__ float se[];  // x_i = s_i / tau, then exp(x_i - max)  (kSmem only)
   const int b = blockIdx.x;
   const float* s = scores + (long long)b * L;
   __shared__ float red[32];
@@ -46,10 +49,15 @@ __global__ void __launch_bounds__(1024)
   __shared__ float s_max, s_sum;
   __shared__ double s_pie;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  (void)inv_tau_num;
+  const bool unit_tau = tau == 1.0f;  // s / 1 is exact: skip the division
+  auto scaled = [&](int i) { return unit_tau ? s[i] : s[i] / tau; };
   float m = -INFINITY;
 #pragma unroll 8
-  for (int i = threadIdx.x; i < L; i += blockDim.x) m = fmaxf(m, s[i] / tau);
+  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+    const float x = scaled(i);
+    if constexpr (kSmem) se[i] = x;
+    m = fmaxf(m, x);
+  }
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) red[warp] = m;
   __syncthreads();
@@ -62,7 +70,16 @@ __global__ void __launch_bounds__(1024)
   const float mx = s_max;
   double sum = 0.0;
 #pragma unroll 8
-  for (int i = threadIdx.x; i < L; i += blockDim.x) sum += (double)expf(s[i] / tau - mx);
+  for (int i = threadIdx.x; i < L; i += blockDim.x) {
+    float e;
+    if constexpr (kSmem) {
+      e = expf(se[i] - mx);
+      se[i] = e;
+    } else {
+      e = expf(scaled(i) - mx);
+    }
+    sum += (double)e;
+  }
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (lane == 0) redd[warp] = sum;
   __syncthreads();
@@ -74,12 +91,17 @@ __global__ void __launch_bounds__(1024)
   __syncthreads();
   const float tot = s_sum;
   const int* ev = evict + (long long)b * n_evict;
+  auto ex = [&](int i) -> float {
+    if ((unsigned)i >= (unsigned)L) {  // evicted index outside the cache
+      record_error(status, CORE_ERR_INVALID_ARG, 802, i);
+      return 0.f;
+    }
+    if constexpr (kSmem) return se[i];
+    else return expf(scaled(i) - mx);
+  };
   double pe = 0.0;
 #pragma unroll 8
-  for (int k = threadIdx.x; k < n_evict; k += blockDim.x) {
-    const float p = expf(s[ev[k]] / tau - mx) / tot;
-    pe += (double)p;
-  }
+  for (int k = threadIdx.x; k < n_evict; k += blockDim.x) pe += (double)(ex(ev[k]) / tot);
   for (int o = 16; o > 0; o >>= 1) pe += __shfl_xor_sync(0xffffffffu, pe, o);
   if (lane == 0) redd[warp] = pe;
   __syncthreads();
@@ -95,7 +117,7 @@ __global__ void __launch_bounds__(1024)
 #pragma unroll 8
   for (int k = threadIdx.x; k < n_ev_pad; k += blockDim.x) {
     float v = 0.f;
-    if (k < n_evict) v = (expf(s[ev[k]] / tau - mx) / tot) / mass;
+    if (k < n_evict) v = (ex(ev[k]) / tot) / mass;
     pb[k] = v;
   }
   if (threadIdx.x == 0) {
@@ -586,8 +608,18 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
   DeviceStatus* st = device_status();
   cudaError_t e;
 
-  mw_mass_kernel<<<d->batch, 1024, 0, s>>>(scores_cal, d->seq_len, evict_idx, n_evict, m.n_ev_pad,
-                                           0.f, student_temp, gamma, Z, pbar, coef, st);
+  if (d->seq_len <= kMassMaxSmem) {
+    e = cudaFuncSetAttribute(mw_mass_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(float) * kMassMaxSmem));
+    if (e != cudaSuccess) return cuda_error(e, "mw_mass_kernel attribute");
+    mw_mass_kernel<true><<<d->batch, 1024, sizeof(float) * (size_t)d->seq_len, s>>>(
+        scores_cal, d->seq_len, evict_idx, n_evict, m.n_ev_pad, student_temp, gamma, Z, pbar, coef,
+        st);
+  } else {
+    mw_mass_kernel<false><<<d->batch, 1024, 0, s>>>(scores_cal, d->seq_len, evict_idx, n_evict,
+                                                   m.n_ev_pad, student_temp, gamma, Z, pbar, coef,
+                                                   st);
+  }
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_mass_kernel launch");
 
   CUtensorMap tmT;

@@ -7,14 +7,15 @@
 // re-sorted ascending.  Equivalently: keep the sinks, then the
 // (n_kept - n_sink) best non-sink tokens ordered by (score desc, index asc).
 //
-// One CTA per batch row: an MSB-first 8-bit radix select over order-preserving
-// uint32 keys of the scores finds the threshold key and how many of the tied
-// tokens at the threshold to keep (lowest indices first); histograms are
+// One CTA per batch row.  The row's order-preserving uint32 keys are staged
+// in shared memory (rows of up to 49152 tokens; longer rows recompute them
+// from the scores).  An MSB-first 8-bit radix select finds the threshold
+// prefix and how many of the tokens tied on it to keep (lowest indices
+// first), stopping early once a whole bin is kept; histograms are
 // warp-aggregated (__match_any_sync) and the digit is picked by one warp's
-// suffix scan.  Then every thread takes a contiguous run of tokens, one
-// block-wide scan of packed (ties, definite keeps) counts gives each run its
-// output offsets, and the kept and evicted indices are written in ascending
-// order.
+// suffix scan.  Compaction: each warp owns a contiguous chunk, ballots rank
+// the tokens inside the warp, one pass of per-warp counts gives the offsets,
+// and kept and evicted indices are written in ascending order.
 #include <cmath>
 
 #include "common.cuh"
@@ -32,54 +33,53 @@ __device__ __forceinline__ uint32_t order_key(float x) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Block-wide exclusive scan of one 64-bit value per thread.
-__device__ __forceinline__ unsigned long long block_exclusive_scan64(unsigned long long v,
-                                                                     unsigned long long* s_warp) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  unsigned long long x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned long long y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) s_warp[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    unsigned long long w = (lane < kWarps) ? s_warp[lane] : 0ull;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned long long y = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += y;
-    }
-    s_warp[lane] = w;  // inclusive warp prefix
-  }
-  __syncthreads();
-  return (warp > 0 ? s_warp[warp - 1] : 0ull) + x - v;
+constexpr int kMaxSmemKeys = 49152;  // 192 KB of keys in shared memory
+
+// Key of token i (i >= sinks): from shared memory when the row fits, else
+// recomputed from the scores.
+template <bool kSmem>
+__device__ __forceinline__ uint32_t key_at(const uint32_t* sk, const float* s, int i) {
+  if constexpr (kSmem) return sk[i];
+  else return order_key(s[i]);
 }
 
+template <bool kSmem>
 __global__ void __launch_bounds__(kThreads)
     topb_kernel(const float* __restrict__ scores, int L, int n_kept, int n_sink,
                 int* __restrict__ keep_idx, int* __restrict__ evict_idx, DeviceStatus* status) {
+  extern __shared__ uint32_t sk[];  // order keys of the row (kSmem only)
   const int b = blockIdx.x;
   const float* s = scores + (long long)b * L;
   const int sinks = (n_sink > 0 && n_sink < L) ? n_sink : 0;
   const int need = n_kept - sinks;  // non-sink tokens to keep (>= 0)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __shared__ int hist[256];
-  __shared__ unsigned long long s_warp[32];
+  __shared__ int s_cnt[kWarps][2];
   __shared__ uint32_t s_prefix, s_mask;
-  __shared__ int s_need, s_bad;
+  __shared__ int s_need, s_bad, s_done;
 
   if (threadIdx.x == 0) {
     s_prefix = 0;
     s_mask = 0;
     s_need = need;
     s_bad = 0;
+    s_done = need <= 0;
+  }
+  bool bad = false;
+  if constexpr (kSmem) {
+#pragma unroll 4
+    for (int i = threadIdx.x; i < L; i += kThreads) {
+      const float x = s[i];
+      bad |= (i >= sinks) && isnan(x);
+      sk[i] = order_key(x);
+    }
   }
   __syncthreads();
-  // ---- radix select: find key T such that #(key > T) < need <= #(key >= T) ----
-  bool bad = false;
-  for (int shift = 24; shift >= 0 && need > 0; shift -= 8) {
+  // ---- radix select over 8-bit digits, MSB first.  Invariant: the tokens with
+  // (key & mask) > prefix are all kept and number need - s_need; s_need of the
+  // tokens with (key & mask) == prefix are kept, lowest index first. ----
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    if (s_done) break;  // uniform: read after a barrier
     for (int i = threadIdx.x; i < 256; i += kThreads) hist[i] = 0;
     __syncthreads();
     const uint32_t prefix = s_prefix, mask = s_mask;
@@ -88,9 +88,14 @@ __global__ void __launch_bounds__(kThreads)
       const int i = i0 + threadIdx.x;
       int bin = -1;
       if (i < L) {
-        const float x = s[i];
-        bad |= isnan(x);
-        const uint32_t k = order_key(x);
+        uint32_t k;
+        if constexpr (kSmem) {
+          k = sk[i];
+        } else {
+          const float x = s[i];
+          bad |= isnan(x);
+          k = order_key(x);
+        }
         if ((k & mask) == prefix) bin = (int)((k >> shift) & 255u);
       }
       const unsigned grp = __match_any_sync(0xffffffffu, bin);
@@ -120,6 +125,7 @@ __global__ void __launch_bounds__(kThreads)
         s_prefix = prefix | ((uint32_t)d << shift);
         s_mask = mask | (255u << shift);
         s_need = rem;
+        if (rem == hist[d]) s_done = 1;  // the whole bin is kept: no tie to break
       }
     }
     __syncthreads();
@@ -127,47 +133,62 @@ __global__ void __launch_bounds__(kThreads)
   if (bad) s_bad = 1;
   __syncthreads();
   if (s_bad && threadIdx.x == 0) record_error(status, CORE_ERR_NONFINITE, 701, b);
-  const uint32_t T = s_prefix;
-  const int ties_keep = s_need;  // tokens equal to T to keep, lowest index first
-  // ---- ascending compaction over contiguous runs ----
-  const int per = (L + kThreads - 1) / kThreads;
-  const int r0 = min(L, threadIdx.x * per), r1 = min(L, r0 + per);
-  int n_def = 0, n_tie = 0;
-  for (int i = r0; i < r1; ++i) {
+  const uint32_t T = s_prefix, TM = s_mask;
+  const int ties_keep = s_need;
+  // ---- ascending compaction: warp w owns a contiguous chunk; ballots give
+  // in-warp ranks, one pass of counts gives the warps' offsets ----
+  auto classify = [&](int i, bool& def, bool& tie) {
+    def = false;
+    tie = false;
     if (i < sinks) {
-      ++n_def;
+      def = true;
     } else if (need > 0) {
-      const uint32_t k = order_key(s[i]);
-      n_def += (k > T);
-      n_tie += (k == T);
+      const uint32_t km = key_at<kSmem>(sk, s, i) & TM;
+      def = km > T;
+      tie = km == T;
     }
+  };
+  const int chunk = ((L + kThreads - 1) / kThreads) * 32;
+  const int c0 = min(L, warp * chunk), c1 = min(L, c0 + chunk);
+  int ndef = 0, ntie = 0;
+  for (int i0 = c0; i0 < c1; i0 += 32) {
+    const int i = i0 + lane;
+    bool def = false, tie = false;
+    if (i < c1) classify(i, def, tie);
+    ndef += __popc(__ballot_sync(0xffffffffu, def));
+    ntie += __popc(__ballot_sync(0xffffffffu, tie));
   }
-  const unsigned long long pre =
-      block_exclusive_scan64(((unsigned long long)n_tie << 32) | (unsigned)n_def, s_warp);
-  int tie_before = (int)(pre >> 32);
-  int kept_before = (int)(pre & 0xFFFFFFFFull) + min(tie_before, ties_keep);
+  if (lane == 0) {
+    s_cnt[warp][0] = ndef;
+    s_cnt[warp][1] = ntie;
+  }
+  __syncthreads();
+  const int def_before = __reduce_add_sync(0xffffffffu, lane < warp ? s_cnt[lane][0] : 0);
+  int tb = __reduce_add_sync(0xffffffffu, lane < warp ? s_cnt[lane][1] : 0);
+  int kept = def_before + min(tb, ties_keep);
+  const unsigned lt = (1u << lane) - 1u;
   int* kout = keep_idx + (long long)b * n_kept;
   int* eout = evict_idx + (long long)b * (L - n_kept);
-  for (int i = r0; i < r1; ++i) {
-    bool keep;
-    if (i < sinks) {
-      keep = true;
-    } else if (need > 0) {
-      const uint32_t k = order_key(s[i]);
-      keep = k > T;
-      if (k == T) keep = tie_before++ < ties_keep;
-    } else {
-      keep = false;
+  for (int i0 = c0; i0 < c1; i0 += 32) {
+    const int i = i0 + lane;
+    bool def = false, tie = false;
+    if (i < c1) classify(i, def, tie);
+    const unsigned tmask = __ballot_sync(0xffffffffu, tie);
+    const bool keep = def || (tie && tb + __popc(tmask & lt) < ties_keep);
+    const unsigned kmask = __ballot_sync(0xffffffffu, keep);
+    const int kpos = kept + __popc(kmask & lt);
+    if (i < c1) {
+      if (keep) {
+        if (kpos < n_kept) kout[kpos] = i;
+      } else {
+        const int epos = i - kpos;  // evicted tokens before i
+        if (epos < L - n_kept) eout[epos] = i;
+      }
     }
-    if (keep) {
-      if (kept_before < n_kept) kout[kept_before] = i;
-      ++kept_before;
-    } else {
-      const int epos = i - kept_before;  // evicted tokens before i
-      if (epos < L - n_kept) eout[epos] = i;
-    }
+    kept += __popc(kmask);
+    tb += __popc(tmask);
   }
-  if (threadIdx.x == kThreads - 1 && kept_before != n_kept)
+  if (warp == kWarps - 1 && lane == 0 && kept != n_kept)
     record_error(status, CORE_ERR_INVALID_ARG, 702, b);
 }
 
@@ -195,8 +216,18 @@ extern "C" int core_topb_select(const float* scores, int32_t batch, int32_t seq_
   if (n_kept < sinks)
     return set_error(CORE_ERR_INVALID_ARG, "core_topb_select: n_kept smaller than the sink count");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  topb::topb_kernel<<<batch, topb::kThreads, 0, s>>>(scores, seq_len, n_kept, n_sink, keep_idx,
-                                                    evict_idx, device_status());
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e;
+  if (seq_len <= topb::kMaxSmemKeys) {
+    const size_t smem = sizeof(uint32_t) * (size_t)seq_len;
+    e = cudaFuncSetAttribute(topb::topb_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(uint32_t) * topb::kMaxSmemKeys));
+    if (e != cudaSuccess) return cuda_error(e, "topb_kernel attribute");
+    topb::topb_kernel<true><<<batch, topb::kThreads, smem, s>>>(scores, seq_len, n_kept, n_sink,
+                                                              keep_idx, evict_idx, device_status());
+  } else {
+    topb::topb_kernel<false><<<batch, topb::kThreads, 0, s>>>(scores, seq_len, n_kept, n_sink,
+                                                            keep_idx, evict_idx, device_status());
+  }
+  e = cudaGetLastError();
   return e == cudaSuccess ? CORE_OK : cuda_error(e, "topb_kernel launch");
 }

@@ -147,3 +147,50 @@ def compress_layer(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
         return dict(keys=keys, values=values, keep=None, evict=None, scores=scores, features=feats)
     return dict(keys=ok, values=ov, keep=keep, evict=evict[:, :n_ev], scores=scores,
                 features=feats)
+
+
+def compress_layers(jobs, *, n_streams: int = 2, workspaces=None, **kwargs) -> list:
+    """Compress independent layers concurrently on ``n_streams`` side streams.
+
+    ``jobs`` is a list of dicts with the per-layer arguments of
+    :func:`compress_layer` (``q``, ``keys``, ``values``, ``weights``,
+    ``positions`` and optionally ``memory``, ``timing_events``, ``special``,
+    ``lse``); ``kwargs`` are shared by all layers.  Layer i runs on side stream
+    i mod n_streams; the side streams start after the work already queued on
+    the current stream and the current stream waits for all of them before
+    returning.  ``workspaces``: optional list of n_streams device buffers, one
+    per side stream.  Pair it with :func:`core_b200.ops.sm_budget` so that the
+    persistent grids of one layer leave SMs for the small kernels of another.
+    """
+    if not jobs:
+        return []
+    dev = jobs[0]["keys"].device
+    main = torch.cuda.current_stream(dev)
+    streams = _side_streams(dev, n_streams)
+    fork = torch.cuda.Event()
+    fork.record(main)
+    for s in streams:
+        s.wait_event(fork)
+    out = [None] * len(jobs)
+    for i, job in enumerate(jobs):
+        s = streams[i % n_streams]
+        for t in (job["q"], job["keys"], job["values"], job["positions"]):
+            t.record_stream(s)
+        with torch.cuda.stream(s):
+            ws = None if workspaces is None else workspaces[i % n_streams]
+            out[i] = compress_layer(**job, **kwargs, workspace=ws)
+    for s in streams:
+        done = torch.cuda.Event()
+        done.record(s)
+        main.wait_event(done)
+    return out
+
+
+_SIDE_STREAMS: dict = {}
+
+
+def _side_streams(dev: torch.device, n: int) -> list:
+    key = (dev.index, n)
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = [torch.cuda.Stream(dev) for _ in range(n)]
+    return _SIDE_STREAMS[key]

@@ -48,6 +48,21 @@ def status(device=None) -> None:
     check(_lib.load().core_check_device_status(_stream(device)))
 
 
+class sm_budget:
+    """Context manager (and plain call) capping the SMs the persistent grids
+    plan for, process-wide; ``sm_budget(0)`` restores all SMs."""
+
+    def __init__(self, n_sms: int):
+        self.n = int(n_sms)
+        check(_lib.load().core_set_sm_budget(self.n))
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        check(_lib.load().core_set_sm_budget(0))
+
+
 # ---------------------------------------------------------------------------
 def qk_features(q: torch.Tensor, k: torch.Tensor, *, topk_qk: int = 4,
                 n_recent_queries: int = 16, lse: torch.Tensor | None = None,

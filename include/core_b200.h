@@ -58,6 +58,12 @@ typedef struct core_dims {
 /* Library version (major*10000 + minor*100 + patch). */
 int core_version(void);
 
+/* Caps the number of SMs the persistent grids plan for (0: all SMs), so that
+ * kernels of another stream can run beside them; process-wide, read when a
+ * call plans its launch (workspace sizes depend on it: query them under the
+ * same budget).  A scheduling setting with no counterpart in the reference. */
+int core_set_sm_budget(int32_t n_sms);
+
 /* Copies the last error message of the calling host thread into buf. */
 int core_last_error(char* buf, size_t buf_len);
 

@@ -135,7 +135,8 @@ def test_indexer_scores_match_oracle(name):
 
 
 @pytest.mark.parametrize("L,n_kept,n_sink", [(5, 4, 4), (96, 48, 4), (333, 133, 4), (4096, 1024, 4),
-                                             (16384, 4096, 4), (1000, 1000, 4), (300, 4, 4)])
+                                             (16384, 4096, 4), (1000, 1000, 4), (300, 4, 4),
+                                             (65536, 16384, 4), (2049, 700, 0)])
 def test_topb_matches_stable_argsort(L, n_kept, n_sink):
     from core_b200 import ops
     dev = _dev()
@@ -151,6 +152,17 @@ def test_topb_matches_stable_argsort(L, n_kept, n_sink):
         assert np.array_equal(keep[b].cpu().numpy(), ref)
         ev = np.setdiff1d(np.arange(L), ref)
         assert np.array_equal(evict[b].cpu().numpy(), ev)
+
+
+@pytest.mark.parametrize("L,n_kept", [(4096, 1000), (70000, 5000)])
+def test_topb_all_equal_scores_keep_lowest_indices(L, n_kept):
+    from core_b200 import ops
+    dev = _dev()
+    s = np.full((1, L), 0.25, np.float32)
+    keep, evict = ops.topb_select(_f32(s, dev), n_kept, 4)
+    ops.status()
+    assert np.array_equal(keep[0].cpu().numpy(), np.arange(n_kept))
+    assert np.array_equal(evict[0].cpu().numpy(), np.arange(n_kept, L))
 
 
 @pytest.mark.parametrize("name", BF16_CASES + [TWO_STEP_CASE])
@@ -251,3 +263,36 @@ def test_compress_layer_keep_set_matches_reference(name):
     near = np.abs(s - boundary) <= 1e-3 * abs(boundary)
     diff = np.setxor1d(keep, gk)
     assert np.all(near[diff]), (diff, s[diff], boundary)
+
+
+def test_compress_layers_concurrent_equals_sequential():
+    """Layers on two streams with an SM budget give the same results as one
+    layer after another under the same budget."""
+    from core_b200 import engine, ops, synthetic
+    dev = _dev()
+    L, nq, hkv, hq = 2048, 64, 8, 32
+    jobs_a, jobs_b = [], []
+    for l in range(4):
+        q, k, v = synthetic.make_layer_inputs(seed=100 + l, batch=1, n_kv_heads=hkv, n_q_heads=hq,
+                                              seq_len=L, n_queries=nq, device=dev)
+        w = synthetic.make_layer_weights(seed=200 + l, n_kv_heads=hkv, n_q_heads=hq, d_mem=128)
+        lw = engine.LayerWeights.prepare(geometry=w["geometry"], prototypes=w["prototypes"],
+                                         hadamard=w["hadamard"], mlp_params=w["mlp"],
+                                         theta=w["theta"], n_kv_heads=hkv, n_q_heads=hq, device=dev)
+        pos = torch.arange(L, device=dev)[None]
+        for jobs in (jobs_a, jobs_b):
+            jobs.append(dict(q=q, keys=k, values=v, weights=lw, positions=pos,
+                             memory=engine.MemoryState.zeros(1, 128, hkv * 128, dev)))
+    n_kept = engine.n_kept_for(L, 0.75, 4)
+    with ops.sm_budget(torch.cuda.get_device_properties(dev).multi_processor_count - 2):
+        seq = [engine.compress_layer(**j, n_kept=n_kept, original_length=L, is_prefill=True)
+               for j in jobs_a]
+        par = engine.compress_layers(jobs_b, n_streams=2, n_kept=n_kept, original_length=L,
+                                     is_prefill=True)
+        torch.cuda.synchronize()
+    ops.status()
+    for a, b, ja, jb in zip(seq, par, jobs_a, jobs_b):
+        assert torch.equal(a["keep"], b["keep"])
+        assert torch.equal(a["scores"], b["scores"])
+        assert torch.equal(a["keys"], b["keys"]) and torch.equal(a["values"], b["values"])
+        assert torch.equal(ja["memory"].M, jb["memory"].M)
