@@ -2,14 +2,19 @@
 // the feature concatenation at core/kvpress_adapter.py:536 and
 // COREIndexerMLP, core/indexer.py:88-108).
 //
-// Four threads per cached token, persistent blocks.  The auxiliary features
-// follow the reference's dtype: for bf16 caches a_value is computed with the
-// same bf16 roundings as the reference's torch ops (squares, per-head sums,
-// the head mean, /d and log1p each round to bf16).  The MLP runs in f32 with
-// its weights staged once per block into shared memory (cp.async) and read as
-// broadcasts: hidden unit k of layer 1 is computed, GELU'd, and immediately
-// accumulated into the 128 layer-2 outputs held in registers, a quarter per
-// thread (an outer-product form, so layer-2 sums run over k in ascending order).
+// Persistent CTAs of 256 threads over tiles of 128 cached tokens; thread
+// (token t = tid % 128, half = tid / 128).
+//   1. auxiliary features: a_value from V with the reference's bf16 roundings
+//      (squares, per-head sums, the head mean, /d and log1p each round to
+//      bf16; heads split over the two halves and summed in head order),
+//      a_age, a_sink, a_phase;
+//   2. layer 1 (14 -> 128, f32 FMAs, exact erf GELU): each half computes 64
+//      hidden units and stores them as three bf16 terms (hi + mid + lo = the
+//      f32 value) in the SW128 K-major layout of a tcgen05 A operand;
+//   3. layer 2 (128 -> 128) on tcgen05: A = hidden terms, B = the three bf16
+//      terms of W2 (built once per CTA), the six products whose term orders
+//      sum to at most 2 accumulated in f32 in TMEM — f32-level accuracy;
+//   4. epilogue: TMEM -> registers, + b2, GELU, dot with w3, + b3.
 #include <cmath>
 
 #include "common.cuh"
@@ -20,26 +25,71 @@ namespace idx {
 
 constexpr int kIn = 14;
 constexpr int kHid = 128;
-constexpr int kThreads = 256;  // 64 tokens x 4 threads
+constexpr int kTile = 128;     // tokens per tile (MMA M)
+constexpr int kThreads = 256;  // 128 tokens x 2 halves
+constexpr int kMaxHkv = 16;
 // packed global layout (floats): [w1 (128,14) | b1 | w2^T (in 128, out 128) | b2 | w3 | b3]
 constexpr int kGW1 = 0;
-constexpr int kGB1 = kGW1 + kHid * kIn;    // 1792
-constexpr int kGW2T = kGB1 + kHid;         // 1920 (16-byte aligned)
-constexpr int kGB3 = kGW2T + kHid * kHid + 2 * kHid;
-// shared layout (floats): w1 rows padded to 16 | b1 | w2^T | b2 | w3 | b3
+constexpr int kGB1 = kGW1 + kHid * kIn;
+constexpr int kGW2T = kGB1 + kHid;
+constexpr int kGB2 = kGW2T + kHid * kHid;
+constexpr int kGW3 = kGB2 + kHid;
+constexpr int kGB3 = kGW3 + kHid;
+// shared memory, from a 1024-byte aligned base
+constexpr uint32_t kTermBytes = kTile * kHid * 2;  // one bf16 term: two K atoms of 16 KB
+constexpr uint32_t kOffW = 0;                      // W2 terms (out, in), B operand
+constexpr uint32_t kOffH = 3 * kTermBytes;         // hidden terms (token, hidden), A operand
+constexpr uint32_t kOffF = 6 * kTermBytes;         // f32 block below
 constexpr int kW1Stride = 16;
-constexpr int kOffW1 = 0;
-constexpr int kOffB1 = kOffW1 + kHid * kW1Stride;  // 2048
-constexpr int kOffW2T = kOffB1 + kHid;             // 2176 (16-byte aligned)
-constexpr int kOffB2 = kOffW2T + kHid * kHid;
-constexpr int kOffW3 = kOffB2 + kHid;
-constexpr int kOffB3 = kOffW3 + kHid;
-constexpr int kSmemFloats = kOffB3 + 4;
-constexpr int kMaxHkv = 16;
-static_assert(kGW2T % 4 == 0 && kOffW2T % 4 == 0, "cp.async chunks need 16-byte alignment");
+constexpr int kFW1 = 0;                            // [128][16]
+constexpr int kFB1 = kFW1 + kHid * kW1Stride;
+constexpr int kFB2 = kFB1 + kHid;
+constexpr int kFW3 = kFB2 + kHid;
+constexpr int kFB3 = kFW3 + kHid;                  // 4 floats
+constexpr int kFHs = kFB3 + 4;                     // per-head value energies [128][kMaxHkv]
+constexpr int kFPart = kFHs + kTile * kMaxHkv;     // half-1 partial scores [128]
+constexpr int kFFloats = kFPart + kTile;
+constexpr uint32_t kOffBar = kOffF + 4u * kFFloats;
+constexpr uint32_t kSmemBytes = kOffBar + 64 + 1024;  // + barrier, TMEM slot, alignment slack
+static_assert(kSmemBytes <= 227u * 1024u, "shared memory budget");
 
 __device__ __forceinline__ float gelu(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+// Byte offset of 16-byte chunk `chunk` (k / 8 inside the atom) of row `row`
+// of a 128-row K-major SW128 operand tile made of two 64-element K atoms.
+__device__ __forceinline__ uint32_t sw128_chunk(int row, int atom, int chunk) {
+  return (uint32_t)atom * 16384u + (uint32_t)row * 128u + (uint32_t)((chunk ^ (row & 7)) << 4);
+}
+
+// Split 8 f32 values into three bf16 terms (x = t0 + t1 + t2 to f32 precision)
+// packed as three uint4 of 8 bf16 each.
+__device__ __forceinline__ void split3(const float (&x)[8], uint4& t0, uint4& t1, uint4& t2) {
+  uint32_t w0[4], w1[4], w2[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float a = x[2 * i], b = x[2 * i + 1];
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    w0[i] = *reinterpret_cast<uint32_t*>(&h);
+    a -= __uint_as_float(w0[i] << 16);
+    b -= __uint_as_float(w0[i] & 0xFFFF0000u);
+    h = __floats2bfloat162_rn(a, b);
+    w1[i] = *reinterpret_cast<uint32_t*>(&h);
+    a -= __uint_as_float(w1[i] << 16);
+    b -= __uint_as_float(w1[i] & 0xFFFF0000u);
+    h = __floats2bfloat162_rn(a, b);
+    w2[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  t0 = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+  t1 = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+  t2 = make_uint4(w2[0], w2[1], w2[2], w2[3]);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, const uint4& v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 struct Params {
@@ -53,48 +103,68 @@ struct Params {
   DeviceStatus* status;
 };
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     indexer_scores_kernel(const Params p) {
-  extern __shared__ __align__(16) float sm[];
-  // w2^T | b2 | w3 are contiguous in both layouts: one asynchronous copy
-  cp_async_block(sm + kOffW2T, p.mlp + kGW2T, (kHid * kHid + 2 * kHid) / 4);
-  {
-    static_assert(kHid * kIn % kThreads == 0 && kHid <= kThreads, "staging layout");
-    float r[kHid * kIn / kThreads + 1];
-#pragma unroll
-    for (int j = 0; j < kHid * kIn / kThreads; ++j) r[j] = p.mlp[kGW1 + threadIdx.x + j * kThreads];
-    if (threadIdx.x < kHid) r[kHid * kIn / kThreads] = p.mlp[kGB1 + threadIdx.x];
-#pragma unroll
-    for (int j = 0; j < kHid * kIn / kThreads; ++j) {
-      const int i = threadIdx.x + j * kThreads;
-      sm[kOffW1 + (i / kIn) * kW1Stride + (i % kIn)] = r[j];
-    }
-    if (threadIdx.x < kHid) sm[kOffB1 + threadIdx.x] = r[kHid * kIn / kThreads];
-    if (threadIdx.x == 0) sm[kOffB3] = p.mlp[kGB3];
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
+  float* sf = reinterpret_cast<float*>(sgen + kOffF);
+  const uint32_t bar = sbase + kOffBar;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + kOffBar + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + kOffBar + 24);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int t = tid & (kTile - 1);  // token row of the tile == TMEM lane
+  const int half = tid >> 7;
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
   }
-  cp_async_wait_all();
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 128);
+    tmem_relinquish();
+  }
+  // ---- once per CTA: W2 as three bf16 terms, (out, in) K-major SW128 ----
+  // unit u: output row o = u % 128, 8-column chunk c = u / 128 (coalesced reads of w2^T)
+  for (int u = tid; u < kHid * (kHid / 8); u += kThreads) {
+    const int o = u & (kHid - 1), c = u >> 7;
+    float x[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = p.mlp[kGW2T + (8 * c + i) * kHid + o];
+    uint4 t0, t1, t2;
+    split3(x, t0, t1, t2);
+    const uint32_t off = sw128_chunk(o, c >> 3, c & 7);
+    st_shared_v4(sbase + kOffW + off, t0);
+    st_shared_v4(sbase + kOffW + kTermBytes + off, t1);
+    st_shared_v4(sbase + kOffW + 2 * kTermBytes + off, t2);
+  }
+  for (int i = tid; i < kHid * kIn; i += kThreads)
+    sf[kFW1 + (i / kIn) * kW1Stride + (i % kIn)] = p.mlp[kGW1 + i];
+  for (int i = tid; i < kHid; i += kThreads) {
+    sf[kFB1 + i] = p.mlp[kGB1 + i];
+    sf[kFB2 + i] = p.mlp[kGB2 + i];
+    sf[kFW3 + i] = p.mlp[kGW3 + i];
+  }
+  if (tid == 0) sf[kFB3] = p.mlp[kGB3];
+  fence_proxy_async_shared();
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
   const long long n = (long long)p.B * p.L;
+  const long long n_tiles = (n + kTile - 1) / kTile;
   const float age_den = log1pf((float)(p.original_length - 1 > 1 ? p.original_length - 1 : 1));
-  const int part = threadIdx.x & 3;       // this thread's quarter of the token's work
-  const int lane = threadIdx.x & 31;
-  const int qbase = lane & ~3;            // lane of part 0 of this token
-  for (long long gi = ((long long)blockIdx.x * kThreads + threadIdx.x) >> 2; ;
-       gi += (long long)gridDim.x * (kThreads / 4)) {
-    const long long g0 = gi - (threadIdx.x >> 2);  // first token of this block's group
-    if (g0 >= n) break;
+  int iter = 0;
+  for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++iter) {
+    const long long gi = tile * kTile + t;
     const bool active = gi < n;
-    float x[kIn];
-    // ---- a_value: heads part, part + 4, ... summed here, combined in head order ----
-    float hs[kMaxHkv / 4];
     const int b = active ? (int)(gi / p.L) : 0;
     const int i = active ? (int)(gi % p.L) : 0;
-#pragma unroll
-    for (int r = 0; r < kMaxHkv / 4; ++r) {
-      hs[r] = 0.f;
-      const int h = 4 * r + part;
-      if (active && h < p.Hkv) {
+    // ---- 1. auxiliary features (features.py:886-921) ----
+    if (active) {
+      for (int h = half; h < p.Hkv; h += 2) {
         const uint4* row =
             reinterpret_cast<const uint4*>(p.v + (((long long)b * p.Hkv + h) * p.L + i) * 128);
         float s = 0.f;
@@ -104,28 +174,22 @@ __global__ void __launch_bounds__(kThreads, 2)
           const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 t = __bfloat1622float2(h2[e]);
-            s += bf16_round(t.x * t.x);
-            s += bf16_round(t.y * t.y);
+            const float2 f2 = __bfloat1622float2(h2[e]);
+            s += bf16_round(f2.x * f2.x);
+            s += bf16_round(f2.y * f2.y);
           }
         }
-        hs[r] = bf16_round(s);
+        sf[kFHs + t * kMaxHkv + h] = bf16_round(s);
       }
     }
-    float hsum = 0.f;
-#pragma unroll
-    for (int r = 0; r < kMaxHkv / 4; ++r) {
-#pragma unroll
-      for (int pp = 0; pp < 4; ++pp) {
-        const float t = __shfl_sync(0xffffffffu, hs[r], qbase | pp);
-        if (4 * r + pp < p.Hkv) hsum += t;
-      }
-    }
+    __syncthreads();
+    float x[kIn];
     if (active) {
-      // ---- auxiliary features (features.py:886-921) ----
+      float hsum = 0.f;
+      for (int h = 0; h < p.Hkv; ++h) hsum += sf[kFHs + t * kMaxHkv + h];
       const long long pos = p.positions[gi];
       const int T = p.original_length;
-      if (part == 0 && (pos < 0 || pos >= T)) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
+      if (half == 0 && (pos < 0 || pos >= T)) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
       const float a_age = log1pf((float)(T - 1 - pos)) / age_den;
       bool sink = pos < p.n_sink;
       if (p.special != nullptr && p.special[gi]) sink = true;
@@ -138,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       x[11] = sink ? 1.0f : 0.0f;
       x[12] = a_value;
       x[13] = p.is_prefill ? 0.0f : 1.0f;
-      if (part == 0) {
+      if (half == 0) {
 #pragma unroll
         for (int k = 10; k < kIn; ++k) f[k] = x[k];
         bool finite = true;
@@ -150,59 +214,86 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int k = 0; k < kIn; ++k) x[k] = 0.f;
     }
-    // ---- MLP.  Hidden unit k = 4 j + pp is computed by part pp and shared by
-    // shuffle; this thread accumulates outputs o = 16 c + 4 part + e (c < 8,
-    // e < 4) over k in ascending order. ----
-    float acc[kHid / 4];
-#pragma unroll
-    for (int o = 0; o < kHid / 4; ++o) acc[o] = 0.f;
+    // ---- 2. layer 1: hidden units [64 half, 64 half + 64) as three bf16 terms ----
 #pragma unroll 1
-    for (int j = 0; j < kHid / 4; ++j) {
-      const int kown = 4 * j + part;
-      const float4* w1 = reinterpret_cast<const float4*>(sm + kOffW1 + kown * kW1Stride);
-      const float4 a0 = w1[0], a1 = w1[1], a2 = w1[2], a3 = w1[3];
-      float t = 0.f;
-      t = fmaf(a0.x, x[0], t);
-      t = fmaf(a0.y, x[1], t);
-      t = fmaf(a0.z, x[2], t);
-      t = fmaf(a0.w, x[3], t);
-      t = fmaf(a1.x, x[4], t);
-      t = fmaf(a1.y, x[5], t);
-      t = fmaf(a1.z, x[6], t);
-      t = fmaf(a1.w, x[7], t);
-      t = fmaf(a2.x, x[8], t);
-      t = fmaf(a2.y, x[9], t);
-      t = fmaf(a2.z, x[10], t);
-      t = fmaf(a2.w, x[11], t);
-      t = fmaf(a3.x, x[12], t);
-      t = fmaf(a3.y, x[13], t);
-      const float hown = gelu(t + sm[kOffB1 + kown]);
+    for (int c = 0; c < 8; ++c) {
+      float hv[8];
 #pragma unroll
-      for (int pp = 0; pp < 4; ++pp) {
-        const float hk = __shfl_sync(0xffffffffu, hown, qbase | pp);
-        const float4* w2 = reinterpret_cast<const float4*>(sm + kOffW2T + (4 * j + pp) * kHid) + part;
+      for (int e = 0; e < 8; ++e) {
+        const int k = 64 * half + 8 * c + e;
+        const float4* w1 = reinterpret_cast<const float4*>(sf + kFW1 + k * kW1Stride);
+        const float4 a0 = w1[0], a1 = w1[1], a2 = w1[2], a3 = w1[3];
+        float acc = 0.f;
+        acc = fmaf(a0.x, x[0], acc);
+        acc = fmaf(a0.y, x[1], acc);
+        acc = fmaf(a0.z, x[2], acc);
+        acc = fmaf(a0.w, x[3], acc);
+        acc = fmaf(a1.x, x[4], acc);
+        acc = fmaf(a1.y, x[5], acc);
+        acc = fmaf(a1.z, x[6], acc);
+        acc = fmaf(a1.w, x[7], acc);
+        acc = fmaf(a2.x, x[8], acc);
+        acc = fmaf(a2.y, x[9], acc);
+        acc = fmaf(a2.z, x[10], acc);
+        acc = fmaf(a2.w, x[11], acc);
+        acc = fmaf(a3.x, x[12], acc);
+        acc = fmaf(a3.y, x[13], acc);
+        hv[e] = gelu(acc + sf[kFB1 + k]);
+      }
+      uint4 t0, t1, t2;
+      split3(hv, t0, t1, t2);
+      const uint32_t off = sw128_chunk(t, half, c);
+      st_shared_v4(sbase + kOffH + off, t0);
+      st_shared_v4(sbase + kOffH + kTermBytes + off, t1);
+      st_shared_v4(sbase + kOffH + 2 * kTermBytes + off, t2);
+    }
+    fence_proxy_async_shared();
+    tc_fence_before();
+    __syncthreads();
+    // ---- 3. layer 2 on tcgen05: sum of hidden-term x weight-term products of order <= 2 ----
+    if (tid == 0) {
+      tc_fence_after();
+      constexpr uint32_t idesc = idesc_bf16(kTile, kHid, 0, 0);
+      constexpr int kTa[6] = {2, 1, 0, 1, 0, 0};  // small products first
+      constexpr int kTb[6] = {0, 1, 2, 0, 1, 0};
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float4 w = w2[4 * c];
-          acc[4 * c] = fmaf(w.x, hk, acc[4 * c]);
-          acc[4 * c + 1] = fmaf(w.y, hk, acc[4 * c + 1]);
-          acc[4 * c + 2] = fmaf(w.z, hk, acc[4 * c + 2]);
-          acc[4 * c + 3] = fmaf(w.w, hk, acc[4 * c + 3]);
+      for (int pi = 0; pi < 6; ++pi) {
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t koff = (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u;
+          const uint64_t a = sdesc_kmajor(sbase + kOffH + (uint32_t)kTa[pi] * kTermBytes + koff);
+          const uint64_t bd = sdesc_kmajor(sbase + kOffW + (uint32_t)kTb[pi] * kTermBytes + koff);
+          mma_bf16(tmem, a, bd, idesc, (pi > 0 || ks > 0) ? 1u : 0u);
         }
       }
+      mma_commit(bar);
     }
-    float out = 0.f;
+    bool ok = bounded_wait(bar, (uint32_t)(iter & 1), abort_flag, p.status, 610);
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    tc_fence_after();
+    // ---- 4. epilogue: outputs [64 half, 64 half + 64) of token t ----
+    float part = 0.f;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int q = 0; q < 2; ++q) {
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(64 * half + 32 * q), v);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int o = 16 * c + 4 * part + e;
-        out = fmaf(sm[kOffW3 + o], gelu(acc[4 * c + e] + sm[kOffB2 + o]), out);
+      for (int j = 0; j < 32; ++j) {
+        const int o = 64 * half + 32 * q + j;
+        part = fmaf(sf[kFW3 + o], gelu(v[j] + sf[kFB2 + o]), part);
       }
     }
-    out += __shfl_xor_sync(0xffffffffu, out, 1);
-    out += __shfl_xor_sync(0xffffffffu, out, 2);
-    if (active && part == 0) p.scores[gi] = out + sm[kOffB3];
+    if (half == 1) sf[kFPart + t] = part;
+    tc_fence_before();
+    __syncthreads();
+    if (half == 0 && active) p.scores[gi] = (part + sf[kFPart + t]) + sf[kFB3];
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
   }
 }
 
@@ -242,13 +333,12 @@ extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const in
   p.scores = scores;
   p.status = device_status();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t smem = sizeof(float) * kSmemFloats;
+  const size_t smem = kSmemBytes;
   cudaError_t e =
       cudaFuncSetAttribute(indexer_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_error(e, "indexer_scores_kernel attribute");
-  const long long n = (long long)p.B * p.L;
-  long long blocks = (n + kThreads / 4 - 1) / (kThreads / 4);
-  if (blocks > 2LL * sm_count()) blocks = 2LL * sm_count();
+  const long long n_tiles = ((long long)p.B * p.L + kTile - 1) / kTile;
+  const long long blocks = n_tiles < sm_count() ? n_tiles : sm_count();
   indexer_scores_kernel<<<(unsigned)blocks, kThreads, smem, s>>>(p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "indexer_scores_kernel launch");
   return CORE_OK;

@@ -204,6 +204,15 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
       const int dh = (int)(u % p.n_dh);
       const long long rest = u / p.n_dh;
       const int et = (int)(rest % p.n_et), b = (int)(rest / p.n_et);
+      // the unit's 128 token rows are the same for all its K chunks: load their
+      // indices once (8 rows per thread: r = tid / 8 + 16 i)
+      constexpr int kPer = kTok * 8 / kProdThreads;
+      int toks[kPer];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int kidx = et * kTok + ((tid + i * kProdThreads) >> 3);
+        toks[i] = kidx < p.n_evict ? p.evict[(long long)b * p.n_evict + kidx] : -1;
+      }
       for (int c = 0; c < n_chunks && ok; ++c, ++it) {
         const int st = it % kPhiStages;
         if (it >= kPhiStages) {
@@ -218,16 +227,15 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
         }
         const int h = c >> 1, e0 = (c & 1) * 64;
         // 128 rows x 8 sixteen-byte pieces = 1024 copies, 8 per thread
-        for (int j = tid; j < kTok * 8; j += kProdThreads) {
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int j = tid + i * kProdThreads;
           const int r = j >> 3, q = j & 7;
           const uint32_t dst = a_base + (uint32_t)r * 128u + (uint32_t)((q ^ (r & 7)) << 4);
-          const int kidx = et * kTok + r;
-          if (kidx < p.n_evict) {
-            const int tok = p.evict[(long long)b * p.n_evict + kidx];
-            cp_async16(dst, p.k + (((long long)b * p.Hkv + h) * p.L + tok) * kD + e0 + q * 8);
-          } else {
+          if (toks[i] >= 0)
+            cp_async16(dst, p.k + (((long long)b * p.Hkv + h) * p.L + toks[i]) * kD + e0 + q * 8);
+          else
             st_shared_zero16(dst);
-          }
         }
         cp_async_commit();
         // one gather group stays in flight: publish the stage issued before this one
@@ -411,6 +419,14 @@ __global__ void __launch_bounds__(kMbThreads, 1)
     int last = 0;  // stages issued
     for (int kc = kc0, it = 0; kc < kc1 && ok; ++kc, ++it) {
       const int st = it % kMbStages;
+      // token indices of this chunk, loaded before waiting for the stage
+      constexpr int kPer = kMbarChunk * kAtoms * 8 / kProdThreads;
+      int toks[kPer];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int kidx = kc * kMbarChunk + (tid + i * kProdThreads) / (kAtoms * 8);
+        toks[i] = kidx < p.n_evict ? p.evict[kidx] : -1;
+      }
       if (it >= kMbStages && !(ok = wait(bar_empty(st), ((it / kMbStages) - 1) & 1, 911))) break;
       const uint32_t base = sbase + st * kMbStage;
       if (tid == 0) {
@@ -420,16 +436,16 @@ __global__ void __launch_bounds__(kMbThreads, 1)
                       t * p.d_pad + jt * 128);
       }
       // 64 token rows x kAtoms MN atoms x 8 pieces
-      for (int j = tid; j < kMbarChunk * kAtoms * 8; j += kProdThreads) {
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int j = tid + i * kProdThreads;
         const int r = j / (kAtoms * 8), a = (j >> 3) % kAtoms, q = j & 7;
         const uint32_t dst = base + kMbA + (uint32_t)a * (kMbarChunk * 128u) + (uint32_t)r * 128u +
                              (uint32_t)((q ^ (r & 7)) << 4);
-        const int kidx = kc * kMbarChunk + r;
-        if (kidx < p.n_evict) {
-          const int tok = p.evict[kidx];
+        if (toks[i] >= 0) {
           const int col = ct * CT + a * 64 + q * 8;  // column of the (Hkv*d) value row
           const int h = col >> 7, e = col & 127;
-          cp_async16(dst, p.v + ((long long)h * p.L + tok) * kD + e);
+          cp_async16(dst, p.v + ((long long)h * p.L + toks[i]) * kD + e);
         } else {
           st_shared_zero16(dst);
         }
