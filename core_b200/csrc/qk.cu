@@ -30,6 +30,9 @@ constexpr int kD = 128;          // head dim
 constexpr int kTile = 128;       // keys per tile == queries per block
 constexpr int kThreads = 320;    // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
 constexpr int kEpiThreads = 256;
+constexpr int kLseTeams = 4;                       // LSE epilogue: 16-key quarters of a sub-tile
+constexpr int kLseEpiThreads = 128 * kLseTeams;
+constexpr int kLseThreads = 64 + kLseEpiThreads;  // warp 0 TMA, warp 1 MMA, 16 epilogue warps
 constexpr int kKStages = 2;
 constexpr uint32_t kKTileBytes = kTile * kD * 2;  // 32 KB
 constexpr uint32_t kAtom = 1024;                  // 8 rows x 128 B
@@ -101,7 +104,7 @@ struct LseSmem {
 };
 
 template <int G>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kLseThreads, 1)
     qk_lse_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const Params p) {
   using S = LseSmem<G>;
@@ -133,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar_t_full(s), 1);
-      mbar_init(bar_t_empty(s), kEpiThreads / 32);
+      mbar_init(bar_t_empty(s), kLseEpiThreads / 32);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -226,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue: online max / sum per (q-head, query) ----------------
     const int ew = warp - 2;
-    const int team = ew >> 2;      // 32-key half of each 64-key sub-tile
+    const int team = ew >> 2;      // 16-key quarter of each 64-key sub-tile
     const int wq = warp & 3;       // TMEM lane quarter
     const int row = wq * 32 + lane;
     float m[G], l[G];
@@ -238,13 +241,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int tq = t.qb * kTile + row;
       if (tq < p.nq) {
         const int c_lo = cta_of_unit(t.grp * (long long)p.n_kt, p.U, P);
-        const int slot = (blockIdx.x - c_lo) * 2 + team;
+        const int slot = (blockIdx.x - c_lo) * kLseTeams + team;
         for (int g = 0; g < G; ++g) {
           const long long r = ((long long)(t.b * p.Hq + t.h * G + g) * p.nq + tq);
           p.part[r * p.slot_stride + slot] = make_float2(m[g], l[g]);
         }
       }
     };
+    const unsigned long long sc2 = f2_pack(p.scale_log2, p.scale_log2);
     for (long long u = u0; u < u1 && ok; ++u) {
       Unit t = decode(u, p);
       if (t.grp != cur) {
@@ -261,30 +265,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = sub & 1, n = sub >> 1;
         if (!(ok = wait(bar_t_full(buf), n & 1, 106))) break;
         tc_fence_after();
-        const int k0 = t.kt * kTile + ss * 64 + team * 32;
-        const bool need_mask = (k0 + 31 > p.q_start + t.qb * kTile) || (k0 + 32 > p.L);
+        const int k0 = t.kt * kTile + ss * 64 + team * 16;
+        const bool need_mask = (k0 + 15 > p.q_start + t.qb * kTile) || (k0 + 16 > p.L);
         for (int g = 0; g < G; ++g) {
-          float v[32];
-          tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * G * 64 + g * 64 + team * 32), v);
-          float cmax = -INFINITY;
+          float v[16];
+          tmem_ld16(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * G * 64 + g * 64 + team * 16), v);
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) bf16_round2(v[j], v[j + 1]);
+          for (int j = 0; j < 16; j += 2) bf16_round2(v[j], v[j + 1]);
+          if (need_mask) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = v[j] * p.scale_log2;
-            if (need_mask) {
+            for (int j = 0; j < 16; ++j) {
               const int kk = k0 + j;
-              if (kk > qpos || kk >= p.L) x = -INFINITY;
+              if (kk > qpos || kk >= p.L) v[j] = -INFINITY;
             }
-            v[j] = x;
-            cmax = fmaxf(cmax, x);
           }
-          const float nm = fmaxf(m[g], cmax);
-          if (nm != -INFINITY) {
-            float s = 0.f;
+          float cmax = v[0];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) s += ex2_approx(v[j] - nm);
-            l[g] = l[g] * ex2_approx(m[g] - nm) + s;
+          for (int j = 1; j < 15; j += 2) cmax = fmax3(cmax, v[j], v[j + 1]);
+          cmax = fmaxf(cmax, v[15]);
+          // scale > 0: the scaled maximum is the scaled raw maximum
+          const float nm = fmaxf(m[g], cmax * p.scale_log2);
+          if (nm != -INFINITY) {
+            const unsigned long long neg2 = f2_pack(-nm, -nm);
+            unsigned long long acc = 0ull;
+#pragma unroll
+            for (int j = 0; j < 16; j += 2) {
+              const unsigned long long y = f2_fma(f2_pack(v[j], v[j + 1]), sc2, neg2);
+              acc = f2_add(acc, f2_pack(ex2_approx(f2_lo(y)), ex2_approx(f2_hi(y))));
+            }
+            l[g] = l[g] * ex2_approx(m[g] - nm) + (f2_lo(acc) + f2_hi(acc));
             m[g] = nm;
           }
         }
@@ -321,7 +330,7 @@ __global__ void lse_combine_kernel2(const Params p, int grid_ctas, float* __rest
   const long long grp = ((long long)b * p.Hkv + h) * p.n_qb + qb;
   const int c_lo = cta_of_unit(grp * (long long)p.n_kt, p.U, grid_ctas);
   const int c_hi = cta_of_unit((grp + 1) * (long long)p.n_kt - 1, p.U, grid_ctas);
-  const int nslots = (c_hi - c_lo + 1) * 2;
+  const int nslots = (c_hi - c_lo + 1) * kLseTeams;
   const float2* s = p.part + i * p.slot_stride;
   float mm = -INFINITY;
   for (int k = 0; k < nslots; ++k) mm = fmaxf(mm, s[k].x);
@@ -375,7 +384,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
   const uint32_t sQ = sbase + S::kQOff;
   const uint32_t sK = sbase + S::kKOff;
-  float2* s_rc = reinterpret_cast<float2*>(sgen + S::kLseOff);
+  float* s_nl = reinterpret_cast<float*>(sgen + S::kLseOff);  // [G][128] -lse
+  float* s_lc = s_nl + G * kTile;                                // [G][128] log|C_t|
   uint32_t* s_xch = reinterpret_cast<uint32_t*>(sgen + S::kXchOff);
   const uint32_t bar = sbase + S::kBarOff;
   const uint32_t bar_q_full = bar + 0, bar_q_empty = bar + 8;
@@ -498,6 +508,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wq = warp & 3;
     const int krow = wq * 32 + lane;  // key row inside the tile
     const float inv_ht = 1.0f / (float)p.head_topk;
+    const unsigned long long sc2 = f2_pack(p.scale, p.scale);
+    const unsigned long long nfloor2 = f2_pack(-kLogFloor, -kLogFloor);
     const bool exact_div = (p.head_topk != 1 && p.head_topk != 2 && p.head_topk != 4);
     const float single_val = log1pf(expf(kLogFloor));
     long long cur = -1;
@@ -515,7 +527,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const long long qpos = (long long)p.q_start + tt;
           const long long cc = (qpos + 1 < p.L) ? qpos + 1 : p.L;
           const float nl = (tt < p.nq) ? -p.lse[(long long)(t.b * p.Hq + t.h * G + g) * p.nq + tt] : 0.f;
-          s_rc[i] = make_float2(nl, logf((float)cc));
+          s_nl[i] = nl;
+          s_lc[i] = logf((float)cc);
         }
         named_barrier(1, kEpiThreads);
         cur = t.grp;
@@ -545,20 +558,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[16];
             tmem_ld16(tmem + ((uint32_t)(wq * 32) << 16) +
                           (uint32_t)(buf * kN + g * 64 + team * 32 + ch * 16), v);
-            const float2* rc = s_rc + g * kTile + c0;
+            const float* nlp = s_nl + g * kTile + c0;
+            const float* lcp = s_lc + g * kTile + c0;
             float rel[16];
             float amin = INFINITY;
+            // pairs of queries in packed f32x2 arithmetic (each lane rounds as the scalar form)
 #pragma unroll
-            for (int j = 0; j < 16; j += 2) bf16_round2(v[j], v[j + 1]);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float2 c = rc[j];
-              const float r = fmaf(v[j], p.scale, c.x) + c.y;
-              const float a = fabsf(r - kLogFloor);
-              amin = fminf(amin, a);
+            for (int j = 0; j < 16; j += 2) {
+              bf16_round2(v[j], v[j + 1]);
+              const unsigned long long nl2 = *reinterpret_cast<const unsigned long long*>(nlp + j);
+              const unsigned long long lc2 = *reinterpret_cast<const unsigned long long*>(lcp + j);
+              const unsigned long long r2 = f2_add(f2_fma(f2_pack(v[j], v[j + 1]), sc2, nl2), lc2);
+              const unsigned long long d2 = f2_add(r2, nfloor2);  // r - log(1e-8)
+              const float a0 = fabsf(f2_lo(d2)), a1 = fabsf(f2_hi(d2));
+              amin = fmin3(amin, a0, a1);
               // exp(-a) < 1.2e-7 for a >= 16: log1p(x) equals x to within half an ulp of x
-              rel[j] = fmaxf(r, kLogFloor) + ex2_approx(-a * kLog2e);
-              v[j] = r;
+              rel[j] = fmaxf(f2_lo(r2), kLogFloor) + ex2_approx(-a0 * kLog2e);
+              rel[j + 1] = fmaxf(f2_hi(r2), kLogFloor) + ex2_approx(-a1 * kLog2e);
+              v[j] = f2_lo(r2);
+              v[j + 1] = f2_hi(r2);
             }
             if (__any_sync(0xffffffffu, amin < 16.0f)) {
 #pragma unroll
@@ -914,7 +932,7 @@ int plan_qk(const core_dims_t* d, int topk, int n_recent, QKPlan* out) {
   p.n_recent = n_recent < p.nq ? n_recent : p.nq;
   const int sms = sm_count();
   out->grid = (int)(p.U < sms ? p.U : sms);
-  // slots: 2 teams x CTAs overlapping one group
+  // slots: kLseTeams epilogue teams x CTAs overlapping one group
   int maxc = 1;
   const long long groups = p.U / p.n_kt;
   for (long long g = 0; g < groups; ++g) {
@@ -922,7 +940,7 @@ int plan_qk(const core_dims_t* d, int topk, int n_recent, QKPlan* out) {
     int hi = cta_of_unit((g + 1) * p.n_kt - 1, p.U, out->grid);
     if (hi - lo + 1 > maxc) maxc = hi - lo + 1;
   }
-  p.slot_stride = 2 * maxc;
+  p.slot_stride = kLseTeams * maxc;
   out->part_elems = (size_t)p.B * p.Hq * p.nq * p.slot_stride;
   out->rec_words = (size_t)p.B * p.L * p.Hkv * p.n_qb * kRecWords;
   return CORE_OK;
@@ -938,7 +956,7 @@ int launch_qk(const QKPlan& plan, const CUtensorMap& tmQ_lse, const CUtensorMap&
     const uint32_t smem = LseSmem<G>::kTotal + 1024;
     e = cudaFuncSetAttribute(qk_lse_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_error(e, "qk_lse_kernel attribute");
-    qk_lse_kernel<G><<<plan.grid, kThreads, smem, s>>>(tmQ_lse, tmK, p);
+    qk_lse_kernel<G><<<plan.grid, kLseThreads, smem, s>>>(tmQ_lse, tmK, p);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_lse_kernel launch");
     const long long n = (long long)p.B * p.Hq * p.nq;
     lse_combine_kernel2<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p, plan.grid, lse_buf);
