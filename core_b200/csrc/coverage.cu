@@ -228,6 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               ss = fmaf(f2.y, f2.y, ss);
             }
           }
+          // order these generic-proxy reads before the TMA (async proxy) refill of the stage
+          fence_proxy_async_shared();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_empty(st));
         }

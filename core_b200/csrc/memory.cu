@@ -149,6 +149,7 @@ constexpr uint32_t kPhiA = kTok * 128;          // 16 KB: 128 tokens x 64 column
 constexpr uint32_t kPhiB = 2u * kNCols * 128;   // 64 KB: two terms x 256 rows x 64 columns
 constexpr uint32_t kPhiStage = kPhiA + kPhiB;
 constexpr int kPhiStages = 2;
+constexpr int kPhiLag = kPhiStages - 1;  // gather groups in flight per producer thread
 constexpr int kPhiThreads = 512;  // warps 0-3 gather, 4 MMA, 8-15 epilogue
 
 __global__ void __launch_bounds__(kPhiThreads, 1)
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
-  const uint32_t red_off = kPhiStages * kPhiStage;            // float [4][256]
+  const uint32_t red_off = kPhiStages * kPhiStage;            // float [4][kNCols]
   float* s_red = reinterpret_cast<float*>(sgen + red_off);
   const uint32_t bar = sbase + red_off + 4 * kNCols * 4;
   auto bar_full = [&](int s) { return bar + 8u * s; };
@@ -184,7 +185,7 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
     fence_barrier_init();
   }
   if (warp == 4) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_alloc(smem_u32(tmem_slot), 2 * kNCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -238,19 +239,20 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
             st_shared_zero16(dst);
         }
         cp_async_commit();
-        // one gather group stays in flight: publish the stage issued before this one
-        if (it >= 1) {
-          cp_async_wait_group<1>();
+        // kPhiLag gather groups stay in flight: publish the oldest one
+        if (it >= kPhiLag) {
+          cp_async_wait_group<kPhiLag>();
           fence_proxy_async_shared();
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar_full((it - 1) % kPhiStages));
+          if (lane == 0) mbar_arrive(bar_full((it - kPhiLag) % kPhiStages));
         }
       }
     }
     cp_async_wait_all();
     fence_proxy_async_shared();
     __syncwarp();
-    if (ok && it >= 1 && lane == 0) mbar_arrive(bar_full((it - 1) % kPhiStages));
+    if (ok && lane == 0)
+      for (int j = it > kPhiLag ? it - kPhiLag : 0; j < it; ++j) mbar_arrive(bar_full(j % kPhiStages));
   } else if (warp == 4) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(128, kNCols, 0, 0);
@@ -280,7 +282,7 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
     }
   } else if (warp >= 8) {
     const int ew = warp - 8;
-    const int team = ew >> 2;       // column half: 0 -> 0..127, 1 -> 128..255
+    const int team = ew >> 2;       // column half of the unit: [0, 128) or [128, 256)
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     int sub = 0;
@@ -294,8 +296,8 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
       tc_fence_after();
       const int kidx = et * kTok + row;
       const float pb = p.pbar[(long long)b * p.n_ev_pad + kidx];  // 0 on padding rows
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const int col0 = team * 128 + q4 * 32;
+      for (int q4 = 0; q4 < kNCols / 64; ++q4) {
+        const int col0 = team * (kNCols / 2) + q4 * 32;
         if (dh * kNCols + col0 >= p.d_pad) continue;  // padding columns of the last unit
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * kNCols + col0), v);
@@ -342,7 +344,7 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
   __syncthreads();
   if (warp == 4) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 2 * kNCols);
   }
 }
 

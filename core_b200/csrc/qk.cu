@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(kLseThreads, 1)
           float v[16];
           tmem_ld16(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * G * 64 + g * 64 + team * 16), v);
 #pragma unroll
-          for (int j = 0; j < 16; j += 2) bf16_round2(v[j], v[j + 1]);
+          for (int j = 0; j < 16; j += 2) bf16_round2(v[j], v[j + 1]);  // bf16 logits (fused_qk.py:83-87)
           if (need_mask) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -317,31 +317,42 @@ __global__ void __launch_bounds__(kLseThreads, 1)
 // ===========================================================================
 // 2. LSE combine
 // ===========================================================================
+// Eight lanes per (b, q-head, query) row: lane j takes slots j, j + 8, ...;
+// the maximum and then the rescaled sums are combined by shuffles.
 __global__ void lse_combine_kernel2(const Params p, int grid_ctas, float* __restrict__ lse_out) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+  const int sl = threadIdx.x & 7;
   const long long n = (long long)p.B * p.Hq * p.nq;
-  if (i >= n) return;
-  const int t = (int)(i % p.nq);
-  const long long bq = i / p.nq;
-  const int qh = (int)(bq % p.Hq);
-  const int b = (int)(bq / p.Hq);
-  const int h = qh / p.G;
-  const int qb = t / kTile;
-  const long long grp = ((long long)b * p.Hkv + h) * p.n_qb + qb;
-  const int c_lo = cta_of_unit(grp * (long long)p.n_kt, p.U, grid_ctas);
-  const int c_hi = cta_of_unit((grp + 1) * (long long)p.n_kt - 1, p.U, grid_ctas);
-  const int nslots = (c_hi - c_lo + 1) * kLseTeams;
-  const float2* s = p.part + i * p.slot_stride;
+  int nslots = 0;
+  const float2* s = p.part;
+  if (i < n) {
+    const int t = (int)(i % p.nq);
+    const long long bq = i / p.nq;
+    const int qh = (int)(bq % p.Hq);
+    const int b = (int)(bq / p.Hq);
+    const int h = qh / p.G;
+    const int qb = t / kTile;
+    const long long grp = ((long long)b * p.Hkv + h) * p.n_qb + qb;
+    const int c_lo = cta_of_unit(grp * (long long)p.n_kt, p.U, grid_ctas);
+    const int c_hi = cta_of_unit((grp + 1) * (long long)p.n_kt - 1, p.U, grid_ctas);
+    nslots = (c_hi - c_lo + 1) * kLseTeams;
+    s = p.part + i * p.slot_stride;
+  }
   float mm = -INFINITY;
-  for (int k = 0; k < nslots; ++k) mm = fmaxf(mm, s[k].x);
+  for (int k = sl; k < nslots; k += 8) mm = fmaxf(mm, s[k].x);
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
   float ll = 0.f;
   if (mm != -INFINITY) {
-    for (int k = 0; k < nslots; ++k) {
+    for (int k = sl; k < nslots; k += 8) {
       const float2 v = s[k];
       if (v.y > 0.f) ll += v.y * ex2_approx(v.x - mm);
     }
   }
-  lse_out[i] = (mm == -INFINITY || ll <= 0.f) ? -INFINITY : (mm + log2f(ll)) * kLn2;
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) ll += __shfl_xor_sync(0xffffffffu, ll, o);
+  if (i < n && sl == 0)
+    lse_out[i] = (mm == -INFINITY || ll <= 0.f) ? -INFINITY : (mm + log2f(ll)) * kLn2;
 }
 
 // ===========================================================================
@@ -605,6 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           const int tabs0 = t.qb * kTile + c0;  // absolute query index of element 0
+          const bool recent_chunk = tabs0 + 15 >= p.nq - p.n_recent;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float R;
@@ -618,10 +630,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (c0 + j >= qb_valid || key > qpos) R = -INFINITY;
             }
             top4_insert(st.top, R);
-            if (tabs0 + j >= p.nq - p.n_recent) top4_insert(st.rtop, R);
+            if (recent_chunk && tabs0 + j >= p.nq - p.n_recent) top4_insert(st.rtop, R);
             const bool pz = R > 0.f;
-            st.psum += pz ? R : 0.f;
-            st.pcnt += pz ? 1u : 0u;
+            st.psum += fmaxf(R, 0.f);  // adds R when positive, +0 otherwise (NaN: +0)
             msk |= (pz ? 1u : 0u) << (ch * 16 + j);
             st.mxnp = fmaxf(st.mxnp, pz ? -INFINITY : R);
           }
@@ -633,6 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         st.mask[hf] = msk;
       }
       if (!ok) break;
+      st.pcnt = (uint32_t)(__popc(st.mask[0]) + __popc(st.mask[1]));  // positive relations
       // merge the two teams (same key, different query quarters) and store
       uint32_t* x = s_xch + krow * 16;
       if (team == 1) {
@@ -959,7 +971,7 @@ int launch_qk(const QKPlan& plan, const CUtensorMap& tmQ_lse, const CUtensorMap&
     qk_lse_kernel<G><<<plan.grid, kLseThreads, smem, s>>>(tmQ_lse, tmK, p);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_lse_kernel launch");
     const long long n = (long long)p.B * p.Hq * p.nq;
-    lse_combine_kernel2<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p, plan.grid, lse_buf);
+    lse_combine_kernel2<<<(unsigned)((8 * n + 255) / 256), 256, 0, s>>>(p, plan.grid, lse_buf);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "lse_combine launch");
   }
   const uint32_t smem = RelSmem<G>::kTotal + 1024;

@@ -36,6 +36,40 @@ def _f32(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
 
 
+def _f3_flip_consistent(got_f3, R, bad_keys, rtol=FEATURE_TOL):
+    """f3 is the mean of the positive relation values of a key.  A relation
+    value within rounding of 0 (one bf16 ulp of its logit) can take either
+    sign on the tensor cores, which moves the count by one and the sum by
+    about nothing; accept a key whose f3 equals psum / (pcnt + j) for j within
+    the number of such values."""
+    nkv, nq, L = R.shape
+    flat = R.reshape(nkv * nq, L).astype(np.float64)
+    for k in bad_keys:
+        col = flat[:, k]
+        pos = col > 0
+        psum, pcnt = col[pos].sum(), int(pos.sum())
+        # one bf16 ulp of a logit moves a relation value by up to ~1e-3
+        near = np.abs(col) <= 2e-3
+        n_minus, n_plus = int((near & pos).sum()), int((near & ~pos & np.isfinite(col)).sum())
+        cands = [psum / max(pcnt + j, 1) for j in range(-n_minus, n_plus + 1)]
+        tol = rtol * max(abs(psum / max(pcnt, 1)), 1e-3)
+        if min(abs(got_f3[k] - c) for c in cands) > tol:
+            return False, k
+    return True, None
+
+
+def _check_qk_features(got, ref, R):
+    err = rel_err(got[:, :4], ref[:, :4])
+    # f1, f2, f4: maxima and top-k means, continuous in the relation values
+    assert np.quantile(err[:, [0, 1, 3]], 0.999) < FEATURE_TOL, err.max(0)
+    assert err[:, [0, 1, 3]].max() < FLIP_TOL, err.max(0)
+    # f3: exact up to sign flips of relation values at 0
+    bad = np.nonzero(err[:, 2] > FEATURE_TOL)[0]
+    assert len(bad) <= max(2, 0.005 * len(err)), len(bad)
+    ok, k = _f3_flip_consistent(got[:, 2], R, bad)
+    assert ok, (k, got[k, 2], ref[k, 2])
+
+
 def _discrete_mismatch(a, b, step):
     """Fraction of entries that differ, and the largest difference in units of step."""
     d = np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64))
@@ -51,11 +85,10 @@ def test_qk_features_match_oracle(name):
     k = _bf16(d["k"], dev)[None]
     feats, lse = ops.qk_features(q, k)
     ops.status()
-    ref, ref_lse, _ = O.qk_features(d["q"], d["k"], groups=m["hq"] // m["hkv"], round_bf16=True)
+    ref, ref_lse, R = O.qk_features(d["q"], d["k"], groups=m["hq"] // m["hkv"], round_bf16=True)
     got = feats[0].cpu().numpy()
     assert np.abs(lse[0].cpu().numpy() - ref_lse).max() <= LSE_TOL * np.abs(ref_lse).max()
-    err = rel_err(got[:, :4], ref[:, :4])
-    assert np.quantile(err, 0.999) < FEATURE_TOL and err.max() < FLIP_TOL, (name, err.max(0))
+    _check_qk_features(got, ref, R)
     nq, hkv = m["nq"], m["hkv"]
     f5_frac, f5_steps = _discrete_mismatch(got[:, 4], ref[:, 4], 1.0 / nq)
     f6_frac, f6_steps = _discrete_mismatch(got[:, 5], ref[:, 5], 1.0 / hkv)
@@ -72,11 +105,10 @@ def test_qk_features_llama_shapes_4096():
     ops.status()
     qn = q[0].float().cpu().numpy()
     kn = k[0].float().cpu().numpy()
-    ref, ref_lse, _ = O.qk_features(qn, kn, groups=4, round_bf16=True)
+    ref, ref_lse, R = O.qk_features(qn, kn, groups=4, round_bf16=True)
     got = feats[0].cpu().numpy()
     assert np.abs(lse[0].cpu().numpy() - ref_lse).max() <= LSE_TOL * np.abs(ref_lse).max()
-    err = rel_err(got[:, :4], ref[:, :4])
-    assert np.quantile(err, 0.999) < FEATURE_TOL and err.max() < FLIP_TOL, err.max(0)
+    _check_qk_features(got, ref, R)
     f5_frac, _ = _discrete_mismatch(got[:, 4], ref[:, 4], 1 / 128)
     f6_frac, _ = _discrete_mismatch(got[:, 5], ref[:, 5], 1 / 8)
     assert f5_frac <= 0.005 and f6_frac <= 0.005, (f5_frac, f6_frac)
