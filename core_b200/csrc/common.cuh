@@ -268,6 +268,11 @@ __device__ __forceinline__ void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Hint: bring the 128-byte line holding p into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Copy n16 16-byte chunks global -> shared with all threads of the block
 // (both addresses 16-byte aligned); completes with cp_async_wait_all().
 __device__ __forceinline__ void cp_async_block(void* dst, const void* src, int n16) {

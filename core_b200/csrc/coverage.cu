@@ -9,7 +9,8 @@
 //                             bf16 terms, so the product is f32-accurate);
 //                             z = y[:64] / (|y[:64]| + eps), zt = y[64:] / (same), and
 //                             per-CTA column sums of z, zt, zt^2.
-//   cov_stats_kernel        : reduces the per-CTA sums (double).
+//   cov_stats_kernel        : reduces the per-CTA sums (double) and finalises the row
+//                             statistics.
 //   cov_assign_kernel       : four threads per token: centred prototype cosines,
 //                             first-max assignment, second best, occupancy
 //                             histogram, d, delta and g.
@@ -302,37 +303,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 // then mean z, mu and sigma2_eff (features.py:812, :830-845) as floats:
 // stats[b] = [mean z (64) | mu (64) | sigma2_eff (64)].
 constexpr int kStatsThreads = 1024;
-constexpr int kMaxPartCtas = 256;  // per-lane unrolled loads cover 8 x 32 CTAs per pass
+constexpr int kMaxPartCtas = 256;
+constexpr int kStatsChunk = 64;  // CTA partials staged in shared memory per pass (96 KB)
 
+// CTA owning unit u under the contiguous static partition of unit_begin.
+__device__ __forceinline__ int cta_of_unit(long long u, long long U, int P) {
+  return (int)(((u + 1) * P + U - 1) / U) - 1;
+}
+
+// Per batch row: the column sums of the CTAs that covered the row (a
+// contiguous CTA range), staged into shared memory with cp.async and summed
+// in CTA order (double), then mean z, mu and sigma2_eff (features.py:812,
+// :830-845) as floats: stats[b] = [mean z (64) | mu (64) | sigma2_eff (64)].
 __global__ void __launch_bounds__(kStatsThreads)
     cov_stats_kernel(const double* __restrict__ part, int grid_ctas, int B, int n_tiles, int L,
                      float rho, float* __restrict__ stats) {
+  extern __shared__ __align__(16) double sp[];  // [kStatsChunk][kNStats]
   __shared__ double s[kNStats];
   __shared__ float var[kP];
   const int b = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tid = threadIdx.x;
   const long long U = (long long)B * n_tiles;
-  const long long lo = (long long)b * n_tiles, hi = lo + n_tiles;
-  // which of this lane's CTAs covered row b (contiguous static partition of the tiles)
-  unsigned covered = 0;
-#pragma unroll
-  for (int j = 0; j < kMaxPartCtas / 32; ++j) {
-    const int c = lane + 32 * j;
-    const long long a = (long long)c * U / grid_ctas, e = (long long)(c + 1) * U / grid_ctas;
-    if (c < grid_ctas && a < hi && e > lo) covered |= 1u << j;
+  const int c_lo = cta_of_unit((long long)b * n_tiles, U, grid_ctas);
+  const int c_hi = cta_of_unit((long long)(b + 1) * n_tiles - 1, U, grid_ctas);
+  constexpr int kPieces = kNStats * 8 / 16;  // 16-byte pieces of one CTA's partial row
+  double acc = 0.0;
+  for (int c0 = c_lo; c0 <= c_hi; c0 += kStatsChunk) {
+    const int n = min(kStatsChunk, c_hi - c0 + 1);
+    const uint32_t d = smem_u32(sp);
+    for (int j = tid; j < n * kPieces; j += kStatsThreads) {
+      const int cc = j / kPieces, q = j % kPieces;
+      cp_async16(d + (uint32_t)(cc * kNStats) * 8u + 16u * q,
+                 part + ((long long)(c0 + cc) * B + b) * kNStats + 2 * q);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    if (tid < kNStats)
+      for (int cc = 0; cc < n; ++cc) acc += sp[cc * kNStats + tid];
+    __syncthreads();
   }
-  for (int i = warp; i < kNStats; i += kStatsThreads / 32) {
-    double v[kMaxPartCtas / 32];
-#pragma unroll
-    for (int j = 0; j < kMaxPartCtas / 32; ++j)
-      v[j] = (covered >> j & 1u) ? part[((long long)(lane + 32 * j) * B + b) * kNStats + i] : 0.0;
-    double acc = 0.0;
-#pragma unroll
-    for (int j = 0; j < kMaxPartCtas / 32; ++j) acc += v[j];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) s[i] = acc;
-  }
+  if (tid < kNStats) s[tid] = acc;
   __syncthreads();
   float* out = stats + (long long)b * kNStats;
   if (threadIdx.x < kP) {
@@ -612,7 +623,13 @@ extern "C" int core_coverage_features(const core_dims_t* d, const void* k,
   if (e != cudaSuccess) return cuda_error(e, "cov_project_kernel attribute");
   cov_project_kernel<<<c.grid, kThreads, smem, s>>>(tmK, tmW, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "cov_project_kernel launch");
-  cov_stats_kernel<<<p.B, kStatsThreads, 0, s>>>(p.part, c.grid, p.B, p.n_tiles, p.L, shrinkage_rho, stats);
+  {
+    const size_t smem = sizeof(double) * kStatsChunk * kNStats;
+    e = cudaFuncSetAttribute(cov_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_error(e, "cov_stats_kernel attribute");
+    cov_stats_kernel<<<p.B, kStatsThreads, smem, s>>>(p.part, c.grid, p.B, p.n_tiles, p.L,
+                                                      shrinkage_rho, stats);
+  }
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "cov_stats_kernel launch");
   const long long n = (long long)p.B * p.L;
   long long ablocks = (n + kAssignThreads / 4 - 1) / (kAssignThreads / 4);

@@ -167,11 +167,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = half; h < p.Hkv; h += 2) {
         const uint4* row =
             reinterpret_cast<const uint4*>(p.v + (((long long)b * p.Hkv + h) * p.L + i) * 128);
+        uint4 w[16];  // the whole 256-byte row in flight at once
+#pragma unroll
+        for (int c = 0; c < 16; ++c) w[c] = __ldg(row + c);
         float s = 0.f;
-#pragma unroll 4
+#pragma unroll
         for (int c = 0; c < 16; ++c) {
-          const uint4 w = __ldg(row + c);
-          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w[c]);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f2 = __bfloat1622float2(h2[e]);

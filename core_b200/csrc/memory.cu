@@ -22,7 +22,9 @@ namespace core {
 namespace mw {
 
 constexpr int kD = 128;
-constexpr int kTok = 128;         // evicted tokens per phi tile
+constexpr int kTok = 128;         // evicted tokens per MMA M tile of phi
+constexpr int kPhiM = 2;          // M tiles per phi unit: both share every Theta stage
+constexpr int kUnitTok = kPhiM * kTok;
 constexpr int kNCols = 256;       // d_mem columns per phi unit (MMA N)
 constexpr int kProdThreads = 128; // 4 gathering warps
 constexpr int kMbarChunk = 64;    // tokens per M_bar K chunk
@@ -145,11 +147,12 @@ struct PhiParams {
   DeviceStatus* status;
 };
 
-constexpr uint32_t kPhiA = kTok * 128;          // 16 KB: 128 tokens x 64 columns
+constexpr uint32_t kPhiA = kUnitTok * 128;      // 32 KB: 256 tokens x 64 columns (two M tiles)
 constexpr uint32_t kPhiB = 2u * kNCols * 128;   // 64 KB: two terms x 256 rows x 64 columns
 constexpr uint32_t kPhiStage = kPhiA + kPhiB;
 constexpr int kPhiStages = 2;
 constexpr int kPhiLag = kPhiStages - 1;  // gather groups in flight per producer thread
+constexpr int kPhiAhead = 3;             // K chunks prefetched into L2 ahead of the gather
 constexpr int kPhiThreads = 512;  // warps 0-3 gather, 4 MMA, 8-15 epilogue
 
 __global__ void __launch_bounds__(kPhiThreads, 1)
@@ -185,7 +188,7 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
     fence_barrier_init();
   }
   if (warp == 4) {
-    tmem_alloc(smem_u32(tmem_slot), 2 * kNCols);
+    tmem_alloc(smem_u32(tmem_slot), kPhiM * kNCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -205,14 +208,22 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
       const int dh = (int)(u % p.n_dh);
       const long long rest = u / p.n_dh;
       const int et = (int)(rest % p.n_et), b = (int)(rest / p.n_et);
-      // the unit's 128 token rows are the same for all its K chunks: load their
-      // indices once (8 rows per thread: r = tid / 8 + 16 i)
-      constexpr int kPer = kTok * 8 / kProdThreads;
+      // the unit's 256 token rows are the same for all its K chunks: load their
+      // indices once (16 rows per thread: r = tid / 8 + 16 i)
+      constexpr int kPer = kUnitTok * 8 / kProdThreads;
       int toks[kPer];
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
-        const int kidx = et * kTok + ((tid + i * kProdThreads) >> 3);
+        const int kidx = et * kUnitTok + ((tid + i * kProdThreads) >> 3);
         toks[i] = kidx < p.n_evict ? p.evict[(long long)b * p.n_evict + kidx] : -1;
+      }
+      if ((tid & 7) == 0) {  // the first chunks of the unit into L2
+        for (int ca = 1; ca < kPhiAhead && ca < n_chunks; ++ca) {
+          const long long hoff = ((long long)b * p.Hkv + (ca >> 1)) * p.L;
+#pragma unroll
+          for (int i = 0; i < kPer; ++i)
+            if (toks[i] >= 0) prefetch_l2(p.k + (hoff + toks[i]) * kD + (ca & 1) * 64);
+        }
       }
       for (int c = 0; c < n_chunks && ok; ++c, ++it) {
         const int st = it % kPhiStages;
@@ -227,18 +238,29 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
                         dh * kNCols, t);
         }
         const int h = c >> 1, e0 = (c & 1) * 64;
-        // 128 rows x 8 sixteen-byte pieces = 1024 copies, 8 per thread
+        // 256 rows x 8 sixteen-byte pieces = 2048 copies, 16 per thread; row r
+        // goes to M tile r / 128
 #pragma unroll
         for (int i = 0; i < kPer; ++i) {
           const int j = tid + i * kProdThreads;
           const int r = j >> 3, q = j & 7;
-          const uint32_t dst = a_base + (uint32_t)r * 128u + (uint32_t)((q ^ (r & 7)) << 4);
+          const uint32_t dst = a_base + (uint32_t)(r >> 7) * (kTok * 128u) +
+                               (uint32_t)(r & (kTok - 1)) * 128u + (uint32_t)((q ^ (r & 7)) << 4);
           if (toks[i] >= 0)
             cp_async16(dst, p.k + (((long long)b * p.Hkv + h) * p.L + toks[i]) * kD + e0 + q * 8);
           else
             st_shared_zero16(dst);
         }
         cp_async_commit();
+        // L2 prefetch of the rows' chunk kPhiAhead stages ahead (the gathers
+        // are latency-bound with two stages of shared memory)
+        if (c + kPhiAhead < n_chunks && (tid & 7) == 0) {
+          const int ca = c + kPhiAhead;
+          const long long hoff = ((long long)b * p.Hkv + (ca >> 1)) * p.L;
+#pragma unroll
+          for (int i = 0; i < kPer; ++i)
+            if (toks[i] >= 0) prefetch_l2(p.k + (hoff + toks[i]) * kD + (ca & 1) * 64);
+        }
         // kPhiLag gather groups stay in flight: publish the oldest one
         if (it >= kPhiLag) {
           cp_async_wait_group<kPhiLag>();
@@ -259,25 +281,27 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
       int it = 0, sub = 0;
       bool ok = true;
       for (long long u = u0; u < u1 && ok; ++u, ++sub) {
-        const int buf = sub & 1, n = sub >> 1;
-        if (sub >= 2 && !(ok = wait(bar_tempty(buf), (n - 1) & 1, 902))) break;
+        // one accumulator set (kPhiM tiles x kNCols columns): wait for the epilogue of the last unit
+        if (sub >= 1 && !(ok = wait(bar_tempty(0), (sub - 1) & 1, 902))) break;
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * kNCols);
         for (int c = 0; c < n_chunks && ok; ++c, ++it) {
           const int st = it % kPhiStages;
           if (!(ok = wait(bar_full(st), (it / kPhiStages) & 1, 903))) break;
           tc_fence_after();
           const uint32_t a_base = sbase + st * kPhiStage;
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t a = sdesc_kmajor(a_base + (uint32_t)ks * 32u);
-            for (int t = 0; t < 2; ++t) {
-              const uint64_t bd = sdesc_kmajor(a_base + kPhiA + (uint32_t)t * kNCols * 128u + (uint32_t)ks * 32u);
-              mma_bf16(d, a, bd, idesc, (c > 0 || ks > 0 || t > 0) ? 1u : 0u);
+          for (int mt = 0; mt < kPhiM; ++mt) {
+            const uint32_t d = tmem + (uint32_t)(mt * kNCols);
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t a = sdesc_kmajor(a_base + (uint32_t)mt * (kTok * 128u) + (uint32_t)ks * 32u);
+              for (int t = 0; t < 2; ++t) {
+                const uint64_t bd = sdesc_kmajor(a_base + kPhiA + (uint32_t)t * kNCols * 128u + (uint32_t)ks * 32u);
+                mma_bf16(d, a, bd, idesc, (c > 0 || ks > 0 || t > 0) ? 1u : 0u);
+              }
             }
           }
           mma_commit(bar_empty(st));
         }
-        if (ok) mma_commit(bar_tfull(buf));
+        if (ok) mma_commit(bar_tfull(0));
       }
     }
   } else if (warp >= 8) {
@@ -291,16 +315,16 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
       const int dh = (int)(u % p.n_dh);
       const long long rest = u / p.n_dh;
       const int et = (int)(rest % p.n_et), b = (int)(rest / p.n_et);
-      const int buf = sub & 1, n = sub >> 1;
-      if (!(ok = wait(bar_tfull(buf), n & 1, 904))) break;
+      if (!(ok = wait(bar_tfull(0), sub & 1, 904))) break;
       tc_fence_after();
-      const int kidx = et * kTok + row;
+      for (int mt = 0; mt < kPhiM; ++mt) {
+      const int kidx = et * kUnitTok + mt * kTok + row;
       const float pb = p.pbar[(long long)b * p.n_ev_pad + kidx];  // 0 on padding rows
       for (int q4 = 0; q4 < kNCols / 64; ++q4) {
         const int col0 = team * (kNCols / 2) + q4 * 32;
         if (dh * kNCols + col0 >= p.d_pad) continue;  // padding columns of the last unit
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * kNCols + col0), v);
+        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(mt * kNCols + col0), v);
         const int jbase = dh * kNCols + col0;
         float u2[32];
 #pragma unroll
@@ -325,11 +349,14 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
             u2[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
           }
         }
-        s_red[wq * kNCols + col0 + lane] = u2[0];
+        // this thread owns s_red[wq][col0 + lane]: tile 0 stores, tile 1 adds
+        float* sr = s_red + wq * kNCols + col0 + lane;
+        *sr = (mt == 0) ? u2[0] : *sr + u2[0];
+      }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_tempty(buf));
+      if (lane == 0) mbar_arrive(bar_tempty(0));
       named_barrier(1, 256);
       // fixed-order reduction of the four lane quarters
       for (int cidx = threadIdx.x - 256; cidx < kNCols && dh * kNCols + cidx < p.d_pad; cidx += 256) {
@@ -344,7 +371,7 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
   __syncthreads();
   if (warp == 4) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * kNCols);
+    tmem_dealloc(tmem, kPhiM * kNCols);
   }
 }
 
@@ -562,8 +589,8 @@ struct MwPlan {
   long long phi_units;
 };
 void plan_mw(const core_dims_t* d, int n_evict, int d_mem, MwPlan* m) {
-  m->n_et = (n_evict + kTok - 1) / kTok;
-  m->n_ev_pad = m->n_et * kTok;
+  m->n_et = (n_evict + kUnitTok - 1) / kUnitTok;
+  m->n_ev_pad = m->n_et * kUnitTok;
   m->d_pad = ((d_mem + 127) / 128) * 128;
   m->n_dh = (m->d_pad + kNCols - 1) / kNCols;
   m->kvw = d->n_kv_heads * kD;

@@ -328,3 +328,32 @@ def test_compress_layers_concurrent_equals_sequential():
         assert torch.equal(a["scores"], b["scores"])
         assert torch.equal(a["keys"], b["keys"]) and torch.equal(a["values"], b["values"])
         assert torch.equal(ja["memory"].M, jb["memory"].M)
+
+
+def test_repeated_calls_are_bitwise_deterministic():
+    """Same inputs, fresh (uninitialised) workspaces, twenty repetitions: the
+    coverage features and the fused layer step reproduce bit for bit."""
+    from core_b200 import engine, ops, synthetic
+    dev = _dev()
+    L, nq, hkv, hq = 2048, 64, 8, 32
+    q, k, v = synthetic.make_layer_inputs(seed=102, batch=1, n_kv_heads=hkv, n_q_heads=hq,
+                                          seq_len=L, n_queries=nq, device=dev)
+    w = synthetic.make_layer_weights(seed=202, n_kv_heads=hkv, n_q_heads=hq, d_mem=128)
+    lw = engine.LayerWeights.prepare(geometry=w["geometry"], prototypes=w["prototypes"],
+                                     hadamard=w["hadamard"], mlp_params=w["mlp"], theta=w["theta"],
+                                     n_kv_heads=hkv, n_q_heads=hq, device=dev)
+    ref = ops.coverage_features(k, lw.geometry_ext, lw.prototypes).clone()
+    for _ in range(20):
+        scratch = torch.randn(1 << 20, device=dev)  # leave different garbage behind
+        del scratch
+        assert torch.equal(ops.coverage_features(k, lw.geometry_ext, lw.prototypes), ref)
+    pos = torch.arange(L, device=dev)[None]
+    n_kept = engine.n_kept_for(L, 0.75, 4)
+    outs = [engine.compress_layer(q, k, v, lw, n_kept=n_kept, positions=pos, original_length=L,
+                                  is_prefill=True,
+                                  memory=engine.MemoryState.zeros(1, 128, hkv * 128, dev))
+            for _ in range(5)]
+    ops.status()
+    for o in outs[1:]:
+        assert torch.equal(o["features"], outs[0]["features"])
+        assert torch.equal(o["keep"], outs[0]["keep"])
