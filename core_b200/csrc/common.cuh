@@ -142,6 +142,21 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that also returns the AND of `pred` over the participating
+// threads: lets a group of warps take one uniform decision after a bounded wait.
+__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %2, 0;\n\t"
+      "bar.red.and.pred q, %1, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"((uint32_t)pred), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05: TMEM allocation, MMA, commit, loads
 // ---------------------------------------------------------------------------

@@ -4,12 +4,13 @@
 //   mw_mass_kernel   : p = softmax(s / tau) over the whole cache, pi_E = sum of
 //                      p over evicted tokens, p_bar = p / pi_E on the evicted
 //                      list (core/indexer.py:55-72, :247-273); Z <- gamma Z + pi_E.
-//   mw_phi_kernel    : phi = K_ev Theta_f^T for 128 gathered evicted tokens on
-//                      tcgen05 (K rows gathered with cp.async into swizzled
-//                      shared memory, Theta_f as two bf16 terms, K exact in
-//                      bf16), epilogue W = p_bar * phi written as bf16 hi/lo in
-//                      (d_mem, token) order, and per-tile column sums of
-//                      p_bar * phi^2 (b_bar partials).
+//   mw_phi_kernel    : phi^T = Theta_f K_ev^T for 128 memory rows x 128 gathered
+//                      evicted tokens on tcgen05 (Theta_f as two bf16 terms by
+//                      TMA, K rows gathered with cp.async into swizzled shared
+//                      memory, K exact in bf16, four stages), epilogue
+//                      W^T = p_bar * phi^T written as bf16 hi/lo in (d_mem,
+//                      token) order and per-row sums of p_bar * phi^2 (b_bar
+//                      partials).
 //   mw_mbar_kernel   : M_bar partial = W^T V_ev on tcgen05 (A = W tiles by TMA,
 //                      B = gathered V rows, MN-major), split over token chunks.
 //   mw_update_kernel : M, b <- (gamma Z M + pi_E eta M_bar) / (Z' + eps).
@@ -22,10 +23,7 @@ namespace core {
 namespace mw {
 
 constexpr int kD = 128;
-constexpr int kTok = 128;         // evicted tokens per MMA M tile of phi
-constexpr int kPhiM = 2;          // M tiles per phi unit: both share every Theta stage
-constexpr int kUnitTok = kPhiM * kTok;
-constexpr int kNCols = 256;       // d_mem columns per phi unit (MMA N)
+constexpr int kTok = 128;         // evicted tokens per phi unit (MMA N)
 constexpr int kProdThreads = 128; // 4 gathering warps
 constexpr int kMbarChunk = 64;    // tokens per M_bar K chunk
 
@@ -147,28 +145,34 @@ struct PhiParams {
   DeviceStatus* status;
 };
 
-constexpr uint32_t kPhiA = kUnitTok * 128;      // 32 KB: 256 tokens x 64 columns (two M tiles)
-constexpr uint32_t kPhiB = 2u * kNCols * 128;   // 64 KB: two terms x 256 rows x 64 columns
+// phi^T tile: M = 128 memory rows of Theta_f (A, two bf16 terms, TMA) x N = 128
+// gathered evicted tokens (B, cp.async), K = the 1024-wide key row in 64-column
+// chunks.  TMEM lanes are memory rows, columns are tokens, so the epilogue
+// writes W^T rows with contiguous token runs and sums b_bar along its own row.
+constexpr int kPhiRows = 128;                    // memory rows per unit (MMA M)
+constexpr uint32_t kPhiA = 2u * kPhiRows * 128;  // 32 KB: two Theta terms x 128 rows x 64 columns
+constexpr uint32_t kPhiB = kTok * 128;           // 16 KB: 128 tokens x 64 columns
 constexpr uint32_t kPhiStage = kPhiA + kPhiB;
-constexpr int kPhiStages = 2;
-constexpr int kPhiLag = kPhiStages - 1;  // gather groups in flight per producer thread
-constexpr int kPhiAhead = 3;             // K chunks prefetched into L2 ahead of the gather
-constexpr int kPhiThreads = 512;  // warps 0-3 gather, 4 MMA, 8-15 epilogue
+constexpr int kPhiStages = 4;
+constexpr int kPhiLag = 2;  // gather groups in flight per producer thread (two stages of MMA slack)
+constexpr int kPhiThreads = 512;         // warps 0-3 gather, 4 MMA, 8-15 epilogue
+constexpr uint32_t kPhiSmem = kPhiStages * kPhiStage + 2 * kTok * 4 + 256 + 1024;
 
 __global__ void __launch_bounds__(kPhiThreads, 1)
     mw_phi_kernel(const __grid_constant__ CUtensorMap tmT, const PhiParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
-  const uint32_t red_off = kPhiStages * kPhiStage;            // float [4][kNCols]
-  float* s_red = reinterpret_cast<float*>(sgen + red_off);
-  const uint32_t bar = sbase + red_off + 4 * kNCols * 4;
+  const uint32_t aux_off = kPhiStages * kPhiStage;
+  float* s_pbar = reinterpret_cast<float*>(sgen + aux_off);  // [128] p_bar of the unit's tokens
+  float* s_bh = s_pbar + kTok;                                // [128] team-1 b_bar halves
+  const uint32_t bar = sbase + aux_off + 2 * kTok * 4;
   auto bar_full = [&](int s) { return bar + 8u * s; };
   auto bar_empty = [&](int s) { return bar + 8u * (kPhiStages + s); };
   auto bar_tfull = [&](int s) { return bar + 8u * (2 * kPhiStages + s); };
   auto bar_tempty = [&](int s) { return bar + 8u * (2 * kPhiStages + 2 + s); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + red_off + 4 * kNCols * 4 + 200);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + red_off + 4 * kNCols * 4 + 208);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + aux_off + 2 * kTok * 4 + 200);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + aux_off + 2 * kTok * 4 + 208);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int P = gridDim.x;
@@ -188,7 +192,7 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
     fence_barrier_init();
   }
   if (warp == 4) {
-    tmem_alloc(smem_u32(tmem_slot), kPhiM * kNCols);
+    tmem_alloc(smem_u32(tmem_slot), 2 * kTok);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -198,69 +202,46 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
   auto wait = [&](uint32_t b, uint32_t parity, int where) -> bool {
     return bounded_wait(b, parity, abort_flag, p.status, where);
   };
-
   if (warp < 4) {
-    // ---- producers: gather K rows with cp.async; thread 0 also loads Theta by TMA ----
+    // ---- producers: Theta by TMA (thread 0), token rows gathered with cp.async ----
     const int tid = threadIdx.x;
     int it = 0;
     bool ok = true;
     for (long long u = u0; u < u1 && ok; ++u) {
-      const int dh = (int)(u % p.n_dh);
+      const int dt = (int)(u % p.n_dh);
       const long long rest = u / p.n_dh;
       const int et = (int)(rest % p.n_et), b = (int)(rest / p.n_et);
-      // the unit's 256 token rows are the same for all its K chunks: load their
-      // indices once (16 rows per thread: r = tid / 8 + 16 i)
-      constexpr int kPer = kUnitTok * 8 / kProdThreads;
+      // the unit's 128 token rows serve all its K chunks: indices loaded once
+      // (8 rows per thread: r = tid / 8 + 16 i)
+      constexpr int kPer = kTok * 8 / kProdThreads;
       int toks[kPer];
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
-        const int kidx = et * kUnitTok + ((tid + i * kProdThreads) >> 3);
+        const int kidx = et * kTok + ((tid + i * kProdThreads) >> 3);
         toks[i] = kidx < p.n_evict ? p.evict[(long long)b * p.n_evict + kidx] : -1;
-      }
-      if ((tid & 7) == 0) {  // the first chunks of the unit into L2
-        for (int ca = 1; ca < kPhiAhead && ca < n_chunks; ++ca) {
-          const long long hoff = ((long long)b * p.Hkv + (ca >> 1)) * p.L;
-#pragma unroll
-          for (int i = 0; i < kPer; ++i)
-            if (toks[i] >= 0) prefetch_l2(p.k + (hoff + toks[i]) * kD + (ca & 1) * 64);
-        }
       }
       for (int c = 0; c < n_chunks && ok; ++c, ++it) {
         const int st = it % kPhiStages;
-        if (it >= kPhiStages) {
-          if (!(ok = wait(bar_empty(st), ((it / kPhiStages) - 1) & 1, 901))) break;
-        }
-        const uint32_t a_base = sbase + st * kPhiStage;
+        if (it >= kPhiStages && !(ok = wait(bar_empty(st), ((it / kPhiStages) - 1) & 1, 901))) break;
+        const uint32_t s_base = sbase + st * kPhiStage;
         if (tid == 0) {
-          mbar_arrive_expect_tx(bar_full(st), kPhiB);
+          mbar_arrive_expect_tx(bar_full(st), kPhiA);
           for (int t = 0; t < 2; ++t)
-            tma_load_3d(a_base + kPhiA + t * (kNCols * 128u), &tmT, bar_full(st), c * 64,
-                        dh * kNCols, t);
+            tma_load_3d(s_base + t * (kPhiRows * 128u), &tmT, bar_full(st), c * 64, dt * kPhiRows, t);
         }
         const int h = c >> 1, e0 = (c & 1) * 64;
-        // 256 rows x 8 sixteen-byte pieces = 2048 copies, 16 per thread; row r
-        // goes to M tile r / 128
+        // 128 rows x 8 sixteen-byte pieces = 1024 copies, 8 per thread
 #pragma unroll
         for (int i = 0; i < kPer; ++i) {
           const int j = tid + i * kProdThreads;
           const int r = j >> 3, q = j & 7;
-          const uint32_t dst = a_base + (uint32_t)(r >> 7) * (kTok * 128u) +
-                               (uint32_t)(r & (kTok - 1)) * 128u + (uint32_t)((q ^ (r & 7)) << 4);
+          const uint32_t dst = s_base + kPhiA + (uint32_t)r * 128u + (uint32_t)((q ^ (r & 7)) << 4);
           if (toks[i] >= 0)
             cp_async16(dst, p.k + (((long long)b * p.Hkv + h) * p.L + toks[i]) * kD + e0 + q * 8);
           else
             st_shared_zero16(dst);
         }
         cp_async_commit();
-        // L2 prefetch of the rows' chunk kPhiAhead stages ahead (the gathers
-        // are latency-bound with two stages of shared memory)
-        if (c + kPhiAhead < n_chunks && (tid & 7) == 0) {
-          const int ca = c + kPhiAhead;
-          const long long hoff = ((long long)b * p.Hkv + (ca >> 1)) * p.L;
-#pragma unroll
-          for (int i = 0; i < kPer; ++i)
-            if (toks[i] >= 0) prefetch_l2(p.k + (hoff + toks[i]) * kD + (ca & 1) * 64);
-        }
         // kPhiLag gather groups stay in flight: publish the oldest one
         if (it >= kPhiLag) {
           cp_async_wait_group<kPhiLag>();
@@ -277,101 +258,93 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
       for (int j = it > kPhiLag ? it - kPhiLag : 0; j < it; ++j) mbar_arrive(bar_full(j % kPhiStages));
   } else if (warp == 4) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(128, kNCols, 0, 0);
+      constexpr uint32_t idesc = idesc_bf16(kPhiRows, kTok, 0, 0);
       int it = 0, sub = 0;
       bool ok = true;
       for (long long u = u0; u < u1 && ok; ++u, ++sub) {
-        // one accumulator set (kPhiM tiles x kNCols columns): wait for the epilogue of the last unit
-        if (sub >= 1 && !(ok = wait(bar_tempty(0), (sub - 1) & 1, 902))) break;
+        const int buf = sub & 1, n = sub >> 1;
+        if (sub >= 2 && !(ok = wait(bar_tempty(buf), (n - 1) & 1, 902))) break;
         tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * kTok);
         for (int c = 0; c < n_chunks && ok; ++c, ++it) {
           const int st = it % kPhiStages;
           if (!(ok = wait(bar_full(st), (it / kPhiStages) & 1, 903))) break;
           tc_fence_after();
-          const uint32_t a_base = sbase + st * kPhiStage;
-          for (int mt = 0; mt < kPhiM; ++mt) {
-            const uint32_t d = tmem + (uint32_t)(mt * kNCols);
-            for (int ks = 0; ks < 4; ++ks) {
-              const uint64_t a = sdesc_kmajor(a_base + (uint32_t)mt * (kTok * 128u) + (uint32_t)ks * 32u);
-              for (int t = 0; t < 2; ++t) {
-                const uint64_t bd = sdesc_kmajor(a_base + kPhiA + (uint32_t)t * kNCols * 128u + (uint32_t)ks * 32u);
-                mma_bf16(d, a, bd, idesc, (c > 0 || ks > 0 || t > 0) ? 1u : 0u);
-              }
+          const uint32_t s_base = sbase + st * kPhiStage;
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t bd = sdesc_kmajor(s_base + kPhiA + (uint32_t)ks * 32u);
+            for (int t = 0; t < 2; ++t) {
+              const uint64_t a = sdesc_kmajor(s_base + (uint32_t)t * kPhiRows * 128u + (uint32_t)ks * 32u);
+              mma_bf16(d, a, bd, idesc, (c > 0 || ks > 0 || t > 0) ? 1u : 0u);
             }
           }
           mma_commit(bar_empty(st));
         }
-        if (ok) mma_commit(bar_tfull(0));
+        if (ok) mma_commit(bar_tfull(buf));
       }
     }
   } else if (warp >= 8) {
-    const int ew = warp - 8;
-    const int team = ew >> 2;       // column half of the unit: [0, 128) or [128, 256)
+    // ---- epilogue: lanes are memory rows, columns tokens ----
+    const int team = (warp - 8) >> 2;  // token half [64 team, 64 team + 64)
     const int wq = warp & 3;
-    const int row = wq * 32 + lane;
+    const int row = wq * 32 + lane;    // memory row inside the unit
+    const int etid = threadIdx.x - 256;
     int sub = 0;
-    bool ok = true;
-    for (long long u = u0; u < u1 && ok; ++u, ++sub) {
-      const int dh = (int)(u % p.n_dh);
+    for (long long u = u0; u < u1; ++u, ++sub) {
+      const int dt = (int)(u % p.n_dh);
       const long long rest = u / p.n_dh;
       const int et = (int)(rest % p.n_et), b = (int)(rest / p.n_et);
-      if (!(ok = wait(bar_tfull(0), sub & 1, 904))) break;
+      named_barrier(1, 256);  // the previous unit's readers of s_pbar / s_bh are done
+      if (etid < kTok) s_pbar[etid] = p.pbar[(long long)b * p.n_ev_pad + et * kTok + etid];
+      const int buf = sub & 1, n = sub >> 1;
+      const bool got = wait(bar_tfull(buf), n & 1, 904);
+      if (!named_barrier_and(1, 256, got)) break;  // uniform: every epilogue warp stops together
       tc_fence_after();
-      for (int mt = 0; mt < kPhiM; ++mt) {
-      const int kidx = et * kUnitTok + mt * kTok + row;
-      const float pb = p.pbar[(long long)b * p.n_ev_pad + kidx];  // 0 on padding rows
-      for (int q4 = 0; q4 < kNCols / 64; ++q4) {
-        const int col0 = team * (kNCols / 2) + q4 * 32;
-        if (dh * kNCols + col0 >= p.d_pad) continue;  // padding columns of the last unit
+      const int drow = dt * kPhiRows + row;  // row of W^T and b_bar (< d_pad)
+      float bsum = 0.f;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int t0 = team * 64 + q * 32;  // first token column of the chunk
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(mt * kNCols + col0), v);
-        const int jbase = dh * kNCols + col0;
-        float u2[32];
+        tmem_ld32(tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * kTok + t0), v);
+        uint32_t hi[16], lo[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float phi = v[j];
-          const float w = phi * pb;                 // phi * w (kvpress_adapter.py:1155)
-          u2[j] = (phi * phi) * pb;                 // (phi*phi) * w (:1157)
-          const __nv_bfloat16 hi = __float2bfloat16_rn(w);
-          const __nv_bfloat16 lo = __float2bfloat16_rn(w - __bfloat162float(hi));
-          const long long o = (long long)(jbase + j) * p.n_ev_pad + kidx;
-          p.wt[o] = hi;
-          p.wt[(long long)p.d_pad * p.n_ev_pad + o] = lo;
+        for (int j = 0; j < 32; j += 2) {
+          const float pb0 = s_pbar[t0 + j], pb1 = s_pbar[t0 + j + 1];
+          const float w0 = v[j] * pb0, w1 = v[j + 1] * pb1;  // phi * w (kvpress_adapter.py:1155)
+          bsum += (v[j] * v[j]) * pb0;                        // (phi*phi) * w (:1157)
+          bsum += (v[j + 1] * v[j + 1]) * pb1;
+          __nv_bfloat162 hh = __floats2bfloat162_rn(w0, w1);
+          const uint32_t hw = *reinterpret_cast<uint32_t*>(&hh);
+          __nv_bfloat162 ll = __floats2bfloat162_rn(w0 - __uint_as_float(hw << 16),
+                                                    w1 - __uint_as_float(hw & 0xFFFF0000u));
+          hi[j >> 1] = hw;
+          lo[j >> 1] = *reinterpret_cast<uint32_t*>(&ll);
         }
-        // column sums over the warp's 32 tokens: lane j ends with column j
+        // 32 tokens of one W^T row: 64 contiguous bytes per term
+        __nv_bfloat16* dst = p.wt + (long long)drow * p.n_ev_pad + et * kTok + t0;
+        uint4* d0 = reinterpret_cast<uint4*>(dst);
+        uint4* d1 = reinterpret_cast<uint4*>(dst + (long long)p.d_pad * p.n_ev_pad);
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-#pragma unroll
-          for (int j = 0; j < off; ++j) {
-            const bool upper = (lane & off) != 0;
-            const float send = upper ? u2[j] : u2[j + off];
-            const float keep = upper ? u2[j + off] : u2[j];
-            u2[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-          }
+        for (int w = 0; w < 4; ++w) {
+          d0[w] = make_uint4(hi[4 * w], hi[4 * w + 1], hi[4 * w + 2], hi[4 * w + 3]);
+          d1[w] = make_uint4(lo[4 * w], lo[4 * w + 1], lo[4 * w + 2], lo[4 * w + 3]);
         }
-        // this thread owns s_red[wq][col0 + lane]: tile 0 stores, tile 1 adds
-        float* sr = s_red + wq * kNCols + col0 + lane;
-        *sr = (mt == 0) ? u2[0] : *sr + u2[0];
-      }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_tempty(0));
+      if (lane == 0) mbar_arrive(bar_tempty(buf));
+      // b_bar partial of this row over the unit's tokens: the two halves in a fixed order
+      if (team == 1) s_bh[row] = bsum;
       named_barrier(1, 256);
-      // fixed-order reduction of the four lane quarters
-      for (int cidx = threadIdx.x - 256; cidx < kNCols && dh * kNCols + cidx < p.d_pad; cidx += 256) {
-        const float s = ((s_red[cidx] + s_red[kNCols + cidx]) + s_red[2 * kNCols + cidx]) +
-                        s_red[3 * kNCols + cidx];
-        p.bpart[((long long)b * p.n_et + et) * p.d_pad + dh * kNCols + cidx] = s;
-      }
-      named_barrier(1, 256);
+      if (team == 0) p.bpart[((long long)b * p.n_et + et) * p.d_pad + drow] = bsum + s_bh[row];
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 4) {
     tc_fence_after();
-    tmem_dealloc(tmem, kPhiM * kNCols);
+    tmem_dealloc(tmem, 2 * kTok);
   }
 }
 
@@ -391,7 +364,7 @@ constexpr uint32_t kMbA = 2u * 128 * 128;           // two terms x 128 rows x 64
 constexpr uint32_t kMbBMax = 4u * kMbarChunk * 128; // up to 4 MN atoms x 64 token rows x 128 B
 constexpr uint32_t kMbStage = kMbA + kMbBMax;       // 64 KB
 constexpr int kMbStages = 3;
-constexpr int kMbLag = kMbStages - 1;  // gather groups in flight per producer thread
+constexpr int kMbLag = 1;  // gather groups in flight per producer thread (two stages of MMA slack)
 constexpr int kMbThreads = 384;  // warps 0-3 gather, 4 MMA, 8-11 epilogue
 
 // CT = value columns per output tile (256, or 128 when Hkv*d is an odd
@@ -480,7 +453,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
         }
       }
       cp_async_commit();
-      // kMbStages - 1 gather groups stay in flight: publish the oldest one
+      // kMbLag gather groups stay in flight: publish the oldest one
       if (it >= kMbLag) {
         cp_async_wait_group<kMbLag>();
         fence_proxy_async_shared();
@@ -589,10 +562,10 @@ struct MwPlan {
   long long phi_units;
 };
 void plan_mw(const core_dims_t* d, int n_evict, int d_mem, MwPlan* m) {
-  m->n_et = (n_evict + kUnitTok - 1) / kUnitTok;
-  m->n_ev_pad = m->n_et * kUnitTok;
+  m->n_et = (n_evict + kTok - 1) / kTok;
+  m->n_ev_pad = m->n_et * kTok;
   m->d_pad = ((d_mem + 127) / 128) * 128;
-  m->n_dh = (m->d_pad + kNCols - 1) / kNCols;
+  m->n_dh = m->d_pad / kPhiRows;
   m->kvw = d->n_kv_heads * kD;
   m->phi_units = (long long)d->batch * m->n_et * m->n_dh;
   const int sms = sm_count();
@@ -672,7 +645,7 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
     const uint64_t kvw = (uint64_t)m.kvw;
     uint64_t dims[3] = {kvw, (uint64_t)d_mem, 2};
     uint64_t str[2] = {kvw * 2, kvw * 2 * (uint64_t)d_mem};
-    uint32_t box[3] = {64, (uint32_t)kNCols, 1};
+    uint32_t box[3] = {64, (uint32_t)kPhiRows, 1};
     if ((rc = make_tmap_bf16(&tmT, theta_split, 3, dims, str, box, true)) != CORE_OK) return rc;
   }
   // W^T is (2, d_pad, n_ev_pad); each batch row reuses the same buffer, so
@@ -684,7 +657,7 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
     uint32_t box[2] = {64, 128};
     if ((rc = make_tmap_bf16(&tmW, wt, 2, dims, str, box, true)) != CORE_OK) return rc;
   }
-  const uint32_t phi_smem = kPhiStages * kPhiStage + 4 * kNCols * 4 + 256 + 1024;
+  const uint32_t phi_smem = kPhiSmem;
   e = cudaFuncSetAttribute(mw_phi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, phi_smem);
   if (e != cudaSuccess) return cuda_error(e, "mw_phi_kernel attribute");
   const uint32_t mb_smem = kMbStages * kMbStage + 256 + 1024;
