@@ -42,7 +42,7 @@ KERNELS_PER_LAYER = 16
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--steps", type=int, default=60)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--layers", type=int, default=32)
@@ -67,6 +67,28 @@ def config_dict(a, n):
             "d_mem": a.d_mem, "parallelism": f"batch-sharded x{n}",
             "l2": "inputs larger than L2 (32 layers x 64 MiB of K/V per step)",
             "layers_in_flight": a.streams, "sm_reserve": a.sm_reserve if a.streams > 1 else 0}
+
+
+# ---------------------------------------------------------------------------
+# multi-rank plumbing (batch sharding: no collective on the data path)
+# ---------------------------------------------------------------------------
+def max_over_ranks(x: float, dist, device) -> float:
+    """The slowest rank's value; every rank calls this at the same point."""
+    if dist is None:
+        return float(x)
+    t = torch.tensor([float(x)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def whole_job_rate(n_ranks: int, tokens_per_rank: int, seconds: float) -> float:
+    """Tokens compressed per second by all ranks together, timed by the slowest."""
+    return n_ranks * tokens_per_rank / seconds
+
+
+def rank_seed(rank: int) -> int:
+    """Each rank compresses its own synthetic sequence."""
+    return 1000 + 7919 * rank
 
 
 # ---------------------------------------------------------------------------
@@ -222,7 +244,7 @@ def main():
     n = world
     from core_b200 import engine, ops
 
-    parts, layers = build_layers(a, dev)
+    parts, layers = build_layers(a, dev, seed_base=rank_seed(rank))
     L = a.seq_len
     n_kept = engine.n_kept_for(L, a.ratio, 4)
     pos = torch.arange(L, device=dev)[None]
@@ -268,11 +290,8 @@ def main():
     ms = t0.elapsed_time(t1) / a.steps
     relation_ms = [e0.elapsed_time(e1) for pairs in ev for e0, e1 in pairs]
     ops.status(dev)
-    if dist is not None:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    value = n * L / (ms / 1e3)
+    ms = max_over_ranks(ms, dist, dev)
+    value = whole_job_rate(n, L, ms / 1e3)
 
     # ---- roofline of the dominant kernel (QK relation pass) ----
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -393,12 +412,9 @@ def run_e2e(a, dev, parts, layers, dist):
         step()
     torch.cuda.synchronize()
     dt = (time.perf_counter() - t0) / a.e2e_steps
-    if dist is not None:
-        t = torch.tensor([dt], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dt = float(t.item())
+    dt = max_over_ranks(dt, dist, dev)
     n = dist.get_world_size() if dist is not None else 1
-    return {"value": n * L / dt, "unit": UNIT, "h2d_bytes_per_step": h2d,
+    return {"value": whole_job_rate(n, L, dt), "unit": UNIT, "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h_per_step[0], "ms_per_step": dt * 1e3,
             "steps": a.e2e_steps,
             "path": "core_b200.press.COREMemoryPress.compress per layer, inputs from pinned host "
