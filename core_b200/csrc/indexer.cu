@@ -127,17 +127,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   // ---- once per CTA: W2 as three bf16 terms, (out, in) K-major SW128 ----
   // unit u: output row o = u % 128, 8-column chunk c = u / 128 (coalesced reads of w2^T)
-  for (int u = tid; u < kHid * (kHid / 8); u += kThreads) {
-    const int o = u & (kHid - 1), c = u >> 7;
-    float x[8];
+  // all 64 values of this thread's 8 units are loaded before any is stored, so
+  // the global loads overlap
+  constexpr int kUnitsPerThread = kHid * (kHid / 8) / kThreads;
+  static_assert(kHid * (kHid / 8) % kThreads == 0, "W2 staging layout");
+  {
+    float x[kUnitsPerThread][8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = p.mlp[kGW2T + (8 * c + i) * kHid + o];
-    uint4 t0, t1, t2;
-    split3(x, t0, t1, t2);
-    const uint32_t off = sw128_chunk(o, c >> 3, c & 7);
-    st_shared_v4(sbase + kOffW + off, t0);
-    st_shared_v4(sbase + kOffW + kTermBytes + off, t1);
-    st_shared_v4(sbase + kOffW + 2 * kTermBytes + off, t2);
+    for (int k = 0; k < kUnitsPerThread; ++k) {
+      const int u = tid + k * kThreads;
+      const int o = u & (kHid - 1), c = u >> 7;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[k][i] = p.mlp[kGW2T + (8 * c + i) * kHid + o];
+    }
+#pragma unroll
+    for (int k = 0; k < kUnitsPerThread; ++k) {
+      const int u = tid + k * kThreads;
+      const int o = u & (kHid - 1), c = u >> 7;
+      uint4 t0, t1, t2;
+      split3(x[k], t0, t1, t2);
+      const uint32_t off = sw128_chunk(o, c >> 3, c & 7);
+      st_shared_v4(sbase + kOffW + off, t0);
+      st_shared_v4(sbase + kOffW + kTermBytes + off, t1);
+      st_shared_v4(sbase + kOffW + 2 * kTermBytes + off, t2);
+    }
   }
   for (int i = tid; i < kHid * kIn; i += kThreads)
     sf[kFW1 + (i / kIn) * kW1Stride + (i % kIn)] = p.mlp[kGW1 + i];
