@@ -227,6 +227,38 @@ def test_memory_write_matches_reference(name):
     assert abs(float(Z[0]) - float(gZ[0])) <= 1e-6
 
 
+@pytest.mark.parametrize("d_mem,L,hkv", [(512, 1536, 8), (256, 1000, 8), (384, 700, 4)])
+def test_memory_write_matches_oracle_wide_memory(d_mem, L, hkv):
+    """Memory widths whose M_bar tiles pair up (d_mem a multiple of 256) and
+    ones that do not; evicted counts that are not multiples of the tiles."""
+    from core_b200 import engine, ops
+    dev = _dev()
+    hq = 4 * hkv
+    rng = np.random.default_rng(d_mem + L)
+    k = O.bf16_round(rng.standard_normal((hkv, L, 128), dtype=np.float32) / np.float32(np.sqrt(128)))
+    v = O.bf16_round(rng.standard_normal((hkv, L, 128), dtype=np.float32))
+    scores = (rng.standard_normal(L) * 0.05).astype(np.float32)
+    theta = (rng.standard_normal((d_mem, hq * 128)) / np.sqrt(hq * 128)).astype(np.float32)
+    n_kept = L // 4
+    keep = O.topb_select(scores[None], n_kept, 4)[0]
+    evict = np.setdiff1d(np.arange(L), keep)
+    mask = np.zeros(L, bool)
+    mask[evict] = True
+    ref_M, ref_b, ref_Z = O.memory_write(k, v, scores, mask, theta, groups=4)
+    ts = ops.split_bf16(engine.fold_groups(_f32(theta, dev), hkv, 4, 128), 2)
+    M = torch.zeros(1, d_mem, hkv * 128, device=dev)
+    b = torch.zeros(1, d_mem, device=dev)
+    Z = torch.zeros(1, device=dev)
+    ops.memory_write(_bf16(k, dev)[None], _bf16(v, dev)[None], _f32(scores, dev)[None],
+                     torch.from_numpy(evict.astype(np.int32)).to(dev)[None], ts, M, b, Z,
+                     gamma=0.9, eta=1.0, student_temp=1.0)
+    ops.status()
+    tol = 2e-3
+    assert np.abs(M[0].cpu().numpy() - ref_M).max() <= tol * np.abs(ref_M).max()
+    assert np.abs(b[0].cpu().numpy() - ref_b).max() <= tol * np.abs(ref_b).max()
+    assert abs(float(Z[0]) - float(ref_Z)) <= 1e-6
+
+
 def test_compact_kv_is_exact_gather():
     from core_b200 import ops, synthetic
     dev = _dev()
