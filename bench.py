@@ -18,6 +18,7 @@ algorithm (oracle/core_oracle.py) on the host cores instead.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -47,6 +48,7 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--seq-len", type=int, default=16384)
+    p.add_argument("--batch", type=int, default=1, help="sequences per rank (batched serving)")
     p.add_argument("--n-queries", type=int, default=128)
     p.add_argument("--ratio", type=float, default=0.75)
     p.add_argument("--d-mem", type=int, default=512)
@@ -59,9 +61,9 @@ def parse():
 
 
 def config_dict(a, n):
-    return {"workload": f"core_full compression step, {a.layers} layers x 1 sequence x "
+    return {"workload": f"core_full compression step, {a.layers} layers x {a.batch} sequence(s) x "
                         f"{a.seq_len} tokens per rank",
-            "layers": a.layers, "batch_per_rank": 1, "seq_len": a.seq_len,
+            "layers": a.layers, "batch_per_rank": a.batch, "seq_len": a.seq_len,
             "n_kv_heads": 8, "n_q_heads": 32, "head_dim": 128, "query_buffer": a.n_queries,
             "compression_ratio": a.ratio, "n_kept": int(a.seq_len * (1 - a.ratio)),
             "d_mem": a.d_mem, "parallelism": f"batch-sharded x{n}",
@@ -212,14 +214,14 @@ def build_layers(a, dev, seed_base=1000):
     geo = parts["geometry"]
     layers = []
     for l in range(a.layers):
-        q, k, v = synthetic.make_layer_inputs(seed=seed_base + 7 * l, batch=1, n_kv_heads=8,
+        q, k, v = synthetic.make_layer_inputs(seed=seed_base + 7 * l, batch=a.batch, n_kv_heads=8,
                                               n_q_heads=32, seq_len=a.seq_len,
                                               n_queries=a.n_queries, device=dev)
         lw = engine.LayerWeights.prepare(
             geometry=geo.weight[l], prototypes=geo.prototypes, hadamard=geo.hadamard,
             mlp_params=parts["indexer"].modules[l], theta=parts["memory"].modules[l][0],
             n_kv_heads=8, n_q_heads=32, device=dev)
-        mem = engine.MemoryState.zeros(1, a.d_mem, 8 * 128, dev)
+        mem = engine.MemoryState.zeros(a.batch, a.d_mem, 8 * 128, dev)
         layers.append((q, k, v, lw, mem))
     return parts, layers
 
@@ -247,8 +249,14 @@ def main():
     parts, layers = build_layers(a, dev, seed_base=rank_seed(rank))
     L = a.seq_len
     n_kept = engine.n_kept_for(L, a.ratio, 4)
-    pos = torch.arange(L, device=dev)[None]
-    ws = [torch.empty(64 << 20, dtype=torch.uint8, device=dev) for _ in range(a.streams)]
+    pos = torch.arange(L, device=dev)[None].expand(a.batch, L).contiguous()
+    n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    budget = ops.sm_budget(max(1, n_sms - a.sm_reserve) if a.streams > 1 else 0)
+    # one workspace per stream, sized under the SM budget the launches will plan with
+    from core_b200 import _lib
+    dims = _lib.CoreDims(a.batch, 32, 8, 128, a.n_queries, L, _lib.CORE_DTYPE_BF16)
+    need = _lib.load().core_compress_layer_workspace_bytes(ctypes.byref(dims), n_kept, a.d_mem)
+    ws = [torch.empty(int(need), dtype=torch.uint8, device=dev) for _ in range(a.streams)]
     # one (start, end) pair per layer and timed step, around the QK relation kernel
     ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(a.layers)] for _ in range(a.steps)]
@@ -257,8 +265,6 @@ def main():
             e0.record()
             e1.record()
     torch.cuda.synchronize()
-    n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    budget = ops.sm_budget(max(1, n_sms - a.sm_reserve) if a.streams > 1 else 0)
 
     def step(pairs):
         jobs = [dict(q=q, keys=k, values=v, weights=lw, positions=pos, memory=mem,
@@ -291,7 +297,7 @@ def main():
     relation_ms = [e0.elapsed_time(e1) for pairs in ev for e0, e1 in pairs]
     ops.status(dev)
     ms = max_over_ranks(ms, dist, dev)
-    value = whole_job_rate(n, L, ms / 1e3)
+    value = whole_job_rate(n, a.batch * L, ms / 1e3)
 
     # ---- roofline of the dominant kernel (QK relation pass) ----
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -315,7 +321,7 @@ def main():
                 "algorithmic": f"2*Hq*nq*L*d = {flops / 1e9:.2f} GFLOP per launch"}
 
     # ---- end to end through the press API with host buffers ----
-    e2e = run_e2e(a, dev, parts, layers, dist)
+    e2e = run_e2e(a, dev, parts, layers, dist) if a.e2e_steps > 0 else None
 
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -355,8 +361,8 @@ def run_e2e(a, dev, parts, layers, dist):
     host = []
     for (q, k, v, _, _) in layers:
         host.append((q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()))
-    full_q = torch.zeros(1, 32, L, 128, dtype=torch.bfloat16, device=dev)
-    hs = torch.zeros(1, L, 1, device=dev)
+    full_q = torch.zeros(a.batch, 32, L, 128, dtype=torch.bfloat16, device=dev)
+    hs = torch.zeros(a.batch, L, 1, device=dev)
     mods = [_FakeAttn(l) for l in range(a.layers)]
     h2d = sum(t.numel() * t.element_size() for h in host for t in h)
     d2h_per_step = [0]
