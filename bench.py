@@ -54,6 +54,12 @@ def parse():
     p.add_argument("--d-mem", type=int, default=512)
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", default="prefill", choices=["prefill", "decode"],
+                   help="prefill: the headline 32-layer compression step; decode: decode-time "
+                        "recompression with the memory readout")
+    p.add_argument("--decode-tokens", type=int, default=512)
+    p.add_argument("--interval", type=int, default=128)
+    p.add_argument("--decode-ratio", type=float, default=0.5)
     p.add_argument("--streams", type=int, default=3, help="layers compressed concurrently")
     p.add_argument("--sm-reserve", type=int, default=2,
                    help="SMs the persistent grids leave free for the other streams' kernels")
@@ -246,6 +252,14 @@ def main():
     n = world
     from core_b200 import engine, ops
 
+    if a.workload == "decode":
+        line = run_decode(a, dev, dist, rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     parts, layers = build_layers(a, dev, seed_base=rank_seed(rank))
     L = a.seq_len
     n_kept = engine.n_kept_for(L, a.ratio, 4)
@@ -336,6 +350,151 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# decode-time recompression (prefill, then decode with readout every step)
+# ---------------------------------------------------------------------------
+DECODE_METRIC = "KV tokens recompressed/sec during decode (readout every step), 32 layers"
+
+
+def run_decode(a, dev, dist, rank):
+    """Prefill compression of every layer to ratio ``--decode-ratio`` (not
+    timed), then ``--decode-tokens`` decode steps: every step appends one K/V
+    row per layer and applies the memory readout to that layer's attention
+    output; every ``--interval`` steps each layer is recompressed back to the
+    post-prefill size with the buffered queries (decode branch).  Decode-step
+    K/V rows, post-RoPE queries and attention outputs are synthetic
+    (the query projection and RoPE of the reference's decode path are library
+    GEMMs and are not part of the timed work)."""
+    from core_b200 import checkpoint as C
+    from core_b200 import engine, ops, synthetic
+    L0, nq, hkv, hq, d = a.seq_len, a.n_queries, 8, 32, 128
+    seed = rank_seed(rank)
+    parts = C.random_checkpoint_parts(seed=seed, n_layers=a.layers, n_kv_heads=hkv, n_q_heads=hq,
+                                      d_mem=a.d_mem)
+    geo = parts["geometry"]
+    n_keep = engine.n_kept_for(L0, a.decode_ratio, 4)
+    cap = n_keep + a.interval
+    g = torch.Generator(device=dev).manual_seed(seed)
+    layers = []
+    for l in range(a.layers):
+        q, k, v = synthetic.make_layer_inputs(seed=seed + 7 * l, batch=1, n_kv_heads=hkv,
+                                              n_q_heads=hq, seq_len=L0, n_queries=nq, device=dev)
+        lw = engine.LayerWeights.prepare(
+            geometry=geo.weight[l], prototypes=geo.prototypes, hadamard=geo.hadamard,
+            mlp_params=parts["indexer"].modules[l], theta=parts["memory"].modules[l][0],
+            n_kv_heads=hkv, n_q_heads=hq, device=dev)
+        mem = engine.MemoryState.zeros(1, a.d_mem, hkv * d, dev)
+        out = engine.compress_layer(q, k, v, lw, n_kept=n_keep,
+                                    positions=torch.arange(L0, device=dev)[None],
+                                    original_length=L0, is_prefill=True, memory=mem)
+        K = torch.empty(1, hkv, cap, d, dtype=torch.bfloat16, device=dev)
+        V = torch.empty_like(K)
+        K[:, :, :n_keep] = out["keys"]
+        V[:, :, :n_keep] = out["values"]
+        pos = torch.empty(1, cap, dtype=torch.int64, device=dev)
+        pos[:, :n_keep] = out["keep"].to(torch.int64)
+        th, gw1, gb1, gw2, gb2 = (t.to(dev).float() for t in parts["memory"].params(l))
+        o_proj = torch.randn(hq * d, hq * d, device=dev, generator=g) / (hq * d) ** 0.5
+        layers.append(dict(K=K, V=V, pos=pos, lw=lw, mem=mem, theta=th.contiguous(),
+                           gate=(gw1.contiguous(), gb1.contiguous(), gw2.reshape(-1).contiguous(),
+                                 gb2.reshape(-1).contiguous()),
+                           o_fold=engine.fold_groups(o_proj, hkv, hq // hkv, d)))
+    steps = a.decode_tokens
+    new_kv = (torch.randn(steps, a.layers, 2, hkv, d, device=dev, generator=g)).to(torch.bfloat16)
+    new_q = (torch.randn(steps, a.layers, hq, d, device=dev, generator=g) / d ** 0.5).to(torch.bfloat16)
+    attn = torch.randn(1, 1, hq * d, device=dev, generator=g).to(torch.bfloat16)
+    qbuf = [torch.empty(1, hq, a.interval, d, dtype=torch.bfloat16, device=dev)
+            for _ in range(a.layers)]
+
+    clock = [L0]  # absolute position of the next decoded token (runs on across passes)
+    # The memory readout of one decode step for all layers, replayed as a CUDA
+    # graph: the per-step inputs are copied into static buffers first.
+    from core_b200 import _lib
+    rdims = _lib.CoreDims(1, hq, hkv, d, 1, 1, _lib.CORE_DTYPE_BF16)
+    ws_ro = torch.empty(int(_lib.load().core_memory_readout_workspace_bytes(
+        ctypes.byref(rdims), 1, a.d_mem, layers[0]["gate"][0].shape[0])) + 256,
+        dtype=torch.uint8, device=dev)
+    q_static = torch.empty(a.layers, 1, hq, 1, d, dtype=torch.bfloat16, device=dev)
+    attn_static = torch.empty(a.layers, 1, 1, hq * d, dtype=torch.bfloat16, device=dev)
+
+    def readouts():
+        for l, st in enumerate(layers):
+            attn_static[l].copy_(attn)
+            ops.memory_readout(q_static[l], st["theta"], st["gate"], st["mem"].M, st["mem"].b,
+                               st["o_fold"], attn_static[l], n_kv_heads=hkv, workspace=ws_ro)
+
+    q_static.copy_(new_q[0].view(a.layers, 1, hq, 1, d))
+    readouts()  # eager once: kernel attributes are set outside the capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        readouts()
+
+    def decode_phase(readout_only=False):
+        recompressed = 0
+        for blk in range(steps // a.interval):
+            s0 = blk * a.interval
+            if not readout_only:
+                # the interval's new K/V rows (written by the attention layers in a model)
+                for l, st in enumerate(layers):
+                    rows = new_kv[s0:s0 + a.interval, l]  # (interval, 2, hkv, d)
+                    st["K"][0, :, n_keep:cap] = rows[:, 0].transpose(0, 1)
+                    st["V"][0, :, n_keep:cap] = rows[:, 1].transpose(0, 1)
+                    st["pos"][0, n_keep:cap] = torch.arange(clock[0], clock[0] + a.interval,
+                                                            device=dev)
+                    qbuf[l].copy_(new_q[s0:s0 + a.interval, l].transpose(0, 1)[None])
+            for step in range(s0, s0 + a.interval):
+                q_static.copy_(new_q[step].view(a.layers, 1, hq, 1, d))
+                graph.replay()
+            if readout_only:
+                continue
+            clock[0] += a.interval
+            for l, st in enumerate(layers):
+                r = engine.compress_layer(
+                    qbuf[l], st["K"], st["V"], st["lw"], n_kept=n_keep, positions=st["pos"],
+                    original_length=clock[0], is_prefill=False, memory=st["mem"])
+                st["K"][:, :, :n_keep] = r["keys"]
+                st["V"][:, :, :n_keep] = r["values"]
+                st["pos"][0, :n_keep] = st["pos"][0][r["keep"][0].long()]
+                recompressed += cap
+        return recompressed
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        return r, e0.elapsed_time(e1)
+
+    decode_phase()  # warm-up pass (memory states keep evolving, as in a real sequence)
+    ops.status(dev)
+    tokens, ms = timed(decode_phase)
+    _, ms_readout = timed(lambda: decode_phase(readout_only=True))
+    ops.status(dev)
+    ms = max_over_ranks(ms, dist, dev)
+    ms_readout = max_over_ranks(ms_readout, dist, dev)
+    n = dist.get_world_size() if dist is not None else 1
+    return {"metric": DECODE_METRIC, "value": whole_job_rate(n, tokens, ms / 1e3),
+            "unit": UNIT, "n_gpus": n, "steps": 1, "warmup": 1, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"decode-time recompression: prefill {L0} tokens to "
+                                   f"{n_keep}, {steps} decode steps, recompression every "
+                                   f"{a.interval} steps ({steps // a.interval} per layer), "
+                                   f"memory readout every step, {a.layers} layers",
+                       "layers": a.layers, "prefill_tokens": L0, "decode_tokens": steps,
+                       "compression_interval": a.interval, "compression_ratio": a.decode_ratio,
+                       "retained": n_keep, "d_mem": a.d_mem},
+            "readout_us_per_layer_step": ms_readout * 1e3 / (steps * a.layers),
+            "recompressed_tokens": tokens}
 
 
 class _FakeAttn:

@@ -37,12 +37,17 @@ __device__ __forceinline__ float gelu(float x) {
 }
 
 // Stage 1: proj = Theta q (d_mem rows) and gate pre-activations W1 q + c1 (gh
-// rows).  One warp per weight row, all q_len queries at once.
-__global__ void readout_proj_kernel(const __nv_bfloat16* __restrict__ q, int Hq, int q_len,
-                                    const float* __restrict__ theta, const float* __restrict__ gw1,
-                                    const float* __restrict__ gb1, int d_mem, int gh,
-                                    float* __restrict__ proj, float* __restrict__ gpre) {
+// rows).  Two warps per weight row (each half of the row, all of its loads in
+// flight at once), the halves added in order; all q_len queries per row.
+constexpr int kProjWarps = 8;  // 4 rows per block
+
+__global__ void __launch_bounds__(kProjWarps * 32)
+    readout_proj_kernel(const __nv_bfloat16* __restrict__ q, int Hq, int q_len,
+                        const float* __restrict__ theta, const float* __restrict__ gw1,
+                        const float* __restrict__ gb1, int d_mem, int gh,
+                        float* __restrict__ proj, float* __restrict__ gpre) {
   extern __shared__ float sq[];  // (q_len, Hq*d) f32 of this batch row
+  __shared__ float s_half[kProjWarps];
   const int b = blockIdx.y;
   const int dm = Hq * kD;
   for (int i = threadIdx.x; i < q_len * dm; i += blockDim.x) {
@@ -51,62 +56,90 @@ __global__ void readout_proj_kernel(const __nv_bfloat16* __restrict__ q, int Hq,
     sq[i] = __bfloat162float(q[(((long long)b * Hq + qh) * q_len + t) * kD + e]);
   }
   __syncthreads();
-  const int warps = blockDim.x / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = blockIdx.x * warps + warp; r < d_mem + gh; r += gridDim.x * warps) {
-    const float* w = (r < d_mem) ? theta + (long long)r * dm : gw1 + (long long)(r - d_mem) * dm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = warp & 1;
+  const int half_len = dm / 2;  // a multiple of 128 (dm = Hq * 128, Hq even)
+  for (int r0 = blockIdx.x * (kProjWarps / 2); r0 < d_mem + gh; r0 += gridDim.x * (kProjWarps / 2)) {
+    const int r = r0 + (warp >> 1);
+    const bool live = r < d_mem + gh;
+    const float* w = !live ? theta
+                     : (r < d_mem) ? theta + (long long)r * dm : gw1 + (long long)(r - d_mem) * dm;
     for (int t = 0; t < q_len; ++t) {
-      const float* x = sq + t * dm;
+      const float* x = sq + t * dm + half * half_len;
+      const float* wh = w + half * half_len;
       float acc = 0.f;
-      for (int c = lane * 4; c < dm; c += 128) {
-        const float4 ww = *reinterpret_cast<const float4*>(w + c);
-        acc = fmaf(ww.x, x[c], acc);
-        acc = fmaf(ww.y, x[c + 1], acc);
-        acc = fmaf(ww.z, x[c + 2], acc);
-        acc = fmaf(ww.w, x[c + 3], acc);
+      if (live) {
+#pragma unroll 16
+        for (int c = lane * 4; c < half_len; c += 128) {
+          const float4 ww = *reinterpret_cast<const float4*>(wh + c);
+          acc = fmaf(ww.x, x[c], acc);
+          acc = fmaf(ww.y, x[c + 1], acc);
+          acc = fmaf(ww.z, x[c + 2], acc);
+          acc = fmaf(ww.w, x[c + 3], acc);
+        }
       }
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) {
-        if (r < d_mem) proj[((long long)b * q_len + t) * d_mem + r] = acc;
-        else gpre[((long long)b * q_len + t) * gh + (r - d_mem)] = acc + gb1[r - d_mem];
+      if (lane == 0) s_half[warp] = acc;
+      __syncthreads();
+      if (live && half == 0 && lane == 0) {
+        const float v = acc + s_half[warp + 1];
+        if (r < d_mem) proj[((long long)b * q_len + t) * d_mem + r] = v;
+        else gpre[((long long)b * q_len + t) * gh + (r - d_mem)] = v + gb1[r - d_mem];
       }
+      __syncthreads();
     }
   }
 }
 
 // Stage 2: m = proj M / sqrt(proj^2 . b + eps), gate, residual rounded to bf16.
-__global__ void readout_mem_kernel(const float* __restrict__ proj, const float* __restrict__ gpre,
-                                   const float* __restrict__ gw2, const float* __restrict__ gb2,
-                                   float gate_override, const float* __restrict__ M,
-                                   const float* __restrict__ bst, int q_len, int d_mem, int gh,
-                                   int kvw, float* __restrict__ res) {
+// A block covers 32 value columns (one per lane); its 8 warps split the d_mem
+// rows of M and their partial sums are added in warp order.
+constexpr int kMemWarps = 16;
+
+__global__ void __launch_bounds__(kMemWarps * 32)
+    readout_mem_kernel(const float* __restrict__ proj, const float* __restrict__ gpre,
+                       const float* __restrict__ gw2, const float* __restrict__ gb2,
+                       float gate_override, const float* __restrict__ M,
+                       const float* __restrict__ bst, int q_len, int d_mem, int gh, int kvw,
+                       float* __restrict__ res) {
   extern __shared__ float sp[];  // proj (d_mem) of this (b, t)
   __shared__ float s_den, s_g;
+  __shared__ float s_part[kMemWarps][32];
   const int b = blockIdx.y, t = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* pr = proj + ((long long)b * q_len + t) * d_mem;
   for (int j = threadIdx.x; j < d_mem; j += blockDim.x) sp[j] = pr[j];
   __syncthreads();
-  if (threadIdx.x < 32) {
+  if (warp == 0) {
     float den = 0.f;
-    for (int j = threadIdx.x; j < d_mem; j += 32) den = fmaf(sp[j] * sp[j], bst[(long long)b * d_mem + j], den);
+    for (int j = lane; j < d_mem; j += 32) den = fmaf(sp[j] * sp[j], bst[(long long)b * d_mem + j], den);
     for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
     float gl = 0.f;
-    for (int o = threadIdx.x; o < gh; o += 32)
+    for (int o = lane; o < gh; o += 32)
       gl = fmaf(gw2[o], gelu(gpre[((long long)b * q_len + t) * gh + o]), gl);
     for (int o = 16; o > 0; o >>= 1) gl += __shfl_xor_sync(0xffffffffu, gl, o);
-    if (threadIdx.x == 0) {
+    if (lane == 0) {
       s_den = den + 1e-8f;
       s_g = gate_override >= 0.f ? gate_override : 1.0f / (1.0f + expf(-(gl + gb2[0])));
     }
   }
-  __syncthreads();
-  const float rs = 1.0f / sqrtf(s_den);
-  const float g = s_g;
+  const int c = blockIdx.x * 32 + lane;
   const float* Mb = M + (long long)b * d_mem * kvw;
-  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < kvw; c += gridDim.x * blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < d_mem; ++j) acc = fmaf(sp[j], Mb[(long long)j * kvw + c], acc);
-    const float m = acc * rs;
-    res[((long long)b * q_len + t) * kvw + c] = bf16_round(g * m);
+  const int j0 = (int)((long long)warp * d_mem / kMemWarps);
+  const int j1 = (int)((long long)(warp + 1) * d_mem / kMemWarps);
+  float acc = 0.f;
+  if (c < kvw) {
+#pragma unroll 32
+    for (int j = j0; j < j1; ++j) acc = fmaf(sp[j], Mb[(long long)j * kvw + c], acc);
+  }
+  s_part[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && c < kvw) {
+    float m = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMemWarps; ++w) m += s_part[w][lane];
+    m *= 1.0f / sqrtf(s_den);
+    res[((long long)b * q_len + t) * kvw + c] = bf16_round(s_g * m);
   }
 }
 
@@ -120,23 +153,37 @@ __global__ void readout_out_kernel(const float* __restrict__ res, const float* _
     sr[i] = res[(long long)b * q_len * kvw + i];
   __syncthreads();
   const int warps = blockDim.x / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int o = blockIdx.x * warps + warp; o < hidden; o += gridDim.x * warps) {
-    const float* w = ofold + (long long)o * kvw;
+  const int stride = gridDim.x * warps;
+  // two output rows per iteration, so that both rows' loads are in flight together
+  for (int o0 = blockIdx.x * warps + warp; o0 < hidden; o0 += 2 * stride) {
+    const int o1 = o0 + stride;
+    const bool has1 = o1 < hidden;
+    const float* w0 = ofold + (long long)o0 * kvw;
+    const float* w1 = ofold + (long long)(has1 ? o1 : o0) * kvw;
     for (int t = 0; t < q_len; ++t) {
       const float* x = sr + t * kvw;
-      float acc = 0.f;
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 8
       for (int c = lane * 4; c < kvw; c += 128) {
-        const float4 ww = *reinterpret_cast<const float4*>(w + c);
-        acc = fmaf(ww.x, x[c], acc);
-        acc = fmaf(ww.y, x[c + 1], acc);
-        acc = fmaf(ww.z, x[c + 2], acc);
-        acc = fmaf(ww.w, x[c + 3], acc);
+        const float4 a = *reinterpret_cast<const float4*>(w0 + c);
+        const float4 bb = *reinterpret_cast<const float4*>(w1 + c);
+        acc0 = fmaf(a.x, x[c], acc0);
+        acc0 = fmaf(a.y, x[c + 1], acc0);
+        acc0 = fmaf(a.z, x[c + 2], acc0);
+        acc0 = fmaf(a.w, x[c + 3], acc0);
+        acc1 = fmaf(bb.x, x[c], acc1);
+        acc1 = fmaf(bb.y, x[c + 1], acc1);
+        acc1 = fmaf(bb.z, x[c + 2], acc1);
+        acc1 = fmaf(bb.w, x[c + 3], acc1);
       }
-      for (int s = 16; s > 0; s >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, s);
+      for (int s = 16; s > 0; s >>= 1) {
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, s);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, s);
+      }
       if (lane == 0) {
-        __nv_bfloat16* dst = out + ((long long)b * q_len + t) * hidden + o;
-        const float r = bf16_round(acc);
-        *dst = __float2bfloat16_rn(__bfloat162float(*dst) + r);
+        __nv_bfloat16* row = out + ((long long)b * q_len + t) * hidden;
+        row[o0] = __float2bfloat16_rn(__bfloat162float(row[o0]) + bf16_round(acc0));
+        if (has1) row[o1] = __float2bfloat16_rn(__bfloat162float(row[o1]) + bf16_round(acc1));
       }
     }
   }
@@ -215,16 +262,16 @@ extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const vo
     e = cudaFuncSetAttribute(readout_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_error(e, "readout_proj attribute");
     const int rows = d_mem + gh;
-    int bx = (rows + 7) / 8;
+    int bx = (rows + kProjWarps / 2 - 1) / (kProjWarps / 2);  // two warps per weight row
     if (bx > sms) bx = sms;
-    readout_proj_kernel<<<dim3(bx, d->batch), 256, smem, s>>>(static_cast<const __nv_bfloat16*>(q),
+    readout_proj_kernel<<<dim3(bx, d->batch), kProjWarps * 32, smem, s>>>(static_cast<const __nv_bfloat16*>(q),
                                                              d->n_q_heads, q_len, theta, gate_w1,
                                                              gate_b1, d_mem, gh, proj, gpre);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_proj launch");
   }
   {
     const size_t smem = (size_t)d_mem * 4;
-    readout_mem_kernel<<<dim3((kvw + 255) / 256, d->batch, q_len), 256, smem, s>>>(
+    readout_mem_kernel<<<dim3((kvw + 31) / 32, d->batch, q_len), kMemWarps * 32, smem, s>>>(
         proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, res);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_mem launch");
   }

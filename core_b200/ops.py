@@ -216,10 +216,13 @@ def compact_kv(k: torch.Tensor, v: torch.Tensor, keep: torch.Tensor):
 
 def memory_readout(q: torch.Tensor, theta: torch.Tensor, gate, M: torch.Tensor,
                    b_state: torch.Tensor, o_fold: torch.Tensor, attn_out: torch.Tensor,
-                   *, n_kv_heads: int, gate_override: float | None = None) -> torch.Tensor:
+                   *, n_kv_heads: int, gate_override: float | None = None,
+                   workspace: torch.Tensor | None = None) -> torch.Tensor:
     """attn_out (B, q_len, hidden) bf16 += o_fold(g(q) m(q)); updated in place and returned.
 
-    gate = (w1 (gh, Hq*d), b1 (gh), w2 (gh), b2 (1)) f32 tensors.
+    gate = (w1 (gh, Hq*d), b1 (gh), w2 (gh), b2 (1)) f32 tensors.  ``workspace``:
+    an optional uint8 device buffer of at least ``core_memory_readout_workspace_bytes``
+    (allocated here when absent or too small).
     """
     _require_cuda(q, theta, M, b_state, o_fold, attn_out)
     q = q.to(torch.bfloat16).contiguous()
@@ -232,8 +235,8 @@ def memory_readout(q: torch.Tensor, theta: torch.Tensor, gate, M: torch.Tensor,
     if not attn_out.is_contiguous() or attn_out.dtype != torch.bfloat16:
         raise ValueError("attn_out must be a contiguous bfloat16 tensor")
     lib = _lib.load()
-    ws = _workspace(lib.core_memory_readout_workspace_bytes(ctypes.byref(dims), q_len, d_mem, gh),
-                    q.device)
+    need = lib.core_memory_readout_workspace_bytes(ctypes.byref(dims), q_len, d_mem, gh)
+    ws = workspace if workspace is not None and workspace.numel() >= need else _workspace(need, q.device)
     go = -1.0 if gate_override is None else float(gate_override)
     check(lib.core_memory_readout(
         ctypes.byref(dims), q_len, _ptr(q), _ptr(theta), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2),
