@@ -108,7 +108,7 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
   return CORE_OK;
 }
 
-int check_dims(const core_dims_t* d, const char* fn) {
+int check_dims(const core_dims_t* d, const char* fn, bool allow_f32) {
   std::string f(fn);
   if (d == nullptr) return set_error(CORE_ERR_INVALID_ARG, f + ": dims is NULL");
   if (d->batch <= 0 || d->n_q_heads <= 0 || d->n_kv_heads <= 0 || d->seq_len <= 0 ||
@@ -120,8 +120,9 @@ int check_dims(const core_dims_t* d, const char* fn) {
   int g = d->n_q_heads / d->n_kv_heads;
   if (g != 1 && g != 2 && g != 4)
     return set_error(CORE_ERR_UNSUPPORTED, f + ": GQA group size must be 1, 2 or 4");
-  if (d->dtype != CORE_DTYPE_BF16)
-    return set_error(CORE_ERR_UNSUPPORTED, f + ": the CUDA path computes in bf16 only");
+  if (d->dtype != CORE_DTYPE_BF16 && !(allow_f32 && d->dtype == CORE_DTYPE_F32))
+    return set_error(CORE_ERR_UNSUPPORTED,
+                     f + (allow_f32 ? ": dtype must be bf16 or f32" : ": this entry point takes bf16 caches only"));
   if (d->n_queries > d->seq_len)
     return set_error(CORE_ERR_INVALID_ARG, f + ": n_queries exceeds seq_len");
   return CORE_OK;

@@ -62,6 +62,7 @@ struct Sizer {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int check_dims(const core_dims_t* d, const char* fn);
+// Validates the shared dimensions; f32 caches pass only where allow_f32.
+int check_dims(const core_dims_t* d, const char* fn, bool allow_f32 = false);
 
 }  // namespace core

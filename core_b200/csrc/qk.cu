@@ -21,6 +21,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "qk_common.cuh"
 #include "host_util.h"
 
 namespace core {
@@ -36,11 +37,6 @@ constexpr int kLseThreads = 64 + kLseEpiThreads;  // warp 0 TMA, warp 1 MMA, 16 
 constexpr int kKStages = 2;
 constexpr uint32_t kKTileBytes = kTile * kD * 2;  // 32 KB
 constexpr uint32_t kAtom = 1024;                  // 8 rows x 128 B
-// log(1e-8) as the float the reference passes to its kernels (fused_qk.py:382, :494).
-constexpr float kLogFloor = -18.420680743952367f;
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
-constexpr int kRecWords = 16;
 
 struct Params {
   int B, Hq, Hkv, G, nq, L, q_start, n_qb, n_kt;
@@ -78,18 +74,6 @@ __device__ __forceinline__ Unit decode(long long u, const Params& p) {
   return r;
 }
 
-__device__ __forceinline__ float logaddexp_floor(float r) {
-  // max(r, f) + log1p(exp(-|r - f|)), f = log(1e-8)  (fused_qk.py:200-202)
-  float a = fabsf(r - kLogFloor);
-  float t;
-  if (a < 16.0f) {
-    t = log1pf(expf(-a));
-  } else {
-    // exp(-a) < 1.2e-7: log1p(x) equals x to within half an ulp of x.
-    t = ex2_approx(-a * kLog2e);
-  }
-  return fmaxf(r, kLogFloor) + t;
-}
 
 // ===========================================================================
 // 1. LSE partial kernel
@@ -698,8 +682,10 @@ struct MergeParams {
   int B, Hq, Hkv, G, nq, L, q_start, n_qb, topk, n_recent, head_topk;
   float scale;
   const uint32_t* rec;
-  const __nv_bfloat16* q;  // (B, Hq, nq, d)
-  const __nv_bfloat16* k;  // (B, Hkv, L, d)
+  const __nv_bfloat16* q;  // (B, Hq, nq, d), bf16 caches
+  const __nv_bfloat16* k;  // (B, Hkv, L, d), bf16 caches
+  const float* qf;         // the same for f32 caches (then q, k are NULL)
+  const float* kf;
   const float* lse;        // (B, Hq, nq)
   float* features;
   int stride;
@@ -731,6 +717,23 @@ __device__ float relation_exact(const MergeParams& p, int b, int h, int key, int
   const long long cc = (qpos + 1 < p.L) ? qpos + 1 : p.L;
   const float lcc = logf((float)cc);
   float dot[4] = {0.f, 0.f, 0.f, 0.f};
+  if (p.qf != nullptr) {  // f32 caches: unrounded logits (fp32 reference path)
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (g < p.G) {
+        const float4* qr4 = reinterpret_cast<const float4*>(
+            p.qf + (((long long)b * p.Hq + h * p.G + g) * p.nq + t) * kD);
+        for (int c = 0; c < kD / 4; ++c) {
+          const float4 w = __ldg(qr4 + c);
+          const float4 kv = reinterpret_cast<const float4*>(s_k)[c];
+          dot[g] = fmaf(w.x, kv.x, dot[g]);
+          dot[g] = fmaf(w.y, kv.y, dot[g]);
+          dot[g] = fmaf(w.z, kv.z, dot[g]);
+          dot[g] = fmaf(w.w, kv.w, dot[g]);
+        }
+      }
+    }
+  } else {
   const uint4* qr[4];
 #pragma unroll
   for (int g = 0; g < 4; ++g)
@@ -755,12 +758,13 @@ __device__ float relation_exact(const MergeParams& p, int b, int h, int key, int
       }
     }
   }
+  }
   float acc = 0.f, mn = INFINITY;
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     if (g < p.G) {
       const int qh = h * p.G + g;
-      const float x = bf16_round(dot[g]);
+      const float x = (p.qf != nullptr) ? dot[g] : bf16_round(dot[g]);
       const float r = fmaf(x, p.scale, -p.lse[((long long)b * p.Hq + qh) * p.nq + t]) + lcc;
       float rel = logaddexp_floor(r);
       if (qpos == 0) rel = log1pf(expf(kLogFloor));
@@ -882,8 +886,9 @@ __global__ void __launch_bounds__(kResolveThreads)
   for (int it = blockIdx.x; it < count; it += gridDim.x) {
     const int2 item = p.queue[it];
     const int bb = (int)(item.x / p.L), kk = (int)(item.x % p.L), h = item.y;
-    const __nv_bfloat16* kr = p.k + (((long long)bb * p.Hkv + h) * p.L + kk) * kD;
-    for (int e = threadIdx.x; e < kD; e += kResolveThreads) s_k[e] = __bfloat162float(kr[e]);
+    const long long krow = (((long long)bb * p.Hkv + h) * p.L + kk) * kD;
+    for (int e = threadIdx.x; e < kD; e += kResolveThreads)
+      s_k[e] = (p.kf != nullptr) ? p.kf[krow + e] : __bfloat162float(p.k[krow + e]);
     __syncthreads();
     for (int t = threadIdx.x; t < p.nq; t += kResolveThreads)
       s_rel[t] = relation_exact(p, bb, h, kk, t, s_k);
@@ -994,7 +999,7 @@ static size_t queue_cap_for(const core_dims_t* d) {
 }
 
 extern "C" size_t core_qk_features_workspace_bytes(const core_dims_t* d) {
-  if (check_dims(d, "core_qk_features_workspace_bytes") != CORE_OK) return 0;
+  if (check_dims(d, "core_qk_features_workspace_bytes", true) != CORE_OK) return 0;
   QKPlan plan;
   plan_qk(d, 4, 16, &plan);
   Sizer z;
@@ -1007,6 +1012,9 @@ extern "C" size_t core_qk_features_workspace_bytes(const core_dims_t* d) {
 }
 
 namespace core {
+int qk_f32_records(const core_dims_t* d, int q_start, int n_qb, int head_topk, int n_recent,
+                   float scale, const float* q, const float* k, bool run_lse, float* lse,
+                   uint32_t* rec, cudaStream_t s);
 int qk_features_impl(const core_dims_t* d, const void* q, const void* k, int32_t topk_qk,
                      int32_t n_recent_queries, const float* lse_in, float* lse_out,
                      float* features, int32_t feature_stride, void* workspace,
@@ -1027,8 +1035,9 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
                            float* features, int32_t feature_stride, void* workspace,
                            size_t workspace_bytes, void* stream, void* ev0_, void* ev1_) {
   cudaEvent_t ev0 = static_cast<cudaEvent_t>(ev0_), ev1 = static_cast<cudaEvent_t>(ev1_);
-  int rc = check_dims(d, "core_qk_features");
+  int rc = check_dims(d, "core_qk_features", true);
   if (rc != CORE_OK) return rc;
+  const bool f32 = d->dtype == CORE_DTYPE_F32;
   if (q == nullptr || k == nullptr || features == nullptr)
     return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: NULL tensor");
   if (d->n_queries <= 0) return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: no queries");
@@ -1063,6 +1072,15 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
   }
   p.lse = lse_buf;
 
+  const bool run_lse = (lse_in == nullptr);
+  if (f32) {
+    if (ev0 != nullptr) cudaEventRecord(ev0, s);
+    rc = qk_f32_records(d, p.q_start, p.n_qb, p.head_topk, p.n_recent, p.scale,
+                        static_cast<const float*>(q), static_cast<const float*>(k), run_lse,
+                        lse_buf, p.rec, s);
+    if (ev1 != nullptr) cudaEventRecord(ev1, s);
+    if (rc != CORE_OK) return rc;
+  } else {
   // Tensor maps: Q as (B*Hq, nq, 128) and K as (B*Hkv, L, 128), bf16, 128 B swizzle.
   CUtensorMap tmQ_lse, tmQ_rel, tmK;
   {
@@ -1079,7 +1097,6 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
     uint32_t box[3] = {64, 128, 1};
     if ((rc = make_tmap_bf16(&tmK, k, 3, dims, str, box, true)) != CORE_OK) return rc;
   }
-  const bool run_lse = (lse_in == nullptr);
   switch (p.G) {
     case 1: rc = launch_qk<1>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s, ev0, ev1); break;
     case 2: rc = launch_qk<2>(plan, tmQ_lse, tmQ_rel, tmK, run_lse, lse_buf, s, ev0, ev1); break;
@@ -1087,13 +1104,16 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
     default: return set_error(CORE_ERR_UNSUPPORTED, "core_qk_features: group size");
   }
   if (rc != CORE_OK) return rc;
+  }
 
   MergeParams mp{};
   mp.B = p.B; mp.Hq = p.Hq; mp.Hkv = p.Hkv; mp.G = p.G; mp.nq = p.nq; mp.L = p.L;
   mp.q_start = p.q_start; mp.n_qb = p.n_qb; mp.topk = topk_qk; mp.n_recent = p.n_recent;
   mp.head_topk = p.head_topk; mp.scale = p.scale; mp.rec = p.rec;
-  mp.q = static_cast<const __nv_bfloat16*>(q);
-  mp.k = static_cast<const __nv_bfloat16*>(k);
+  mp.q = f32 ? nullptr : static_cast<const __nv_bfloat16*>(q);
+  mp.k = f32 ? nullptr : static_cast<const __nv_bfloat16*>(k);
+  mp.qf = f32 ? static_cast<const float*>(q) : nullptr;
+  mp.kf = f32 ? static_cast<const float*>(k) : nullptr;
   mp.lse = lse_buf; mp.features = features; mp.stride = feature_stride; mp.status = p.status;
   mp.queue_count = queue_count; mp.queue = queue; mp.queue_cap = (int)queue_cap_for(d);
   if ((p.Hkv & (p.Hkv - 1)) != 0)

@@ -31,11 +31,16 @@ def _require_cuda(*ts):
             raise ValueError("core_b200 operates on CUDA tensors only (no CPU path)")
 
 
-def _dims(keys: torch.Tensor, n_q_heads: int, n_queries: int) -> CoreDims:
+def _dims(keys: torch.Tensor, n_q_heads: int, n_queries: int,
+          allow_f32: bool = False) -> CoreDims:
     b, hkv, L, d = keys.shape
-    if keys.dtype != torch.bfloat16:
-        raise TypeError(f"core_b200 computes in bfloat16; got {keys.dtype}")
-    return CoreDims(b, n_q_heads, hkv, d, n_queries, L, _lib.CORE_DTYPE_BF16)
+    if keys.dtype == torch.bfloat16:
+        code = _lib.CORE_DTYPE_BF16
+    elif allow_f32 and keys.dtype == torch.float32:
+        code = _lib.CORE_DTYPE_F32
+    else:
+        raise TypeError(f"core_b200 takes bfloat16 caches here; got {keys.dtype}")
+    return CoreDims(b, n_q_heads, hkv, d, n_queries, L, code)
 
 
 def _workspace(nbytes: int, device) -> torch.Tensor:
@@ -69,16 +74,18 @@ def qk_features(q: torch.Tensor, k: torch.Tensor, *, topk_qk: int = 4,
                 features: torch.Tensor | None = None):
     """f1..f6 of every cached key (``strict_causal_qk_features``).
 
-    q: (B, Hq, nq, 128) bf16, k: (B, Hkv, L, 128) bf16.  Returns
+    q: (B, Hq, nq, 128), k: (B, Hkv, L, 128), both bf16 (tensor-core path,
+    logits rounded to bf16 like the reference's bf16 matmul) or both f32
+    (CUDA-core path, unrounded f32 logits).  Returns
     (features (B, L, 6) or the given (B, L, F>=6) buffer, lse (B, Hq, nq)).
     """
     _require_cuda(q, k, lse)
     q = q.contiguous()
     k = k.contiguous()
     B, Hq, nq, d = q.shape
-    dims = _dims(k, Hq, nq)
-    if q.dtype != torch.bfloat16 or d != HEAD_DIM:
-        raise TypeError("q must be bfloat16 with head_dim 128")
+    dims = _dims(k, Hq, nq, allow_f32=True)
+    if q.dtype != k.dtype or d != HEAD_DIM:
+        raise TypeError("q must have the cache dtype and head_dim 128")
     lib = _lib.load()
     if features is None:
         features = torch.empty(B, k.shape[2], 6, dtype=torch.float32, device=k.device)

@@ -46,10 +46,15 @@ def test_invalid_arguments_rejected_on_host():
     rc = lib.core_qk_features(ctypes.byref(dims), ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 16,
                               None, None, ctypes.c_void_p(16), 14, None, 0, None)
     assert rc == -2 and "group size" in _lib.last_error()
+    dims = _lib.CoreDims(1, 32, 8, 128, 16, 128, 99)  # unknown dtype code
+    rc = lib.core_qk_features(ctypes.byref(dims), ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 16,
+                              None, None, ctypes.c_void_p(16), 14, None, 0, None)
+    assert rc == -2 and "dtype" in _lib.last_error()
+    # f32 caches pass the dimension checks and stop at the (missing) workspace
     dims = _lib.CoreDims(1, 32, 8, 128, 16, 128, _lib.CORE_DTYPE_F32)
     rc = lib.core_qk_features(ctypes.byref(dims), ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 16,
                               None, None, ctypes.c_void_p(16), 14, None, 0, None)
-    assert rc == -2 and "bf16" in _lib.last_error()
+    assert rc == -6 and "workspace" in _lib.last_error()
     dims = _lib.CoreDims(1, 32, 8, 128, 256, 128, _lib.CORE_DTYPE_BF16)  # nq > L
     rc = lib.core_qk_features(ctypes.byref(dims), ctypes.c_void_p(16), ctypes.c_void_p(16), 4, 16,
                               None, None, ctypes.c_void_p(16), 14, None, 0, None)

@@ -126,6 +126,59 @@ def test_qk_features_batch_rows_are_independent():
     assert torch.equal(lse2[1], lse1[0])
 
 
+# f32 caches: CUDA-core path with unrounded f32 logits.  Only the summation
+# order differs from the oracle, so the continuous features agree to 1e-4
+# relative (floored at 1e-3 absolute scale) and the discrete ones almost
+# everywhere (a relation value within f32 rounding of 0 may flip).
+F32_FEATURE_TOL = 1e-4
+F32_LSE_TOL = 2e-6
+
+
+def test_qk_features_f32_matches_golden():
+    from core_b200 import ops
+    dev = _dev()
+    d, m = load_case("fp32_decode_L512_Q64")
+    q = _f32(d["q"], dev)[None]
+    k = _f32(d["k"], dev)[None]
+    feats, lse = ops.qk_features(q, k)
+    ops.status()
+    ref, ref_lse, _ = O.qk_features(d["q"], d["k"], groups=m["hq"] // m["hkv"],
+                                    round_bf16=False)
+    got = feats[0].cpu().numpy()
+    assert np.abs(lse[0].cpu().numpy() - ref_lse).max() <= F32_LSE_TOL * np.abs(ref_lse).max()
+    assert rel_err(got[:, :4], ref[:, :4]).max() < F32_FEATURE_TOL
+    assert rel_err(got[:, :4], d["features"][:, :4]).max() < F32_FEATURE_TOL
+    nq, hkv = m["nq"], m["hkv"]
+    f5_frac, f5_steps = _discrete_mismatch(got[:, 4], d["features"][:, 4], 1.0 / nq)
+    f6_frac, f6_steps = _discrete_mismatch(got[:, 5], d["features"][:, 5], 1.0 / hkv)
+    assert f5_frac <= 0.002 and f5_steps <= 1.01, (f5_frac, f5_steps)
+    assert f6_frac <= 0.002 and f6_steps <= 1.01, (f6_frac, f6_steps)
+
+
+def test_qk_features_f32_ragged_and_given_lse():
+    """f32 path at a ragged length with several q-blocks, batch 2, group 4, and
+    with the LSE supplied by the caller (the decode readout order)."""
+    from core_b200 import ops
+    dev = _dev()
+    g = torch.Generator().manual_seed(21)
+    B, hkv, hq, L, nq = 2, 2, 8, 1000, 200
+    q = (torch.randn(B, hq, nq, 128, generator=g) * 0.5).to(dev)
+    k = (torch.randn(B, hkv, L, 128, generator=g) * 0.5).to(dev)
+    feats, lse = ops.qk_features(q, k)
+    feats2, lse2 = ops.qk_features(q, k, lse=lse)
+    ops.status()
+    assert torch.equal(feats, feats2)
+    for b in range(B):
+        ref, ref_lse, _ = O.qk_features(q[b].cpu().numpy(), k[b].cpu().numpy(), groups=4,
+                                        round_bf16=False)
+        got = feats[b].cpu().numpy()
+        assert np.abs(lse[b].cpu().numpy() - ref_lse).max() <= F32_LSE_TOL * np.abs(ref_lse).max()
+        assert rel_err(got[:, :4], ref[:, :4]).max() < F32_FEATURE_TOL
+        f5_frac, _ = _discrete_mismatch(got[:, 4], ref[:, 4], 1.0 / nq)
+        f6_frac, _ = _discrete_mismatch(got[:, 5], ref[:, 5], 1.0 / hkv)
+        assert f5_frac <= 0.002 and f6_frac <= 0.002, (f5_frac, f6_frac)
+
+
 @pytest.mark.parametrize("name", BF16_CASES)
 def test_coverage_matches_oracle(name):
     from core_b200 import ops
