@@ -22,7 +22,7 @@ static core_dims_t kv_dims(const core_dims_t* d) {
 
 extern "C" size_t core_compress_layer_workspace_bytes(const core_dims_t* d, int32_t n_kept,
                                                       int32_t d_mem) {
-  if (check_dims(d, "core_compress_layer_workspace_bytes") != CORE_OK) return 0;
+  if (check_dims(d, "core_compress_layer_workspace_bytes", true) != CORE_OK) return 0;
   size_t ws = core_qk_features_workspace_bytes(d);
   core_dims_t e = kv_dims(d);
   size_t c = core_coverage_workspace_bytes(&e);
@@ -43,7 +43,7 @@ extern "C" int core_compress_layer(const core_dims_t* d, const void* q, const vo
                                    float* Z, void* out_k, void* out_v, void* workspace,
                                    size_t workspace_bytes, void* stream, void* ev_begin,
                                    void* ev_end) {
-  int rc = check_dims(d, "core_compress_layer");
+  int rc = check_dims(d, "core_compress_layer", true);
   if (rc != CORE_OK) return rc;
   if (w == nullptr || a == nullptr)
     return set_error(CORE_ERR_INVALID_ARG, "core_compress_layer: NULL weights or args");

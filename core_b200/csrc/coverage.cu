@@ -302,6 +302,151 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Per batch row: the column sums over the CTAs that covered the row (double),
 // then mean z, mu and sigma2_eff (features.py:812, :830-845) as floats:
 // stats[b] = [mean z (64) | mu (64) | sigma2_eff (64)].
+// ---------------------------------------------------------------------------
+// f32 keys: the same projection on CUDA cores, with the unit partition,
+// outputs and per-CTA partial sums of cov_project_kernel, so cov_stats_kernel
+// and the assignment kernels run unchanged.  W_ext is rebuilt in f32 from its
+// three bf16 terms ((hi + mid) is exact; + lo restores the 24-bit significand).
+// Thread (tr = tid / 16, tc = tid % 16) owns tokens tr + 16 i and output
+// columns tc + 16 j (i, j < 8): columns j < 4 are z, j >= 4 the rotated zt.
+// ---------------------------------------------------------------------------
+constexpr int kF32Threads = 256;
+constexpr int kF32Pad = kD + 1;  // padded rows: a warp's 16 column owners hit distinct banks
+constexpr size_t kF32Smem =
+    sizeof(double) * kNStats + sizeof(float) * (2 * (size_t)kTile * kF32Pad + kTile);
+
+__global__ void __launch_bounds__(kF32Threads, 1)
+    cov_project_f32_kernel(const float* __restrict__ k, const __nv_bfloat16* __restrict__ wext,
+                           const Params p) {
+  extern __shared__ __align__(16) uint8_t sraw[];
+  double* sRed = reinterpret_cast<double*>(sraw);            // [192] column sums of the row
+  float* sK = reinterpret_cast<float*>(sraw + kNStats * 8);  // [128][kF32Pad] keys of a head; then y
+  float* sW = sK + kTile * kF32Pad;                          // [128][kF32Pad] W_ext columns of a head
+  float* sInv = sW + kTile * kF32Pad;                        // [128] 1 / (|k_h| + eps)
+  const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  const long long in = (long long)p.Hkv * kD;
+  const long long term = (long long)kNExt * in;
+  const long long u0 = unit_begin(blockIdx.x, p.U, gridDim.x);
+  const long long u1 = unit_begin(blockIdx.x + 1, p.U, gridDim.x);
+  for (int i = tid; i < kNStats; i += kF32Threads) sRed[i] = 0.0;
+  auto flush = [&](int bb) {
+    __syncthreads();
+    for (int i = tid; i < kNStats; i += kF32Threads) {
+      p.part[((long long)blockIdx.x * p.B + bb) * kNStats + i] = sRed[i];
+      sRed[i] = 0.0;
+    }
+    __syncthreads();
+  };
+  int cur_b = -1;
+  for (long long u = u0; u < u1; ++u) {
+    const int b = (int)(u / p.n_tiles), tile = (int)(u % p.n_tiles);
+    if (b != cur_b) {
+      if (cur_b >= 0) flush(cur_b);
+      cur_b = b;
+    }
+    float y[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[i][j] = 0.f;
+    for (int h = 0; h < p.Hkv; ++h) {
+      __syncthreads();  // the previous head's (or unit's) readers of sK, sW, sInv are done
+      const float* kb = k + ((long long)b * p.Hkv + h) * p.L * kD;
+      for (int i = tid; i < kTile * (kD / 4); i += kF32Threads) {
+        const int r = i / (kD / 4), c4 = i % (kD / 4);
+        const int tok = tile * kTile + r;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tok < p.L) x = __ldg(reinterpret_cast<const float4*>(kb + (long long)tok * kD) + c4);
+        float* dst = sK + r * kF32Pad + 4 * c4;
+        dst[0] = x.x;
+        dst[1] = x.y;
+        dst[2] = x.z;
+        dst[3] = x.w;
+      }
+      for (int i = tid; i < kNExt * kD; i += kF32Threads) {
+        const int o = i / kD, e = i % kD;
+        const long long g = (long long)o * in + (long long)h * kD + e;
+        sW[o * kF32Pad + e] = (__bfloat162float(wext[g]) + __bfloat162float(wext[term + g])) +
+                              __bfloat162float(wext[2 * term + g]);
+      }
+      __syncthreads();
+      if (tid < kTile) {
+        float ss = 0.f;
+        for (int e = 0; e < kD; ++e) {
+          const float x = sK[tid * kF32Pad + e];
+          ss = fmaf(x, x, ss);
+        }
+        sInv[tid] = 1.0f / (sqrtf(ss) + 1e-8f);
+      }
+      float acc[8][8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+#pragma unroll 2
+      for (int e = 0; e < kD; ++e) {
+        float kv[8], wv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) kv[i] = sK[(tr + 16 * i) * kF32Pad + e];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wv[j] = sW[(tc + 16 * j) * kF32Pad + e];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(kv[i], wv[j], acc[i][j]);
+      }
+      __syncthreads();  // sInv is complete
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float inv = sInv[tr + 16 * i];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[i][j] = fmaf(acc[i][j], inv, y[i][j]);
+      }
+    }
+    // z = y[:64] / (|y[:64]| + eps); zt = y[64:] / (same) = R z
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float nn = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) nn = fmaf(y[i][j], y[i][j], nn);
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) nn += __shfl_xor_sync(0xffffffffu, nn, o);
+      const float inv = 1.0f / (sqrtf(nn) + 1e-8f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[i][j] *= inv;
+    }
+    __syncthreads();  // the last head's readers of sK are done: sK now holds y
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = tr + 16 * i;
+      const int tok = tile * kTile + r;
+      const bool valid = tok < p.L;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sK[r * kF32Pad + tc + 16 * j] = valid ? y[i][j] : 0.f;
+      if (valid) {
+        float* zr = p.z + ((long long)b * p.L + tok) * kP;
+        float* ztr = p.zt + ((long long)b * p.L + tok) * kP;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          zr[tc + 16 * j] = y[i][j];
+          ztr[tc + 16 * j] = y[i][4 + j];
+        }
+      }
+    }
+    __syncthreads();
+    if (tid < kNStats) {  // columns: sum z (0..63), sum zt (64..127), sum zt^2 (128..191)
+      const int c = tid < 2 * kP ? tid : tid - kP;
+      float sum = 0.f;
+      for (int r = 0; r < kTile; ++r) {
+        const float x = sK[r * kF32Pad + c];
+        sum += tid < 2 * kP ? x : x * x;
+      }
+      sRed[tid] += (double)sum;
+    }
+  }
+  if (cur_b >= 0) flush(cur_b);
+}
+
 constexpr int kStatsThreads = 1024;
 constexpr int kMaxPartCtas = 256;
 constexpr int kStatsChunk = 64;  // CTA partials staged in shared memory per pass (96 KB)
@@ -562,7 +707,7 @@ extern "C" int core_prepare_geometry(const float* geometry, const float* hadamar
 }
 
 extern "C" size_t core_coverage_workspace_bytes(const core_dims_t* d) {
-  if (check_dims(d, "core_coverage_workspace_bytes") != CORE_OK) return 0;
+  if (check_dims(d, "core_coverage_workspace_bytes", true) != CORE_OK) return 0;
   CovPlan c;
   plan_cov(d, &c);
   Sizer z;
@@ -580,7 +725,7 @@ extern "C" int core_coverage_features(const core_dims_t* d, const void* k,
                                       float shrinkage_rho, float* features, int32_t feature_stride,
                                       int32_t col0, void* workspace, size_t workspace_bytes,
                                       void* stream) {
-  int rc = check_dims(d, "core_coverage_features");
+  int rc = check_dims(d, "core_coverage_features", true);
   if (rc != CORE_OK) return rc;
   if (k == nullptr || geometry_ext == nullptr || prototypes == nullptr || features == nullptr)
     return set_error(CORE_ERR_INVALID_ARG, "core_coverage_features: NULL tensor");
@@ -604,6 +749,14 @@ extern "C" int core_coverage_features(const core_dims_t* d, const void* k,
   cudaError_t e = cudaMemsetAsync(hist, 0, sizeof(int) * (size_t)p.B * kNP, s);
   if (e != cudaSuccess) return cuda_error(e, "coverage histogram clear");
 
+  if (d->dtype == CORE_DTYPE_F32) {
+    e = cudaFuncSetAttribute(cov_project_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kF32Smem);
+    if (e != cudaSuccess) return cuda_error(e, "cov_project_f32_kernel attribute");
+    cov_project_f32_kernel<<<c.grid, kF32Threads, kF32Smem, s>>>(
+        static_cast<const float*>(k), static_cast<const __nv_bfloat16*>(geometry_ext), p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "cov_project_f32_kernel launch");
+  } else {
   CUtensorMap tmK, tmW;
   {
     uint64_t dims[3] = {128, (uint64_t)p.L, (uint64_t)p.B * p.Hkv};
@@ -623,6 +776,7 @@ extern "C" int core_coverage_features(const core_dims_t* d, const void* k,
   if (e != cudaSuccess) return cuda_error(e, "cov_project_kernel attribute");
   cov_project_kernel<<<c.grid, kThreads, smem, s>>>(tmK, tmW, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "cov_project_kernel launch");
+  }
   {
     const size_t smem = sizeof(double) * kStatsChunk * kNStats;
     e = cudaFuncSetAttribute(cov_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -94,7 +94,8 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, const uint4& v) {
 
 struct Params {
   int B, Hkv, L, original_length, is_prefill, n_sink;
-  const __nv_bfloat16* v;
+  const __nv_bfloat16* v;   // bf16 values, or
+  const float* vf;          // f32 values (then v is NULL and no bf16 roundings apply)
   const int64_t* positions;
   const uint8_t* special;
   float* features;
@@ -176,7 +177,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int b = active ? (int)(gi / p.L) : 0;
     const int i = active ? (int)(gi % p.L) : 0;
     // ---- 1. auxiliary features (features.py:886-921) ----
-    if (active) {
+    if (active && p.vf != nullptr) {
+      for (int h = half; h < p.Hkv; h += 2) {
+        const float4* row =
+            reinterpret_cast<const float4*>(p.vf + (((long long)b * p.Hkv + h) * p.L + i) * 128);
+        float s = 0.f;
+#pragma unroll
+        for (int c0 = 0; c0 < 32; c0 += 16) {
+          float4 w[16];  // half the 512-byte row in flight at once
+#pragma unroll
+          for (int c = 0; c < 16; ++c) w[c] = __ldg(row + c0 + c);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            s = fmaf(w[c].x, w[c].x, s);
+            s = fmaf(w[c].y, w[c].y, s);
+            s = fmaf(w[c].z, w[c].z, s);
+            s = fmaf(w[c].w, w[c].w, s);
+          }
+        }
+        sf[kFHs + t * kMaxHkv + h] = s;
+      }
+    } else if (active) {
       for (int h = half; h < p.Hkv; h += 2) {
         const uint4* row =
             reinterpret_cast<const uint4*>(p.v + (((long long)b * p.Hkv + h) * p.L + i) * 128);
@@ -208,8 +229,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float a_age = log1pf((float)(T - 1 - pos)) / age_den;
       bool sink = pos < p.n_sink;
       if (p.special != nullptr && p.special[gi]) sink = true;
-      const float vmean = bf16_round(hsum / (float)p.Hkv);
-      const float a_value = bf16_round(log1pf(bf16_round(vmean / 128.0f)));
+      float a_value;
+      if (p.vf != nullptr) {  // f32 arithmetic (features.py:914-915 on f32 values)
+        a_value = log1pf((hsum / (float)p.Hkv) / 128.0f);
+      } else {                // every step rounded to bf16 like the bf16 tensor ops
+        const float vmean = bf16_round(hsum / (float)p.Hkv);
+        a_value = bf16_round(log1pf(bf16_round(vmean / 128.0f)));
+      }
       float* f = p.features + gi * kIn;
 #pragma unroll
       for (int k = 0; k < 10; ++k) x[k] = f[k];
@@ -322,7 +348,7 @@ extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const in
                                    const uint8_t* special, int32_t original_length,
                                    int32_t is_prefill, int32_t n_sink, float* features,
                                    const float* mlp, float* scores, void* stream) {
-  int rc = check_dims(d, "core_indexer_scores");
+  int rc = check_dims(d, "core_indexer_scores", true);
   if (rc != CORE_OK) return rc;
   if (v == nullptr || positions == nullptr || features == nullptr || mlp == nullptr ||
       scores == nullptr)
@@ -340,7 +366,9 @@ extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const in
   p.original_length = original_length;
   p.is_prefill = is_prefill;
   p.n_sink = n_sink;
-  p.v = static_cast<const __nv_bfloat16*>(v);
+  const bool f32 = d->dtype == CORE_DTYPE_F32;
+  p.v = f32 ? nullptr : static_cast<const __nv_bfloat16*>(v);
+  p.vf = f32 ? static_cast<const float*>(v) : nullptr;
   p.positions = positions;
   p.special = special;
   p.features = features;

@@ -218,7 +218,9 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
         const int kidx = et * kTok + ((tid + i * kProdThreads) >> 3);
-        toks[i] = kidx < p.n_evict ? p.evict[(long long)b * p.n_evict + kidx] : -1;
+        // an index outside the cache (error 802 of the mass kernel) gathers a zero row
+        const int ix = kidx < p.n_evict ? p.evict[(long long)b * p.n_evict + kidx] : -1;
+        toks[i] = (unsigned)ix < (unsigned)p.L ? ix : -1;
       }
       for (int c = 0; c < n_chunks && ok; ++c, ++it) {
         const int st = it % kPhiStages;
@@ -427,7 +429,8 @@ __global__ void __launch_bounds__(kMbThreads, 1)
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
         const int kidx = kc * kMbarChunk + (tid + i * kProdThreads) / (kAtoms * 8);
-        toks[i] = kidx < p.n_evict ? p.evict[kidx] : -1;
+        const int ix = kidx < p.n_evict ? p.evict[kidx] : -1;
+        toks[i] = (unsigned)ix < (unsigned)p.L ? ix : -1;  // outside the cache: zero row
       }
       if (it >= kMbStages && !(ok = wait(bar_empty(st), ((it / kMbStages) - 1) & 1, 911))) break;
       const uint32_t base = sbase + st * kMbStage;
@@ -518,6 +521,152 @@ __global__ void __launch_bounds__(kMbThreads, 1)
 }
 
 // ===========================================================================
+// f32 caches on CUDA cores: phi/W/b_bar and M_bar with the workspace layouts
+// of the tensor-core kernels (W^T as f32 (d_pad, n_ev_pad) in the bytes of the
+// two bf16 terms), so mw_update_kernel is shared.  Theta_f is the folded f32
+// projection (d_mem, Hkv*d); evicted indices outside the cache gather zero rows.
+// ===========================================================================
+constexpr int kF32Rows = 64;   // memory rows per block
+constexpr int kF32Chunk = 32;  // reduction chunk
+constexpr int kF32Pad = kF32Chunk + 1;
+
+// W^T[m, e] = p_bar_e * (Theta_f K_ev^T)[m, e] for 64 rows x 128 tokens and
+// the b_bar partial sum over those tokens.  Thread (tm = tid % 16, tt = tid / 16)
+// owns rows tm + 16 i (i < 4) and tokens tt + 16 j (j < 8).
+__global__ void __launch_bounds__(256)
+    mw_phi_f32_kernel(const float* __restrict__ theta, const float* __restrict__ k,
+                      const int* __restrict__ evict, const float* __restrict__ pbar, int Hkv, int L,
+                      int n_evict, int n_ev_pad, int d_mem, int d_pad, float* __restrict__ wt,
+                      float* __restrict__ bpart) {
+  __shared__ float sT[kF32Rows][kF32Pad];
+  __shared__ float sK[kTok][kF32Pad];
+  __shared__ float sB[16][kF32Rows];
+  __shared__ int sTok[kTok];
+  const int tid = threadIdx.x, tm = tid & 15, tt = tid >> 4;
+  const int et = blockIdx.x, m0 = blockIdx.y * kF32Rows;
+  const int kvw = Hkv * kD;
+  if (tid < kTok) {
+    const int e = et * kTok + tid;
+    const int ix = e < n_evict ? evict[e] : -1;
+    sTok[tid] = (unsigned)ix < (unsigned)L ? ix : -1;
+  }
+  float acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  for (int c0 = 0; c0 < kvw; c0 += kF32Chunk) {
+    __syncthreads();  // sTok ready; the previous chunk's readers are done
+    const int h = c0 / kD, e0 = c0 % kD;
+    for (int i = tid; i < kF32Rows * kF32Chunk; i += 256) {
+      const int r = i / kF32Chunk, cc = i % kF32Chunk;
+      sT[r][cc] = (m0 + r < d_mem) ? theta[(long long)(m0 + r) * kvw + c0 + cc] : 0.f;
+    }
+    for (int i = tid; i < kTok * kF32Chunk; i += 256) {
+      const int r = i / kF32Chunk, cc = i % kF32Chunk;
+      const int tok = sTok[r];
+      sK[r][cc] = tok >= 0 ? k[((long long)h * L + tok) * kD + e0 + cc] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int cc = 0; cc < kF32Chunk; ++cc) {
+      float tv[4], kv[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tv[i] = sT[tm + 16 * i][cc];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) kv[j] = sK[tt + 16 * j][cc];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(tv[i], kv[j], acc[i][j]);
+    }
+  }
+  float bsum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = et * kTok + tt + 16 * j;
+    const float w = pbar[e];  // zero on the padding
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float phi = acc[i][j];
+      const float wphi = w * phi;
+      wt[(long long)(m0 + tm + 16 * i) * n_ev_pad + e] = wphi;
+      bsum[i] = fmaf(wphi, phi, bsum[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) sB[tt][tm + 16 * i] = bsum[i];
+  __syncthreads();
+  if (tid < kF32Rows) {
+    float t = 0.f;
+    for (int g = 0; g < 16; ++g) t += sB[g][tid];
+    bpart[(long long)et * d_pad + m0 + tid] = t;
+  }
+}
+
+// M_bar partial of one token split: (W^T V_ev)[m, c] for 64 rows x 64 value
+// columns.  Thread (tm = tid % 16, tc = tid / 16) owns rows tm + 16 i and
+// columns tc + 16 j (i, j < 4).
+__global__ void __launch_bounds__(256)
+    mw_mbar_f32_kernel(const float* __restrict__ wt, const float* __restrict__ v,
+                       const int* __restrict__ evict, int Hkv, int L, int n_evict, int n_ev_pad,
+                       int d_pad, int splits, long long split_stride, float* __restrict__ mpart) {
+  __shared__ float sW[kF32Rows][kF32Pad];
+  __shared__ float sV[kF32Chunk][kF32Rows + 1];
+  __shared__ int sTok[kF32Chunk];
+  const int tid = threadIdx.x, tm = tid & 15, tc = tid >> 4;
+  const int c0 = blockIdx.x * 64, m0 = blockIdx.y * kF32Rows, sp = blockIdx.z;
+  const int kvw = Hkv * kD;
+  const int h = c0 / kD, col0 = c0 % kD;
+  const int n_chunks = n_ev_pad / kF32Chunk;
+  const int per = (n_chunks + splits - 1) / splits;
+  const int ch0 = sp * per, ch1 = min(n_chunks, ch0 + per);
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int ch = ch0; ch < ch1; ++ch) {
+    const int e0 = ch * kF32Chunk;
+    __syncthreads();  // the previous chunk's readers are done
+    if (tid < kF32Chunk) {
+      const int e = e0 + tid;
+      const int ix = e < n_evict ? evict[e] : -1;
+      sTok[tid] = (unsigned)ix < (unsigned)L ? ix : -1;
+    }
+    for (int i = tid; i < kF32Rows * kF32Chunk; i += 256) {
+      const int r = i / kF32Chunk, cc = i % kF32Chunk;
+      sW[r][cc] = wt[(long long)(m0 + r) * n_ev_pad + e0 + cc];
+    }
+    __syncthreads();
+    for (int i = tid; i < kF32Chunk * 64; i += 256) {
+      const int r = i / 64, cc = i % 64;
+      const int tok = sTok[r];
+      sV[r][cc] = tok >= 0 ? v[((long long)h * L + tok) * kD + col0 + cc] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int e = 0; e < kF32Chunk; ++e) {
+      float wv[4], vv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) wv[i] = sW[tm + 16 * i][e];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) vv[j] = sV[e][tc + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], vv[j], acc[i][j]);
+    }
+  }
+  float* out = mpart + (long long)sp * split_stride;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      out[(long long)(m0 + tm + 16 * i) * kvw + c0 + tc + 16 * j] = acc[i][j];
+}
+
+// ===========================================================================
 // recurrence
 // ===========================================================================
 __global__ void mw_update_kernel(const float* __restrict__ mpart, int splits, int B, int d_mem,
@@ -584,7 +733,7 @@ void plan_mw(const core_dims_t* d, int n_evict, int d_mem, MwPlan* m) {
 
 extern "C" size_t core_memory_write_workspace_bytes(const core_dims_t* d, int32_t n_evict,
                                                     int32_t d_mem) {
-  if (check_dims(d, "core_memory_write_workspace_bytes") != CORE_OK || n_evict <= 0 || d_mem <= 0)
+  if (check_dims(d, "core_memory_write_workspace_bytes", true) != CORE_OK || n_evict <= 0 || d_mem <= 0)
     return 0;
   MwPlan m;
   plan_mw(d, n_evict, d_mem, &m);
@@ -603,7 +752,7 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
                                  float gamma, float eta, float student_temp, float* M,
                                  float* b_state, float* Z, void* workspace,
                                  size_t workspace_bytes, void* stream) {
-  int rc = check_dims(d, "core_memory_write");
+  int rc = check_dims(d, "core_memory_write", true);
   if (rc != CORE_OK) return rc;
   if (k == nullptr || v == nullptr || scores_cal == nullptr || evict_idx == nullptr ||
       theta_split == nullptr || M == nullptr || b_state == nullptr || Z == nullptr)
@@ -640,6 +789,22 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_mass_kernel launch");
 
+  if (d->dtype == CORE_DTYPE_F32) {
+    float* wtf = reinterpret_cast<float*>(wt);  // (d_pad, n_ev_pad) f32 in the bytes of the two terms
+    for (int b = 0; b < d->batch; ++b) {
+      const long long kv_off = (long long)b * d->n_kv_heads * d->seq_len * kD;
+      mw_phi_f32_kernel<<<dim3(m.n_et, m.d_pad / kF32Rows), 256, 0, s>>>(
+          static_cast<const float*>(theta_split), static_cast<const float*>(k) + kv_off,
+          evict_idx + (long long)b * n_evict, pbar + (long long)b * m.n_ev_pad, d->n_kv_heads,
+          d->seq_len, n_evict, m.n_ev_pad, d_mem, m.d_pad, wtf, bpart + (long long)b * m.n_et * m.d_pad);
+      if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_phi_f32_kernel launch");
+      mw_mbar_f32_kernel<<<dim3(m.kvw / 64, m.d_pad / kF32Rows, m.splits), 256, 0, s>>>(
+          wtf, static_cast<const float*>(v) + kv_off, evict_idx + (long long)b * n_evict,
+          d->n_kv_heads, d->seq_len, n_evict, m.n_ev_pad, m.d_pad, m.splits,
+          (long long)d->batch * m.d_pad * m.kvw, mpart + (long long)b * m.d_pad * m.kvw);
+      if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_mbar_f32_kernel launch");
+    }
+  } else {
   CUtensorMap tmT;
   {
     const uint64_t kvw = (uint64_t)m.kvw;
@@ -697,6 +862,7 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
     else
       mw_mbar_kernel<128><<<(unsigned)(m.splits * m.n_jt * m.n_ct), kMbThreads, mb_smem, s>>>(tmW, mq);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_mbar_kernel launch");
+  }
   }
   const long long n = (long long)d->batch * d_mem * m.kvw;
   mw_update_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(mpart, m.splits, d->batch, d_mem, m.d_pad,

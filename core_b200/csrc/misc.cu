@@ -11,26 +11,32 @@ namespace misc {
 
 constexpr int kD = 128;
 
-// out[b, h, j, :] = in[b, h, keep[b, j], :]; a half-warp moves one 256-byte row
-// with 16-byte accesses.
+// out[b, h, j, :] = in[b, h, keep[b, j], :]; kVec lanes move one row with
+// 16-byte accesses (16 for a 256-byte bf16 row, 32 for a 512-byte f32 row).
+template <int kVec>
 __global__ void compact_kernel(const uint4* __restrict__ k, const uint4* __restrict__ v,
                                const int* __restrict__ keep, int Hkv, int L, int n_kept,
                                uint4* __restrict__ ok, uint4* __restrict__ ov) {
-  const long long rows = (long long)gridDim.y * Hkv * n_kept;  // gridDim.y = B
-  const int b = blockIdx.y;
+  const int b = blockIdx.y;  // gridDim.y = B
   const long long per_b = (long long)Hkv * n_kept;
-  for (long long r = (long long)blockIdx.x * (blockDim.x / 16) + (threadIdx.x >> 4); r < per_b;
-       r += (long long)gridDim.x * (blockDim.x / 16)) {
+  for (long long r = (long long)blockIdx.x * (blockDim.x / kVec) + (threadIdx.x / kVec); r < per_b;
+       r += (long long)gridDim.x * (blockDim.x / kVec)) {
     const int h = (int)(r / n_kept), j = (int)(r % n_kept);
     const int src = keep[(long long)b * n_kept + j];
-    const int q = threadIdx.x & 15;
-    const long long si = (((long long)b * Hkv + h) * L + src) * 16 + q;
-    const long long di = (((long long)b * Hkv + h) * n_kept + j) * 16 + q;
+    const int q = threadIdx.x % kVec;
+    const long long si = (((long long)b * Hkv + h) * L + src) * kVec + q;
+    const long long di = (((long long)b * Hkv + h) * n_kept + j) * kVec + q;
     ok[di] = k[si];
     ov[di] = v[si];
   }
-  (void)rows;
 }
+
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ __nv_bfloat16 add_out(__nv_bfloat16 a, float r) {
+  return __float2bfloat16_rn(__bfloat162float(a) + bf16_round(r));
+}
+__device__ __forceinline__ float add_out(float a, float r) { return a + r; }
 
 __device__ __forceinline__ float gelu(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
@@ -41,8 +47,9 @@ __device__ __forceinline__ float gelu(float x) {
 // flight at once), the halves added in order; all q_len queries per row.
 constexpr int kProjWarps = 8;  // 4 rows per block
 
+template <typename T>
 __global__ void __launch_bounds__(kProjWarps * 32)
-    readout_proj_kernel(const __nv_bfloat16* __restrict__ q, int Hq, int q_len,
+    readout_proj_kernel(const T* __restrict__ q, int Hq, int q_len,
                         const float* __restrict__ theta, const float* __restrict__ gw1,
                         const float* __restrict__ gb1, int d_mem, int gh,
                         float* __restrict__ proj, float* __restrict__ gpre) {
@@ -53,7 +60,7 @@ __global__ void __launch_bounds__(kProjWarps * 32)
   for (int i = threadIdx.x; i < q_len * dm; i += blockDim.x) {
     const int t = i / dm, c = i % dm;
     const int qh = c / kD, e = c % kD;
-    sq[i] = __bfloat162float(q[(((long long)b * Hq + qh) * q_len + t) * kD + e]);
+    sq[i] = to_f32(q[(((long long)b * Hq + qh) * q_len + t) * kD + e]);
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -91,7 +98,8 @@ __global__ void __launch_bounds__(kProjWarps * 32)
   }
 }
 
-// Stage 2: m = proj M / sqrt(proj^2 . b + eps), gate, residual rounded to bf16.
+// Stage 2: m = proj M / sqrt(proj^2 . b + eps), gate, residual (rounded to
+// bf16 when the attention output is bf16).
 // A block covers 32 value columns (one per lane); its 8 warps split the d_mem
 // rows of M and their partial sums are added in warp order.
 constexpr int kMemWarps = 16;
@@ -101,7 +109,7 @@ __global__ void __launch_bounds__(kMemWarps * 32)
                        const float* __restrict__ gw2, const float* __restrict__ gb2,
                        float gate_override, const float* __restrict__ M,
                        const float* __restrict__ bst, int q_len, int d_mem, int gh, int kvw,
-                       float* __restrict__ res) {
+                       bool round_bf16, float* __restrict__ res) {
   extern __shared__ float sp[];  // proj (d_mem) of this (b, t)
   __shared__ float s_den, s_g;
   __shared__ float s_part[kMemWarps][32];
@@ -139,14 +147,16 @@ __global__ void __launch_bounds__(kMemWarps * 32)
 #pragma unroll
     for (int w = 0; w < kMemWarps; ++w) m += s_part[w][lane];
     m *= 1.0f / sqrtf(s_den);
-    res[((long long)b * q_len + t) * kvw + c] = bf16_round(s_g * m);
+    const float r = s_g * m;
+    res[((long long)b * q_len + t) * kvw + c] = round_bf16 ? bf16_round(r) : r;
   }
 }
 
-// Stage 3: out += bf16(o_fold res); one warp per output row.
+// Stage 3: out += o_fold res (bf16 outputs: the product rounded to bf16, then
+// the sum); one warp per output row.
+template <typename T>
 __global__ void readout_out_kernel(const float* __restrict__ res, const float* __restrict__ ofold,
-                                   int q_len, int kvw, int hidden,
-                                   __nv_bfloat16* __restrict__ out) {
+                                   int q_len, int kvw, int hidden, T* __restrict__ out) {
   extern __shared__ float sr[];  // (q_len, kvw)
   const int b = blockIdx.y;
   for (int i = threadIdx.x; i < q_len * kvw; i += blockDim.x)
@@ -181,9 +191,9 @@ __global__ void readout_out_kernel(const float* __restrict__ res, const float* _
         acc1 += __shfl_xor_sync(0xffffffffu, acc1, s);
       }
       if (lane == 0) {
-        __nv_bfloat16* row = out + ((long long)b * q_len + t) * hidden;
-        row[o0] = __float2bfloat16_rn(__bfloat162float(row[o0]) + bf16_round(acc0));
-        if (has1) row[o1] = __float2bfloat16_rn(__bfloat162float(row[o1]) + bf16_round(acc1));
+        T* row = out + ((long long)b * q_len + t) * hidden;
+        row[o0] = add_out(row[o0], acc0);
+        if (has1) row[o1] = add_out(row[o1], acc1);
       }
     }
   }
@@ -198,7 +208,7 @@ using namespace core::misc;
 extern "C" int core_compact_kv(const core_dims_t* d, const void* k, const void* v,
                                const int32_t* keep_idx, int32_t n_kept, void* out_k, void* out_v,
                                void* stream) {
-  int rc = check_dims(d, "core_compact_kv");
+  int rc = check_dims(d, "core_compact_kv", true);
   if (rc != CORE_OK) return rc;
   if (k == nullptr || v == nullptr || keep_idx == nullptr || out_k == nullptr || out_v == nullptr)
     return set_error(CORE_ERR_INVALID_ARG, "core_compact_kv: NULL tensor");
@@ -209,13 +219,21 @@ extern "C" int core_compact_kv(const core_dims_t* d, const void* k, const void* 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long rows = (long long)d->n_kv_heads * n_kept;
   const int threads = 256;
-  long long blocks = (rows + (threads / 16) - 1) / (threads / 16);
+  const int vec = d->dtype == CORE_DTYPE_F32 ? 32 : 16;  // 16-byte pieces of a row
+  long long blocks = (rows + (threads / vec) - 1) / (threads / vec);
   const long long cap = (long long)sm_count() * 8;
   if (blocks > cap) blocks = cap;
   dim3 grid((unsigned)blocks, (unsigned)d->batch);
-  compact_kernel<<<grid, threads, 0, s>>>(static_cast<const uint4*>(k), static_cast<const uint4*>(v),
-                                          keep_idx, d->n_kv_heads, d->seq_len, n_kept,
-                                          static_cast<uint4*>(out_k), static_cast<uint4*>(out_v));
+  const uint4* kk = static_cast<const uint4*>(k);
+  const uint4* vv = static_cast<const uint4*>(v);
+  uint4* okk = static_cast<uint4*>(out_k);
+  uint4* ovv = static_cast<uint4*>(out_v);
+  if (vec == 32)
+    compact_kernel<32><<<grid, threads, 0, s>>>(kk, vv, keep_idx, d->n_kv_heads, d->seq_len, n_kept,
+                                                okk, ovv);
+  else
+    compact_kernel<16><<<grid, threads, 0, s>>>(kk, vv, keep_idx, d->n_kv_heads, d->seq_len, n_kept,
+                                                okk, ovv);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CORE_OK : cuda_error(e, "compact_kernel launch");
 }
@@ -245,6 +263,9 @@ extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const vo
     return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout: NULL tensor");
   if (q_len <= 0 || d_mem <= 0 || hidden <= 0 || gate_hidden < 0)
     return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout: bad sizes");
+  if (d->dtype != CORE_DTYPE_BF16 && d->dtype != CORE_DTYPE_F32)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_memory_readout: dtype must be bf16 or f32");
+  const bool f32 = d->dtype == CORE_DTYPE_F32;
   const int dm = d->n_q_heads * kD, kvw = d->n_kv_heads * kD;
   if ((size_t)q_len * dm * 4 > 200 * 1024 || (size_t)q_len * kvw * 4 > 200 * 1024)
     return set_error(CORE_ERR_UNSUPPORTED, "core_memory_readout: q_len too large for one call");
@@ -259,30 +280,46 @@ extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const vo
   const int gh = gate_override >= 0.f ? 0 : gate_hidden;
   {
     const size_t smem = (size_t)q_len * dm * 4;
-    e = cudaFuncSetAttribute(readout_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = f32 ? cudaFuncSetAttribute(readout_proj_kernel<float>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+            : cudaFuncSetAttribute(readout_proj_kernel<__nv_bfloat16>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_error(e, "readout_proj attribute");
     const int rows = d_mem + gh;
     int bx = (rows + kProjWarps / 2 - 1) / (kProjWarps / 2);  // two warps per weight row
     if (bx > sms) bx = sms;
-    readout_proj_kernel<<<dim3(bx, d->batch), kProjWarps * 32, smem, s>>>(static_cast<const __nv_bfloat16*>(q),
-                                                             d->n_q_heads, q_len, theta, gate_w1,
-                                                             gate_b1, d_mem, gh, proj, gpre);
+    const dim3 grid(bx, d->batch);
+    if (f32)
+      readout_proj_kernel<float><<<grid, kProjWarps * 32, smem, s>>>(
+          static_cast<const float*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1, d_mem, gh,
+          proj, gpre);
+    else
+      readout_proj_kernel<__nv_bfloat16><<<grid, kProjWarps * 32, smem, s>>>(
+          static_cast<const __nv_bfloat16*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1,
+          d_mem, gh, proj, gpre);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_proj launch");
   }
   {
     const size_t smem = (size_t)d_mem * 4;
     readout_mem_kernel<<<dim3((kvw + 31) / 32, d->batch, q_len), kMemWarps * 32, smem, s>>>(
-        proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, res);
+        proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, !f32, res);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_mem launch");
   }
   {
     const size_t smem = (size_t)q_len * kvw * 4;
-    e = cudaFuncSetAttribute(readout_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = f32 ? cudaFuncSetAttribute(readout_out_kernel<float>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+            : cudaFuncSetAttribute(readout_out_kernel<__nv_bfloat16>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_error(e, "readout_out attribute");
     int bx = (hidden + 7) / 8;
     if (bx > sms) bx = sms;
-    readout_out_kernel<<<dim3(bx, d->batch), 256, smem, s>>>(res, o_fold, q_len, kvw, hidden,
-                                                            static_cast<__nv_bfloat16*>(attn_out));
+    if (f32)
+      readout_out_kernel<float><<<dim3(bx, d->batch), 256, smem, s>>>(
+          res, o_fold, q_len, kvw, hidden, static_cast<float*>(attn_out));
+    else
+      readout_out_kernel<__nv_bfloat16><<<dim3(bx, d->batch), 256, smem, s>>>(
+          res, o_fold, q_len, kvw, hidden, static_cast<__nv_bfloat16*>(attn_out));
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_out launch");
   }
   return CORE_OK;

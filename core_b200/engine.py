@@ -16,6 +16,12 @@ import torch
 from . import ops
 
 
+def cache_dtype(dtype: torch.dtype) -> torch.dtype:
+    """Compute type of the CUDA path for caches of ``dtype``: f32 caches keep
+    f32 (the reference's fp32 arithmetic), every other dtype runs as bf16."""
+    return torch.float32 if dtype == torch.float32 else torch.bfloat16
+
+
 def n_kept_for(k_len: int, compression_ratio: float, n_sink: int) -> int:
     """Retained budget of ``COREMemoryPress.compress`` (core/kvpress_adapter.py:1002-1011)."""
     return max(1, min(max(int(k_len * (1 - compression_ratio)), min(n_sink, k_len)), k_len))
@@ -38,6 +44,8 @@ class LayerWeights:
     mlp            : packed f32 indexer MLP (see ops.pack_mlp)
     theta          : (d_mem, Hq*d) f32 memory projection (readout side)
     theta_split    : (2, d_mem, Hkv*d) bf16 terms of the group-folded projection
+                     (the memory write of bf16 caches)
+    theta_fold     : (d_mem, Hkv*d) f32 group-folded projection (that of f32 caches)
     gate           : (w1 (gh, Hq*d), b1 (gh), w2 (gh), b2 (1)) f32
     """
 
@@ -47,6 +55,11 @@ class LayerWeights:
     theta: torch.Tensor | None = None
     theta_split: torch.Tensor | None = None
     gate: tuple | None = None
+    theta_fold: torch.Tensor | None = None
+
+    def write_theta(self, dtype: torch.dtype) -> torch.Tensor | None:
+        """The memory-write projection in the form caches of ``dtype`` take."""
+        return self.theta_fold if cache_dtype(dtype) == torch.float32 else self.theta_split
 
     @classmethod
     def prepare(cls, *, geometry, prototypes, hadamard, mlp_params, theta=None, gate=None,
@@ -54,10 +67,11 @@ class LayerWeights:
         dev = torch.device(device)
         geo = ops.prepare_geometry(geometry.to(dev, torch.float32), hadamard.to(dev, torch.float32))
         groups = n_q_heads // n_kv_heads
-        th = ths = g = None
+        th = ths = thf = g = None
         if theta is not None:
             th = theta.to(dev, torch.float32).contiguous()
-            ths = ops.split_bf16(fold_groups(th, n_kv_heads, groups, head_dim), 2)
+            thf = fold_groups(th, n_kv_heads, groups, head_dim)
+            ths = ops.split_bf16(thf, 2)
         if gate is not None:
             g = tuple(x.to(dev, torch.float32).reshape(-1).contiguous() if i else
                       x.to(dev, torch.float32).contiguous() for i, x in enumerate(gate))
@@ -65,7 +79,7 @@ class LayerWeights:
             geometry_ext=geo,
             prototypes=prototypes.to(dev, torch.float32).contiguous(),
             mlp=ops.pack_mlp([t.to(dev) for t in mlp_params]),
-            theta=th, theta_split=ths, gate=g)
+            theta=th, theta_split=ths, gate=g, theta_fold=thf)
 
 
 @dataclass
@@ -92,8 +106,10 @@ def compress_layer(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
     """Score, select, write memory and gather for one layer (all batch rows)
     with a single call of ``core_compress_layer``.
 
-    q: (B, Hq, nq, 128) bf16 post-RoPE queries of the scoring window;
-    keys/values: (B, Hkv, L, 128) bf16.  ``memory`` is updated in place.
+    q: (B, Hq, nq, 128) post-RoPE queries of the scoring window;
+    keys/values: (B, Hkv, L, 128).  f32 caches run the f32 path, any other
+    dtype the bf16 one (q, keys and values are cast to that type).
+    ``memory`` is updated in place.
     ``timing_events``: optional (start, end) torch.cuda.Event pair recorded
     around the QK relation kernel.  Returns dict(keys, values, keep, evict,
     scores, features); keep/evict are None and keys/values the inputs when
@@ -103,22 +119,24 @@ def compress_layer(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
 
     from . import _lib
     ops._require_cuda(q, keys, values, positions)
-    q = q.to(torch.bfloat16).contiguous()
-    k = keys.to(torch.bfloat16).contiguous()
-    v = values.to(torch.bfloat16).contiguous()
+    dt = cache_dtype(keys.dtype)
+    q = q.to(dt).contiguous()
+    k = keys.to(dt).contiguous()
+    v = values.to(dt).contiguous()
     B, hkv, L, d = k.shape
     Hq, nq = q.shape[1], q.shape[2]
     dev = k.device
-    dims = _lib.CoreDims(B, Hq, hkv, d, nq, L, _lib.CORE_DTYPE_BF16)
-    write = memory is not None and weights.theta_split is not None
-    d_mem = weights.theta_split.shape[1] if write else 0
+    dims = _lib.CoreDims(B, Hq, hkv, d, nq, L, ops._dtype_code(dt))
+    theta_w = weights.write_theta(dt)
+    write = memory is not None and theta_w is not None
+    d_mem = theta_w.shape[-2] if write else 0
     feats = torch.empty(B, L, 14, dtype=torch.float32, device=dev)
     scores = torch.empty(B, L, dtype=torch.float32, device=dev)
     n_ev = max(L - n_kept, 0)
     keep = torch.empty(B, max(n_kept, 1), dtype=torch.int32, device=dev)
     evict = torch.empty(B, max(n_ev, 1), dtype=torch.int32, device=dev)
     compact = n_kept < L
-    ok = torch.empty(B, hkv, n_kept, d, dtype=torch.bfloat16, device=dev) if compact else k
+    ok = torch.empty(B, hkv, n_kept, d, dtype=dt, device=dev) if compact else k
     ov = torch.empty_like(ok) if compact else v
     lib = _lib.load()
     need = lib.core_compress_layer_workspace_bytes(ctypes.byref(dims), int(n_kept), int(d_mem))
@@ -126,7 +144,7 @@ def compress_layer(q: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
         workspace = torch.empty(max(int(need), 256), dtype=torch.uint8, device=dev)
     w = _lib.CoreLayerWeights(weights.geometry_ext.data_ptr(), weights.prototypes.data_ptr(),
                               weights.mlp.data_ptr(),
-                              weights.theta_split.data_ptr() if write else 0, int(d_mem))
+                              theta_w.data_ptr() if write else 0, int(d_mem))
     a = _lib.CoreCompressArgs(int(n_kept), int(n_sink), int(topk_qk), int(n_recent_queries),
                               float(shrinkage_rho), int(original_length), int(bool(is_prefill)),
                               float(gamma), float(eta), float(student_temp))

@@ -31,16 +31,20 @@ def _require_cuda(*ts):
             raise ValueError("core_b200 operates on CUDA tensors only (no CPU path)")
 
 
-def _dims(keys: torch.Tensor, n_q_heads: int, n_queries: int,
-          allow_f32: bool = False) -> CoreDims:
+_DTYPES = {torch.bfloat16: _lib.CORE_DTYPE_BF16, torch.float32: _lib.CORE_DTYPE_F32}
+
+
+def _dtype_code(dtype: torch.dtype) -> int:
+    """bf16 caches run on the tensor cores with the reference's bf16 roundings;
+    f32 caches (the reference's fp32 path) on CUDA cores in f32."""
+    if dtype not in _DTYPES:
+        raise TypeError(f"core_b200 takes bfloat16 or float32 caches; got {dtype}")
+    return _DTYPES[dtype]
+
+
+def _dims(keys: torch.Tensor, n_q_heads: int, n_queries: int) -> CoreDims:
     b, hkv, L, d = keys.shape
-    if keys.dtype == torch.bfloat16:
-        code = _lib.CORE_DTYPE_BF16
-    elif allow_f32 and keys.dtype == torch.float32:
-        code = _lib.CORE_DTYPE_F32
-    else:
-        raise TypeError(f"core_b200 takes bfloat16 caches here; got {keys.dtype}")
-    return CoreDims(b, n_q_heads, hkv, d, n_queries, L, code)
+    return CoreDims(b, n_q_heads, hkv, d, n_queries, L, _dtype_code(keys.dtype))
 
 
 def _workspace(nbytes: int, device) -> torch.Tensor:
@@ -83,7 +87,7 @@ def qk_features(q: torch.Tensor, k: torch.Tensor, *, topk_qk: int = 4,
     q = q.contiguous()
     k = k.contiguous()
     B, Hq, nq, d = q.shape
-    dims = _dims(k, Hq, nq, allow_f32=True)
+    dims = _dims(k, Hq, nq)
     if q.dtype != k.dtype or d != HEAD_DIM:
         raise TypeError("q must have the cache dtype and head_dim 128")
     lib = _lib.load()
@@ -185,14 +189,28 @@ def memory_write(k: torch.Tensor, v: torch.Tensor, scores_cal: torch.Tensor,
                  evict: torch.Tensor, theta_split: torch.Tensor, M: torch.Tensor,
                  b_state: torch.Tensor, Z: torch.Tensor, *, gamma: float, eta: float,
                  student_temp: float) -> None:
-    """Update (M, b, Z) in place with the evicted tokens (``compress`` memory write)."""
+    """Update (M, b, Z) in place with the evicted tokens (``compress`` memory write).
+
+    ``theta_split``: for bf16 caches the (2, d_mem, Hkv*d) bf16 terms of the
+    group-folded Theta (``split_bf16(fold, 2)``); for f32 caches the folded
+    (d_mem, Hkv*d) f32 Theta itself.
+    """
     _require_cuda(k, v, scores_cal, evict, theta_split, M, b_state, Z)
     k = k.contiguous()
     v = v.contiguous()
     B, hkv, L, d = k.shape
     dims = _dims(k, hkv, 0)
+    if v.dtype != k.dtype:
+        raise TypeError("keys and values must have one dtype")
     n_evict = evict.shape[1]
-    d_mem = theta_split.shape[1]
+    if k.dtype == torch.float32:
+        if theta_split.dim() != 2 or theta_split.dtype != torch.float32:
+            raise ValueError("f32 caches take the folded (d_mem, Hkv*d) f32 Theta")
+        d_mem = theta_split.shape[0]
+    else:
+        if theta_split.dim() != 3 or theta_split.dtype != torch.bfloat16:
+            raise ValueError("bf16 caches take the (2, d_mem, Hkv*d) bf16 terms of Theta")
+        d_mem = theta_split.shape[1]
     for name, t, shape in (("M", M, (B, d_mem, hkv * d)), ("b", b_state, (B, d_mem)), ("Z", Z, (B,))):
         if tuple(t.shape) != shape or t.dtype != torch.float32 or not t.is_contiguous():
             raise ValueError(f"{name} must be a contiguous float32 tensor of shape {shape}")
@@ -225,22 +243,24 @@ def memory_readout(q: torch.Tensor, theta: torch.Tensor, gate, M: torch.Tensor,
                    b_state: torch.Tensor, o_fold: torch.Tensor, attn_out: torch.Tensor,
                    *, n_kv_heads: int, gate_override: float | None = None,
                    workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """attn_out (B, q_len, hidden) bf16 += o_fold(g(q) m(q)); updated in place and returned.
+    """attn_out (B, q_len, hidden) += o_fold(g(q) m(q)); updated in place and returned.
+    attn_out's dtype (bf16 or f32) selects the arithmetic; q is cast to it.
 
     gate = (w1 (gh, Hq*d), b1 (gh), w2 (gh), b2 (1)) f32 tensors.  ``workspace``:
     an optional uint8 device buffer of at least ``core_memory_readout_workspace_bytes``
     (allocated here when absent or too small).
     """
     _require_cuda(q, theta, M, b_state, o_fold, attn_out)
-    q = q.to(torch.bfloat16).contiguous()
+    code = _dtype_code(attn_out.dtype)
+    q = q.to(attn_out.dtype).contiguous()
     B, Hq, q_len, d = q.shape
-    dims = CoreDims(B, Hq, n_kv_heads, d, q_len, max(q_len, 1), _lib.CORE_DTYPE_BF16)
+    dims = CoreDims(B, Hq, n_kv_heads, d, q_len, max(q_len, 1), code)
     d_mem = theta.shape[0]
     hidden = o_fold.shape[0]
     w1, b1, w2, b2 = gate
     gh = w1.shape[0]
-    if not attn_out.is_contiguous() or attn_out.dtype != torch.bfloat16:
-        raise ValueError("attn_out must be a contiguous bfloat16 tensor")
+    if not attn_out.is_contiguous():
+        raise ValueError("attn_out must be contiguous")
     lib = _lib.load()
     need = lib.core_memory_readout_workspace_bytes(ctypes.byref(dims), q_len, d_mem, gh)
     ws = workspace if workspace is not None and workspace.numel() >= need else _workspace(need, q.device)

@@ -537,7 +537,7 @@ class COREScorerPress(ScorerPress):
                 q = q[None]
         if q.shape[0] != B:
             q = q.expand(B, -1, -1, -1)
-        return q.to(torch.bfloat16).contiguous(), lse
+        return q.to(engine.cache_dtype(keys.dtype)).contiguous(), lse
 
     def _special_mask(self, ids):
         fe = self.feature_extractor
@@ -556,8 +556,9 @@ class COREScorerPress(ScorerPress):
         q, lse = self._scoring_queries(module, hidden_states, keys, is_prefill, kwargs)
         cfg = self.feature_extractor.config
         lw = self.layer_weights(layer_idx, keys.device)
-        k = keys.to(torch.bfloat16).contiguous()
-        v = values.to(torch.bfloat16).contiguous()
+        dt = engine.cache_dtype(keys.dtype)
+        k = keys.to(dt).contiguous()
+        v = values.to(dt).contiguous()
         feats = torch.empty(B, L, 14, dtype=torch.float32, device=keys.device)
         ops.qk_features(q, k, topk_qk=int(cfg.topk_qk), n_recent_queries=int(cfg.n_recent_queries),
                         lse=lse, features=feats)
@@ -717,12 +718,17 @@ class COREMemoryPress(BasePress):
         if self.memory_uniform_fraction != 0.0:
             raise NotImplementedError("memory_uniform_fraction != 0 is not supported by core_b200")
 
-    def _theta_split(self, layer_idx, num_kv_heads, num_groups, head_dim, device):
-        key = (self.memory_module.module_index(layer_idx), num_kv_heads, num_groups, str(device))
+    def _theta_split(self, layer_idx, num_kv_heads, num_groups, head_dim, device, dtype):
+        """Folded memory-write projection in the form caches of ``dtype`` take:
+        bf16 hi/lo terms, or the f32 fold itself for f32 caches."""
+        f32 = engine.cache_dtype(dtype) == torch.float32
+        key = (self.memory_module.module_index(layer_idx), num_kv_heads, num_groups, str(device),
+               f32)
         ts = self._folded_theta.get(key)
         if ts is None:
             theta = self.memory_module.params(layer_idx)[0].to(device)
-            ts = ops.split_bf16(engine.fold_groups(theta, num_kv_heads, num_groups, head_dim), 2)
+            fold = engine.fold_groups(theta, num_kv_heads, num_groups, head_dim)
+            ts = fold if f32 else ops.split_bf16(fold, 2)
             self._folded_theta[key] = ts
         return ts
 
@@ -760,15 +766,17 @@ class COREMemoryPress(BasePress):
         write = self.enable_memory_writing and self.memory_module is not None
         if write:
             self._check_spaces()
-        k = keys.to(torch.bfloat16).contiguous()
-        v = values.to(torch.bfloat16).contiguous()
+        dt = engine.cache_dtype(keys.dtype)
+        k = keys.to(dt).contiguous()
+        v = values.to(dt).contiguous()
         state = None
         ts = None
         if write:
             d_mem = self.memory_module.d_mem
             M, b, Z = self._state(layer_idx, bsz, d_mem, num_kv_heads * head_dim, keys.device)
             state = engine.MemoryState(M, b, Z)
-            ts = self._theta_split(layer_idx, num_kv_heads, num_groups, head_dim, keys.device)
+            ts = self._theta_split(layer_idx, num_kv_heads, num_groups, head_dim, keys.device,
+                                   keys.dtype)
         reuse = (not bp._is_scoring_layer(layer_idx)) and bp._cached_memory_scores is not None
         if reuse or bp.recency_alpha > 0.0:
             # scores first (reused across layers, or adjusted by the recency bonus)
@@ -792,7 +800,10 @@ class COREMemoryPress(BasePress):
             q, lse = bp._scoring_queries(module, hidden_states, keys, is_prefill, kwargs or {})
             cfg = bp.feature_extractor.config
             lw = bp.layer_weights(layer_idx, keys.device)
-            lw.theta_split = ts
+            if dt == torch.float32:
+                lw.theta_fold = ts
+            else:
+                lw.theta_split = ts
             out = engine.compress_layer(
                 q, k, v, lw, n_kept=n_kept, positions=positions, original_length=int(original_length),
                 is_prefill=is_prefill, n_sink=n_sink, topk_qk=int(cfg.topk_qk),
@@ -854,7 +865,7 @@ class COREMemoryPress(BasePress):
         head_dim = q.shape[-1]
         theta, gate, o_fold = self._readout_params(module, layer_idx, n_kv_heads,
                                                    n_q_heads // n_kv_heads, head_dim, hidden.device)
-        attn = output[0].to(torch.bfloat16).contiguous().clone()
+        attn = output[0].to(engine.cache_dtype(output[0].dtype)).contiguous().clone()
         ops.memory_readout(q, theta, gate, M, b, o_fold, attn, n_kv_heads=n_kv_heads,
                            gate_override=self.memory_gate_override)
         new_attn = attn.to(output[0].dtype)

@@ -16,8 +16,11 @@
  * Tensor layouts are those of the reference press (HF DynamicCache layers):
  *   Q  : (B, Hq, nq, d)    post-RoPE queries of the query buffer
  *   K,V: (B, Hkv, L, d)    cached keys / values
- * with d = 128 and Hq = G * Hkv, G <= 4.  bf16 (CORE_DTYPE_BF16) is the
- * supported compute type of the CUDA path.
+ * with d = 128 and Hq = G * Hkv, G <= 4.  dims.dtype names the element type
+ * of Q, K and V.  CORE_DTYPE_BF16 runs the contractions on tcgen05 and rounds
+ * where the reference's bf16 tensor ops round (logits, the a_value steps, the
+ * readout residual).  CORE_DTYPE_F32 (the reference's fp32 path) runs them on
+ * CUDA cores in f32 without those roundings.
  *
  * The reference is pure Python; each entry point below names the reference
  * function (file:line in the reference project) whose behaviour it replaces.
@@ -156,7 +159,9 @@ int core_topb_select(const float* scores, int32_t batch, int32_t seq_len, int32_
  * Z/M/b recurrence).
  *   scores_cal  : (B, L) f32 calibrated (unsaturated) scores
  *   evict_idx   : (B, n_evict) int32 from core_topb_select
- *   theta_split : (2, d_mem, Hkv*d) bf16 hi/lo of the group-folded Theta
+ *   theta_split : bf16 caches: (2, d_mem, Hkv*d) bf16 hi/lo of the
+ *                 group-folded Theta; f32 caches: that Theta itself,
+ *                 (d_mem, Hkv*d) f32
  *   M           : (B, d_mem, Hkv*d) f32, updated in place
  *   b_state     : (B, d_mem) f32, updated in place
  *   Z           : (B,) f32, updated in place (0 for a fresh layer)
@@ -182,12 +187,13 @@ int core_compact_kv(const core_dims_t* dims, const void* k, const void* v,
  * Replaces MemoryModule.readout (core/indexer.py:165-207) and the folded
  * o_proj projection of COREMemoryPress.apply_memory_readout
  * (core/kvpress_adapter.py:1302-1352).
- *   q        : (B, Hq, q_len, d) post-RoPE queries (bf16)
+ *   q        : (B, Hq, q_len, d) post-RoPE queries (dims.dtype)
  *   theta    : (d_mem, Hq*d) f32;  gate_w1 : (gh, Hq*d) f32; gate_b1 : (gh)
  *   gate_w2  : (gh) f32; gate_b2 : scalar f32 (pointer)
  *   M, b     : layer fast state (B, d_mem, Hkv*d), (B, d_mem) f32
  *   o_fold   : (hidden, Hkv*d) f32 group-folded o_proj
- *   attn_out : (B, q_len, hidden) bf16, updated in place
+ *   attn_out : (B, q_len, hidden) of dims.dtype, updated in place (bf16:
+ *              the residual and the o_proj product are rounded to bf16)
  * gate_override < 0 uses the learned gate, otherwise the constant gate.
  * ------------------------------------------------------------------------- */
 size_t core_memory_readout_workspace_bytes(const core_dims_t* dims, int32_t q_len,
@@ -232,7 +238,7 @@ typedef struct core_layer_weights {
   const void* geometry_ext;   /* (3, 128, Hkv*d) bf16 from core_prepare_geometry */
   const float* prototypes;    /* (64, 64) f32 */
   const float* mlp;           /* packed indexer MLP (see core_indexer_scores) */
-  const void* theta_split;    /* (2, d_mem, Hkv*d) bf16, or NULL: no memory write */
+  const void* theta_split;    /* as core_memory_write's (by dims.dtype), or NULL: no write */
   int32_t d_mem;
 } core_layer_weights_t;
 

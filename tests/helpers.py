@@ -44,3 +44,25 @@ def rel_err(a, b, floor=1e-3):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return np.abs(a - b) / np.maximum(np.abs(b), floor)
+
+
+def f3_flip_consistent(got_f3, R, bad_keys, *, rtol, near=2e-3):
+    """f3 is the mean of the positive relation values of a key.  A relation
+    value within rounding of 0 can take either sign in another summation order
+    (one bf16 ulp of a logit moves it by up to ~1e-3; in f32 far less), which
+    moves the count by one and the sum by about nothing.  Accept a key whose f3
+    equals psum / (pcnt + j) for j within the number of values with
+    |R| <= ``near``.  Returns (ok, first failing key)."""
+    nkv, nq, L = R.shape
+    flat = R.reshape(nkv * nq, L).astype(np.float64)
+    for k in bad_keys:
+        col = flat[:, k]
+        pos = col > 0
+        psum, pcnt = col[pos].sum(), int(pos.sum())
+        close = np.abs(col) <= near
+        n_minus, n_plus = int((close & pos).sum()), int((close & ~pos & np.isfinite(col)).sum())
+        cands = [psum / max(pcnt + j, 1) for j in range(-n_minus, n_plus + 1)]
+        tol = rtol * max(abs(psum / max(pcnt, 1)), 1e-3)
+        if min(abs(got_f3[k] - c) for c in cands) > tol:
+            return False, k
+    return True, None

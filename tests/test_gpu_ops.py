@@ -5,7 +5,8 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import SINGLE_STEP_CASES, TWO_STEP_CASE, layer_weights, load_case, rel_err
+from helpers import (SINGLE_STEP_CASES, TWO_STEP_CASE, f3_flip_consistent, layer_weights,
+                     load_case, rel_err)
 from oracle import core_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -36,28 +37,6 @@ def _f32(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
 
 
-def _f3_flip_consistent(got_f3, R, bad_keys, rtol=FEATURE_TOL):
-    """f3 is the mean of the positive relation values of a key.  A relation
-    value within rounding of 0 (one bf16 ulp of its logit) can take either
-    sign on the tensor cores, which moves the count by one and the sum by
-    about nothing; accept a key whose f3 equals psum / (pcnt + j) for j within
-    the number of such values."""
-    nkv, nq, L = R.shape
-    flat = R.reshape(nkv * nq, L).astype(np.float64)
-    for k in bad_keys:
-        col = flat[:, k]
-        pos = col > 0
-        psum, pcnt = col[pos].sum(), int(pos.sum())
-        # one bf16 ulp of a logit moves a relation value by up to ~1e-3
-        near = np.abs(col) <= 2e-3
-        n_minus, n_plus = int((near & pos).sum()), int((near & ~pos & np.isfinite(col)).sum())
-        cands = [psum / max(pcnt + j, 1) for j in range(-n_minus, n_plus + 1)]
-        tol = rtol * max(abs(psum / max(pcnt, 1)), 1e-3)
-        if min(abs(got_f3[k] - c) for c in cands) > tol:
-            return False, k
-    return True, None
-
-
 def _check_qk_features(got, ref, R):
     err = rel_err(got[:, :4], ref[:, :4])
     # f1, f2, f4: maxima and top-k means, continuous in the relation values
@@ -66,7 +45,7 @@ def _check_qk_features(got, ref, R):
     # f3: exact up to sign flips of relation values at 0
     bad = np.nonzero(err[:, 2] > FEATURE_TOL)[0]
     assert len(bad) <= max(2, 0.005 * len(err)), len(bad)
-    ok, k = _f3_flip_consistent(got[:, 2], R, bad)
+    ok, k = f3_flip_consistent(got[:, 2], R, bad, rtol=FEATURE_TOL)
     assert ok, (k, got[k, 2], ref[k, 2])
 
 
