@@ -93,6 +93,21 @@ SIGNATURES = {
                                                    _P, _P, _P, _I, _P, _P]),
     "core_set_sm_budget": (ctypes.c_int, [_I]),
     "core_split_bf16": (ctypes.c_int, [_P, ctypes.c_int64, _I, _P, _P]),
+    "core_qk_summary_words": (_I, [_I]),
+    "core_qk_head_summary": (ctypes.c_int, [_D, _P, _P, _I, _I, _P, _P, _P, _S, _P]),
+    "core_qk_merge_summaries": (ctypes.c_int, [_P, _I, ctypes.c_int64, _I, _I, _I, _I, _I, _I, _I,
+                                               _P, _I, _P]),
+    "core_coverage_partial_projection": (ctypes.c_int, [_D, _P, _P, _P, _P, _S, _P]),
+    "core_coverage_range_workspace_bytes": (_S, [_I]),
+    "core_coverage_range_totals": (ctypes.c_int, [_P, _I, _P, _P, _P, _P, _P, _S, _P]),
+    "core_coverage_range_assign": (ctypes.c_int, [_P, _I, _F, _P, _P, _I, _P, _P, _P, _P, _I, _I,
+                                                  _P, _S, _P]),
+    "core_coverage_range_occupancy": (ctypes.c_int, [_P, _P, _I, _P, _I, _I, _P]),
+    "core_value_head_sums": (ctypes.c_int, [_D, _P, _P, ctypes.c_int64, _P]),
+    "core_indexer_scores_from_sums": (ctypes.c_int, [_I, _I, _P, ctypes.c_int64, _P, _P, _I, _I,
+                                                     _I, _P, _P, _P, _P]),
+    "core_memory_write_gathered": (ctypes.c_int, [_D, _P, _P, _P, _P, _I, _P, _I, _F, _F, _F, _P,
+                                                  _P, _P, _P, _S, _P]),
     "core_compress_layer_workspace_bytes": (_S, [_D, _I, _I]),
     "core_compress_layer": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P,
                                            ctypes.POINTER(CoreLayerWeights),

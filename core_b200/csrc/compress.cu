@@ -9,7 +9,8 @@ namespace core {
 int qk_features_impl(const core_dims_t* d, const void* q, const void* k, int32_t topk_qk,
                      int32_t n_recent_queries, const float* lse_in, float* lse_out,
                      float* features, int32_t feature_stride, void* workspace,
-                     size_t workspace_bytes, void* stream, void* ev0, void* ev1);
+                     size_t workspace_bytes, void* stream, void* ev0, void* ev1,
+                     uint32_t* summary = nullptr);
 }
 
 using namespace core;

@@ -41,6 +41,7 @@ constexpr int kNStats = 3 * kP;                      // sum z, sum zt, sum zt^2
 struct Params {
   int B, Hkv, L, n_tiles;
   long long U;
+  int partial;           // 1: write the raw projection of this rank's heads (head-sharded caches)
   float* z;              // (B, L, 64)
   float* zt;             // (B, L, 64)
   double* part;          // (grid, B, 192) per-CTA sums
@@ -253,6 +254,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(bar_tempty(slot));
       }
       if (!ok) break;
+      if (p.partial) {  // uniform: y[:64] = sum over this rank's heads, reduced across ranks later
+        if (team == 0 && tok < p.L) {
+          float4* dst = reinterpret_cast<float4*>(p.z + ((long long)b * p.L + tok) * kP);
+#pragma unroll
+          for (int j = 0; j < kP / 4; ++j)
+            dst[j] = make_float4(y[4 * j], y[4 * j + 1], y[4 * j + 2], y[4 * j + 3]);
+        }
+        continue;
+      }
       if (team == 0) {
         float nn = 0.f;
 #pragma unroll
@@ -445,6 +455,77 @@ __global__ void __launch_bounds__(kF32Threads, 1)
     }
   }
   if (cur_b >= 0) flush(cur_b);
+}
+
+// ---------------------------------------------------------------------------
+// Head-sharded caches, one sequence: after the ranks' raw projections are
+// summed, each rank finishes the keys of its range.  cov_range_finalize_kernel:
+// 128 keys per block, z = y / (|y| + eps), zt = R z (CUDA cores, the rotation
+// in f32), and per-block column sums of z, zt, zt^2 in key order;
+// cov_range_totals_kernel adds the blocks in order (f64).  Across ranks the
+// totals are summed and cov_stats_kernel finishes them as for one GPU.
+// ---------------------------------------------------------------------------
+constexpr int kRangeKeys = 128;
+constexpr int kRangePad = kP + 1;
+constexpr size_t kRangeSmem = sizeof(float) * ((size_t)kP * kP + 2 * (size_t)kRangeKeys * kRangePad);
+
+__global__ void __launch_bounds__(kRangeKeys)
+    cov_range_finalize_kernel(const float* __restrict__ y, int n, const float* __restrict__ R,
+                              float* __restrict__ z, float* __restrict__ zt,
+                              float* __restrict__ block_sums) {
+  extern __shared__ float sm_range[];
+  float* sR = sm_range;                      // [64][64] rotation
+  float* sZ = sR + kP * kP;                  // [128][kRangePad] y, then z
+  float* sT = sZ + kRangeKeys * kRangePad;   // [128][kRangePad] zt
+  const int tid = threadIdx.x;
+  const int k0 = blockIdx.x * kRangeKeys;
+  for (int i = tid; i < kP * kP; i += kRangeKeys) sR[i] = R[i];
+  for (int i = tid; i < kRangeKeys * kP; i += kRangeKeys) {
+    const int r = i / kP, c = i % kP;
+    sZ[r * kRangePad + c] = (k0 + r < n) ? y[(long long)(k0 + r) * kP + c] : 0.f;
+  }
+  __syncthreads();
+  {
+    const int r = tid;
+    float nn = 0.f;
+    for (int c = 0; c < kP; ++c) nn = fmaf(sZ[r * kRangePad + c], sZ[r * kRangePad + c], nn);
+    const float inv = 1.0f / (sqrtf(nn) + 1e-8f);
+    for (int c = 0; c < kP; ++c) sZ[r * kRangePad + c] *= inv;
+    for (int i = 0; i < kP; ++i) {  // zt_i = sum_j R_ij z_j (features.py:259-261)
+      float a = 0.f;
+      for (int j = 0; j < kP; ++j) a = fmaf(sR[i * kP + j], sZ[r * kRangePad + j], a);
+      sT[r * kRangePad + i] = (k0 + r < n) ? a : 0.f;
+    }
+    if (k0 + r >= n)
+      for (int c = 0; c < kP; ++c) sZ[r * kRangePad + c] = 0.f;
+  }
+  __syncthreads();
+  for (int i = tid; i < kRangeKeys * kP; i += kRangeKeys) {
+    const int r = i / kP, c = i % kP;
+    if (k0 + r < n) {
+      z[(long long)(k0 + r) * kP + c] = sZ[r * kRangePad + c];
+      zt[(long long)(k0 + r) * kP + c] = sT[r * kRangePad + c];
+    }
+  }
+  for (int col = tid; col < kNStats; col += kRangeKeys) {
+    const float* src = col < kP ? sZ : sT;
+    const int c = col < kP ? col : (col < 2 * kP ? col - kP : col - 2 * kP);
+    float a = 0.f;
+    for (int r = 0; r < kRangeKeys; ++r) {
+      const float x = src[r * kRangePad + c];
+      a += col < 2 * kP ? x : x * x;
+    }
+    block_sums[(long long)blockIdx.x * kNStats + col] = a;
+  }
+}
+
+__global__ void cov_range_totals_kernel(const float* __restrict__ block_sums, int n_blocks,
+                                        double* __restrict__ totals) {
+  const int col = threadIdx.x;
+  if (col >= kNStats) return;
+  double a = 0.0;
+  for (int i = 0; i < n_blocks; ++i) a += (double)block_sums[(long long)i * kNStats + col];
+  totals[col] = a;
 }
 
 constexpr int kStatsThreads = 1024;
@@ -796,4 +877,135 @@ extern "C" int core_coverage_features(const core_dims_t* d, const void* k,
                                                                   feature_stride, col0);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "cov_occupancy_kernel launch");
   return CORE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Head-sharded caches (one sequence; each rank holds some KV heads).
+// ---------------------------------------------------------------------------
+extern "C" int core_coverage_partial_projection(const core_dims_t* d, const void* k,
+                                                const void* geometry_ext, float* y,
+                                                void* workspace, size_t workspace_bytes,
+                                                void* stream) {
+  int rc = check_dims(d, "core_coverage_partial_projection");
+  if (rc != CORE_OK) return rc;
+  if (k == nullptr || geometry_ext == nullptr || y == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_coverage_partial_projection: NULL tensor");
+  if (reinterpret_cast<uintptr_t>(y) % 16 != 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_coverage_partial_projection: y must be 16-byte aligned");
+  CovPlan c;
+  plan_cov(d, &c);
+  Params& p = c.p;
+  p.partial = 1;
+  Carver cv(workspace, workspace_bytes);
+  p.part = cv.take<double>((size_t)c.grid * p.B * kNStats);
+  if (cv.overflow)
+    return set_error(CORE_ERR_WORKSPACE, "core_coverage_partial_projection: workspace too small");
+  p.z = y;
+  p.zt = nullptr;
+  p.status = device_status();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap tmK, tmW;
+  {
+    uint64_t dims[3] = {128, (uint64_t)p.L, (uint64_t)p.B * p.Hkv};
+    uint64_t str[2] = {256, (uint64_t)p.L * 256};
+    uint32_t box[3] = {64, 128, 1};
+    if ((rc = make_tmap_bf16(&tmK, k, 3, dims, str, box, true)) != CORE_OK) return rc;
+  }
+  {
+    const uint64_t in = (uint64_t)p.Hkv * kD;
+    uint64_t dims[2] = {in, 3u * kNExt};
+    uint64_t str[1] = {in * 2};
+    uint32_t box[2] = {64, (uint32_t)kNExt};
+    if ((rc = make_tmap_bf16(&tmW, geometry_ext, 2, dims, str, box, true)) != CORE_OK) return rc;
+  }
+  const uint32_t smem = Smem::kTotal + 1024;
+  cudaError_t e = cudaFuncSetAttribute(cov_project_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_error(e, "cov_project_kernel attribute");
+  cov_project_kernel<<<c.grid, kThreads, smem, s>>>(tmK, tmW, p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "cov_project_kernel launch");
+}
+
+extern "C" size_t core_coverage_range_workspace_bytes(int32_t n_keys) {
+  Sizer z;
+  z.take<float>((size_t)((n_keys + kRangeKeys - 1) / kRangeKeys) * kNStats);  // block sums
+  z.take<float>((size_t)kNStats);                                            // statistics
+  return z.used;
+}
+
+extern "C" int core_coverage_range_totals(const float* y, int32_t n_keys, const float* hadamard,
+                                          float* z, float* zt, double* totals, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  if (y == nullptr || hadamard == nullptr || z == nullptr || zt == nullptr || totals == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_coverage_range_totals: NULL tensor");
+  if (n_keys < 0) return set_error(CORE_ERR_INVALID_ARG, "core_coverage_range_totals: n_keys < 0");
+  Carver cv(workspace, workspace_bytes);
+  const int n_blocks = (n_keys + kRangeKeys - 1) / kRangeKeys;
+  float* bs = cv.take<float>((size_t)(n_blocks > 0 ? n_blocks : 1) * kNStats);
+  if (cv.overflow) return set_error(CORE_ERR_WORKSPACE, "core_coverage_range_totals: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (n_blocks > 0) {
+    e = cudaFuncSetAttribute(cov_range_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kRangeSmem);
+    if (e != cudaSuccess) return cuda_error(e, "cov_range_finalize_kernel attribute");
+    cov_range_finalize_kernel<<<n_blocks, kRangeKeys, kRangeSmem, s>>>(y, n_keys, hadamard, z, zt, bs);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "cov_range_finalize_kernel launch");
+  }
+  cov_range_totals_kernel<<<1, 256, 0, s>>>(bs, n_blocks, totals);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "cov_range_totals_kernel launch");
+}
+
+extern "C" int core_coverage_range_assign(const double* totals, int32_t seq_len, float shrinkage_rho,
+                                          const float* z, const float* zt, int32_t n_keys,
+                                          const float* prototypes, int32_t* assign, int32_t* hist,
+                                          float* features, int32_t feature_stride, int32_t col0,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (totals == nullptr || z == nullptr || zt == nullptr || prototypes == nullptr ||
+      assign == nullptr || hist == nullptr || features == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_coverage_range_assign: NULL tensor");
+  if (seq_len <= 0 || n_keys < 0 || n_keys > seq_len || col0 < 0 || col0 + 4 > feature_stride)
+    return set_error(CORE_ERR_INVALID_ARG, "core_coverage_range_assign: bad sizes");
+  if (reinterpret_cast<uintptr_t>(totals) % 16 != 0 || reinterpret_cast<uintptr_t>(prototypes) % 16 != 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_coverage_range_assign: totals and prototypes must be 16-byte aligned");
+  Carver cv(workspace, workspace_bytes);
+  const int n_blocks = (n_keys + kRangeKeys - 1) / kRangeKeys;
+  cv.take<float>((size_t)(n_blocks > 0 ? n_blocks : 1) * kNStats);
+  float* stats = cv.take<float>((size_t)kNStats);
+  if (cv.overflow) return set_error(CORE_ERR_WORKSPACE, "core_coverage_range_assign: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(hist, 0, sizeof(int) * kNP, s);
+  if (e != cudaSuccess) return cuda_error(e, "coverage histogram clear");
+  {
+    // the summed totals are one "CTA" covering the whole sequence
+    const size_t smem = sizeof(double) * kStatsChunk * kNStats;
+    e = cudaFuncSetAttribute(cov_stats_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_error(e, "cov_stats_kernel attribute");
+    cov_stats_kernel<<<1, kStatsThreads, smem, s>>>(totals, 1, 1, 1, seq_len, shrinkage_rho, stats);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "cov_stats_kernel launch");
+  }
+  if (n_keys == 0) return CORE_OK;
+  long long ablocks = ((long long)n_keys + kAssignThreads / 4 - 1) / (kAssignThreads / 4);
+  if (ablocks > 4LL * sm_count()) ablocks = 4LL * sm_count();
+  cov_assign_kernel<<<(unsigned)ablocks, kAssignThreads, 0, s>>>(z, zt, stats, prototypes, 1, n_keys,
+                                                                 assign, hist, features,
+                                                                 feature_stride, col0, device_status());
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "cov_assign_kernel launch");
+}
+
+extern "C" int core_coverage_range_occupancy(const int32_t* assign, const int32_t* hist,
+                                             int32_t n_keys, float* features,
+                                             int32_t feature_stride, int32_t col0, void* stream) {
+  if (assign == nullptr || hist == nullptr || features == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_coverage_range_occupancy: NULL tensor");
+  if (n_keys < 0 || col0 < 0 || col0 + 4 > feature_stride)
+    return set_error(CORE_ERR_INVALID_ARG, "core_coverage_range_occupancy: bad sizes");
+  if (n_keys == 0) return CORE_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cov_occupancy_kernel<<<(unsigned)((n_keys + 127) / 128), 128, 0, s>>>(assign, hist, 1, n_keys,
+                                                                        features, feature_stride, col0);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "cov_occupancy_kernel launch");
 }

@@ -96,6 +96,8 @@ struct Params {
   int B, Hkv, L, original_length, is_prefill, n_sink;
   const __nv_bfloat16* v;   // bf16 values, or
   const float* vf;          // f32 values (then v is NULL and no bf16 roundings apply)
+  const float* head_sums;   // or per-head value sums (h, token) from value_head_sums_kernel
+  long long hs_stride;      // (head-sharded caches: the heads live on other ranks)
   const int64_t* positions;
   const uint8_t* special;
   float* features;
@@ -177,7 +179,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int b = active ? (int)(gi / p.L) : 0;
     const int i = active ? (int)(gi % p.L) : 0;
     // ---- 1. auxiliary features (features.py:886-921) ----
-    if (active && p.vf != nullptr) {
+    if (active && p.head_sums != nullptr) {
+      for (int h = half; h < p.Hkv; h += 2)
+        sf[kFHs + t * kMaxHkv + h] = p.head_sums[(long long)h * p.hs_stride + gi];
+    } else if (active && p.vf != nullptr) {
       for (int h = half; h < p.Hkv; h += 2) {
         const float4* row =
             reinterpret_cast<const float4*>(p.vf + (((long long)b * p.Hkv + h) * p.L + i) * 128);
@@ -338,6 +343,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Per-(head, token) value sums of squares in the arithmetic of the indexer's
+// auxiliary block (squares rounded to bf16 and added in index order, the sum
+// rounded to bf16), for head-sharded caches: out[h * out_stride + token].
+// One thread per row, like the indexer, so the sums agree bit for bit.
+__global__ void value_head_sums_kernel(const __nv_bfloat16* __restrict__ v, int Hkv, int L,
+                                       float* __restrict__ out, long long out_stride) {
+  const long long row = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= (long long)Hkv * L) return;
+  const uint4* rowp = reinterpret_cast<const uint4*>(v + row * 128);
+  uint4 w[16];  // the whole 256-byte row in flight at once
+#pragma unroll
+  for (int c = 0; c < 16; ++c) w[c] = __ldg(rowp + c);
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w[c]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f2 = __bfloat1622float2(h2[e]);
+      s += bf16_round(f2.x * f2.x);
+      s += bf16_round(f2.y * f2.y);
+    }
+  }
+  const int h = (int)(row / L), t = (int)(row % L);
+  out[(long long)h * out_stride + t] = bf16_round(s);
+}
+
 }  // namespace idx
 }  // namespace core
 
@@ -385,4 +417,66 @@ extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const in
   indexer_scores_kernel<<<(unsigned)blocks, kThreads, smem, s>>>(p);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "indexer_scores_kernel launch");
   return CORE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Head-sharded caches (one sequence).
+// ---------------------------------------------------------------------------
+extern "C" int core_value_head_sums(const core_dims_t* d, const void* v, float* out,
+                                    int64_t out_stride, void* stream) {
+  int rc = check_dims(d, "core_value_head_sums");
+  if (rc != CORE_OK) return rc;
+  if (v == nullptr || out == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_value_head_sums: NULL tensor");
+  if (d->batch != 1) return set_error(CORE_ERR_UNSUPPORTED, "core_value_head_sums: one sequence");
+  if (out_stride < d->seq_len)
+    return set_error(CORE_ERR_INVALID_ARG, "core_value_head_sums: out_stride < seq_len");
+  const long long rows = (long long)d->n_kv_heads * d->seq_len;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  value_head_sums_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(v), d->n_kv_heads, d->seq_len, out, out_stride);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "value_head_sums_kernel launch");
+}
+
+extern "C" int core_indexer_scores_from_sums(int32_t n_kv_heads, int32_t n_keys,
+                                             const float* head_sums, int64_t hs_stride,
+                                             const int64_t* positions, const uint8_t* special,
+                                             int32_t original_length, int32_t is_prefill,
+                                             int32_t n_sink, float* features, const float* mlp,
+                                             float* scores, void* stream) {
+  if (head_sums == nullptr || positions == nullptr || features == nullptr || mlp == nullptr ||
+      scores == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores_from_sums: NULL tensor");
+  if (reinterpret_cast<uintptr_t>(mlp) % 16 != 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores_from_sums: mlp must be 16-byte aligned");
+  if (n_kv_heads <= 0 || n_kv_heads > kMaxHkv)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_indexer_scores_from_sums: 1 to 16 KV heads");
+  if (n_keys < 0 || hs_stride < n_keys || original_length < n_keys)
+    return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores_from_sums: bad sizes");
+  if (n_keys == 0) return CORE_OK;
+  Params p{};
+  p.B = 1;
+  p.Hkv = n_kv_heads;
+  p.L = n_keys;
+  p.original_length = original_length;
+  p.is_prefill = is_prefill;
+  p.n_sink = n_sink;
+  p.head_sums = head_sums;
+  p.hs_stride = hs_stride;
+  p.positions = positions;
+  p.special = special;
+  p.features = features;
+  p.mlp = mlp;
+  p.scores = scores;
+  p.status = device_status();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e =
+      cudaFuncSetAttribute(indexer_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return cuda_error(e, "indexer_scores_kernel attribute");
+  const long long n_tiles = ((long long)n_keys + kTile - 1) / kTile;
+  const long long blocks = n_tiles < sm_count() ? n_tiles : sm_count();
+  indexer_scores_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, s>>>(p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "indexer_scores_kernel launch");
 }

@@ -219,7 +219,10 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
       for (int i = 0; i < kPer; ++i) {
         const int kidx = et * kTok + ((tid + i * kProdThreads) >> 3);
         // an index outside the cache (error 802 of the mass kernel) gathers a zero row
-        const int ix = kidx < p.n_evict ? p.evict[(long long)b * p.n_evict + kidx] : -1;
+        // evict NULL: the rows are already gathered (row kidx is evicted token kidx)
+        const int ix = kidx < p.n_evict
+                           ? (p.evict != nullptr ? p.evict[(long long)b * p.n_evict + kidx] : kidx)
+                           : -1;
         toks[i] = (unsigned)ix < (unsigned)p.L ? ix : -1;
       }
       for (int c = 0; c < n_chunks && ok; ++c, ++it) {
@@ -429,7 +432,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
         const int kidx = kc * kMbarChunk + (tid + i * kProdThreads) / (kAtoms * 8);
-        const int ix = kidx < p.n_evict ? p.evict[kidx] : -1;
+        const int ix = kidx < p.n_evict ? (p.evict != nullptr ? p.evict[kidx] : kidx) : -1;
         toks[i] = (unsigned)ix < (unsigned)p.L ? ix : -1;  // outside the cache: zero row
       }
       if (it >= kMbStages && !(ok = wait(bar_empty(st), ((it / kMbStages) - 1) & 1, 911))) break;
@@ -547,7 +550,7 @@ __global__ void __launch_bounds__(256)
   const int kvw = Hkv * kD;
   if (tid < kTok) {
     const int e = et * kTok + tid;
-    const int ix = e < n_evict ? evict[e] : -1;
+    const int ix = e < n_evict ? (evict != nullptr ? evict[e] : e) : -1;
     sTok[tid] = (unsigned)ix < (unsigned)L ? ix : -1;
   }
   float acc[4][8];
@@ -631,7 +634,7 @@ __global__ void __launch_bounds__(256)
     __syncthreads();  // the previous chunk's readers are done
     if (tid < kF32Chunk) {
       const int e = e0 + tid;
-      const int ix = e < n_evict ? evict[e] : -1;
+      const int ix = e < n_evict ? (evict != nullptr ? evict[e] : e) : -1;
       sTok[tid] = (unsigned)ix < (unsigned)L ? ix : -1;
     }
     for (int i = tid; i < kF32Rows * kF32Chunk; i += 256) {
@@ -746,12 +749,13 @@ extern "C" size_t core_memory_write_workspace_bytes(const core_dims_t* d, int32_
   return z.used;
 }
 
-extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void* v,
-                                 const float* scores_cal, const int32_t* evict_idx,
-                                 int32_t n_evict, const void* theta_split, int32_t d_mem,
-                                 float gamma, float eta, float student_temp, float* M,
-                                 float* b_state, float* Z, void* workspace,
-                                 size_t workspace_bytes, void* stream) {
+// gathered: k, v hold only the evicted rows, (B, Hkv, n_evict, d) in evict_idx
+// order; evict_idx still indexes scores_cal (the softmax runs over the cache).
+static int memory_write_impl(const core_dims_t* d, const void* k, const void* v,
+                             const float* scores_cal, const int32_t* evict_idx, int32_t n_evict,
+                             const void* theta_split, int32_t d_mem, float gamma, float eta,
+                             float student_temp, float* M, float* b_state, float* Z,
+                             void* workspace, size_t workspace_bytes, void* stream, bool gathered) {
   int rc = check_dims(d, "core_memory_write", true);
   if (rc != CORE_OK) return rc;
   if (k == nullptr || v == nullptr || scores_cal == nullptr || evict_idx == nullptr ||
@@ -764,6 +768,7 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
   if (!(student_temp > 0.f)) return set_error(CORE_ERR_INVALID_ARG, "student_temp must be > 0");
   MwPlan m;
   plan_mw(d, n_evict, d_mem, &m);
+  const int kv_rows = gathered ? n_evict : d->seq_len;  // rows per (batch, head) of k and v
   Carver cv(workspace, workspace_bytes);
   float* pbar = cv.take<float>((size_t)d->batch * m.n_ev_pad);
   float* coef = cv.take<float>((size_t)d->batch * 3);
@@ -792,15 +797,17 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
   if (d->dtype == CORE_DTYPE_F32) {
     float* wtf = reinterpret_cast<float*>(wt);  // (d_pad, n_ev_pad) f32 in the bytes of the two terms
     for (int b = 0; b < d->batch; ++b) {
-      const long long kv_off = (long long)b * d->n_kv_heads * d->seq_len * kD;
+      const long long kv_off = (long long)b * d->n_kv_heads * kv_rows * kD;
       mw_phi_f32_kernel<<<dim3(m.n_et, m.d_pad / kF32Rows), 256, 0, s>>>(
           static_cast<const float*>(theta_split), static_cast<const float*>(k) + kv_off,
-          evict_idx + (long long)b * n_evict, pbar + (long long)b * m.n_ev_pad, d->n_kv_heads,
-          d->seq_len, n_evict, m.n_ev_pad, d_mem, m.d_pad, wtf, bpart + (long long)b * m.n_et * m.d_pad);
+          gathered ? nullptr : evict_idx + (long long)b * n_evict, pbar + (long long)b * m.n_ev_pad,
+          d->n_kv_heads, kv_rows, n_evict, m.n_ev_pad, d_mem, m.d_pad, wtf,
+          bpart + (long long)b * m.n_et * m.d_pad);
       if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_phi_f32_kernel launch");
       mw_mbar_f32_kernel<<<dim3(m.kvw / 64, m.d_pad / kF32Rows, m.splits), 256, 0, s>>>(
-          wtf, static_cast<const float*>(v) + kv_off, evict_idx + (long long)b * n_evict,
-          d->n_kv_heads, d->seq_len, n_evict, m.n_ev_pad, m.d_pad, m.splits,
+          wtf, static_cast<const float*>(v) + kv_off,
+          gathered ? nullptr : evict_idx + (long long)b * n_evict, d->n_kv_heads, kv_rows, n_evict,
+          m.n_ev_pad, m.d_pad, m.splits,
           (long long)d->batch * m.d_pad * m.kvw, mpart + (long long)b * m.d_pad * m.kvw);
       if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_mbar_f32_kernel launch");
     }
@@ -833,12 +840,12 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
 
   for (int b = 0; b < d->batch; ++b) {
     PhiParams pp{};
-    pp.B = 1; pp.Hkv = d->n_kv_heads; pp.L = d->seq_len; pp.n_evict = n_evict;
+    pp.B = 1; pp.Hkv = d->n_kv_heads; pp.L = kv_rows; pp.n_evict = n_evict;
     pp.n_ev_pad = m.n_ev_pad; pp.n_et = m.n_et; pp.d_mem = d_mem; pp.d_pad = m.d_pad;
     pp.n_dh = m.n_dh;
     pp.U = (long long)m.n_et * m.n_dh;
-    pp.k = static_cast<const __nv_bfloat16*>(k) + (long long)b * d->n_kv_heads * d->seq_len * kD;
-    pp.evict = evict_idx + (long long)b * n_evict;
+    pp.k = static_cast<const __nv_bfloat16*>(k) + (long long)b * d->n_kv_heads * kv_rows * kD;
+    pp.evict = gathered ? nullptr : evict_idx + (long long)b * n_evict;
     pp.pbar = pbar + (long long)b * m.n_ev_pad;
     pp.wt = wt;
     pp.bpart = bpart + (long long)b * m.n_et * m.d_pad;
@@ -849,12 +856,12 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_phi_kernel launch");
 
     MbarParams mq{};
-    mq.Hkv = d->n_kv_heads; mq.L = d->seq_len; mq.n_evict = n_evict;
+    mq.Hkv = d->n_kv_heads; mq.L = kv_rows; mq.n_evict = n_evict;
     mq.n_ev_pad = m.n_ev_pad; mq.d_pad = m.d_pad; mq.kvw = m.kvw; mq.n_jt = m.n_jt;
     mq.n_ct = m.n_ct; mq.splits = m.splits;
     mq.split_stride = (long long)d->batch * m.d_pad * m.kvw;
-    mq.v = static_cast<const __nv_bfloat16*>(v) + (long long)b * d->n_kv_heads * d->seq_len * kD;
-    mq.evict = evict_idx + (long long)b * n_evict;
+    mq.v = static_cast<const __nv_bfloat16*>(v) + (long long)b * d->n_kv_heads * kv_rows * kD;
+    mq.evict = gathered ? nullptr : evict_idx + (long long)b * n_evict;
     mq.mpart = mpart + (long long)b * m.d_pad * m.kvw;
     mq.status = st;
     if (m.ct == 256)
@@ -869,4 +876,24 @@ extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void
                                                              m.kvw, bpart, m.n_et, coef, eta, M, b_state);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_update_kernel launch");
   return CORE_OK;
+}
+
+extern "C" int core_memory_write(const core_dims_t* d, const void* k, const void* v,
+                                 const float* scores_cal, const int32_t* evict_idx,
+                                 int32_t n_evict, const void* theta_split, int32_t d_mem,
+                                 float gamma, float eta, float student_temp, float* M,
+                                 float* b_state, float* Z, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  return memory_write_impl(d, k, v, scores_cal, evict_idx, n_evict, theta_split, d_mem, gamma, eta,
+                           student_temp, M, b_state, Z, workspace, workspace_bytes, stream, false);
+}
+
+extern "C" int core_memory_write_gathered(const core_dims_t* d, const void* k_ev, const void* v_ev,
+                                          const float* scores_cal, const int32_t* evict_idx,
+                                          int32_t n_evict, const void* theta_split, int32_t d_mem,
+                                          float gamma, float eta, float student_temp, float* M,
+                                          float* b_state, float* Z, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  return memory_write_impl(d, k_ev, v_ev, scores_cal, evict_idx, n_evict, theta_split, d_mem, gamma,
+                           eta, student_temp, M, b_state, Z, workspace, workspace_bytes, stream, true);
 }

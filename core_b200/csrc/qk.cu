@@ -689,6 +689,11 @@ struct MergeParams {
   const float* lse;        // (B, Hq, nq)
   float* features;
   int stride;
+  uint32_t* summary;     // summary mode (head-sharded caches): per-key summaries instead of features
+  int sum_words;         // words per summary: kSumHead + 4 n_qb
+  float* f6_target;      // where qk_f6_resolve_kernel adds a positive head: features[:, 5] or summary word 10
+  int f6_stride;
+  float f6_inc;          // 1 / Hkv (features) or 1 (summary count)
   int* queue_count;      // undecided f6 (key, head) pairs, resolved by qk_f6_resolve_kernel
   int2* queue;
   int queue_cap;
@@ -802,6 +807,7 @@ __global__ void __launch_bounds__(kMergeThreads)
   int f6pos = 0;
   const uint32_t* base = p.rec + ((long long)b * p.L + key) * p.Hkv * p.n_qb * kRecWords;
   // f5: OR over heads of the per-query positive bits, per query block
+  uint32_t* sum_out = p.summary != nullptr ? p.summary + gi * p.sum_words : nullptr;
   for (int qb = 0; qb < p.n_qb; ++qb) {
     uint32_t w[4] = {0, 0, 0, 0};
     for (int h = 0; h < p.Hkv; ++h) {
@@ -813,6 +819,8 @@ __global__ void __launch_bounds__(kMergeThreads)
       w[3] |= r3.y;
     }
     f5cnt += __popc(w[0]) + __popc(w[1]) + __popc(w[2]) + __popc(w[3]);
+    if (sum_out != nullptr)
+      reinterpret_cast<uint4*>(sum_out + kSumHead)[qb] = make_uint4(w[0], w[1], w[2], w[3]);
   }
   for (int h = 0; h < p.Hkv; ++h) {
     float hs = 0.f, mx = -INFINITY;
@@ -852,6 +860,15 @@ __global__ void __launch_bounds__(kMergeThreads)
         else record_error(p.status, CORE_ERR_UNSUPPORTED, 401, key);
       }
     }
+  }
+  if (sum_out != nullptr) {  // this rank's heads only: the cross-rank merge finishes f1..f6
+    uint4* o = reinterpret_cast<uint4*>(sum_out);
+    o[0] = make_uint4(__float_as_uint(top[0]), __float_as_uint(top[1]), __float_as_uint(top[2]),
+                      __float_as_uint(top[3]));
+    o[1] = make_uint4(__float_as_uint(rtop[0]), __float_as_uint(rtop[1]), __float_as_uint(rtop[2]),
+                      __float_as_uint(rtop[3]));
+    o[2] = make_uint4(__float_as_uint(psum), (uint32_t)pcnt, __float_as_uint((float)f6pos), 0u);
+    return;
   }
   float f[6];
   f[0] = top[0];
@@ -909,11 +926,90 @@ __global__ void __launch_bounds__(kResolveThreads)
       const int kfr = max((vld + 3) / 4, 1);
       float sum = 0.f;
       for (int i = 0; i < kfr; ++i) sum += s_sorted[i];
-      if (sum / (float)kfr > 0.f)
-        atomicAdd(p.features + (long long)item.x * p.stride + 5, 1.0f / (float)p.Hkv);
+      if (sum / (float)kfr > 0.f) atomicAdd(p.f6_target + (long long)item.x * p.f6_stride, p.f6_inc);
     }
     __syncthreads();
   }
+}
+
+
+// Cross-rank merge of head-sharded summaries (one sequence): for keys key0 +
+// [0, n) the n_parts summaries of the ranks' KV heads (each written by
+// qk_merge_kernel in summary mode over that rank's heads) combine into f1..f6
+// exactly as qk_merge_kernel combines heads: the union's top 4 (order-free),
+// summed positive mass and counts, the OR of the positive-query bits, and the
+// positive-head count over all Hkv heads.
+struct SumMergeParams {
+  const uint32_t* parts;   // (n_parts, part_rows, sum_words)
+  long long part_rows;
+  int n_parts, n, key0, L, nq, q_start, n_qb, Hkv, topk, n_recent, sum_words;
+  float* features;         // rows key0 .. key0 + n - 1 at features + i * stride
+  int stride;
+  DeviceStatus* status;
+};
+
+__global__ void __launch_bounds__(kMergeThreads)
+    qk_summary_merge_kernel(const SumMergeParams p) {
+  const int i = blockIdx.x * kMergeThreads + threadIdx.x;
+  if (i >= p.n) return;
+  const int key = p.key0 + i;
+  int valid = p.nq - max(key - p.q_start, 0);
+  valid = min(max(valid, 1), p.nq);
+  const int k2max = min(p.topk, p.nq * p.Hkv);
+  const int k2 = min(max(valid * p.Hkv, 1), k2max);
+  const int nrec = p.n_recent;
+  const int rstart = p.q_start + p.nq - nrec;
+  int rvalid = p.q_start + p.nq - max(key, rstart);
+  rvalid = min(max(rvalid, 1), nrec);
+  const int k4max = min(p.topk, nrec * p.Hkv);
+  const int k4 = min(max(rvalid * p.Hkv, 1), k4max);
+  float top[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  float rtop[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+  float psum = 0.f, f6pos = 0.f;
+  unsigned long long pcnt = 0;
+  for (int part = 0; part < p.n_parts; ++part) {
+    const uint4* r = reinterpret_cast<const uint4*>(
+        p.parts + ((long long)part * p.part_rows + i) * p.sum_words);
+    const uint4 r0 = r[0], r1 = r[1], r2 = r[2];
+    top4_insert(top, __uint_as_float(r0.x));
+    top4_insert(top, __uint_as_float(r0.y));
+    top4_insert(top, __uint_as_float(r0.z));
+    top4_insert(top, __uint_as_float(r0.w));
+    top4_insert(rtop, __uint_as_float(r1.x));
+    top4_insert(rtop, __uint_as_float(r1.y));
+    top4_insert(rtop, __uint_as_float(r1.z));
+    top4_insert(rtop, __uint_as_float(r1.w));
+    psum += __uint_as_float(r2.x);
+    pcnt += r2.y;
+    f6pos += __uint_as_float(r2.z);
+  }
+  int f5cnt = 0;
+  for (int qb = 0; qb < p.n_qb; ++qb) {
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    for (int part = 0; part < p.n_parts; ++part) {
+      const uint4 x = reinterpret_cast<const uint4*>(
+          p.parts + ((long long)part * p.part_rows + i) * p.sum_words + kSumHead)[qb];
+      w.x |= x.x;
+      w.y |= x.y;
+      w.z |= x.z;
+      w.w |= x.w;
+    }
+    f5cnt += __popc(w.x) + __popc(w.y) + __popc(w.z) + __popc(w.w);
+  }
+  float f[6];
+  f[0] = top[0];
+  f[1] = sum_top_desc(top, k2) / (float)k2;
+  f[2] = psum / (float)(pcnt > 0 ? pcnt : 1);
+  f[3] = sum_top_desc(rtop, k4) / (float)k4;
+  f[4] = (float)f5cnt / (float)p.nq;
+  f[5] = f6pos / (float)p.Hkv;
+  float* out = p.features + (long long)i * p.stride;
+  bool finite = true;
+  for (int j = 0; j < 6; ++j) {
+    out[j] = f[j];
+    finite &= isfinite(f[j]);
+  }
+  if (!finite) record_error(p.status, CORE_ERR_NONFINITE, 403, key);
 }
 
 }  // namespace qk
@@ -1018,7 +1114,8 @@ int qk_f32_records(const core_dims_t* d, int q_start, int n_qb, int head_topk, i
 int qk_features_impl(const core_dims_t* d, const void* q, const void* k, int32_t topk_qk,
                      int32_t n_recent_queries, const float* lse_in, float* lse_out,
                      float* features, int32_t feature_stride, void* workspace,
-                     size_t workspace_bytes, void* stream, void* ev0, void* ev1);
+                     size_t workspace_bytes, void* stream, void* ev0, void* ev1,
+                     uint32_t* summary = nullptr);
 }
 
 extern "C" int core_qk_features(const core_dims_t* d, const void* q, const void* k,
@@ -1033,12 +1130,13 @@ extern "C" int core_qk_features(const core_dims_t* d, const void* q, const void*
 int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, int32_t topk_qk,
                            int32_t n_recent_queries, const float* lse_in, float* lse_out,
                            float* features, int32_t feature_stride, void* workspace,
-                           size_t workspace_bytes, void* stream, void* ev0_, void* ev1_) {
+                           size_t workspace_bytes, void* stream, void* ev0_, void* ev1_,
+                           uint32_t* summary) {
   cudaEvent_t ev0 = static_cast<cudaEvent_t>(ev0_), ev1 = static_cast<cudaEvent_t>(ev1_);
   int rc = check_dims(d, "core_qk_features", true);
   if (rc != CORE_OK) return rc;
   const bool f32 = d->dtype == CORE_DTYPE_F32;
-  if (q == nullptr || k == nullptr || features == nullptr)
+  if (q == nullptr || k == nullptr || (features == nullptr && summary == nullptr))
     return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: NULL tensor");
   if (d->n_queries <= 0) return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: no queries");
   if (topk_qk <= 0 || topk_qk > 4)
@@ -1048,7 +1146,8 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
     return set_error(CORE_ERR_UNSUPPORTED,
                      "core_qk_features: requires topk_qk >= group size - 1 (fused_qk.py:19-21)");
   if (n_recent_queries <= 0) return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: n_recent <= 0");
-  if (feature_stride < 6) return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: feature_stride < 6");
+  if (summary == nullptr && feature_stride < 6)
+    return set_error(CORE_ERR_INVALID_ARG, "core_qk_features: feature_stride < 6");
   QKPlan plan;
   plan_qk(d, topk_qk, n_recent_queries, &plan);
   Params& p = plan.p;
@@ -1116,6 +1215,17 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
   mp.kf = f32 ? static_cast<const float*>(k) : nullptr;
   mp.lse = lse_buf; mp.features = features; mp.stride = feature_stride; mp.status = p.status;
   mp.queue_count = queue_count; mp.queue = queue; mp.queue_cap = (int)queue_cap_for(d);
+  mp.summary = summary;
+  mp.sum_words = kSumHead + 4 * p.n_qb;
+  if (summary != nullptr) {
+    mp.f6_target = reinterpret_cast<float*>(summary) + 10;
+    mp.f6_stride = mp.sum_words;
+    mp.f6_inc = 1.0f;
+  } else {
+    mp.f6_target = features + 5;
+    mp.f6_stride = feature_stride;
+    mp.f6_inc = 1.0f / (float)p.Hkv;
+  }
   if ((p.Hkv & (p.Hkv - 1)) != 0)
     return set_error(CORE_ERR_UNSUPPORTED, "core_qk_features: n_kv_heads must be a power of two");
   e = cudaMemsetAsync(queue_count, 0, sizeof(int), s);
@@ -1131,4 +1241,60 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
     if (e != cudaSuccess) return cuda_error(e, "core_qk_features lse copy out");
   }
   return CORE_OK;
+}
+
+extern "C" int32_t core_qk_summary_words(int32_t n_queries) {
+  if (n_queries <= 0) return 0;
+  return kSumHead + 4 * ((n_queries + kTile - 1) / kTile);
+}
+
+extern "C" int core_qk_head_summary(const core_dims_t* d, const void* q, const void* k,
+                                    int32_t topk_qk, int32_t n_recent_queries, float* lse_out,
+                                    uint32_t* summary, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  if (summary == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_qk_head_summary: NULL summary");
+  if (reinterpret_cast<uintptr_t>(summary) % 16 != 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_qk_head_summary: summary must be 16-byte aligned");
+  return core::qk_features_impl(d, q, k, topk_qk, n_recent_queries, nullptr, lse_out, nullptr, 0,
+                                workspace, workspace_bytes, stream, nullptr, nullptr, summary);
+}
+
+extern "C" int core_qk_merge_summaries(const uint32_t* parts, int32_t n_parts, int64_t part_rows,
+                                       int32_t key0, int32_t n_keys, int32_t seq_len,
+                                       int32_t n_queries, int32_t n_kv_heads, int32_t topk_qk,
+                                       int32_t n_recent_queries, float* features,
+                                       int32_t feature_stride, void* stream) {
+  if (parts == nullptr || features == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_qk_merge_summaries: NULL tensor");
+  if (reinterpret_cast<uintptr_t>(parts) % 16 != 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_qk_merge_summaries: parts must be 16-byte aligned");
+  if (n_parts <= 0 || n_keys < 0 || key0 < 0 || key0 + n_keys > seq_len || part_rows < n_keys ||
+      n_queries <= 0 || n_queries > seq_len || n_kv_heads <= 0 || feature_stride < 6)
+    return set_error(CORE_ERR_INVALID_ARG, "core_qk_merge_summaries: bad sizes");
+  if (topk_qk <= 0 || topk_qk > 4 || n_recent_queries <= 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_qk_merge_summaries: bad topk / n_recent");
+  if (n_keys == 0) return CORE_OK;
+  SumMergeParams p{};
+  p.parts = parts;
+  p.part_rows = part_rows;
+  p.n_parts = n_parts;
+  p.n = n_keys;
+  p.key0 = key0;
+  p.L = seq_len;
+  p.nq = n_queries;
+  p.q_start = seq_len - n_queries;
+  p.n_qb = (n_queries + kTile - 1) / kTile;
+  p.Hkv = n_kv_heads;
+  p.topk = topk_qk;
+  p.n_recent = n_recent_queries < n_queries ? n_recent_queries : n_queries;
+  p.sum_words = kSumHead + 4 * p.n_qb;
+  p.features = features;
+  p.stride = feature_stride;
+  p.status = device_status();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  qk_summary_merge_kernel<<<(unsigned)((n_keys + kMergeThreads - 1) / kMergeThreads), kMergeThreads,
+                            0, s>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "qk_summary_merge_kernel launch");
 }

@@ -20,6 +20,12 @@ constexpr float kLn2 = 0.6931471805599453f;
 //   [10..13] positive-R bits, query 32 w + b of the block in word w, bit b
 //   [14]    max of the non-positive R      [15] unused
 constexpr int kRecWords = 16;
+// Per-key summary of one rank's KV heads (head-sharded caches), sum_words =
+// kSumHead + 4 n_qb words: 0-3 top-4 relation values (descending), 4-7 top-4
+// of the recent queries, 8 positive sum (f32), 9 positive count, 10 positive-
+// head count for f6 (f32), 11 unused, then 4 words of positive-query bits (OR
+// over the heads) per 128-query block.
+constexpr int kSumHead = 12;
 
 __device__ __forceinline__ float logaddexp_floor(float r) {
   // max(r, f) + log1p(exp(-|r - f|)), f = log(1e-8)  (fused_qk.py:200-202)

@@ -270,3 +270,179 @@ def memory_readout(q: torch.Tensor, theta: torch.Tensor, gate, M: torch.Tensor,
         d_mem, gh, go, _ptr(M), _ptr(b_state), _ptr(o_fold), hidden, _ptr(attn_out), _ptr(ws),
         ws.numel(), _stream(q.device)))
     return attn_out
+
+
+# ---------------------------------------------------------------------------
+# Head-sharded caches (one sequence, KV heads split across ranks).  Each call
+# is one rank's part of a layer step; the cross-head sums between them are
+# the caller's (core_b200.sharded runs them with NCCL).
+# ---------------------------------------------------------------------------
+
+def qk_summary_words(n_queries: int) -> int:
+    return int(_lib.load().core_qk_summary_words(int(n_queries)))
+
+
+def qk_head_summary(q: torch.Tensor, k: torch.Tensor, summary: torch.Tensor, *,
+                    topk_qk: int = 4, n_recent_queries: int = 16) -> torch.Tensor:
+    """Per-key summaries of this rank's heads into ``summary`` (rows >= L,
+    core_qk_summary_words(nq)) int32; returns the rank's LSE (Hq_rank, nq)."""
+    _require_cuda(q, k, summary)
+    q = q.contiguous()
+    k = k.contiguous()
+    B, Hq, nq, d = q.shape
+    if B != 1 or k.dtype != torch.bfloat16 or q.dtype != torch.bfloat16:
+        raise ValueError("head-sharded summaries take one bf16 sequence")
+    words = qk_summary_words(nq)
+    if (summary.dim() != 2 or summary.shape[0] < k.shape[2] or summary.shape[1] != words
+            or summary.dtype != torch.int32 or not summary.is_contiguous()):
+        raise ValueError(f"summary must be a contiguous (>= L, {words}) int32 tensor")
+    dims = _dims(k, Hq, nq)
+    lib = _lib.load()
+    lse = torch.empty(Hq, nq, dtype=torch.float32, device=k.device)
+    ws = _workspace(lib.core_qk_features_workspace_bytes(ctypes.byref(dims)), k.device)
+    check(lib.core_qk_head_summary(ctypes.byref(dims), _ptr(q), _ptr(k), int(topk_qk),
+                                   int(n_recent_queries), _ptr(lse), _ptr(summary), _ptr(ws),
+                                   ws.numel(), _stream(k.device)))
+    return lse
+
+
+def qk_merge_summaries(parts: torch.Tensor, features: torch.Tensor, *, key0: int, n_keys: int,
+                       seq_len: int, n_queries: int, n_kv_heads: int, topk_qk: int = 4,
+                       n_recent_queries: int = 16) -> None:
+    """f1..f6 of keys key0 .. key0 + n_keys - 1 into features[:n_keys, :6] from
+    the ranks' summaries ``parts`` (n_parts, rows, words)."""
+    _require_cuda(parts, features)
+    if parts.dim() != 3 or not parts.is_contiguous() or parts.dtype != torch.int32:
+        raise ValueError("parts must be a contiguous (n_parts, rows, words) int32 tensor")
+    if features.dim() != 2 or not features.is_contiguous() or features.shape[0] < n_keys:
+        raise ValueError("features must be a contiguous (>= n_keys, F) float32 tensor")
+    check(_lib.load().core_qk_merge_summaries(
+        _ptr(parts), parts.shape[0], parts.shape[1], int(key0), int(n_keys), int(seq_len),
+        int(n_queries), int(n_kv_heads), int(topk_qk), int(n_recent_queries), _ptr(features),
+        features.shape[1], _stream(parts.device)))
+
+
+def coverage_partial_projection(k: torch.Tensor, geometry_ext: torch.Tensor, y: torch.Tensor) -> None:
+    """y[:L] = sum over this rank's heads of W_h k_h / |k_h| (raw, (L, 64) f32)."""
+    _require_cuda(k, geometry_ext, y)
+    k = k.contiguous()
+    B, hkv, L, d = k.shape
+    if B != 1:
+        raise ValueError("head-sharded coverage takes one sequence")
+    if tuple(geometry_ext.shape) != (3, 128, hkv * d):
+        raise ValueError("geometry_ext must hold this rank's columns, (3, 128, Hkv_rank*d)")
+    if y.dim() != 2 or y.shape[0] < L or y.shape[1] != 64 or not y.is_contiguous():
+        raise ValueError("y must be a contiguous (>= L, 64) float32 tensor")
+    dims = _dims(k, hkv, 0)
+    lib = _lib.load()
+    ws = _workspace(lib.core_coverage_workspace_bytes(ctypes.byref(dims)), k.device)
+    check(lib.core_coverage_partial_projection(ctypes.byref(dims), _ptr(k),
+                                               _ptr(geometry_ext.contiguous()), _ptr(y), _ptr(ws),
+                                               ws.numel(), _stream(k.device)))
+
+
+def coverage_range_totals(y: torch.Tensor, hadamard: torch.Tensor):
+    """(z, zt, totals (192,) f64) for the summed projections y (n, 64) of a key range."""
+    _require_cuda(y, hadamard)
+    n = y.shape[0]
+    y = y.contiguous()
+    z = torch.empty(n, 64, dtype=torch.float32, device=y.device)
+    zt = torch.empty_like(z)
+    totals = torch.empty(192, dtype=torch.float64, device=y.device)
+    lib = _lib.load()
+    ws = _workspace(lib.core_coverage_range_workspace_bytes(n), y.device)
+    check(lib.core_coverage_range_totals(_ptr(y), n, _ptr(hadamard.float().contiguous()), _ptr(z),
+                                         _ptr(zt), _ptr(totals), _ptr(ws), ws.numel(),
+                                         _stream(y.device)))
+    return z, zt, totals
+
+
+def coverage_range_assign(totals: torch.Tensor, seq_len: int, z: torch.Tensor, zt: torch.Tensor,
+                          prototypes: torch.Tensor, features: torch.Tensor, *, col0: int = 6,
+                          shrinkage_rho: float = 0.1):
+    """Statistics of the summed totals, then d, delta and g of the range's keys
+    into features[:, col0 + 1 .. col0 + 3]; returns (assign, hist (64,) int32)."""
+    _require_cuda(totals, z, zt, prototypes, features)
+    n = z.shape[0]
+    assign = torch.empty(max(n, 1), dtype=torch.int32, device=z.device)
+    hist = torch.empty(64, dtype=torch.int32, device=z.device)
+    lib = _lib.load()
+    ws = _workspace(lib.core_coverage_range_workspace_bytes(n), z.device)
+    check(lib.core_coverage_range_assign(
+        _ptr(totals.contiguous()), int(seq_len), float(shrinkage_rho), _ptr(z), _ptr(zt), n,
+        _ptr(prototypes.float().contiguous()), _ptr(assign), _ptr(hist), _ptr(features),
+        features.shape[-1], int(col0), _ptr(ws), ws.numel(), _stream(z.device)))
+    return assign, hist
+
+
+def coverage_range_occupancy(assign: torch.Tensor, hist: torch.Tensor, features: torch.Tensor,
+                             n_keys: int, *, col0: int = 6) -> None:
+    _require_cuda(assign, hist, features)
+    check(_lib.load().core_coverage_range_occupancy(_ptr(assign), _ptr(hist.contiguous()),
+                                                    int(n_keys), _ptr(features),
+                                                    features.shape[-1], int(col0),
+                                                    _stream(features.device)))
+
+
+def value_head_sums(v: torch.Tensor, out: torch.Tensor) -> None:
+    """out[h, :L] = the bf16 sum of bf16 squares of each value row of this rank's heads."""
+    _require_cuda(v, out)
+    v = v.contiguous()
+    B, hkv, L, d = v.shape
+    if out.dim() != 2 or out.shape[0] != hkv or out.shape[1] < L or not out.is_contiguous():
+        raise ValueError("out must be a contiguous (Hkv_rank, >= L) float32 tensor")
+    dims = _dims(v, hkv, 0)
+    check(_lib.load().core_value_head_sums(ctypes.byref(dims), _ptr(v), _ptr(out), out.shape[1],
+                                           _stream(v.device)))
+
+
+def indexer_scores_from_sums(head_sums: torch.Tensor, key0: int, n_keys: int,
+                             positions: torch.Tensor, features: torch.Tensor,
+                             mlp_packed: torch.Tensor, *, original_length: int, is_prefill: bool,
+                             n_sink: int = 4, special: torch.Tensor | None = None) -> torch.Tensor:
+    """Scores of keys key0 .. key0 + n_keys - 1 from all heads' value sums
+    head_sums (Hkv, stride); positions/special are the whole sequence's,
+    features (n_keys, 14) the range's."""
+    _require_cuda(head_sums, positions, features, mlp_packed, special)
+    if not head_sums.is_contiguous() or head_sums.dim() != 2:
+        raise ValueError("head_sums must be a contiguous (Hkv, stride) float32 tensor")
+    if features.shape[0] < n_keys or features.shape[1] != 14 or not features.is_contiguous():
+        raise ValueError("features must be a contiguous (>= n_keys, 14) float32 tensor")
+    pos = positions.to(torch.int64).reshape(-1).contiguous()
+    sp = None if special is None else special.to(torch.uint8).reshape(-1).contiguous()
+    scores = torch.empty(max(n_keys, 1), dtype=torch.float32, device=features.device)
+    hs_ptr = head_sums.data_ptr() + 4 * int(key0)
+    pos_ptr = pos.data_ptr() + 8 * int(key0)
+    sp_ptr = None if sp is None else sp.data_ptr() + int(key0)
+    check(_lib.load().core_indexer_scores_from_sums(
+        head_sums.shape[0], int(n_keys), ctypes.c_void_p(hs_ptr), head_sums.shape[1],
+        ctypes.c_void_p(pos_ptr), ctypes.c_void_p(sp_ptr), int(original_length), int(is_prefill),
+        int(n_sink), _ptr(features), _ptr(mlp_packed), _ptr(scores), _stream(features.device)))
+    return scores[:n_keys]
+
+
+def memory_write_gathered(k_ev: torch.Tensor, v_ev: torch.Tensor, scores_cal: torch.Tensor,
+                          evict: torch.Tensor, theta_split: torch.Tensor, M: torch.Tensor,
+                          b_state: torch.Tensor, Z: torch.Tensor, *, gamma: float, eta: float,
+                          student_temp: float) -> None:
+    """``memory_write`` with the evicted rows already gathered: k_ev, v_ev =
+    (B, Hkv, n_evict, d) in evict order; scores_cal (B, L)."""
+    _require_cuda(k_ev, v_ev, scores_cal, evict, theta_split, M, b_state, Z)
+    k_ev = k_ev.contiguous()
+    v_ev = v_ev.contiguous()
+    B, hkv, n_evict, d = k_ev.shape
+    L = scores_cal.shape[-1]
+    if evict.shape != (B, n_evict):
+        raise ValueError("evict must be (B, n_evict)")
+    if k_ev.dtype != torch.bfloat16 or theta_split.dim() != 3:
+        raise ValueError("gathered memory write takes bf16 rows and the (2, d_mem, Hkv*d) terms")
+    d_mem = theta_split.shape[1]
+    dims = CoreDims(B, hkv, hkv, d, 0, L, _lib.CORE_DTYPE_BF16)
+    lib = _lib.load()
+    ws = _workspace(lib.core_memory_write_workspace_bytes(ctypes.byref(dims), n_evict, d_mem),
+                    k_ev.device)
+    check(lib.core_memory_write_gathered(
+        ctypes.byref(dims), _ptr(k_ev), _ptr(v_ev), _ptr(scores_cal.float().contiguous()),
+        _ptr(evict.to(torch.int32).contiguous()), n_evict, _ptr(theta_split.contiguous()), d_mem,
+        float(gamma), float(eta), float(student_temp), _ptr(M), _ptr(b_state), _ptr(Z), _ptr(ws),
+        ws.numel(), _stream(k_ev.device)))

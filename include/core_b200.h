@@ -272,6 +272,98 @@ int core_compress_layer(const core_dims_t* dims, const void* q, const void* k, c
  * ------------------------------------------------------------------------- */
 int core_split_bf16(const float* src, int64_t n, int32_t terms, void* dst, void* stream);
 
+/* ===========================================================================
+ * Head-sharded caches: one sequence whose KV heads are split across ranks
+ * (one process per GPU).  The reference runs one process with all heads; these
+ * entry points are its per-layer functions split at their cross-head
+ * reductions, which the caller performs between the calls with NCCL:
+ *   rank r holds KV heads [r*Hkv/N, (r+1)*Hkv/N) and their query heads, and
+ *   finishes the features and scores of keys [r*Lc, min(L, (r+1)*Lc)),
+ *   Lc = ceil(L/N).  All are bf16-only and take dims with batch 1 and the
+ *   rank's own head counts, unless noted.
+ * ======================================================================== */
+
+/* Words per per-key QK summary for n_queries buffered queries (a multiple
+ * of 4). */
+int32_t core_qk_summary_words(int32_t n_queries);
+
+/* strict_causal_qk_features (core/fused_qk.py:373-587) over this rank's heads,
+ * stopped before the cross-head reduction: per key, the top-4 and recent top-4
+ * relation values, positive sum and count, the count of heads whose f6 test
+ * is positive, and the positive-query bits (OR over the heads).
+ *   summary : (L, core_qk_summary_words(nq)) uint32, 16-byte aligned
+ *   lse_out : optional (Hq_rank, nq) f32
+ * Workspace: core_qk_features_workspace_bytes(dims). */
+int core_qk_head_summary(const core_dims_t* dims, const void* q, const void* k, int32_t topk_qk,
+                         int32_t n_recent_queries, float* lse_out, uint32_t* summary,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* The cross-head reduction of core/fused_qk.py:505-582 for keys
+ * key0 .. key0 + n_keys - 1: parts = (n_parts, part_rows, words) summaries
+ * of those keys from every rank (row i = key key0 + i), n_kv_heads the total
+ * head count; writes f1..f6 to features[i * feature_stride + 0..5]. */
+int core_qk_merge_summaries(const uint32_t* parts, int32_t n_parts, int64_t part_rows,
+                            int32_t key0, int32_t n_keys, int32_t seq_len, int32_t n_queries,
+                            int32_t n_kv_heads, int32_t topk_qk, int32_t n_recent_queries,
+                            float* features, int32_t feature_stride, void* stream);
+
+/* LayerwiseKeyGeometryProjector.forward (core/features.py:53-77) before the
+ * head concatenation is complete: y = sum over this rank's heads of
+ * W_h k_h / (|k_h| + eps), (L, 64) f32, 16-byte aligned.  geometry_ext holds
+ * only this rank's columns, (3, 128, Hkv_rank*d) from core_prepare_geometry.
+ * Workspace: core_coverage_workspace_bytes(dims). */
+int core_coverage_partial_projection(const core_dims_t* dims, const void* k,
+                                     const void* geometry_ext, float* y, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
+/* The rest of compute_coverage_features (core/features.py:790-858) for the
+ * n_keys keys of a range, in three calls with two sums across ranks between
+ * them.  range_totals: z = y / (|y| + eps) for the summed y, zt = R z
+ * (HadamardProjector.rotate, :259-261; hadamard (64, 64) f32), and this
+ * range's column sums of z, zt, zt^2 as totals (192) f64.  range_assign:
+ * the statistics of the summed totals over all seq_len keys (mean z, mu,
+ * sigma2_eff), prototype assignment, d_proto, delta_proto and g, and this
+ * range's assignment histogram hist (64) int32.  range_occupancy: o from the
+ * summed histogram.  Workspace: core_coverage_range_workspace_bytes(n_keys). */
+size_t core_coverage_range_workspace_bytes(int32_t n_keys);
+int core_coverage_range_totals(const float* y, int32_t n_keys, const float* hadamard, float* z,
+                               float* zt, double* totals, void* workspace,
+                               size_t workspace_bytes, void* stream);
+int core_coverage_range_assign(const double* totals, int32_t seq_len, float shrinkage_rho,
+                               const float* z, const float* zt, int32_t n_keys,
+                               const float* prototypes, int32_t* assign, int32_t* hist,
+                               float* features, int32_t feature_stride, int32_t col0,
+                               void* workspace, size_t workspace_bytes, void* stream);
+int core_coverage_range_occupancy(const int32_t* assign, const int32_t* hist, int32_t n_keys,
+                                  float* features, int32_t feature_stride, int32_t col0,
+                                  void* stream);
+
+/* The per-head sums of compute_auxiliary_features' a_value
+ * (core/features.py:914-915) in the bf16 arithmetic of core_indexer_scores:
+ * out[h * out_stride + token] for this rank's heads. */
+int core_value_head_sums(const core_dims_t* dims, const void* v, float* out, int64_t out_stride,
+                         void* stream);
+
+/* core_indexer_scores for n_keys keys of one sequence, with the values'
+ * per-head sums (all n_kv_heads heads, head_sums[h * hs_stride + i] for key
+ * i of the range) in place of V; positions, special, features (n_keys, 14)
+ * and scores (n_keys) start at the range's first key. */
+int core_indexer_scores_from_sums(int32_t n_kv_heads, int32_t n_keys, const float* head_sums,
+                                  int64_t hs_stride, const int64_t* positions,
+                                  const uint8_t* special, int32_t original_length,
+                                  int32_t is_prefill, int32_t n_sink, float* features,
+                                  const float* mlp, float* scores, void* stream);
+
+/* core_memory_write on rows already gathered: k_ev, v_ev = (B, Hkv, n_evict,
+ * d) hold the evicted rows in evict_idx order (all heads, e.g. collected on
+ * the rank that owns the layer's memory state); evict_idx still indexes
+ * scores_cal (B, seq_len).  Same workspace as core_memory_write. */
+int core_memory_write_gathered(const core_dims_t* dims, const void* k_ev, const void* v_ev,
+                               const float* scores_cal, const int32_t* evict_idx, int32_t n_evict,
+                               const void* theta_split, int32_t d_mem, float gamma, float eta,
+                               float student_temp, float* M, float* b_state, float* Z,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,7 +15,7 @@ HEADER = ROOT / "include" / "core_b200.h"
 
 def declared_symbols():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^(?:int|size_t)\s+(core_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^(?:int|int32_t|size_t)\s+(core_\w+)\s*\(", text, flags=re.M)))
 
 
 def test_library_exports_every_declared_symbol():
