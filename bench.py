@@ -47,14 +47,17 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--layers", type=int, default=32)
-    p.add_argument("--seq-len", type=int, default=16384)
+    p.add_argument("--seq-len", type=int, default=None,
+                   help="cached tokens (default 16384; 131072 for --workload long)")
     p.add_argument("--batch", type=int, default=1, help="sequences per rank (batched serving)")
-    p.add_argument("--n-queries", type=int, default=128)
-    p.add_argument("--ratio", type=float, default=0.75)
+    p.add_argument("--n-queries", type=int, default=None,
+                   help="query buffer (default 128; 512 for --workload long)")
+    p.add_argument("--ratio", type=float, default=None,
+                   help="compression_ratio (default 0.75; 0.9 for --workload long)")
     p.add_argument("--d-mem", type=int, default=512)
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", default="prefill", choices=["prefill", "decode"],
+    p.add_argument("--workload", default="prefill", choices=["prefill", "decode", "long"],
                    help="prefill: the headline 32-layer compression step; decode: decode-time "
                         "recompression with the memory readout")
     p.add_argument("--decode-tokens", type=int, default=512)
@@ -63,7 +66,15 @@ def parse():
     p.add_argument("--streams", type=int, default=3, help="layers compressed concurrently")
     p.add_argument("--sm-reserve", type=int, default=2,
                    help="SMs the persistent grids leave free for the other streams' kernels")
-    return p.parse_args()
+    a = p.parse_args()
+    long = a.workload == "long"
+    if a.seq_len is None:
+        a.seq_len = 131072 if long else 16384
+    if a.n_queries is None:
+        a.n_queries = 512 if long else 128
+    if a.ratio is None:
+        a.ratio = 0.9 if long else 0.75
+    return a
 
 
 def config_dict(a, n):
@@ -151,12 +162,16 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU: the oracle port on a bounded sample
 # ---------------------------------------------------------------------------
+CPU_SAMPLE_MAX_LEN = 16384  # longer caches are sampled at this length (cost per token ~ constant)
+
+
 def cpu_layer_sample(a, seed=0):
-    """Time the oracle's compress_layer on one layer of the workload."""
+    """Time the oracle's compress_layer on one layer of the workload (at most
+    CPU_SAMPLE_MAX_LEN cached tokens)."""
     from core_b200 import checkpoint as C
     from oracle import core_oracle as O
     rng = np.random.default_rng(seed)
-    L, nq = a.seq_len, a.n_queries
+    L, nq = min(a.seq_len, CPU_SAMPLE_MAX_LEN), a.n_queries
     out_idx = np.stack([rng.choice(128, 4, replace=False) for _ in range(8)])
 
     def go(h, n, idx):
@@ -177,13 +192,22 @@ def cpu_layer_sample(a, seed=0):
     return time.perf_counter() - t0
 
 
+def _sample_note(a):
+    Ls = min(a.seq_len, CPU_SAMPLE_MAX_LEN)
+    if Ls == a.seq_len:
+        return f"L={Ls}"
+    return (f"L={Ls} standing in for L={a.seq_len}: the work per cached token is the same "
+            f"(nq fixed), so tokens/s carry over")
+
+
 def cpu_baseline(a):
     t = cpu_layer_sample(a)
-    return {"value": a.seq_len / (t * a.layers), "unit": UNIT, "cores": os.cpu_count(),
+    Ls = min(a.seq_len, CPU_SAMPLE_MAX_LEN)
+    return {"value": Ls / (t * a.layers), "unit": UNIT, "cores": os.cpu_count(),
             "kind": "port",
-            "sample": f"1 of {a.layers} layers (L={a.seq_len}, nq={a.n_queries}, bf16-rounded "
-                      f"inputs) through oracle.core_oracle.compress_layer in {t:.2f} s, "
-                      f"scaled by 1/{a.layers}; numpy/BLAS threads = host cores"}
+            "sample": f"1 of {a.layers} layers ({_sample_note(a)}, nq={a.n_queries}, "
+                      f"r={a.ratio}, bf16-rounded inputs) through oracle.core_oracle.compress_layer "
+                      f"in {t:.2f} s, scaled by 1/{a.layers}; numpy/BLAS threads = host cores"}
 
 
 def run_reference(a, rank):
@@ -195,14 +219,19 @@ def run_reference(a, rank):
         cpu_layer_sample(a, seed=1)
     times = [cpu_layer_sample(a, seed=2 + i) for i in range(steps)]
     t = statistics.median(times)
-    value = a.seq_len / (t * a.layers)
+    Ls = min(a.seq_len, CPU_SAMPLE_MAX_LEN)
+    value = Ls / (t * a.layers)
     sample = (f"{steps} timed samples (+{warm} warm-up) of 1 of {a.layers} layers each "
-              f"(L={a.seq_len}, nq={a.n_queries}) through oracle.core_oracle.compress_layer, "
-              f"median {t:.2f} s per layer, scaled by 1/{a.layers}")
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": a.gpus,
-            "steps": steps, "warmup": warm, "ms_per_step": t * a.layers * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic", "config": config_dict(a, 1),
+              f"({_sample_note(a)}, nq={a.n_queries}, r={a.ratio}) through "
+              f"oracle.core_oracle.compress_layer, median {t:.2f} s per layer, scaled by "
+              f"1/{a.layers}")
+    long = a.workload == "long"
+    line = {"metric": LONG_METRIC if long else METRIC, "value": value, "unit": UNIT,
+            "impl": "reference", "n_gpus": a.gpus,
+            "steps": steps, "warmup": warm, "ms_per_step": t * a.layers * a.seq_len / Ls * 1e3,
+            "higher_is_better": True, "scaling": "strong" if long else "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": long_config(a, 1) if long else config_dict(a, 1),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -252,6 +281,14 @@ def main():
     n = world
     from core_b200 import engine, ops
 
+    if a.workload == "long":
+        line = run_long(a, dev, dist, rank, world)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if a.workload == "decode":
         line = run_decode(a, dev, dist, rank)
         if rank == 0:
@@ -350,6 +387,170 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# long context: one sequence, KV heads sharded across the ranks
+# ---------------------------------------------------------------------------
+LONG_METRIC = ("KV tokens compressed/sec, one 131072-token sequence, 32 layers, "
+               "KV heads sharded across GPUs")
+
+
+def long_config(a, n):
+    return {"workload": f"core_full compression step, {a.layers} layers x 1 sequence x "
+                        f"{a.seq_len} tokens, KV heads sharded over {n} GPU(s)",
+            "layers": a.layers, "seq_len": a.seq_len, "n_kv_heads": 8, "n_q_heads": 32,
+            "head_dim": 128, "query_buffer": a.n_queries, "compression_ratio": a.ratio,
+            "n_kept": int(a.seq_len * (1 - a.ratio)), "d_mem": a.d_mem,
+            "parallelism": f"head-sharded x{n}" if n > 1 else "1 GPU",
+            "l2": f"inputs larger than L2 ({a.layers} x {a.seq_len * 8 * 128 * 4 >> 20} MiB of K/V)"}
+
+
+def run_long(a, dev, dist, rank, world):
+    """One long sequence; one GPU runs the fused layer step (layers on
+    concurrent streams), several GPUs the head-sharded step: rank r holds KV
+    heads [8r/N, 8(r+1)/N) of every layer and the memory state of the layers
+    l = r mod N, with NCCL for the cross-head reductions."""
+    from core_b200 import checkpoint as C
+    from core_b200 import engine, ops, synthetic
+    from core_b200.sharded import DistExchange, HeadShard, ShardWeights, compress_layer_sharded
+    L, nq, hkv, hq, d = a.seq_len, a.n_queries, 8, 32, 128
+    G = hq // hkv
+    seed = 5000  # one sequence: the same inputs on every rank
+    parts = C.random_checkpoint_parts(seed=seed, n_layers=a.layers, n_kv_heads=hkv, n_q_heads=hq,
+                                      d_mem=a.d_mem)
+    geo = parts["geometry"]
+    n_kept = engine.n_kept_for(L, a.ratio, 4)
+    sh = HeadShard(rank, world, hkv, L)
+    layers = []
+    for l in range(a.layers):
+        q, k, v = synthetic.make_layer_inputs(seed=seed + 7 * l, batch=1, n_kv_heads=hkv,
+                                              n_q_heads=hq, seq_len=L, n_queries=nq, device=dev)
+        theta = parts["memory"].modules[l][0]
+        if world == 1:
+            lw = engine.LayerWeights.prepare(
+                geometry=geo.weight[l], prototypes=geo.prototypes, hadamard=geo.hadamard,
+                mlp_params=parts["indexer"].modules[l], theta=theta, n_kv_heads=hkv,
+                n_q_heads=hq, device=dev)
+            layers.append((q, k, v, lw, engine.MemoryState.zeros(1, a.d_mem, hkv * d, dev)))
+        else:
+            inp = dict(q=q[:, sh.h0 * G:sh.h1 * G].contiguous(), keys=k[:, sh.h0:sh.h1].contiguous(),
+                       values=v[:, sh.h0:sh.h1].contiguous())
+            del q, k, v
+            own = HeadShard.owner(l, world) == rank
+            wt = ShardWeights.prepare(sh, geometry=geo.weight[l], prototypes=geo.prototypes,
+                                      hadamard=geo.hadamard, mlp_params=parts["indexer"].modules[l],
+                                      theta=theta if own else None, n_q_heads=hq, device=dev)
+            mem = engine.MemoryState.zeros(1, a.d_mem, hkv * d, dev) if own else None
+            layers.append((inp, wt, mem))
+    torch.cuda.empty_cache()
+    pos = torch.arange(L, device=dev)
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(a.layers)] for _ in range(a.steps)]
+    for pairs in ev:
+        for e0, e1 in pairs:
+            e0.record()
+            e1.record()
+    torch.cuda.synchronize()
+    budget = None
+    if world == 1:
+        n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        budget = ops.sm_budget(max(1, n_sms - a.sm_reserve) if a.streams > 1 else 0)
+        from core_b200 import _lib
+        dims = _lib.CoreDims(1, hq, hkv, d, nq, L, _lib.CORE_DTYPE_BF16)
+        need = _lib.load().core_compress_layer_workspace_bytes(ctypes.byref(dims), n_kept, a.d_mem)
+        ws = [torch.empty(int(need), dtype=torch.uint8, device=dev) for _ in range(a.streams)]
+        pos2 = pos[None]
+
+        def step(pairs):
+            jobs = [dict(q=q, keys=k, values=v, weights=lw, positions=pos2, memory=mem,
+                         timing_events=None if pairs is None else pairs[l])
+                    for l, (q, k, v, lw, mem) in enumerate(layers)]
+            engine.compress_layers(jobs, n_streams=a.streams, workspaces=ws, n_kept=n_kept,
+                                   original_length=L, is_prefill=True)
+    else:
+        ex = DistExchange()
+        # Layers on side streams, so that one layer's exchanges and its owner's
+        # memory write overlap the next layers' QK work.  The host issues every
+        # layer's collectives in layer order on every rank.
+        n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        budget = ops.sm_budget(max(1, n_sms - a.sm_reserve) if a.streams > 1 else 0)
+        streams = [torch.cuda.Stream(dev) for _ in range(max(1, a.streams))]
+
+        def step(pairs):
+            main = torch.cuda.current_stream(dev)
+            fork = torch.cuda.Event()
+            fork.record(main)
+            for st in streams:
+                st.wait_event(fork)
+            for l, (inp, wt, mem) in enumerate(layers):
+                with torch.cuda.stream(streams[l % len(streams)]):
+                    compress_layer_sharded(ex, [sh], [inp], [wt], layer_idx=l, n_kept=n_kept,
+                                           positions=pos, original_length=L, is_prefill=True,
+                                           memory=mem,
+                                           qk_events=None if pairs is None else pairs[l])
+            for st in streams:
+                done = torch.cuda.Event()
+                done.record(st)
+                main.wait_event(done)
+
+    for _ in range(a.warmup):
+        step(None)
+    torch.cuda.synchronize()
+    ops.status(dev)
+    with ClockSampler(dev.index) as clocks:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(a.steps):
+            step(ev[i])
+        t1.record()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+    if budget is not None:
+        budget.__exit__(None, None, None)
+    ops.status(dev)
+    ms = max_over_ranks(t0.elapsed_time(t1) / a.steps, dist, dev)
+    qk_ms = statistics.mean(e0.elapsed_time(e1) for pairs in ev for e0, e1 in pairs)
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    peak, peak_src = 1590.0, "fallback"
+    if os.path.exists(peaks_path):
+        pk = json.load(open(peaks_path))
+        peak, peak_src = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))), "measured"
+    if world == 1:
+        flops = 2.0 * hq * nq * L * d
+        kernel = "qk_relation_kernel (QK pass 2: relation + per-key statistics)"
+        alg = f"2*Hq*nq*L*d = {flops / 1e9:.2f} GFLOP per launch"
+    else:
+        flops = 2 * 2.0 * (hq // world) * nq * L * d
+        kernel = ("QK stage of one rank (qk_lse_kernel + qk_relation_kernel + merge over the "
+                  "rank's heads)")
+        alg = f"2 passes x 2*Hq_rank*nq*L*d = {flops / 1e9:.2f} GFLOP per layer"
+    achieved = flops / (qk_ms / 1e3) / 1e12
+    roofline = {"kernel": kernel, "bound": "tensor", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": f"{peak_src} bf16_tflops_sustained", "traffic": None,
+                "avg_launch_ms": qk_ms, "algorithmic": alg}
+    if world == 1:
+        launches = KERNELS_PER_LAYER * a.layers * a.steps
+    else:
+        # per layer: 5 QK summary, 1 merge, 1 partial projection, 2 range totals, 2 statistics
+        # + assignment, 1 occupancy, 1 value sums, 1 scores, 1 Top-B, 2 gathers; 4 memory-write
+        # kernels on the layers this rank owns
+        owned = sum(1 for l in range(a.layers) if HeadShard.owner(l, world) == rank)
+        launches = (18 * a.layers + 4 * owned) * a.steps
+    line = {"metric": LONG_METRIC, "value": L / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": long_config(a, world), "roofline": roofline, "e2e": None,
+            "gpu_launches": launches, "clocks": clocks.summary()}
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(a)
+    return line
 
 
 # ---------------------------------------------------------------------------

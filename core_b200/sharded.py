@@ -253,7 +253,7 @@ def compress_layer_sharded(ex: Exchange, shards, inputs, weights, *, layer_idx: 
                            memory: engine.MemoryState | None = None, gamma: float = 0.9,
                            eta: float = 1.0, student_temp: float = 1.0,
                            special: torch.Tensor | None = None,
-                           keep_features: bool = False) -> list:
+                           keep_features: bool = False, qk_events=None) -> list:
     """One layer of one sequence on head-sharded caches.
 
     ``shards``, ``inputs`` and ``weights`` are lists indexed like
@@ -263,6 +263,8 @@ def compress_layer_sharded(ex: Exchange, shards, inputs, weights, *, layer_idx: 
     with the rank's retained ``keys``/``values``, ``keep``/``evict`` (1, n)
     int32 (the same on every rank), ``scores`` (1, L) and, with
     ``keep_features``, the rank's range of features (n_keys, 14).
+    ``qk_events``: optional (start, end) CUDA events recorded on the current
+    stream around the QK summaries (LSE, relation and the rank's merge).
     ``write_memory`` must be the same on every rank: it decides whether the
     ranks take part in gathering the evicted rows to the owner, which then
     writes ``memory`` with its ``theta_split``.
@@ -280,8 +282,12 @@ def compress_layer_sharded(ex: Exchange, shards, inputs, weights, *, layer_idx: 
     summ = []
     for i in R:
         s = torch.zeros(shards[i].padded, words, dtype=torch.int32, device=dev)
+        if qk_events is not None:
+            qk_events[0].record()
         ops.qk_head_summary(inputs[i]["q"], inputs[i]["keys"], s, topk_qk=topk_qk,
                             n_recent_queries=n_recent_queries)
+        if qk_events is not None:
+            qk_events[1].record()
         summ.append(s)
     parts = ex.all_to_all(summ)
     feats = []

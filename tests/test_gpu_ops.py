@@ -200,7 +200,9 @@ def test_indexer_scores_match_oracle(name):
 
 @pytest.mark.parametrize("L,n_kept,n_sink", [(5, 4, 4), (96, 48, 4), (333, 133, 4), (4096, 1024, 4),
                                              (16384, 4096, 4), (1000, 1000, 4), (300, 4, 4),
-                                             (65536, 16384, 4), (2049, 700, 0)])
+                                             (65536, 16384, 4), (2049, 700, 0), (8191, 3000, 4),
+                                             (8192, 2000, 4), (8193, 8192, 4), (131072, 13107, 4),
+                                             (131072, 4, 4), (100003, 99000, 0), (400000, 40000, 4)])
 def test_topb_matches_stable_argsort(L, n_kept, n_sink):
     from core_b200 import ops
     dev = _dev()
@@ -218,7 +220,7 @@ def test_topb_matches_stable_argsort(L, n_kept, n_sink):
         assert np.array_equal(evict[b].cpu().numpy(), ev)
 
 
-@pytest.mark.parametrize("L,n_kept", [(4096, 1000), (70000, 5000)])
+@pytest.mark.parametrize("L,n_kept", [(4096, 1000), (70000, 5000), (131072, 13107)])
 def test_topb_all_equal_scores_keep_lowest_indices(L, n_kept):
     from core_b200 import ops
     dev = _dev()
@@ -289,6 +291,21 @@ def test_memory_write_matches_oracle_wide_memory(d_mem, L, hkv):
     assert np.abs(M[0].cpu().numpy() - ref_M).max() <= tol * np.abs(ref_M).max()
     assert np.abs(b[0].cpu().numpy() - ref_b).max() <= tol * np.abs(ref_b).max()
     assert abs(float(Z[0]) - float(ref_Z)) <= 1e-6
+
+
+def test_topb_cluster_rows_are_independent():
+    """Three batch rows of a long cache (one cluster each) equal each row alone."""
+    from core_b200 import ops
+    dev = _dev()
+    rng = np.random.default_rng(7)
+    s = rng.standard_normal((3, 50000)).astype(np.float32)
+    s[1, ::3] = 0.5
+    keep, evict = ops.topb_select(_f32(s, dev), 9000, 4)
+    for b in range(3):
+        k1, e1 = ops.topb_select(_f32(s[b:b + 1], dev), 9000, 4)
+        assert torch.equal(keep[b], k1[0]) and torch.equal(evict[b], e1[0])
+        assert np.array_equal(keep[b].cpu().numpy(), O.topb_select(s[b:b + 1], 9000, 4)[0])
+    ops.status()
 
 
 def test_compact_kv_is_exact_gather():
