@@ -17,7 +17,8 @@ step is split at its cross-head reductions:
    scores, and every rank runs the same Top-B (identical inputs, identical
    keep sets, no further exchange).
 5. Memory write: the layer's memory state lives on rank ``layer % N``,
-   which gathers the evicted K/V rows of all heads and runs the write.
+   which gathers the K/V rows of all heads (the whole caches when most rows
+   are evicted, else the evicted rows only) and runs the write.
 6. Each rank gathers its own heads' retained K/V.
 
 Collectives go through an :class:`Exchange`.  :class:`DistExchange` runs
@@ -123,6 +124,12 @@ class Exchange:
         """xs[i]: (n, ...) -> on the owner (world * n, ...) in rank order, elsewhere None."""
         raise NotImplementedError
 
+    def gather_to_async(self, owner: int, xs):
+        """gather_to without ordering later work on the current stream after it:
+        returns (outputs, wait); wait() orders the current stream after the gather."""
+        out = self.gather_to(owner, xs)
+        return out, (lambda: None)
+
 
 class LocalExchange(Exchange):
     """All ``world`` ranks in this process (sums in rank order)."""
@@ -208,12 +215,22 @@ class DistExchange(Exchange):
         return [out]
 
     def gather_to(self, owner: int, xs):
+        out, wait = self.gather_to_async(owner, xs)
+        wait()
+        return out
+
+    def gather_to_async(self, owner: int, xs):
         (x,) = xs
         x = x.contiguous()
         me = self.ranks[0]
-        parts = [torch.empty_like(x) for _ in range(self.world)] if me == owner else None
-        self._dist.gather(x, gather_list=parts, dst=owner, group=self.group)
-        return [torch.cat(parts) if me == owner else None]
+        if me == owner:  # the ranks' parts land in one buffer, in rank order
+            buf = torch.empty((self.world * x.shape[0], *x.shape[1:]), dtype=x.dtype,
+                              device=x.device)
+            parts = list(buf.chunk(self.world))
+        else:
+            buf, parts = None, None
+        work = self._dist.gather(x, gather_list=parts, dst=owner, group=self.group, async_op=True)
+        return [buf], work.wait
 
 
 @dataclass
@@ -253,23 +270,32 @@ def compress_layer_sharded(ex: Exchange, shards, inputs, weights, *, layer_idx: 
                            memory: engine.MemoryState | None = None, gamma: float = 0.9,
                            eta: float = 1.0, student_temp: float = 1.0,
                            special: torch.Tensor | None = None,
-                           keep_features: bool = False, qk_events=None) -> list:
+                           keep_features: bool = False, qk_events=None,
+                           bulk: Exchange | None = None) -> list:
     """One layer of one sequence on head-sharded caches.
 
     ``shards``, ``inputs`` and ``weights`` are lists indexed like
     ``ex.ranks``: inputs[i] = dict(q (1, Hq_rank, nq, d), keys, values
     (1, Hkv_rank, L, d)) bf16.  ``memory`` is the layer's state on its owner
-    rank (ignored elsewhere; None: no memory write).  Returns per rank a dict
-    with the rank's retained ``keys``/``values``, ``keep``/``evict`` (1, n)
-    int32 (the same on every rank), ``scores`` (1, L) and, with
-    ``keep_features``, the rank's range of features (n_keys, 14).
-    ``qk_events``: optional (start, end) CUDA events recorded on the current
-    stream around the QK summaries (LSE, relation and the rank's merge).
+    rank (ignored elsewhere).  Returns per rank a dict with the rank's retained
+    ``keys``/``values``, ``keep``/``evict`` (1, n) int32 (the same on every
+    rank), ``scores`` (1, L) and, with ``keep_features``, the rank's range of
+    features (n_keys, 14).
+
     ``write_memory`` must be the same on every rank: it decides whether the
-    ranks take part in gathering the evicted rows to the owner, which then
-    writes ``memory`` with its ``theta_split``.
+    ranks take part in gathering K/V rows to the owner, which then writes
+    ``memory`` with its ``theta_split``.  ``bulk``: an exchange over a second
+    communicator for that gather, so that it overlaps the rest of the layer
+    (default: ``ex``).  ``qk_events``: optional (start, end) CUDA events
+    recorded around the QK summaries (LSE, relation, the rank's merge).
+
+    Issue order: every exchange is issued as soon as its inputs are queued,
+    and the exchanges that depend only on the first compute stage go back to
+    back, so that the ranks' small kernels do not wait on one another more
+    often than the reductions require.
     """
     R = range(len(ex.ranks))
+    bulk = bulk or ex
     L = shards[0].seq_len
     nq = inputs[0]["q"].shape[2]
     hkv = shards[0].n_kv_heads
@@ -277,39 +303,53 @@ def compress_layer_sharded(ex: Exchange, shards, inputs, weights, *, layer_idx: 
     dev = inputs[0]["keys"].device
     pos = positions.to(torch.int64).reshape(-1).contiguous()
     sp = None if special is None else special.reshape(-1).contiguous()
+    compact = n_kept < L
+    n_ev = L - n_kept
+    write = compact and write_memory
+    # Memory write inputs: when most of the cache is evicted the ranks send
+    # their whole K/V (no copy on the sender, the owner gathers the rows);
+    # otherwise the evicted rows only, after Top-B.
+    whole = 4 * n_ev >= 3 * L
+    owner = HeadShard.owner(layer_idx, ex.world)
+    if write and whole:
+        kv_all, kv_wait = [], []
+        for t in ("keys", "values"):
+            out, wait = bulk.gather_to_async(owner, [inputs[i][t][0] for i in R])
+            kv_all.append(out)
+            kv_wait.append(wait)
 
-    # 1. QK summaries -> all-to-all by key range -> f1..f6 of the range
-    summ = []
+    # stage A: the rank's own heads over all keys
+    summ, ys, hs = [], [], []
     for i in R:
-        s = torch.zeros(shards[i].padded, words, dtype=torch.int32, device=dev)
+        sh = shards[i]
+        s_ = torch.empty(sh.padded, words, dtype=torch.int32, device=dev)
         if qk_events is not None:
             qk_events[0].record()
-        ops.qk_head_summary(inputs[i]["q"], inputs[i]["keys"], s, topk_qk=topk_qk,
+        ops.qk_head_summary(inputs[i]["q"], inputs[i]["keys"], s_, topk_qk=topk_qk,
                             n_recent_queries=n_recent_queries)
         if qk_events is not None:
             qk_events[1].record()
-        summ.append(s)
+        y = torch.empty(sh.padded, 64, dtype=torch.float32, device=dev)
+        ops.coverage_partial_projection(inputs[i]["keys"], weights[i].geometry_ext, y)
+        h = torch.empty(sh.heads_per_rank, sh.padded, dtype=torch.float32, device=dev)
+        ops.value_head_sums(inputs[i]["values"], h)
+        summ.append(s_)
+        ys.append(y)
+        hs.append(h)
     parts = ex.all_to_all(summ)
-    feats = []
+    y_range = ex.reduce_scatter_sum(ys)
+    hs = ex.all_gather(hs)
+
+    # stage B: the rank's key range
+    feats, zs, totals = [], [], []
     for i in R:
         sh = shards[i]
-        f = torch.zeros(max(sh.chunk, 1), 14, dtype=torch.float32, device=dev)
+        f = torch.empty(max(sh.chunk, 1), 14, dtype=torch.float32, device=dev)
         ops.qk_merge_summaries(parts[i].contiguous(), f, key0=sh.k0, n_keys=sh.n_keys, seq_len=L,
                                n_queries=nq, n_kv_heads=hkv, topk_qk=topk_qk,
                                n_recent_queries=n_recent_queries)
+        z, zt, tot = ops.coverage_range_totals(y_range[i][:sh.n_keys], weights[i].hadamard)
         feats.append(f)
-
-    # 2. coverage: partial projections -> reduce-scatter -> range statistics
-    ys = []
-    for i in R:
-        y = torch.zeros(shards[i].padded, 64, dtype=torch.float32, device=dev)
-        ops.coverage_partial_projection(inputs[i]["keys"], weights[i].geometry_ext, y)
-        ys.append(y)
-    y_range = ex.reduce_scatter_sum(ys)
-    zs = []
-    totals = []
-    for i in R:
-        z, zt, tot = ops.coverage_range_totals(y_range[i][:shards[i].n_keys], weights[i].hadamard)
         zs.append((z, zt))
         totals.append(tot)
     totals = ex.all_reduce_sum(totals)
@@ -321,58 +361,46 @@ def compress_layer_sharded(ex: Exchange, shards, inputs, weights, *, layer_idx: 
         assigns.append(a)
         hists.append(h)
     hists = ex.all_reduce_sum(hists)
-    for i in R:
-        ops.coverage_range_occupancy(assigns[i], hists[i], feats[i], shards[i].n_keys, col0=6)
-
-    # 3. per-head value sums -> all-gather (heads in rank order)
-    hs = []
-    for i in R:
-        h = torch.zeros(shards[i].heads_per_rank, shards[i].padded, dtype=torch.float32,
-                        device=dev)
-        ops.value_head_sums(inputs[i]["values"], h)
-        hs.append(h)
-    hs = ex.all_gather(hs)
-
-    # 4. scores of the range -> all-gather -> the same Top-B everywhere
     sc = []
     for i in R:
         sh = shards[i]
-        s = torch.zeros(sh.chunk, dtype=torch.float32, device=dev)
+        ops.coverage_range_occupancy(assigns[i], hists[i], feats[i], sh.n_keys, col0=6)
+        s_ = torch.empty(sh.chunk, dtype=torch.float32, device=dev)
         if sh.n_keys > 0:
-            s[:sh.n_keys] = ops.indexer_scores_from_sums(
+            s_[:sh.n_keys] = ops.indexer_scores_from_sums(
                 hs[i], sh.k0, sh.n_keys, pos, feats[i], weights[i].mlp,
                 original_length=original_length, is_prefill=is_prefill, n_sink=n_sink,
                 special=sp)
-        sc.append(s)
-    scores = [s[:L][None] for s in ex.all_gather(sc)]
-    out = []
-    compact = n_kept < L
-    keeps = []
-    for i in R:
-        if compact:
-            keeps.append(ops.topb_select(scores[i], n_kept, n_sink))
-        else:
-            keeps.append((None, None))
+        sc.append(s_)
+    # every rank gets all scores and runs the same Top-B (identical keep sets)
+    scores = [x[:L][None] for x in ex.all_gather(sc)]
+    keeps = [ops.topb_select(scores[i], n_kept, n_sink) if compact else (None, None) for i in R]
 
-    # 5. memory write on the layer's owner, from all heads' evicted rows
-    if compact and write_memory:
-        owner = HeadShard.owner(layer_idx, ex.world)
-        k_ev, v_ev = [], []
-        for i in R:
-            ke, ve = ops.compact_kv(inputs[i]["keys"], inputs[i]["values"], keeps[i][1])
-            k_ev.append(ke[0])
-            v_ev.append(ve[0])
-        k_all = ex.gather_to(owner, k_ev)
-        v_all = ex.gather_to(owner, v_ev)
+    # memory write on the layer's owner
+    if write:
+        if whole:
+            k_all, v_all = kv_all
+        else:
+            k_send, v_send = [], []
+            for i in R:
+                ke, ve = ops.compact_kv(inputs[i]["keys"], inputs[i]["values"], keeps[i][1])
+                k_send.append(ke[0])
+                v_send.append(ve[0])
+            k_all, wk = bulk.gather_to_async(owner, k_send)
+            v_all, wv = bulk.gather_to_async(owner, v_send)
+            kv_wait = [wk, wv]
+        for w in kv_wait:
+            w()
         for i in R:
             if ex.ranks[i] == owner:
                 if memory is None or weights[i].theta_split is None:
                     raise ValueError("the owner of the layer needs its memory state and theta_split")
-                ops.memory_write_gathered(k_all[i][None], v_all[i][None], scores[i], keeps[i][1],
-                                          weights[i].theta_split, memory.M, memory.b, memory.Z,
-                                          gamma=gamma, eta=eta, student_temp=student_temp)
+                fn = ops.memory_write if whole else ops.memory_write_gathered
+                fn(k_all[i][None], v_all[i][None], scores[i], keeps[i][1], weights[i].theta_split,
+                   memory.M, memory.b, memory.Z, gamma=gamma, eta=eta, student_temp=student_temp)
 
-    # 6. the rank's own retained K/V
+    # the rank's own retained K/V
+    out = []
     for i in R:
         keep, evict = keeps[i]
         if compact:

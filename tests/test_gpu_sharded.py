@@ -26,12 +26,12 @@ def _dev():
     return torch.device("cuda", 0)
 
 
-def _layer(dev):
+def _layer(dev, ratio=0.75):
     from core_b200 import engine, synthetic
     q, k, v = synthetic.make_layer_inputs(seed=31, batch=1, n_kv_heads=HKV, n_q_heads=HQ,
                                           seq_len=L, n_queries=NQ, device=dev)
     w = synthetic.make_layer_weights(seed=32, n_kv_heads=HKV, n_q_heads=HQ, d_mem=D_MEM)
-    return q, k, v, w, engine.n_kept_for(L, 0.75, 4)
+    return q, k, v, w, engine.n_kept_for(L, ratio, 4)
 
 
 def _unsharded(q, k, v, w, n_kept, dev):
@@ -66,10 +66,11 @@ def _sharded(world, q, k, v, w, n_kept, dev):
     return shards, outs, mem
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_head_sharded_step_matches_unsharded(world):
+# r = 0.75: the owner receives the compacted evicted rows; r = 0.9: whole caches
+@pytest.mark.parametrize("world,ratio", [(2, 0.75), (4, 0.75), (8, 0.75), (2, 0.9), (8, 0.9)])
+def test_head_sharded_step_matches_unsharded(world, ratio):
     dev = _dev()
-    q, k, v, w, n_kept = _layer(dev)
+    q, k, v, w, n_kept = _layer(dev, ratio)
     ref, ref_mem = _unsharded(q, k, v, w, n_kept, dev)
     shards, outs, mem = _sharded(world, q, k, v, w, n_kept, dev)
     feats = torch.cat([o["features"] for o in outs]).cpu().numpy()
