@@ -29,8 +29,11 @@ namespace qk {
 
 constexpr int kD = 128;          // head dim
 constexpr int kTile = 128;       // keys per tile == queries per block
-constexpr int kThreads = 320;    // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
-constexpr int kEpiThreads = 256;
+constexpr int kRelTeams = 4;                 // relation epilogue: 16-query quarters of each half
+constexpr int kRelQ = 64 / kRelTeams;        // queries per thread per half (one chunk of 16)
+constexpr int kEpiThreads = 128 * kRelTeams;
+constexpr int kThreads = 64 + kEpiThreads;   // warp 0 TMA, warp 1 MMA, 16 epilogue warps
+static_assert(kRelTeams == 4, "the team merge packs two 16-query masks per record word");
 constexpr int kLseTeams = 4;                       // LSE epilogue: 16-key quarters of a sub-tile
 constexpr int kLseEpiThreads = 128 * kLseTeams;
 constexpr int kLseThreads = 64 + kLseEpiThreads;  // warp 0 TMA, warp 1 MMA, 16 epilogue warps
@@ -349,8 +352,8 @@ struct RelSmem {
   static constexpr uint32_t kKOff = kQOff + kQBytes;
   static constexpr uint32_t kLseOff = kKOff + kKStages * kKTileBytes;  // float2 [G][128]: (-lse, log|C|)
   static constexpr uint32_t kCcOff = kLseOff + G * kTile * 8;          // unused
-  static constexpr uint32_t kXchOff = kCcOff + kTile * 4;              // uint32 [128][16]
-  static constexpr uint32_t kBarOff = kXchOff + kTile * 16 * 4;
+  static constexpr uint32_t kXchOff = kCcOff + kTile * 4;  // uint32 [teams - 1][128][16]
+  static constexpr uint32_t kBarOff = kXchOff + (kRelTeams - 1) * kTile * 16 * 4;
   static constexpr uint32_t kTotal = kBarOff + 256;
 };
 
@@ -369,6 +372,7 @@ struct KeyStats {
   }
 };
 
+// 18 warps: five share one scheduler's 16K registers, so 96 registers a thread
 template <int G, bool kLoo>
 __global__ void __launch_bounds__(kThreads, 1)
     qk_relation_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -499,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue ----------------
     const int ew = warp - 2;
-    const int team = ew >> 2;  // which 32 of each 64-query half
+    const int team = ew >> 2;  // which 16 of each 64-query half
     const int wq = warp & 3;
     const int krow = wq * 32 + lane;  // key row inside the tile
     const float inv_ht = 1.0f / (float)p.head_topk;
@@ -538,13 +542,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int buf = sub & 1, n = sub >> 1;
         if (!(ok = wait(bar_t_full(buf), n & 1, 206))) break;
         tc_fence_after();
-        const int tl0 = hf * 64 + team * 32;  // query index within the block of j = 0
+        const int tl0 = hf * 64 + team * kRelQ;  // query index within the block of j = 0
         const bool full = (t.kt * kTile + kTile - 1 <= qb_first_pos) &&
-                          (t.kt * kTile + kTile <= p.L) && (tl0 + 32 <= qb_valid);
-        // 32 queries per thread, processed as two chunks of 16 to bound registers
+                          (t.kt * kTile + kTile <= p.L) && (tl0 + kRelQ <= qb_valid);
+        // kRelQ queries per thread, in chunks of 16 to bound registers
         uint32_t msk = 0;
 #pragma unroll 1
-        for (int ch = 0; ch < 2; ++ch) {
+        for (int ch = 0; ch < kRelQ / 16; ++ch) {
           const int c0 = tl0 + ch * 16;  // query index within the block of element 0
           float acc[16];
           float mn[kLoo ? 16 : 1];
@@ -552,7 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int g = 0; g < G; ++g) {
             float v[16];
             tmem_ld16(tmem + ((uint32_t)(wq * 32) << 16) +
-                          (uint32_t)(buf * kN + g * 64 + team * 32 + ch * 16), v);
+                          (uint32_t)(buf * kN + g * 64 + team * kRelQ + ch * 16), v);
             const float* nlp = s_nl + g * kTile + c0;
             const float* lcp = s_lc + g * kTile + c0;
             float rel[16];
@@ -629,9 +633,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       st.pcnt = (uint32_t)(__popc(st.mask[0]) + __popc(st.mask[1]));  // positive relations
-      // merge the two teams (same key, different query quarters) and store
-      uint32_t* x = s_xch + krow * 16;
-      if (team == 1) {
+      // merge the teams (same key, different query quarters) into team 0 and store
+      if (team > 0) {
+        uint32_t* x = s_xch + ((team - 1) * kTile + krow) * 16;
         for (int i = 0; i < 4; ++i) {
           x[i] = __float_as_uint(st.top[i]);
           x[4 + i] = __float_as_uint(st.rtop[i]);
@@ -644,13 +648,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       named_barrier(2, kEpiThreads);
       if (team == 0) {
-        for (int i = 0; i < 4; ++i) {
-          top4_insert(st.top, __uint_as_float(x[i]));
-          top4_insert(st.rtop, __uint_as_float(x[4 + i]));
+        // query word w (32 queries) of half hf holds teams 2 (w % 2) and 2 (w % 2) + 1
+        uint32_t qw[4] = {st.mask[0], 0u, st.mask[1], 0u};
+        float psum = st.psum, mxnp = st.mxnp;
+        uint32_t pcnt = st.pcnt;
+        for (int tm = 1; tm < kRelTeams; ++tm) {
+          const uint32_t* x = s_xch + ((tm - 1) * kTile + krow) * 16;
+          for (int i = 0; i < 4; ++i) {
+            top4_insert(st.top, __uint_as_float(x[i]));
+            top4_insert(st.rtop, __uint_as_float(x[4 + i]));
+          }
+          psum += __uint_as_float(x[8]);
+          pcnt += x[9];
+          mxnp = fmaxf(mxnp, __uint_as_float(x[12]));
+          const int w = tm >> 1, sh = (tm & 1) * kRelQ;
+          qw[w] |= x[10] << sh;
+          qw[2 + w] |= x[11] << sh;
         }
-        const float psum = st.psum + __uint_as_float(x[8]);
-        const uint32_t pcnt = st.pcnt + x[9];
-        const float mxnp = fmaxf(st.mxnp, __uint_as_float(x[12]));
         if (key < p.L) {
           uint4* dst = reinterpret_cast<uint4*>(
               p.rec + ((((long long)t.b * p.L + key) * p.Hkv + t.h) * p.n_qb + t.qb) * kRecWords);
@@ -658,9 +672,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                               __float_as_uint(st.top[2]), __float_as_uint(st.top[3]));
           dst[1] = make_uint4(__float_as_uint(st.rtop[0]), __float_as_uint(st.rtop[1]),
                               __float_as_uint(st.rtop[2]), __float_as_uint(st.rtop[3]));
-          // query words: 0 -> (half 0, team 0), 1 -> (half 0, team 1), 2 -> (1, 0), 3 -> (1, 1)
-          dst[2] = make_uint4(__float_as_uint(psum), pcnt, st.mask[0], x[10]);
-          dst[3] = make_uint4(st.mask[1], x[11], __float_as_uint(mxnp), 0u);
+          dst[2] = make_uint4(__float_as_uint(psum), pcnt, qw[0], qw[1]);
+          dst[3] = make_uint4(qw[2], qw[3], __float_as_uint(mxnp), 0u);
         }
       }
       named_barrier(2, kEpiThreads);
