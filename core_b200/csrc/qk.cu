@@ -383,8 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
   const uint32_t sQ = sbase + S::kQOff;
   const uint32_t sK = sbase + S::kKOff;
-  float* s_nl = reinterpret_cast<float*>(sgen + S::kLseOff);  // [G][128] -lse
-  float* s_lc = s_nl + G * kTile;                                // [G][128] log|C_t|
+  float* s_nc = reinterpret_cast<float*>(sgen + S::kLseOff);  // [G][128] -lse + log|C_t|
   uint32_t* s_xch = reinterpret_cast<uint32_t*>(sgen + S::kXchOff);
   const uint32_t bar = sbase + S::kBarOff;
   const uint32_t bar_q_full = bar + 0, bar_q_empty = bar + 8;
@@ -508,7 +507,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int krow = wq * 32 + lane;  // key row inside the tile
     const float inv_ht = 1.0f / (float)p.head_topk;
     const unsigned long long sc2 = f2_pack(p.scale, p.scale);
-    const unsigned long long nfloor2 = f2_pack(-kLogFloor, -kLogFloor);
     const bool exact_div = (p.head_topk != 1 && p.head_topk != 2 && p.head_topk != 4);
     const float single_val = log1pf(expf(kLogFloor));
     long long cur = -1;
@@ -525,9 +523,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int tt = t.qb * kTile + tq;
           const long long qpos = (long long)p.q_start + tt;
           const long long cc = (qpos + 1 < p.L) ? qpos + 1 : p.L;
-          const float nl = (tt < p.nq) ? -p.lse[(long long)(t.b * p.Hq + t.h * G + g) * p.nq + tt] : 0.f;
-          s_nl[i] = nl;
-          s_lc[i] = logf((float)cc);
+          s_nc[i] = (tt < p.nq)
+                        ? relation_offset(p.lse[(long long)(t.b * p.Hq + t.h * G + g) * p.nq + tt], cc)
+                        : 0.f;
         }
         named_barrier(1, kEpiThreads);
         cur = t.grp;
@@ -557,49 +555,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v[16];
             tmem_ld16(tmem + ((uint32_t)(wq * 32) << 16) +
                           (uint32_t)(buf * kN + g * 64 + team * kRelQ + ch * 16), v);
-            const float* nlp = s_nl + g * kTile + c0;
-            const float* lcp = s_lc + g * kTile + c0;
-            float rel[16];
-            float amin = INFINITY;
-            // pairs of queries in packed f32x2 arithmetic (each lane rounds as the scalar form)
+            const float* ncp = s_nc + g * kTile + c0;
+            float rmin = INFINITY;
+            // r for pairs of queries in packed f32x2 arithmetic (each lane rounds as the
+            // scalar form), kept in v
 #pragma unroll
             for (int j = 0; j < 16; j += 2) {
               bf16_round2(v[j], v[j + 1]);
-              const unsigned long long nl2 = *reinterpret_cast<const unsigned long long*>(nlp + j);
-              const unsigned long long lc2 = *reinterpret_cast<const unsigned long long*>(lcp + j);
-              const unsigned long long r2 = f2_add(f2_fma(f2_pack(v[j], v[j + 1]), sc2, nl2), lc2);
-              const unsigned long long d2 = f2_add(r2, nfloor2);  // r - log(1e-8)
-              const float a0 = fabsf(f2_lo(d2)), a1 = fabsf(f2_hi(d2));
-              amin = fmin3(amin, a0, a1);
-              // exp(-a) < 1.2e-7 for a >= 16: log1p(x) equals x to within half an ulp of x
-              rel[j] = fmaxf(f2_lo(r2), kLogFloor) + ex2_approx(-a0 * kLog2e);
-              rel[j + 1] = fmaxf(f2_hi(r2), kLogFloor) + ex2_approx(-a1 * kLog2e);
+              const unsigned long long nc2 = *reinterpret_cast<const unsigned long long*>(ncp + j);
+              const unsigned long long r2 = f2_fma(f2_pack(v[j], v[j + 1]), sc2, nc2);
               v[j] = f2_lo(r2);
               v[j + 1] = f2_hi(r2);
+              rmin = fmin3(rmin, v[j], v[j + 1]);
             }
-            if (__any_sync(0xffffffffu, amin < 16.0f)) {
+            // v = logaddexp_floor_fast(r): max(r, floor) unless some r of the chunk lies
+            // within 16 of the floor (rare): then the exact form (warp-uniform branch)
+            if (__any_sync(0xffffffffu, rmin < kLogFloor + 16.0f)) {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const float a = fabsf(v[j] - kLogFloor);
-                if (a < 16.0f) rel[j] = fmaxf(v[j], kLogFloor) + log1pf(expf(-a));
-              }
-            }
-            if (!full) {
+              for (int j = 0; j < 16; ++j) v[j] = logaddexp_floor_fast(v[j]);
+            } else {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int qpos = qb_first_pos + c0 + j;
-                if (key > qpos) rel[j] = kLogFloor;
-                else if (qpos == 0) rel[j] = single_val;
-              }
+              for (int j = 0; j < 16; ++j) v[j] = fmaxf(v[j], kLogFloor);
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
+              float rel = v[j];
+              if (!full) {
+                const int qpos = qb_first_pos + c0 + j;
+                if (key > qpos) rel = kLogFloor;
+                else if (qpos == 0) rel = single_val;
+              }
               if (g == 0) {
-                acc[j] = rel[j];
-                if (kLoo) mn[kLoo ? j : 0] = rel[j];
+                acc[j] = rel;
+                if (kLoo) mn[kLoo ? j : 0] = rel;
               } else {
-                acc[j] += rel[j];
-                if (kLoo) mn[kLoo ? j : 0] = fminf(mn[kLoo ? j : 0], rel[j]);
+                acc[j] += rel;
+                if (kLoo) mn[kLoo ? j : 0] = fminf(mn[kLoo ? j : 0], rel);
               }
             }
           }
@@ -733,7 +724,6 @@ __device__ float relation_exact(const MergeParams& p, int b, int h, int key, int
   const long long qpos = (long long)p.q_start + t;
   if (key > qpos) return kLogFloor;
   const long long cc = (qpos + 1 < p.L) ? qpos + 1 : p.L;
-  const float lcc = logf((float)cc);
   float dot[4] = {0.f, 0.f, 0.f, 0.f};
   if (p.qf != nullptr) {  // f32 caches: unrounded logits (fp32 reference path)
 #pragma unroll
@@ -782,9 +772,10 @@ __device__ float relation_exact(const MergeParams& p, int b, int h, int key, int
   for (int g = 0; g < 4; ++g) {
     if (g < p.G) {
       const int qh = h * p.G + g;
-      const float x = (p.qf != nullptr) ? dot[g] : bf16_round(dot[g]);
-      const float r = fmaf(x, p.scale, -p.lse[((long long)b * p.Hq + qh) * p.nq + t]) + lcc;
-      float rel = logaddexp_floor(r);
+      const bool f32 = p.qf != nullptr;
+      const float x = f32 ? dot[g] : bf16_round(dot[g]);
+      const float r = fmaf(x, p.scale, relation_offset(p.lse[((long long)b * p.Hq + qh) * p.nq + t], cc));
+      float rel = f32 ? logaddexp_floor(r) : logaddexp_floor_fast(r);
       if (qpos == 0) rel = log1pf(expf(kLogFloor));
       acc = (g == 0) ? rel : acc + rel;
       mn = fminf(mn, rel);

@@ -27,6 +27,19 @@ constexpr int kRecWords = 16;
 // over the heads) per 128-query block.
 constexpr int kSumHead = 12;
 
+// -LSE + log|C_t| of one (q-head, query): with it r = fmaf(s x, offset).
+__device__ __forceinline__ float relation_offset(float lse, long long count) {
+  return -lse + logf((float)count);
+}
+
+// logaddexp(r, f) without the correction term where it is below 1.2e-7
+// (|r - f| >= 16): that term moves the result by at most two f32 ulps.  The
+// bf16 relation kernels use this; the f32 kernels keep the exact form below.
+__device__ __forceinline__ float logaddexp_floor_fast(float r) {
+  const float a = fabsf(r - kLogFloor);
+  return a < 16.0f ? fmaxf(r, kLogFloor) + log1pf(expf(-a)) : fmaxf(r, kLogFloor);
+}
+
 __device__ __forceinline__ float logaddexp_floor(float r) {
   // max(r, f) + log1p(exp(-|r - f|)), f = log(1e-8)  (fused_qk.py:200-202)
   float a = fabsf(r - kLogFloor);

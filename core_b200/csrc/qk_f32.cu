@@ -22,6 +22,7 @@ namespace qkf {
 using qk::kLogFloor;
 using qk::kRecWords;
 using qk::logaddexp_floor;
+using qk::relation_offset;
 
 constexpr int kD = 128;
 constexpr int kThreads = 256;
@@ -155,8 +156,7 @@ __global__ void __launch_bounds__(kThreads)
   extern __shared__ float sm[];
   float* sK = sm;                               // [64][kPad]
   float* sQT = sK + kRelK * kPad;               // [d][4][kQuarter]: q of the head, transposed
-  float* s_nl = sQT + kD * 4 * kQuarter;        // [128] -lse of the head's queries
-  float* s_lc = s_nl + kRelQ;                   // [128] log|C_t|
+  float* s_nc = sQT + kD * 4 * kQuarter;        // [128] -lse + log|C_t| of the head's queries
   const int k0 = blockIdx.x * kRelK;
   const int h = blockIdx.y % p.Hkv, qb = blockIdx.y / p.Hkv;
   const int b = blockIdx.z;
@@ -182,8 +182,8 @@ __global__ void __launch_bounds__(kThreads)
     for (int t = tid; t < kRelQ; t += kThreads) {
       const long long qpos = (long long)p.q_start + tq0 + t;
       const long long cc = (qpos + 1 < p.L) ? qpos + 1 : p.L;
-      s_nl[t] = (t < qvalid) ? -p.lse[(long long)(b * p.Hq + qh) * p.nq + tq0 + t] : 0.f;
-      s_lc[t] = logf((float)cc);
+      s_nc[t] = (t < qvalid) ? relation_offset(p.lse[(long long)(b * p.Hq + qh) * p.nq + tq0 + t], cc)
+                             : 0.f;
     }
     __syncthreads();
     float dot[32];
@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int j = 0; j < 32; ++j) {
       const int t = qq * 32 + j;
       const long long qpos = (long long)p.q_start + tq0 + t;
-      const float r = fmaf(dot[j], p.scale, s_nl[t]) + s_lc[t];
+      const float r = fmaf(dot[j], p.scale, s_nc[t]);
       float rel = logaddexp_floor(r);
       if (key > qpos) rel = kLogFloor;
       else if (qpos == 0) rel = single_val;
