@@ -11,6 +11,10 @@ int qk_features_impl(const core_dims_t* d, const void* q, const void* k, int32_t
                      float* features, int32_t feature_stride, void* workspace,
                      size_t workspace_bytes, void* stream, void* ev0, void* ev1,
                      uint32_t* summary = nullptr);
+int indexer_scores_split(const core_dims_t* d, const void* v, const int64_t* positions,
+                         const uint8_t* special, int32_t original_length, int32_t is_prefill,
+                         int32_t n_sink, float* features, const float* mlp, float* scores,
+                         void* workspace, size_t workspace_bytes, void* stream);
 }
 
 using namespace core;
@@ -28,6 +32,8 @@ extern "C" size_t core_compress_layer_workspace_bytes(const core_dims_t* d, int3
   core_dims_t e = kv_dims(d);
   size_t c = core_coverage_workspace_bytes(&e);
   if (c > ws) ws = c;
+  const size_t hs = sizeof(float) * (size_t)d->batch * d->seq_len * d->n_kv_heads + 256;
+  if (hs > ws) ws = hs;  // per-head value sums of the indexer
   const int n_evict = d->seq_len - n_kept;
   if (d_mem > 0 && n_evict > 0) {
     size_t m = core_memory_write_workspace_bytes(&e, n_evict, d_mem);
@@ -58,8 +64,9 @@ extern "C" int core_compress_layer(const core_dims_t* d, const void* q, const vo
   if ((rc = core_coverage_features(&e, k, w->geometry_ext, w->prototypes, a->shrinkage_rho,
                                    features, 14, 6, workspace, workspace_bytes, stream)) != CORE_OK)
     return rc;
-  if ((rc = core_indexer_scores(&e, v, positions, special, a->original_length, a->is_prefill,
-                                a->n_sink, features, w->mlp, scores, stream)) != CORE_OK)
+  if ((rc = indexer_scores_split(&e, v, positions, special, a->original_length, a->is_prefill,
+                                 a->n_sink, features, w->mlp, scores, workspace, workspace_bytes,
+                                 stream)) != CORE_OK)
     return rc;
   if (a->n_kept >= L) return CORE_OK;  // nothing to evict: the caller keeps the cache
   if ((rc = core_topb_select(scores, d->batch, L, a->n_kept, a->n_sink, keep_idx, evict_idx,

@@ -345,12 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Per-(head, token) value sums of squares in the arithmetic of the indexer's
 // auxiliary block (squares rounded to bf16 and added in index order, the sum
-// rounded to bf16), for head-sharded caches: out[h * out_stride + token].
-// One thread per row, like the indexer, so the sums agree bit for bit.
-__global__ void value_head_sums_kernel(const __nv_bfloat16* __restrict__ v, int Hkv, int L,
+// rounded to bf16): out[h * out_stride + b * L + token].  One thread per row,
+// like the indexer, so the sums agree bit for bit.  Many small blocks keep
+// enough loads in flight for HBM; the indexer then reads 4 bytes per row.
+__global__ void value_head_sums_kernel(const __nv_bfloat16* __restrict__ v, int B, int Hkv, int L,
                                        float* __restrict__ out, long long out_stride) {
   const long long row = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= (long long)Hkv * L) return;
+  if (row >= (long long)B * Hkv * L) return;
   const uint4* rowp = reinterpret_cast<const uint4*>(v + row * 128);
   uint4 w[16];  // the whole 256-byte row in flight at once
 #pragma unroll
@@ -366,8 +367,9 @@ __global__ void value_head_sums_kernel(const __nv_bfloat16* __restrict__ v, int 
       s += bf16_round(f2.y * f2.y);
     }
   }
-  const int h = (int)(row / L), t = (int)(row % L);
-  out[(long long)h * out_stride + t] = bf16_round(s);
+  const long long bh = row / L;
+  const int b = (int)(bh / Hkv), h = (int)(bh % Hkv), t = (int)(row % L);
+  out[(long long)h * out_stride + (long long)b * L + t] = bf16_round(s);
 }
 
 }  // namespace idx
@@ -434,7 +436,7 @@ extern "C" int core_value_head_sums(const core_dims_t* d, const void* v, float* 
   const long long rows = (long long)d->n_kv_heads * d->seq_len;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   value_head_sums_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
-      static_cast<const __nv_bfloat16*>(v), d->n_kv_heads, d->seq_len, out, out_stride);
+      static_cast<const __nv_bfloat16*>(v), 1, d->n_kv_heads, d->seq_len, out, out_stride);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CORE_OK : cuda_error(e, "value_head_sums_kernel launch");
 }
@@ -480,3 +482,60 @@ extern "C" int core_indexer_scores_from_sums(int32_t n_kv_heads, int32_t n_keys,
   e = cudaGetLastError();
   return e == cudaSuccess ? CORE_OK : cuda_error(e, "indexer_scores_kernel launch");
 }
+
+namespace core {
+// core_indexer_scores for bf16 caches in two launches: the per-head value sums
+// into the workspace (B * L * Hkv floats), then the indexer reading them.
+// Same results, bit for bit, as the one-launch form.
+int indexer_scores_split(const core_dims_t* d, const void* v, const int64_t* positions,
+                         const uint8_t* special, int32_t original_length, int32_t is_prefill,
+                         int32_t n_sink, float* features, const float* mlp, float* scores,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (d == nullptr || d->dtype != CORE_DTYPE_BF16 || workspace == nullptr)
+    return core_indexer_scores(d, v, positions, special, original_length, is_prefill, n_sink,
+                               features, mlp, scores, stream);
+  int rc = check_dims(d, "core_indexer_scores");
+  if (rc != CORE_OK) return rc;
+  if (v == nullptr || positions == nullptr || features == nullptr || mlp == nullptr ||
+      scores == nullptr)
+    return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores: NULL tensor");
+  if (reinterpret_cast<uintptr_t>(mlp) % 16 != 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores: mlp must be 16-byte aligned");
+  if (original_length < d->seq_len)
+    return set_error(CORE_ERR_INVALID_ARG, "core_indexer_scores: original_length < seq_len");
+  if (d->n_kv_heads > kMaxHkv)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_indexer_scores: at most 16 KV heads");
+  const long long BL = (long long)d->batch * d->seq_len;
+  Carver cv(workspace, workspace_bytes);
+  float* hs = cv.take<float>((size_t)BL * d->n_kv_heads);
+  if (cv.overflow) return set_error(CORE_ERR_WORKSPACE, "core_indexer_scores: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long rows = BL * d->n_kv_heads;
+  value_head_sums_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(v), d->batch, d->n_kv_heads, d->seq_len, hs, BL);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "value_head_sums_kernel launch");
+  Params p{};
+  p.B = d->batch;
+  p.Hkv = d->n_kv_heads;
+  p.L = d->seq_len;
+  p.original_length = original_length;
+  p.is_prefill = is_prefill;
+  p.n_sink = n_sink;
+  p.head_sums = hs;
+  p.hs_stride = BL;
+  p.positions = positions;
+  p.special = special;
+  p.features = features;
+  p.mlp = mlp;
+  p.scores = scores;
+  p.status = device_status();
+  e = cudaFuncSetAttribute(indexer_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return cuda_error(e, "indexer_scores_kernel attribute");
+  const long long n_tiles = (BL + kTile - 1) / kTile;
+  const long long blocks = n_tiles < sm_count() ? n_tiles : sm_count();
+  indexer_scores_kernel<<<(unsigned)blocks, kThreads, kSmemBytes, s>>>(p);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "indexer_scores_kernel launch");
+}
+}  // namespace core

@@ -308,6 +308,29 @@ def test_topb_cluster_rows_are_independent():
     ops.status()
 
 
+def test_layer_step_indexer_equals_public_entry():
+    """The fused layer step computes the value sums in a separate launch; its
+    auxiliary features and scores equal core_indexer_scores' bit for bit."""
+    from core_b200 import engine, ops, synthetic
+    dev = _dev()
+    L = 3000
+    q, k, v = synthetic.make_layer_inputs(seed=17, batch=2, n_kv_heads=8, n_q_heads=32,
+                                          seq_len=L, n_queries=64, device=dev)
+    w = synthetic.make_layer_weights(seed=18, n_kv_heads=8, n_q_heads=32, d_mem=128)
+    lw = engine.LayerWeights.prepare(geometry=w["geometry"], prototypes=w["prototypes"],
+                                     hadamard=w["hadamard"], mlp_params=w["mlp"], theta=w["theta"],
+                                     n_kv_heads=8, n_q_heads=32, device=dev)
+    pos = torch.arange(L, device=dev)[None].expand(2, L).contiguous()
+    out = engine.compress_layer(q, k, v, lw, n_kept=700, positions=pos, original_length=L + 5,
+                                is_prefill=False)
+    feats = out["features"].clone()
+    feats[:, :, 10:] = 0
+    scores = ops.indexer_scores(v, pos, feats, lw.mlp, original_length=L + 5, is_prefill=False)
+    ops.status()
+    assert torch.equal(feats, out["features"])
+    assert torch.equal(scores, out["scores"])
+
+
 def test_compact_kv_is_exact_gather():
     from core_b200 import ops, synthetic
     dev = _dev()
