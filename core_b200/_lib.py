@@ -16,6 +16,12 @@ CORE_OK = 0
 CORE_DTYPE_BF16 = 1
 CORE_DTYPE_F32 = 2
 
+CORE_ERR_INVALID_ARG = -1
+CORE_ERR_UNSUPPORTED = -2
+CORE_ERR_NONFINITE = -3
+CORE_ERR_TIMEOUT = -4
+CORE_ERR_CUDA = -5
+CORE_ERR_WORKSPACE = -6
 ERRORS = {
     -1: "invalid argument",
     -2: "unsupported",
@@ -92,6 +98,7 @@ SIGNATURES = {
     "core_memory_readout_noalloc": (ctypes.c_int, [_D, _I, _P, _P, _P, _P, _P, _P, _I, _I, _F,
                                                    _P, _P, _P, _I, _P, _P]),
     "core_set_sm_budget": (ctypes.c_int, [_I]),
+    "core_selftest_wait_timeout": (ctypes.c_int, [_I, _P]),
     "core_split_bf16": (ctypes.c_int, [_P, ctypes.c_int64, _I, _P, _P]),
     "core_qk_summary_words": (_I, [_I]),
     "core_qk_head_summary": (ctypes.c_int, [_D, _P, _P, _I, _I, _P, _P, _P, _S, _P]),

@@ -97,14 +97,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 // flag is raised by another thread or when kWaitLimitNs passes (then records
 // CORE_ERR_TIMEOUT and raises the flag); callers then stop issuing work.
 __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                             DeviceStatus* st, int where) {
+                                             DeviceStatus* st, int where,
+                                             uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         record_error(st, CORE_ERR_TIMEOUT, where, (int)blockIdx.x);
         *abort_flag = 1;
         return false;

@@ -194,3 +194,34 @@ extern "C" int core_set_sm_budget(int32_t n_sms) {
   g_sm_budget.store(n_sms, std::memory_order_relaxed);
   return CORE_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Self-test of the bounded wait: one warp waits on an mbarrier that nothing
+// arrives at, with the given limit, through the same bounded_wait the kernels
+// use; the wait gives up, records CORE_ERR_TIMEOUT (site 990) in the device
+// status and the kernel returns normally, leaving the context usable.
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void selftest_wait_kernel(uint64_t limit_ns, core::DeviceStatus* st) {
+  __shared__ __align__(8) uint64_t bar_storage;
+  __shared__ int abort_flag;
+  const uint32_t bar = core::smem_u32(&bar_storage);
+  if (threadIdx.x == 0) {
+    core::mbar_init(bar, 1);
+    abort_flag = 0;
+    core::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) core::bounded_wait(bar, 0, &abort_flag, st, 990, limit_ns);
+  __syncthreads();
+}
+}  // namespace
+
+extern "C" int core_selftest_wait_timeout(int32_t limit_us, void* stream) {
+  if (limit_us <= 0 || limit_us > 1000000)
+    return set_error(CORE_ERR_INVALID_ARG, "core_selftest_wait_timeout: limit must be 1 us to 1 s");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  selftest_wait_kernel<<<1, 32, 0, s>>>((uint64_t)limit_us * 1000ull, core::device_status());
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "selftest_wait_kernel launch");
+}

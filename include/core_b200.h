@@ -272,6 +272,15 @@ int core_compress_layer(const core_dims_t* dims, const void* q, const void* k, c
  * ------------------------------------------------------------------------- */
 int core_split_bf16(const float* src, int64_t n, int32_t terms, void* dst, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Self-test of the device-side bounded wait (no reference counterpart): one
+ * warp waits, for limit_us microseconds (1 us .. 1 s), on an mbarrier that
+ * nothing completes, using the wait every pipelined kernel uses; the wait
+ * gives up and records CORE_ERR_TIMEOUT, which core_check_device_status then
+ * returns (and clears).  The kernel itself ends normally.
+ * ------------------------------------------------------------------------- */
+int core_selftest_wait_timeout(int32_t limit_us, void* stream);
+
 /* ===========================================================================
  * Head-sharded caches: one sequence whose KV heads are split across ranks
  * (one process per GPU).  The reference runs one process with all heads; these

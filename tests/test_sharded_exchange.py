@@ -94,3 +94,50 @@ def test_dist_exchange_matches_local_emulation():
     # the all-to-all hands rank r the r-th chunk of every rank, in rank order
     assert torch.equal(want["a2a"][1][0], xs[0]["a2a"][3:6])
     assert torch.equal(want["a2a"][0][1], xs[1]["a2a"][0:3])
+
+
+def _leaver(rank, world, port, out):
+    """Rank 1 leaves between layers; rank 0's next collective must end with
+    an error within the group's short timeout instead of waiting for good."""
+    import datetime
+    import sys
+    import time
+    sys.path.insert(0, ROOT)
+    from core_b200.sharded import DistExchange
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    ex = DistExchange()
+    x = torch.ones(world * 4, 3)
+    ex.all_to_all([x])                     # layer 0: both ranks
+    if rank == 1:
+        out[rank] = "left"
+        os._exit(0)                        # leaves between layers, nothing in flight
+    t0 = time.perf_counter()
+    try:
+        ex.all_to_all([x])                 # layer 1: the peer is gone
+        out[rank] = "no error"
+    except Exception as e:  # noqa: BLE001 - any collective error ends the wait
+        out[rank] = f"error after {time.perf_counter() - t0:.1f} s: {type(e).__name__}"
+    os._exit(0)
+
+
+def test_peer_leaving_ends_the_next_collective_with_an_error():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        out = m.dict()
+        procs = [ctx.Process(target=_leaver, args=(r, world, port, out)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=60)
+        alive = [p.is_alive() for p in procs]
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+        res = dict(out)
+    assert not any(alive), "a rank was still waiting"
+    assert res.get(1) == "left"
+    assert str(res.get(0, "")).startswith("error after"), res
