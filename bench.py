@@ -36,8 +36,9 @@ if ROOT not in sys.path:
 
 METRIC = "KV tokens compressed/sec per B200 (16K ctx, 32 layers); % tensor/HBM roofline"
 UNIT = "tokens/s"
-# LSE, combine, relation, merge, f6 resolve, 4 coverage, scores, Top-B, 4 memory write, gather
-KERNELS_PER_LAYER = 16
+# LSE, combine, relation, merge, f6 resolve, 4 coverage, value sums, scores, Top-B,
+# 4 memory write, gather
+KERNELS_PER_LAYER = 17
 
 
 def parse():
@@ -544,11 +545,12 @@ def run_long(a, dev, dist, rank, world):
     if world == 1:
         launches = KERNELS_PER_LAYER * a.layers * a.steps
     else:
-        # per layer: 5 QK summary, 1 merge, 1 partial projection, 2 range totals, 2 statistics
-        # + assignment, 1 occupancy, 1 value sums, 1 scores, 1 Top-B, 2 gathers; 4 memory-write
-        # kernels on the layers this rank owns
+        # per layer: 5 QK summary, 1 partial projection, 1 value sums, 1 summary merge,
+        # 2 range totals, 2 statistics + assignment, 1 occupancy, 1 scores, 1 Top-B, 1 gather
+        # of the kept rows (the owner gathers the evicted rows by index: r >= 0.75); 4
+        # memory-write kernels on the layers this rank owns
         owned = sum(1 for l in range(a.layers) if HeadShard.owner(l, world) == rank)
-        launches = (18 * a.layers + 4 * owned) * a.steps
+        launches = (16 * a.layers + 4 * owned) * a.steps
     line = {"metric": LONG_METRIC, "value": L / (ms / 1e3), "unit": UNIT, "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
