@@ -65,6 +65,11 @@ def parse():
     p.add_argument("--interval", type=int, default=128)
     p.add_argument("--decode-ratio", type=float, default=0.5)
     p.add_argument("--streams", type=int, default=3, help="layers compressed concurrently")
+    p.add_argument("--sharded", action="store_true",
+                   help="--workload long: the head-sharded step even on one rank (under torchrun)")
+    p.add_argument("--graph", action="store_true",
+                   help="--workload long, head-sharded: replay the step (kernels and NCCL "
+                        "collectives of all layers) as one CUDA graph")
     p.add_argument("--sm-reserve", type=int, default=2,
                    help="SMs the persistent grids leave free for the other streams' kernels")
     a = p.parse_args()
@@ -271,7 +276,7 @@ def main():
         run_reference(a, rank)
         return
     dist = None
-    if world > 1:
+    if world > 1 or (a.workload == "long" and a.sharded):
         import datetime
 
         import torch.distributed as dist
@@ -403,7 +408,8 @@ def long_config(a, n):
             "layers": a.layers, "seq_len": a.seq_len, "n_kv_heads": 8, "n_q_heads": 32,
             "head_dim": 128, "query_buffer": a.n_queries, "compression_ratio": a.ratio,
             "n_kept": int(a.seq_len * (1 - a.ratio)), "d_mem": a.d_mem,
-            "parallelism": f"head-sharded x{n}" if n > 1 else "1 GPU",
+            "parallelism": f"head-sharded x{n}" if n > 1 or a.sharded else "1 GPU",
+            "cuda_graph": bool(a.graph and (n > 1 or a.sharded)),
             "l2": f"inputs larger than L2 ({a.layers} x {a.seq_len * 8 * 128 * 4 >> 20} MiB of K/V)"}
 
 
@@ -423,12 +429,13 @@ def run_long(a, dev, dist, rank, world):
     geo = parts["geometry"]
     n_kept = engine.n_kept_for(L, a.ratio, 4)
     sh = HeadShard(rank, world, hkv, L)
+    sharded = world > 1 or a.sharded
     layers = []
     for l in range(a.layers):
         q, k, v = synthetic.make_layer_inputs(seed=seed + 7 * l, batch=1, n_kv_heads=hkv,
                                               n_q_heads=hq, seq_len=L, n_queries=nq, device=dev)
         theta = parts["memory"].modules[l][0]
-        if world == 1:
+        if not sharded:
             lw = engine.LayerWeights.prepare(
                 geometry=geo.weight[l], prototypes=geo.prototypes, hadamard=geo.hadamard,
                 mlp_params=parts["indexer"].modules[l], theta=theta, n_kv_heads=hkv,
@@ -454,7 +461,7 @@ def run_long(a, dev, dist, rank, world):
             e1.record()
     torch.cuda.synchronize()
     budget = None
-    if world == 1:
+    if not sharded:
         n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
         budget = ops.sm_budget(max(1, n_sms - a.sm_reserve) if a.streams > 1 else 0)
         from core_b200 import _lib
@@ -502,6 +509,21 @@ def run_long(a, dev, dist, rank, world):
         step(None)
     torch.cuda.synchronize()
     ops.status(dev)
+    graph = None
+    if a.graph and sharded:
+        # one eager step with the QK events for the roofline, then the capture
+        step(ev[0])
+        torch.cuda.synchronize()
+        qk_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev[0])
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.graph(graph, stream=cap):
+            step(None)
+        torch.cuda.synchronize()
+        graph.replay()  # one replay before the timed region
+        torch.cuda.synchronize()
+        ops.status(dev)
     with ClockSampler(dev.index) as clocks:
         if dist is not None:
             dist.barrier()
@@ -511,7 +533,10 @@ def run_long(a, dev, dist, rank, world):
         t0.record()
         h0 = time.perf_counter()
         for i in range(a.steps):
-            step(ev[i])
+            if graph is not None:
+                graph.replay()
+            else:
+                step(ev[i])
         host_ms = (time.perf_counter() - h0) * 1e3 / a.steps  # time to issue a step
         t1.record()
         torch.cuda.synchronize()
@@ -522,13 +547,17 @@ def run_long(a, dev, dist, rank, world):
     ops.status(dev)
     ms = max_over_ranks(t0.elapsed_time(t1) / a.steps, dist, dev)
     host_ms = max_over_ranks(host_ms, dist, dev)
-    qk_ms = statistics.mean(e0.elapsed_time(e1) for pairs in ev for e0, e1 in pairs)
+    if graph is None:
+        qk_ms = statistics.mean(e0.elapsed_time(e1) for pairs in ev for e0, e1 in pairs)
+    else:
+        del graph  # graphs holding NCCL calls go before the process group
+        torch.cuda.synchronize()
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     peak, peak_src = 1590.0, "fallback"
     if os.path.exists(peaks_path):
         pk = json.load(open(peaks_path))
         peak, peak_src = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))), "measured"
-    if world == 1:
+    if not sharded:
         flops = 2.0 * hq * nq * L * d
         kernel = "qk_relation_kernel (QK pass 2: relation + per-key statistics)"
         alg = f"2*Hq*nq*L*d = {flops / 1e9:.2f} GFLOP per launch"
@@ -542,7 +571,7 @@ def run_long(a, dev, dist, rank, world):
                 "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"{peak_src} bf16_tflops_sustained", "traffic": None,
                 "avg_launch_ms": qk_ms, "algorithmic": alg}
-    if world == 1:
+    if not sharded:
         launches = KERNELS_PER_LAYER * a.layers * a.steps
     else:
         # per layer: 5 QK summary, 1 partial projection, 1 value sums, 1 summary merge,
