@@ -67,9 +67,9 @@ def parse():
     p.add_argument("--streams", type=int, default=3, help="layers compressed concurrently")
     p.add_argument("--sharded", action="store_true",
                    help="--workload long: the head-sharded step even on one rank (under torchrun)")
-    p.add_argument("--graph", action="store_true",
-                   help="--workload long, head-sharded: replay the step (kernels and NCCL "
-                        "collectives of all layers) as one CUDA graph")
+    p.add_argument("--graph", action=argparse.BooleanOptionalAction, default=True,
+                   help="replay the whole step (all layers' kernels and, head-sharded, the "
+                        "NCCL collectives) as one CUDA graph (--no-graph: issue it eagerly)")
     p.add_argument("--sm-reserve", type=int, default=2,
                    help="SMs the persistent grids leave free for the other streams' kernels")
     a = p.parse_args()
@@ -91,7 +91,8 @@ def config_dict(a, n):
             "compression_ratio": a.ratio, "n_kept": int(a.seq_len * (1 - a.ratio)),
             "d_mem": a.d_mem, "parallelism": f"batch-sharded x{n}",
             "l2": "inputs larger than L2 (32 layers x 64 MiB of K/V per step)",
-            "layers_in_flight": a.streams, "sm_reserve": a.sm_reserve if a.streams > 1 else 0}
+            "layers_in_flight": a.streams, "sm_reserve": a.sm_reserve if a.streams > 1 else 0,
+            "cuda_graph": bool(a.graph)}
 
 
 # ---------------------------------------------------------------------------
@@ -334,6 +335,21 @@ def main():
         step(None)
     torch.cuda.synchronize()
     ops.status(dev)
+    graph = None
+    if a.graph:
+        # one eager step with the relation events for the roofline, then the capture
+        step(ev[0])
+        torch.cuda.synchronize()
+        relation_ms = [e0.elapsed_time(e1) for e0, e1 in ev[0]]
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.graph(graph, stream=cap):
+            step(None)
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        ops.status(dev)
 
     # ---- timed region: device-resident inputs ----
     with ClockSampler(local) as clocks:
@@ -343,15 +359,24 @@ def main():
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
+        h0 = time.perf_counter()
         for i in range(a.steps):
-            step(ev[i])
+            if graph is not None:
+                graph.replay()
+            else:
+                step(ev[i])
+        host_ms = (time.perf_counter() - h0) * 1e3 / a.steps  # time to issue a step
         t1.record()
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
     budget.__exit__(None, None, None)  # the e2e leg below uses the press on one stream
     ms = t0.elapsed_time(t1) / a.steps
-    relation_ms = [e0.elapsed_time(e1) for pairs in ev for e0, e1 in pairs]
+    if graph is None:
+        relation_ms = [e0.elapsed_time(e1) for pairs in ev for e0, e1 in pairs]
+    else:
+        del graph
+        torch.cuda.synchronize()
     ops.status(dev)
     ms = max_over_ranks(ms, dist, dev)
     value = whole_job_rate(n, a.batch * L, ms / 1e3)
@@ -385,7 +410,7 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": config_dict(a, n), "roofline": roofline, "e2e": e2e,
             "gpu_launches": KERNELS_PER_LAYER * a.layers * a.steps,
-            "clocks": clocks.summary()}
+            "host_issue_ms_per_step": host_ms, "clocks": clocks.summary()}
     if rank == 0 and n == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(a)
     if rank == 0:
@@ -409,7 +434,7 @@ def long_config(a, n):
             "head_dim": 128, "query_buffer": a.n_queries, "compression_ratio": a.ratio,
             "n_kept": int(a.seq_len * (1 - a.ratio)), "d_mem": a.d_mem,
             "parallelism": f"head-sharded x{n}" if n > 1 or a.sharded else "1 GPU",
-            "cuda_graph": bool(a.graph and (n > 1 or a.sharded)),
+            "cuda_graph": bool(a.graph),
             "l2": f"inputs larger than L2 ({a.layers} x {a.seq_len * 8 * 128 * 4 >> 20} MiB of K/V)"}
 
 
@@ -510,7 +535,7 @@ def run_long(a, dev, dist, rank, world):
     torch.cuda.synchronize()
     ops.status(dev)
     graph = None
-    if a.graph and sharded:
+    if a.graph:
         # one eager step with the QK events for the roofline, then the capture
         step(ev[0])
         torch.cuda.synchronize()
