@@ -14,10 +14,14 @@
 //   mw_mbar_kernel   : M_bar partial = W^T V_ev on tcgen05 (A = W tiles by TMA,
 //                      B = gathered V rows, MN-major), split over token chunks.
 //   mw_update_kernel : M, b <- (gamma Z M + pi_E eta M_bar) / (Z' + eps).
+#include <cooperative_groups.h>
+
 #include <cmath>
 
 #include "common.cuh"
 #include "host_util.h"
+
+namespace cg = cooperative_groups;
 
 namespace core {
 namespace mw {
@@ -129,6 +133,115 @@ __global__ void __launch_bounds__(1024)
     Z[b] = zt;
     if (!isfinite(pie) || !isfinite(tot)) record_error(status, CORE_ERR_NONFINITE, 801, b);
   }
+}
+
+// Long rows: the same softmax mass on one cluster of kMassCluster CTAs per
+// batch row.  CTA c caches exp(x_i - max) of tokens [c Lc, (c + 1) Lc) in its
+// shared memory; the maximum, the f64 sums and pi_E are combined across the
+// cluster in CTA order, and the evicted list (split evenly over the CTAs)
+// reads each term from the CTA that holds it through distributed shared
+// memory.  Same arithmetic per term as mw_mass_kernel; only the order of the
+// f64 partial sums differs.
+constexpr int kMassCluster = 8;
+constexpr int kMassClusterMinLen = 8192;  // shorter rows: one CTA
+
+__device__ __forceinline__ double block_sum_f64(double v, double* red, int lane, int warp) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int w = 0; w < (int)(blockDim.x / 32); ++w) t += red[w];
+  return t;
+}
+
+__global__ void __cluster_dims__(kMassCluster, 1, 1) __launch_bounds__(1024)
+    mw_mass_cluster_kernel(const float* __restrict__ scores, int L, const int* __restrict__ evict,
+                           int n_evict, int n_ev_pad, float tau, float gamma,
+                           float* __restrict__ Z, float* __restrict__ pbar,
+                           float* __restrict__ coef, DeviceStatus* status) {
+  extern __shared__ float se[];  // exp(x_i - max) of this CTA's tokens
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cr = (int)cluster.block_rank();
+  const int b = blockIdx.x / kMassCluster;
+  const float* s = scores + (long long)b * L;
+  const int Lc = (L + kMassCluster - 1) / kMassCluster;
+  const int lo = min(L, cr * Lc), hi = min(L, lo + Lc);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __shared__ float redf[32];
+  __shared__ double redd[32];
+  __shared__ float s_part_max;
+  __shared__ double s_part_sum, s_part_pe;
+  const bool unit_tau = tau == 1.0f;
+  // ---- maximum ----
+  float m = -INFINITY;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float x = unit_tau ? s[i] : s[i] / tau;
+    se[i - lo] = x;
+    m = fmaxf(m, x);
+  }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) redf[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = redf[0];
+    for (int w = 1; w < (int)(blockDim.x / 32); ++w) mm = fmaxf(mm, redf[w]);
+    s_part_max = mm;
+  }
+  cluster.sync();
+  float mx = -INFINITY;
+  for (int c = 0; c < kMassCluster; ++c) mx = fmaxf(mx, *cluster.map_shared_rank(&s_part_max, c));
+  // ---- sum of the exps ----
+  double sum = 0.0;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    const float e = expf(se[i - lo] - mx);
+    se[i - lo] = e;
+    sum += (double)e;
+  }
+  sum = block_sum_f64(sum, redd, lane, warp);
+  if (threadIdx.x == 0) s_part_sum = sum;
+  cluster.sync();
+  double tot_d = 0.0;
+  for (int c = 0; c < kMassCluster; ++c) tot_d += *cluster.map_shared_rank(&s_part_sum, c);
+  const float tot = (float)tot_d;
+  // ---- evicted mass: CTA c takes evicted entries [c Kc, (c + 1) Kc) ----
+  const int* ev = evict + (long long)b * n_evict;
+  float* pb = pbar + (long long)b * n_ev_pad;
+  const int Kc = (n_evict + kMassCluster - 1) / kMassCluster;
+  const int k_lo = min(n_evict, cr * Kc), k_hi = min(n_evict, k_lo + Kc);
+  double pe = 0.0;
+  for (int k = k_lo + threadIdx.x; k < k_hi; k += blockDim.x) {
+    const int i = ev[k];
+    float p = 0.f;
+    if ((unsigned)i >= (unsigned)L) {  // evicted index outside the cache
+      record_error(status, CORE_ERR_INVALID_ARG, 802, i);
+    } else {
+      const float e = cluster.map_shared_rank(se, i / Lc)[i % Lc];
+      p = e / tot;
+    }
+    pb[k] = p;
+    pe += (double)p;
+  }
+  pe = block_sum_f64(pe, redd, lane, warp);
+  if (threadIdx.x == 0) s_part_pe = pe;
+  cluster.sync();
+  double pie_d = 0.0;
+  for (int c = 0; c < kMassCluster; ++c) pie_d += *cluster.map_shared_rank(&s_part_pe, c);
+  const float pie = (float)pie_d;
+  const float mass = pie > 0.f ? pie : 1.0f;
+  for (int k = k_lo + threadIdx.x; k < k_hi; k += blockDim.x) pb[k] = pb[k] / mass;
+  if (cr == kMassCluster - 1)
+    for (int k = n_evict + threadIdx.x; k < n_ev_pad; k += blockDim.x) pb[k] = 0.f;
+  if (cr == 0 && threadIdx.x == 0) {
+    const float gz = gamma * Z[b];
+    const float zt = gz + pie;
+    coef[b * 3 + 0] = gz;
+    coef[b * 3 + 1] = pie;
+    coef[b * 3 + 2] = zt + 1e-8f;
+    Z[b] = zt;
+    if (!isfinite(pie) || !isfinite(tot)) record_error(status, CORE_ERR_NONFINITE, 801, b);
+  }
+  cluster.sync();  // no CTA leaves while another may still read its shared memory
 }
 
 // ===========================================================================
@@ -780,7 +893,15 @@ static int memory_write_impl(const core_dims_t* d, const void* k, const void* v,
   DeviceStatus* st = device_status();
   cudaError_t e;
 
-  if (d->seq_len <= kMassMaxSmem) {
+  if (d->seq_len >= kMassClusterMinLen && d->seq_len <= kMassCluster * kMassMaxSmem) {
+    const int Lc = (d->seq_len + kMassCluster - 1) / kMassCluster;
+    e = cudaFuncSetAttribute(mw_mass_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(float) * kMassMaxSmem));
+    if (e != cudaSuccess) return cuda_error(e, "mw_mass_cluster_kernel attribute");
+    mw_mass_cluster_kernel<<<d->batch * kMassCluster, 1024, sizeof(float) * (size_t)Lc, s>>>(
+        scores_cal, d->seq_len, evict_idx, n_evict, m.n_ev_pad, student_temp, gamma, Z, pbar, coef,
+        st);
+  } else if (d->seq_len <= kMassMaxSmem) {
     e = cudaFuncSetAttribute(mw_mass_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)(sizeof(float) * kMassMaxSmem));
     if (e != cudaSuccess) return cuda_error(e, "mw_mass_kernel attribute");

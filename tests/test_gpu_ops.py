@@ -261,7 +261,8 @@ def test_memory_write_matches_reference(name):
     assert abs(float(Z[0]) - float(gZ[0])) <= 1e-6
 
 
-@pytest.mark.parametrize("d_mem,L,hkv", [(512, 1536, 8), (256, 1000, 8), (384, 700, 4)])
+@pytest.mark.parametrize("d_mem,L,hkv", [(512, 1536, 8), (256, 1000, 8), (384, 700, 4),
+                                         (256, 16384, 8), (128, 70001, 2)])
 def test_memory_write_matches_oracle_wide_memory(d_mem, L, hkv):
     """Memory widths whose M_bar tiles pair up (d_mem a multiple of 256) and
     ones that do not; evicted counts that are not multiples of the tiles."""
