@@ -785,10 +785,48 @@ __device__ float relation_exact(const MergeParams& p, int b, int h, int key, int
   return __fdiv_rn(acc, (float)p.head_topk);
 }
 
+// One lane per KV head, Hkv lanes per key (Hkv a power of two, at most 16):
+// each lane walks its head's records of the key (contiguous, n_qb x 64 B),
+// keeps that head's f6 test to itself, and the key's lanes combine the rest
+// with shuffles: the top-4 lists (order-free), the positive sums and counts,
+// and the OR of the positive-query bits of every query block.
+template <int kLanes>
+__device__ __forceinline__ void merge_top4_lanes(float (&t)[4]) {
+#pragma unroll
+  for (int off = 1; off < kLanes; off <<= 1) {
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, t[i], off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) top4_insert(t, o[i]);
+  }
+}
+
+template <int kLanes, typename T>
+__device__ __forceinline__ T lanes_sum(T v) {
+#pragma unroll
+  for (int off = 1; off < kLanes; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+template <int kLanes>
+__device__ __forceinline__ uint32_t lanes_or(uint32_t v) {
+#pragma unroll
+  for (int off = 1; off < kLanes; off <<= 1) v |= __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+template <int kLanes>
 __global__ void __launch_bounds__(kMergeThreads)
     qk_merge_kernel(const MergeParams p) {
-  const long long gi = (long long)blockIdx.x * kMergeThreads + threadIdx.x;
-  if (gi >= (long long)p.B * p.L) return;
+  const long long tid = (long long)blockIdx.x * kMergeThreads + threadIdx.x;
+  const long long gi_raw = tid / kLanes;
+  const int h = (int)(tid % kLanes);  // this lane's KV head
+  // whole key groups stay in the grid (kLanes divides the block), so the
+  // shuffles below always see all lanes of the key; lanes past the last key
+  // compute on a clamped key and store nothing
+  const bool live = gi_raw < (long long)p.B * p.L;
+  const long long gi = live ? gi_raw : 0;
   const int b = (int)(gi / p.L);
   const int key = (int)(gi % p.L);
   int valid = p.nq - max(key - p.q_start, 0);
@@ -805,73 +843,64 @@ __global__ void __launch_bounds__(kMergeThreads)
 
   float top[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   float rtop[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-  float psum = 0.f;
-  unsigned long long pcnt = 0;
+  float hs = 0.f, mx = -INFINITY;
+  unsigned int hc = 0;
   int f5cnt = 0;
-  int f6pos = 0;
-  const uint32_t* base = p.rec + ((long long)b * p.L + key) * p.Hkv * p.n_qb * kRecWords;
-  // f5: OR over heads of the per-query positive bits, per query block
-  uint32_t* sum_out = p.summary != nullptr ? p.summary + gi * p.sum_words : nullptr;
+  uint32_t* sum_out = (p.summary != nullptr && live) ? p.summary + gi * p.sum_words : nullptr;
+  const uint32_t* base = p.rec + (gi * p.Hkv + h) * (long long)p.n_qb * kRecWords;
   for (int qb = 0; qb < p.n_qb; ++qb) {
-    uint32_t w[4] = {0, 0, 0, 0};
-    for (int h = 0; h < p.Hkv; ++h) {
-      const uint4* r = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords);
-      const uint4 r2 = r[2], r3 = r[3];
-      w[0] |= r2.z;
-      w[1] |= r2.w;
-      w[2] |= r3.x;
-      w[3] |= r3.y;
-    }
-    f5cnt += __popc(w[0]) + __popc(w[1]) + __popc(w[2]) + __popc(w[3]);
-    if (sum_out != nullptr)
-      reinterpret_cast<uint4*>(sum_out + kSumHead)[qb] = make_uint4(w[0], w[1], w[2], w[3]);
+    const uint4* r = reinterpret_cast<const uint4*>(base + (long long)qb * kRecWords);
+    const uint4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
+    top4_insert(top, __uint_as_float(r0.x));
+    top4_insert(top, __uint_as_float(r0.y));
+    top4_insert(top, __uint_as_float(r0.z));
+    top4_insert(top, __uint_as_float(r0.w));
+    top4_insert(rtop, __uint_as_float(r1.x));
+    top4_insert(rtop, __uint_as_float(r1.y));
+    top4_insert(rtop, __uint_as_float(r1.z));
+    top4_insert(rtop, __uint_as_float(r1.w));
+    hs += __uint_as_float(r2.x);
+    hc += r2.y;
+    mx = fmaxf(mx, __uint_as_float(r3.z));
+    // f5: OR over the heads of the positive-query bits of this block
+    const uint32_t w0 = lanes_or<kLanes>(r2.z), w1 = lanes_or<kLanes>(r2.w);
+    const uint32_t w2 = lanes_or<kLanes>(r3.x), w3 = lanes_or<kLanes>(r3.y);
+    f5cnt += __popc(w0) + __popc(w1) + __popc(w2) + __popc(w3);
+    if (sum_out != nullptr && h == 0)
+      reinterpret_cast<uint4*>(sum_out + kSumHead)[qb] = make_uint4(w0, w1, w2, w3);
   }
-  for (int h = 0; h < p.Hkv; ++h) {
-    float hs = 0.f, mx = -INFINITY;
-    unsigned int hc = 0;
-    for (int qb = 0; qb < p.n_qb; ++qb) {
-      const uint4* r = reinterpret_cast<const uint4*>(base + ((long long)h * p.n_qb + qb) * kRecWords);
-      const uint4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
-      top4_insert(top, __uint_as_float(r0.x));
-      top4_insert(top, __uint_as_float(r0.y));
-      top4_insert(top, __uint_as_float(r0.z));
-      top4_insert(top, __uint_as_float(r0.w));
-      top4_insert(rtop, __uint_as_float(r1.x));
-      top4_insert(rtop, __uint_as_float(r1.y));
-      top4_insert(rtop, __uint_as_float(r1.z));
-      top4_insert(rtop, __uint_as_float(r1.w));
-      hs += __uint_as_float(r2.x);
-      hc += r2.y;
-      mx = fmaxf(mx, __uint_as_float(r3.z));
-    }
-    psum += hs;
-    pcnt += hc;
-    // f6 for head h: sign of the mean of the top-kf relations over queries
-    if ((int)hc >= kf) {
-      ++f6pos;
-    } else if (hc > 0) {
-      const float rem = (float)(kf - (int)hc);
-      const float hi = hs + rem * mx;                       // remaining values <= mx
-      const float lo = hs + rem * (kLogFloor * 1.0001f);    // and >= the floor
-      const float tol = 1e-5f * (fabsf(hs) + rem * fabsf(kLogFloor));
-      if (hi < -tol) {
-        // definitely not positive
-      } else if (lo > tol) {
-        ++f6pos;
-      } else {
-        const int slot = atomicAdd(p.queue_count, 1);
-        if (slot < p.queue_cap) p.queue[slot] = make_int2((int)gi, h);
-        else record_error(p.status, CORE_ERR_UNSUPPORTED, 401, key);
-      }
+  // f6 for this lane's head: sign of the mean of the top-kf relations over queries
+  int f6pos = 0;
+  if ((int)hc >= kf) {
+    f6pos = 1;
+  } else if (hc > 0) {
+    const float rem = (float)(kf - (int)hc);
+    const float hi = hs + rem * mx;                       // remaining values <= mx
+    const float lo = hs + rem * (kLogFloor * 1.0001f);    // and >= the floor
+    const float tol = 1e-5f * (fabsf(hs) + rem * fabsf(kLogFloor));
+    if (hi < -tol) {
+      // definitely not positive
+    } else if (lo > tol) {
+      f6pos = 1;
+    } else if (live) {
+      const int slot = atomicAdd(p.queue_count, 1);
+      if (slot < p.queue_cap) p.queue[slot] = make_int2((int)gi, h);
+      else record_error(p.status, CORE_ERR_UNSUPPORTED, 401, key);
     }
   }
+  merge_top4_lanes<kLanes>(top);
+  merge_top4_lanes<kLanes>(rtop);
+  const float psum = lanes_sum<kLanes>(hs);
+  const unsigned int pcnt = lanes_sum<kLanes>(hc);
+  f6pos = lanes_sum<kLanes>(f6pos);
+  if (!live || h != 0) return;
   if (sum_out != nullptr) {  // this rank's heads only: the cross-rank merge finishes f1..f6
     uint4* o = reinterpret_cast<uint4*>(sum_out);
     o[0] = make_uint4(__float_as_uint(top[0]), __float_as_uint(top[1]), __float_as_uint(top[2]),
                       __float_as_uint(top[3]));
     o[1] = make_uint4(__float_as_uint(rtop[0]), __float_as_uint(rtop[1]), __float_as_uint(rtop[2]),
                       __float_as_uint(rtop[3]));
-    o[2] = make_uint4(__float_as_uint(psum), (uint32_t)pcnt, __float_as_uint((float)f6pos), 0u);
+    o[2] = make_uint4(__float_as_uint(psum), pcnt, __float_as_uint((float)f6pos), 0u);
     return;
   }
   float f[6];
@@ -1235,7 +1264,19 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
   e = cudaMemsetAsync(queue_count, 0, sizeof(int), s);
   if (e != cudaSuccess) return cuda_error(e, "core_qk_features queue clear");
   const long long n = (long long)p.B * p.L;
-  qk_merge_kernel<<<(unsigned)((n + kMergeThreads - 1) / kMergeThreads), kMergeThreads, 0, s>>>(mp);
+  {
+    // Hkv lanes per key (a power of two, checked above)
+    const long long threads = n * p.Hkv;
+    const unsigned blocks = (unsigned)((threads + kMergeThreads - 1) / kMergeThreads);
+    switch (p.Hkv) {
+      case 1: qk_merge_kernel<1><<<blocks, kMergeThreads, 0, s>>>(mp); break;
+      case 2: qk_merge_kernel<2><<<blocks, kMergeThreads, 0, s>>>(mp); break;
+      case 4: qk_merge_kernel<4><<<blocks, kMergeThreads, 0, s>>>(mp); break;
+      case 8: qk_merge_kernel<8><<<blocks, kMergeThreads, 0, s>>>(mp); break;
+      case 16: qk_merge_kernel<16><<<blocks, kMergeThreads, 0, s>>>(mp); break;
+      default: return set_error(CORE_ERR_UNSUPPORTED, "core_qk_features: at most 16 KV heads");
+    }
+  }
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_merge_kernel launch");
   qk_f6_resolve_kernel<<<4 * sm_count(), kResolveThreads, 0, s>>>(mp);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_f6_resolve_kernel launch");
