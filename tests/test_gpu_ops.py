@@ -93,6 +93,27 @@ def test_qk_features_llama_shapes_4096():
     assert f5_frac <= 0.005 and f6_frac <= 0.005, (f5_frac, f6_frac)
 
 
+def test_qk_features_full_scope_prefill_2048():
+    """Full-scope prefill (every cached token also a query, Q = L, the
+    reference's prefill_qk_scope="all") at the largest supported query count."""
+    from core_b200 import ops, synthetic
+    dev = _dev()
+    L = 2048
+    q, k, _ = synthetic.make_layer_inputs(seed=12, batch=1, n_kv_heads=4, n_q_heads=16,
+                                          seq_len=L, n_queries=L, device=dev)
+    feats, lse = ops.qk_features(q, k)
+    ops.status()
+    qn = q[0].float().cpu().numpy()
+    kn = k[0].float().cpu().numpy()
+    ref, ref_lse, R = O.qk_features(qn, kn, groups=4, round_bf16=True)
+    got = feats[0].cpu().numpy()
+    assert np.abs(lse[0].cpu().numpy() - ref_lse).max() <= LSE_TOL * np.abs(ref_lse).max()
+    _check_qk_features(got, ref, R)
+    f5_frac, _ = _discrete_mismatch(got[:, 4], ref[:, 4], 1 / L)
+    f6_frac, _ = _discrete_mismatch(got[:, 5], ref[:, 5], 1 / 4)
+    assert f5_frac <= 0.005 and f6_frac <= 0.005, (f5_frac, f6_frac)
+
+
 def test_qk_features_batch_rows_are_independent():
     from core_b200 import ops, synthetic
     dev = _dev()
