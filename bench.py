@@ -592,9 +592,15 @@ def run_long(a, dev, dist, rank, world):
                   "rank's heads)")
         alg = f"2 passes x 2*Hq_rank*nq*L*d = {flops / 1e9:.2f} GFLOP per layer"
     achieved = flops / (qk_ms / 1e3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", f"qk_relation_L{L}_traffic.txt")
+    if not sharded and os.path.exists(tpath):
+        rec = dict(line.split(None, 1) for line in open(tpath) if line.strip())
+        if int(rec.get("seq_len", 0)) == L:
+            traffic = int(rec["bytes_per_launch"])
     roofline = {"kernel": kernel, "bound": "tensor", "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": achieved / peak,
-                "peak_source": f"{peak_src} bf16_tflops_sustained", "traffic": None,
+                "peak_source": f"{peak_src} bf16_tflops_sustained", "traffic": traffic,
                 "avg_launch_ms": qk_ms, "algorithmic": alg}
     if not sharded:
         launches = KERNELS_PER_LAYER * a.layers * a.steps
