@@ -336,19 +336,25 @@ def main():
     torch.cuda.synchronize()
     ops.status(dev)
     graph = None
+    graph_note = None
     if a.graph:
         # one eager step with the relation events for the roofline, then the capture
         step(ev[0])
         torch.cuda.synchronize()
         relation_ms = [e0.elapsed_time(e1) for e0, e1 in ev[0]]
-        graph = torch.cuda.CUDAGraph()
-        cap = torch.cuda.Stream(dev)
-        cap.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.graph(graph, stream=cap):
-            step(None)
-        torch.cuda.synchronize()
-        graph.replay()
-        torch.cuda.synchronize()
+        try:
+            graph = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream(dev)
+            cap.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.graph(graph, stream=cap):
+                step(None)
+            torch.cuda.synchronize()
+            graph.replay()
+            torch.cuda.synchronize()
+        except RuntimeError as exc:  # the step has no collectives: this rank issues eagerly
+            graph = None
+            graph_note = f"graph capture failed, eager issue: {str(exc).splitlines()[0][:160]}"
+            torch.cuda.synchronize()
         ops.status(dev)
 
     # ---- timed region: device-resident inputs ----
@@ -411,6 +417,9 @@ def main():
             "config": config_dict(a, n), "roofline": roofline, "e2e": e2e,
             "gpu_launches": KERNELS_PER_LAYER * a.layers * a.steps,
             "host_issue_ms_per_step": host_ms, "clocks": clocks.summary()}
+    if graph_note is not None:
+        line["config"]["cuda_graph"] = False
+        line["graph_note"] = graph_note
     if rank == 0 and n == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(a)
     if rank == 0:
