@@ -2,6 +2,9 @@
 // gated latent-memory readout (replaces core/indexer.py:165-207 and
 // core/kvpress_adapter.py:1302-1352).
 #include <cmath>
+#include <cstdint>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -9,6 +12,7 @@
 namespace core {
 namespace misc {
 
+namespace cg = cooperative_groups;
 constexpr int kD = 128;
 
 // out[b, h, j, :] = in[b, h, keep[b, j], :]; kVec lanes move one row with
@@ -98,6 +102,81 @@ __global__ void __launch_bounds__(kProjWarps * 32)
   }
 }
 
+// Stage 1 for rows that fit in registers (Hq a multiple of 4, Hq/4 <= kMaxV):
+// four warps split each weight row; a lane loads its whole weight segment and
+// the q elements of the same columns straight from global memory, so one
+// round trip to HBM covers the block.  The four parts are added in order.
+constexpr int kProjSplit = 4;          // warps per weight row
+constexpr int kProjRowsPerBlock = 2;   // 8 warps
+
+__device__ __forceinline__ float4 ldg4(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+__device__ __forceinline__ float4 ldq4(const float* p) { return ldg4(p); }
+__device__ __forceinline__ float4 ldq4(const __nv_bfloat16* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+  const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+  return make_float4(__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi));
+}
+__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
+  acc = fmaf(a.x, b.x, acc);
+  acc = fmaf(a.y, b.y, acc);
+  acc = fmaf(a.z, b.z, acc);
+  return fmaf(a.w, b.w, acc);
+}
+
+template <typename T, int kMaxV>
+__global__ void __launch_bounds__(kProjSplit * kProjRowsPerBlock * 32)
+    readout_proj_reg_kernel(const T* __restrict__ q, int Hq, int q_len,
+                            const float* __restrict__ theta, const float* __restrict__ gw1,
+                            const float* __restrict__ gb1, int d_mem, int gh,
+                            float* __restrict__ proj, float* __restrict__ gpre) {
+  __shared__ float s_part[kProjSplit * kProjRowsPerBlock];
+  const int b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dm = Hq * kD, rows = d_mem + gh;
+  const int r = blockIdx.x * kProjRowsPerBlock + warp / kProjSplit;
+  const int part = warp % kProjSplit;
+  const bool live = r < rows;
+  const int nv = Hq / kProjSplit;  // float4 per lane: column part*seg + i*128 + lane*4
+  const float* w = !live ? theta
+                   : (r < d_mem ? theta + (long long)r * dm : gw1 + (long long)(r - d_mem) * dm);
+  w += part * nv * 128 + lane * 4;
+  // q head part*nv + i holds the columns of float4 i; element lane*4 of that head
+  const T* qb = q + (((long long)b * Hq + part * nv) * q_len) * kD + lane * 4;
+  float4 wv[kMaxV], xv[kMaxV];
+#pragma unroll
+  for (int i = 0; i < kMaxV; ++i) {
+    const bool on = live && i < nv;
+    wv[i] = on ? ldg4(w + i * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
+    xv[i] = on ? ldq4(qb + (long long)i * q_len * kD) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int t = 0; t < q_len; ++t) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxV; ++i) acc = dot4(wv[i], xv[i], acc);
+    if (t + 1 < q_len) {
+#pragma unroll
+      for (int i = 0; i < kMaxV; ++i)
+        if (live && i < nv) xv[i] = ldq4(qb + ((long long)i * q_len + t + 1) * kD);
+    }
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    __syncthreads();  // the previous t's parts are consumed
+    if (lane == 0) s_part[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x < kProjRowsPerBlock) {
+      const int rr = blockIdx.x * kProjRowsPerBlock + threadIdx.x;
+      if (rr < rows) {
+        float v = 0.f;
+        for (int pp = 0; pp < kProjSplit; ++pp) v += s_part[threadIdx.x * kProjSplit + pp];
+        if (rr < d_mem) proj[((long long)b * q_len + t) * d_mem + rr] = v;
+        else gpre[((long long)b * q_len + t) * gh + (rr - d_mem)] = v + gb1[rr - d_mem];
+      }
+    }
+  }
+}
+
 // Stage 2: m = proj M / sqrt(proj^2 . b + eps), gate, residual (rounded to
 // bf16 when the attention output is bf16).
 // A block covers 32 value columns (one per lane); its 8 warps split the d_mem
@@ -149,6 +228,154 @@ __global__ void __launch_bounds__(kMemWarps * 32)
     m *= 1.0f / sqrtf(s_den);
     const float r = s_g * m;
     res[((long long)b * q_len + t) * kvw + c] = round_bf16 ? bf16_round(r) : r;
+  }
+}
+
+// Stage 2 as an 8-CTA cluster per 128 columns of M (d_mem <= 64 * kMaxR): CTA
+// rank c of the cluster takes rows [c*d_mem/8, (c+1)*d_mem/8), each of its 8
+// warps a slice of those rows with every row's float4 loaded at once; the
+// warps' sums, then the CTAs' sums, are added in rank order, the second
+// through distributed shared memory on rank 0, which applies the norm and
+// gate.  The norm's 8 partial sums are formed the same way.
+constexpr int kMemCluster = 8;
+constexpr int kMemCWarps = 8;
+
+template <int kMaxR>
+__global__ void __cluster_dims__(1, kMemCluster, 1) __launch_bounds__(kMemCWarps * 32)
+    readout_mem_cluster_kernel(const float* __restrict__ proj, const float* __restrict__ gpre,
+                               const float* __restrict__ gw2, const float* __restrict__ gb2,
+                               float gate_override, const float* __restrict__ M,
+                               const float* __restrict__ bst, int q_len, int d_mem, int gh,
+                               int kvw, bool round_bf16, float* __restrict__ res) {
+  __shared__ float4 s_w[kMemCWarps][32];
+  __shared__ float s_wden[kMemCWarps];
+  __shared__ float4 s_cta[32];  // this CTA's sum over its rows, read by rank 0
+  __shared__ float s_den;
+  __shared__ float s_g;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int z = blockIdx.z, b = z / q_len;  // z = b * q_len + t
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x * 128 + lane * 4;
+  const int r0 = (int)((long long)rank * d_mem / kMemCluster);
+  const int r1 = (int)((long long)(rank + 1) * d_mem / kMemCluster);
+  const int j0 = r0 + (int)((long long)warp * (r1 - r0) / kMemCWarps);
+  const int j1 = r0 + (int)((long long)(warp + 1) * (r1 - r0) / kMemCWarps);
+  const float* pr = proj + (long long)z * d_mem;
+  const float* Mb = M + (long long)b * d_mem * kvw + c;
+  const float* bb = bst + (long long)b * d_mem;
+  float4 mv[kMaxR];
+  float pv[kMaxR], bv[kMaxR];
+#pragma unroll
+  for (int i = 0; i < kMaxR; ++i) {
+    const bool on = j0 + i < j1;
+    mv[i] = on ? ldg4(Mb + (long long)(j0 + i) * kvw) : make_float4(0.f, 0.f, 0.f, 0.f);
+    pv[i] = on ? __ldg(pr + j0 + i) : 0.f;
+    bv[i] = on ? __ldg(bb + j0 + i) : 0.f;
+  }
+  float gl = 0.f;
+  if (rank == 0 && warp == kMemCWarps - 1) {
+    for (int o = lane; o < gh; o += 32) gl = fmaf(gw2[o], gelu(gpre[(long long)z * gh + o]), gl);
+    for (int o = 16; o > 0; o >>= 1) gl += __shfl_xor_sync(0xffffffffu, gl, o);
+  }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxR; ++i) {
+    acc.x = fmaf(pv[i], mv[i].x, acc.x);
+    acc.y = fmaf(pv[i], mv[i].y, acc.y);
+    acc.z = fmaf(pv[i], mv[i].z, acc.z);
+    acc.w = fmaf(pv[i], mv[i].w, acc.w);
+    den = fmaf(pv[i] * pv[i], bv[i], den);
+  }
+  s_w[warp][lane] = acc;
+  if (lane == 0) s_wden[warp] = den;
+  if (rank == 0 && warp == kMemCWarps - 1 && lane == 0)
+    s_g = gate_override >= 0.f ? gate_override : 1.0f / (1.0f + expf(-(gl + gb2[0])));
+  __syncthreads();
+  if (warp == 0) {
+    float4 v = s_w[0][lane];
+    for (int w2 = 1; w2 < kMemCWarps; ++w2) {
+      const float4 u = s_w[w2][lane];
+      v.x += u.x; v.y += u.y; v.z += u.z; v.w += u.w;
+    }
+    s_cta[lane] = v;
+    if (lane == 0) {
+      float dd = 0.f;
+      for (int w2 = 0; w2 < kMemCWarps; ++w2) dd += s_wden[w2];
+      s_den = dd;
+    }
+  }
+  cluster.sync();
+  if (rank == 0 && warp == 0) {
+    float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
+    float dd = 0.f;
+    for (int k = 0; k < kMemCluster; ++k) {
+      const float4 u = *cluster.map_shared_rank(&s_cta[lane], k);
+      m.x += u.x; m.y += u.y; m.z += u.z; m.w += u.w;
+      dd += *cluster.map_shared_rank(&s_den, k);
+    }
+    const float sc = 1.0f / sqrtf(dd + 1e-8f), g = s_g;
+    float4 o;
+    o.x = g * (m.x * sc);
+    o.y = g * (m.y * sc);
+    o.z = g * (m.z * sc);
+    o.w = g * (m.w * sc);
+    if (round_bf16) {
+      o.x = bf16_round(o.x); o.y = bf16_round(o.y); o.z = bf16_round(o.z); o.w = bf16_round(o.w);
+    }
+    *reinterpret_cast<float4*>(res + (long long)z * kvw + c) = o;
+  }
+  cluster.sync();  // rank 0 has read every CTA's shared memory
+}
+
+// Stage 3 for rows that fit in registers (kvw <= 128 * kMaxV): kRows output
+// rows per warp, each lane loading its float4 of every row and of the
+// residual straight from global memory; the block needs no shared memory.
+constexpr int kOutWarps = 8;
+
+template <typename T, int kRows, int kMaxV>
+__global__ void __launch_bounds__(kOutWarps * 32)
+    readout_out_reg_kernel(const float* __restrict__ res, const float* __restrict__ ofold,
+                           int q_len, int kvw, int hidden, T* __restrict__ out) {
+  const int b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o0 = (blockIdx.x * kOutWarps + warp) * kRows;
+  const int nv = kvw / 128;
+  const float* rb = res + (long long)b * q_len * kvw + lane * 4;
+  float4 wv[kRows][kMaxV], xv[kMaxV];
+#pragma unroll
+  for (int k = 0; k < kRows; ++k) {
+    const bool live = o0 + k < hidden;
+    const float* w = ofold + (long long)(live ? o0 + k : 0) * kvw + lane * 4;
+#pragma unroll
+    for (int i = 0; i < kMaxV; ++i)
+      wv[k][i] = (live && i < nv) ? ldg4(w + i * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int i = 0; i < kMaxV; ++i) xv[i] = i < nv ? ldg4(rb + i * 128) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int t = 0; t < q_len; ++t) {
+    float acc[kRows];
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) {
+      acc[k] = 0.f;
+#pragma unroll
+      for (int i = 0; i < kMaxV; ++i) acc[k] = dot4(wv[k][i], xv[i], acc[k]);
+    }
+    if (t + 1 < q_len) {
+#pragma unroll
+      for (int i = 0; i < kMaxV; ++i)
+        if (i < nv) xv[i] = ldg4(rb + (long long)(t + 1) * kvw + i * 128);
+    }
+#pragma unroll
+    for (int k = 0; k < kRows; ++k)
+      for (int sft = 16; sft > 0; sft >>= 1) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], sft);
+    if (lane == 0) {
+      T* row = out + ((long long)b * q_len + t) * hidden;
+#pragma unroll
+      for (int k = 0; k < kRows; ++k)
+        if (o0 + k < hidden) row[o0 + k] = add_out(row[o0 + k], acc[k]);
+    }
   }
 }
 
@@ -278,7 +505,33 @@ extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const vo
   cudaError_t e;
   const int sms = sm_count();
   const int gh = gate_override >= 0.f ? 0 : gate_hidden;
-  {
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  // register paths: 16-byte weight rows and 8-byte (bf16) or 16-byte (f32) q groups
+  const bool q_al = (reinterpret_cast<uintptr_t>(q) & (f32 ? 15 : 7)) == 0;
+  const int pv = d->n_q_heads / kProjSplit;
+  const bool proj_reg = d->n_q_heads % kProjSplit == 0 && pv <= 16 && q_al && al16(theta) &&
+                        (gh == 0 || al16(gate_w1));
+  if (proj_reg) {
+    const dim3 grid((d_mem + gh + kProjRowsPerBlock - 1) / kProjRowsPerBlock, d->batch);
+    const int threads = kProjSplit * kProjRowsPerBlock * 32;
+    if (f32 && pv <= 8)
+      readout_proj_reg_kernel<float, 8><<<grid, threads, 0, s>>>(
+          static_cast<const float*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1, d_mem, gh,
+          proj, gpre);
+    else if (f32)
+      readout_proj_reg_kernel<float, 16><<<grid, threads, 0, s>>>(
+          static_cast<const float*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1, d_mem, gh,
+          proj, gpre);
+    else if (pv <= 8)
+      readout_proj_reg_kernel<__nv_bfloat16, 8><<<grid, threads, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1,
+          d_mem, gh, proj, gpre);
+    else
+      readout_proj_reg_kernel<__nv_bfloat16, 16><<<grid, threads, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1,
+          d_mem, gh, proj, gpre);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_proj launch");
+  } else {
     const size_t smem = (size_t)q_len * dm * 4;
     e = f32 ? cudaFuncSetAttribute(readout_proj_kernel<float>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
@@ -299,13 +552,40 @@ extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const vo
           d_mem, gh, proj, gpre);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_proj launch");
   }
-  {
+  if (d_mem <= 64 * 16 && al16(M) && (long long)d->batch * q_len <= 65535) {
+    const dim3 grid(kvw / 128, kMemCluster, d->batch * q_len);
+    if (d_mem <= 64 * 8)
+      readout_mem_cluster_kernel<8><<<grid, kMemCWarps * 32, 0, s>>>(
+          proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, !f32,
+          res);
+    else
+      readout_mem_cluster_kernel<16><<<grid, kMemCWarps * 32, 0, s>>>(
+          proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, !f32,
+          res);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_mem launch");
+  } else {
     const size_t smem = (size_t)d_mem * 4;
     readout_mem_kernel<<<dim3((kvw + 31) / 32, d->batch, q_len), kMemWarps * 32, smem, s>>>(
         proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, !f32, res);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_mem launch");
   }
-  {
+  if (kvw <= 128 * 16 && al16(o_fold)) {
+    const int rpw = kvw <= 128 * 8 ? 2 : 1;  // rows per warp
+    const dim3 grid((hidden + kOutWarps * rpw - 1) / (kOutWarps * rpw), d->batch);
+    if (f32 && rpw == 2)
+      readout_out_reg_kernel<float, 2, 8><<<grid, kOutWarps * 32, 0, s>>>(
+          res, o_fold, q_len, kvw, hidden, static_cast<float*>(attn_out));
+    else if (f32)
+      readout_out_reg_kernel<float, 1, 16><<<grid, kOutWarps * 32, 0, s>>>(
+          res, o_fold, q_len, kvw, hidden, static_cast<float*>(attn_out));
+    else if (rpw == 2)
+      readout_out_reg_kernel<__nv_bfloat16, 2, 8><<<grid, kOutWarps * 32, 0, s>>>(
+          res, o_fold, q_len, kvw, hidden, static_cast<__nv_bfloat16*>(attn_out));
+    else
+      readout_out_reg_kernel<__nv_bfloat16, 1, 16><<<grid, kOutWarps * 32, 0, s>>>(
+          res, o_fold, q_len, kvw, hidden, static_cast<__nv_bfloat16*>(attn_out));
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_out launch");
+  } else {
     const size_t smem = (size_t)q_len * kvw * 4;
     e = f32 ? cudaFuncSetAttribute(readout_out_kernel<float>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)

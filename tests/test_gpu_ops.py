@@ -387,6 +387,53 @@ def test_memory_readout_matches_reference():
         assert (diff > 0).mean() < 0.02 and diff.max() <= 2 ** -7 * np.abs(ref).max(), diff.max()
 
 
+# (Hkv, Hq, d_mem, gate_hidden, hidden, q_len): the register kernels with 8 and
+# 16 float4 a lane, ragged row slices and partial warps, and (Hq not a multiple
+# of 4, d_mem above 1024, Hkv*d above 2048) the general kernels
+READOUT_SHAPES = [(8, 32, 512, 64, 4096, 1), (16, 64, 700, 48, 96, 3), (1, 4, 20, 8, 40, 5),
+                  (18, 18, 1100, 16, 64, 2)]
+
+
+@pytest.mark.parametrize("shape", READOUT_SHAPES, ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_memory_readout_shapes_match_oracle(shape, dtype):
+    from core_b200 import ops
+    dev = _dev()
+    hkv, hq, d_mem, gh, hidden, ql = shape
+    rng = np.random.default_rng(sum(shape))
+    f = np.float32
+    q = rng.standard_normal((ql, hq * 128)).astype(f)
+    theta = (rng.standard_normal((d_mem, hq * 128)) / np.sqrt(hq * 128)).astype(f)
+    w1 = (rng.standard_normal((gh, hq * 128)) / np.sqrt(hq * 128)).astype(f)
+    b1 = (rng.standard_normal(gh) * 0.1).astype(f)
+    w2 = (rng.standard_normal(gh) * 0.1).astype(f)
+    b2 = f([0.2])
+    M = rng.standard_normal((d_mem, hkv * 128)).astype(f)
+    b = np.abs(rng.standard_normal(d_mem)).astype(f)
+    ofold = (rng.standard_normal((hidden, hkv * 128)) / np.sqrt(hkv * 128)).astype(f)
+    attn = rng.standard_normal((ql, hidden)).astype(f)
+    bf = dtype == "bf16"
+    if bf:  # the inputs the bf16 path sees
+        q = O.bf16_round(q)
+        attn = O.bf16_round(attn)
+    ref = O.memory_readout(q, theta, w1, b1, w2[None], b2, M, b, ofold, attn, out_bf16=bf)
+    cast = _bf16 if bf else _f32
+    qt = cast(q, dev).reshape(ql, hq, 128).permute(1, 0, 2)[None].contiguous()
+    out = cast(attn, dev)[None].contiguous()
+    ops.memory_readout(qt, _f32(theta, dev), (_f32(w1, dev), _f32(b1, dev), _f32(w2, dev),
+                                              _f32(b2, dev)),
+                       _f32(M, dev)[None], _f32(b, dev)[None], _f32(ofold, dev), out,
+                       n_kv_heads=hkv)
+    ops.status()
+    got = out[0].float().cpu().numpy()
+    if bf:
+        # equal up to one bf16 ulp of the residual or of the sum on a few entries
+        diff = np.abs(got - ref)
+        assert (diff > 0).mean() < 0.02 and diff.max() <= 2 ** -7 * np.abs(ref).max(), diff.max()
+    else:
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
+
+
 @pytest.mark.parametrize("name", BF16_CASES)
 def test_compress_layer_keep_set_matches_reference(name):
     from core_b200 import engine, ops
