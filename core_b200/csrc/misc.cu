@@ -470,7 +470,7 @@ extern "C" size_t core_memory_readout_workspace_bytes(const core_dims_t* d, int3
   if (d == nullptr || q_len <= 0) return 0;
   Sizer z;
   z.take<float>((size_t)d->batch * q_len * d_mem);
-  z.take<float>((size_t)d->batch * q_len * gate_hidden);
+  z.take<float>((size_t)d->batch * q_len * (gate_hidden > 0 ? gate_hidden : 1));
   z.take<float>((size_t)d->batch * q_len * d->n_kv_heads * kD);
   return z.used;
 }

@@ -83,3 +83,13 @@ def test_ops_refuse_cpu_tensors():
     k = torch.zeros(1, 2, 16, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         ops.qk_features(q, k)
+
+
+def test_readout_workspace_covers_a_call_without_gate():
+    """The readout carves at least one gate float even when gate_hidden is 0
+    (a fixed gate); the size query must count it too (pure host arithmetic)."""
+    lib = _lib.load()
+    dims = _lib.CoreDims(1, 32, 8, 128, 1, 1, _lib.CORE_DTYPE_BF16)
+    f = lib.core_memory_readout_workspace_bytes
+    assert f(ctypes.byref(dims), 1, 512, 0) == f(ctypes.byref(dims), 1, 512, 1)
+    assert f(ctypes.byref(dims), 1, 512, 64) >= 4 * (512 + 64 + 8 * 128)

@@ -387,11 +387,12 @@ def test_memory_readout_matches_reference():
         assert (diff > 0).mean() < 0.02 and diff.max() <= 2 ** -7 * np.abs(ref).max(), diff.max()
 
 
-# (Hkv, Hq, d_mem, gate_hidden, hidden, q_len): the register kernels with 8 and
-# 16 float4 a lane, ragged row slices and partial warps, and (Hq not a multiple
-# of 4, d_mem above 1024, Hkv*d above 2048) the general kernels
-READOUT_SHAPES = [(8, 32, 512, 64, 4096, 1), (16, 64, 700, 48, 96, 3), (1, 4, 20, 8, 40, 5),
-                  (18, 18, 1100, 16, 64, 2)]
+# (Hkv, Hq, d_mem, gate_hidden, hidden, q_len): one decode query at the
+# benchmark's sizes and at sizes where most blocks hold no rows, the register
+# kernels with 8 and 16 float4 a lane, ragged row slices and partial warps, and
+# (Hq not a multiple of 4, d_mem above 1024, Hkv*d above 2048) the general kernels
+READOUT_SHAPES = [(8, 32, 512, 64, 4096, 1), (1, 4, 20, 8, 40, 1), (16, 64, 700, 48, 96, 3),
+                  (1, 4, 20, 8, 40, 5), (18, 18, 1100, 16, 64, 2)]
 
 
 @pytest.mark.parametrize("shape", READOUT_SHAPES, ids=lambda s: "x".join(map(str, s)))
@@ -530,3 +531,43 @@ def test_repeated_calls_are_bitwise_deterministic():
     for o in outs[1:]:
         assert torch.equal(o["features"], outs[0]["features"])
         assert torch.equal(o["keep"], outs[0]["keep"])
+
+
+def test_memory_readout_sees_writes_of_the_kernels_just_before_it():
+    """The state and weights written by the kernels right before the call are
+    the ones read: the result equals a readout on the same values made after a
+    full synchronisation, bit for bit."""
+    from core_b200 import ops
+    dev = _dev()
+    hkv, hq, d_mem, gh, hidden = 8, 32, 512, 64, 4096
+    g = torch.Generator(device=dev).manual_seed(5)
+    q = (torch.randn(1, hq, 1, 128, device=dev, generator=g)).to(torch.bfloat16)
+    theta = torch.randn(d_mem, hq * 128, device=dev, generator=g) / 64
+    gate = (torch.randn(gh, hq * 128, device=dev, generator=g) / 64,
+            torch.randn(gh, device=dev, generator=g) * 0.1,
+            torch.randn(gh, device=dev, generator=g) * 0.1, torch.full((1,), 0.2, device=dev))
+    M = torch.randn(1, d_mem, hkv * 128, device=dev, generator=g)
+    b = torch.rand(1, d_mem, device=dev, generator=g) + 0.5
+    ofold = torch.randn(hidden, hkv * 128, device=dev, generator=g) / 32
+    attn = torch.randn(1, 1, hidden, device=dev, generator=g).to(torch.bfloat16)
+
+    def scaled():
+        return theta * 1.5, M * 2.0, b * 3.0, ofold * 0.5, attn * 2
+
+    th2, M2, b2, of2, at2 = scaled()
+    torch.cuda.synchronize()
+    want = ops.memory_readout(q, th2, gate, M2, b2, of2, at2.clone(), n_kv_heads=hkv)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        th, Mx, bx, of, at = theta.clone(), M.clone(), b.clone(), ofold.clone(), attn.clone()
+        torch.cuda.synchronize()
+        # each in-place scale is a kernel of the same stream, the last right before the call
+        th.mul_(1.5)
+        Mx.mul_(2.0)
+        bx.mul_(3.0)
+        at.mul_(2)
+        of.mul_(0.5)
+        got = ops.memory_readout(q, th, gate, Mx, bx, of, at, n_kv_heads=hkv)
+        ops.status()
+        assert torch.equal(got, want)
+
