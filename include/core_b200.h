@@ -195,6 +195,8 @@ int core_compact_kv(const core_dims_t* dims, const void* k, const void* v,
  *   attn_out : (B, q_len, hidden) of dims.dtype, updated in place (bf16:
  *              the residual and the o_proj product are rounded to bf16)
  * gate_override < 0 uses the learned gate, otherwise the constant gate.
+ * Any alignment is accepted; 16-byte aligned theta, gate_w1, M and o_fold
+ * (and q aligned to 8 bytes for bf16, 16 for f32) take the faster kernels.
  * ------------------------------------------------------------------------- */
 size_t core_memory_readout_workspace_bytes(const core_dims_t* dims, int32_t q_len,
                                            int32_t d_mem, int32_t gate_hidden);
