@@ -308,12 +308,20 @@ __global__ void __cluster_dims__(1, kMemCluster, 1) __launch_bounds__(kMemCWarps
   }
   cluster.sync();
   if (rank == 0 && warp == 0) {
+    // all remote reads first, then the sums in rank order
+    float4 u[kMemCluster];
+    float dv[kMemCluster];
+#pragma unroll
+    for (int k = 0; k < kMemCluster; ++k) {
+      u[k] = *cluster.map_shared_rank(&s_cta[lane], k);
+      dv[k] = *cluster.map_shared_rank(&s_den, k);
+    }
     float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
     float dd = 0.f;
+#pragma unroll
     for (int k = 0; k < kMemCluster; ++k) {
-      const float4 u = *cluster.map_shared_rank(&s_cta[lane], k);
-      m.x += u.x; m.y += u.y; m.z += u.z; m.w += u.w;
-      dd += *cluster.map_shared_rank(&s_den, k);
+      m.x += u[k].x; m.y += u[k].y; m.z += u[k].z; m.w += u[k].w;
+      dd += dv[k];
     }
     const float sc = 1.0f / sqrtf(dd + 1e-8f), g = s_g;
     float4 o;
