@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libcore_b200.so"
 CORE_OK = 0
 CORE_DTYPE_BF16 = 1
 CORE_DTYPE_F32 = 2
+CORE_DTYPE_F16 = 3
 
 CORE_ERR_INVALID_ARG = -1
 CORE_ERR_UNSUPPORTED = -2
@@ -115,6 +116,8 @@ SIGNATURES = {
                                                      _I, _P, _P, _P, _P]),
     "core_memory_write_gathered": (ctypes.c_int, [_D, _P, _P, _P, _P, _I, _P, _I, _F, _F, _F, _P,
                                                   _P, _P, _P, _S, _P]),
+    "core_rope_queries": (ctypes.c_int, [_I, _I, _I, _I, _I, _P, ctypes.c_int64, _P, _P, _F, _P,
+                                         _P, _I, _P, _P]),
     "core_compress_layer_workspace_bytes": (_S, [_D, _I, _I]),
     "core_compress_layer": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P,
                                            ctypes.POINTER(CoreLayerWeights),

@@ -3,6 +3,8 @@
 // core/kvpress_adapter.py:1302-1352).
 #include <cmath>
 #include <cstdint>
+#include <type_traits>
+#include <cuda_fp16.h>
 
 #include <cooperative_groups.h>
 
@@ -36,11 +38,28 @@ __global__ void compact_kernel(const uint4* __restrict__ k, const uint4* __restr
 }
 
 __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
 __device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float f16_round(float x) { return __half2float(__float2half_rn(x)); }
+// out += residual product, in the attention output's dtype: the product is
+// rounded to that dtype first, then the sum (reference: .to(dtype) then +)
 __device__ __forceinline__ __nv_bfloat16 add_out(__nv_bfloat16 a, float r) {
   return __float2bfloat16_rn(__bfloat162float(a) + bf16_round(r));
 }
+__device__ __forceinline__ __half add_out(__half a, float r) {
+  return __float2half_rn(__half2float(a) + f16_round(r));
+}
 __device__ __forceinline__ float add_out(float a, float r) { return a + r; }
+
+// Rounding of the gated residual to the attention output's dtype before the
+// o_proj product (kvpress_adapter.py:1320: residual.to(output[0].dtype)).
+enum RoundMode { kRoundNone = 0, kRoundBf16 = 1, kRoundF16 = 2 };
+__device__ __forceinline__ float round_to(float x, int mode) {
+  return mode == kRoundBf16 ? bf16_round(x) : mode == kRoundF16 ? f16_round(x) : x;
+}
+// A gate_override that is NaN selects the learned gate; any other value is
+// the fixed gate, as MemoryModule.readout's torch.full_like(denom, override).
+__device__ __forceinline__ bool learned_gate(float gate_override) { return gate_override != gate_override; }
 
 __device__ __forceinline__ float gelu(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
@@ -119,6 +138,12 @@ __device__ __forceinline__ float4 ldq4(const __nv_bfloat16* p) {
   const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
   return make_float4(__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi));
 }
+__device__ __forceinline__ float4 ldq4(const __half* p) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  const __half2 lo = *reinterpret_cast<const __half2*>(&u.x);
+  const __half2 hi = *reinterpret_cast<const __half2*>(&u.y);
+  return make_float4(__low2float(lo), __high2float(lo), __low2float(hi), __high2float(hi));
+}
 __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
   acc = fmaf(a.x, b.x, acc);
   acc = fmaf(a.y, b.y, acc);
@@ -188,7 +213,7 @@ __global__ void __launch_bounds__(kMemWarps * 32)
                        const float* __restrict__ gw2, const float* __restrict__ gb2,
                        float gate_override, const float* __restrict__ M,
                        const float* __restrict__ bst, int q_len, int d_mem, int gh, int kvw,
-                       bool round_bf16, float* __restrict__ res) {
+                       int round_mode, float* __restrict__ res) {
   extern __shared__ float sp[];  // proj (d_mem) of this (b, t)
   __shared__ float s_den, s_g;
   __shared__ float s_part[kMemWarps][32];
@@ -207,7 +232,7 @@ __global__ void __launch_bounds__(kMemWarps * 32)
     for (int o = 16; o > 0; o >>= 1) gl += __shfl_xor_sync(0xffffffffu, gl, o);
     if (lane == 0) {
       s_den = den + 1e-8f;
-      s_g = gate_override >= 0.f ? gate_override : 1.0f / (1.0f + expf(-(gl + gb2[0])));
+      s_g = learned_gate(gate_override) ? 1.0f / (1.0f + expf(-(gl + gb2[0]))) : gate_override;
     }
   }
   const int c = blockIdx.x * 32 + lane;
@@ -225,9 +250,9 @@ __global__ void __launch_bounds__(kMemWarps * 32)
     float m = 0.f;
 #pragma unroll
     for (int w = 0; w < kMemWarps; ++w) m += s_part[w][lane];
-    m *= 1.0f / sqrtf(s_den);
+    m = __fdiv_rn(m, sqrtf(s_den));
     const float r = s_g * m;
-    res[((long long)b * q_len + t) * kvw + c] = round_bf16 ? bf16_round(r) : r;
+    res[((long long)b * q_len + t) * kvw + c] = round_to(r, round_mode);
   }
 }
 
@@ -246,7 +271,7 @@ __global__ void __cluster_dims__(1, kMemCluster, 1) __launch_bounds__(kMemCWarps
                                const float* __restrict__ gw2, const float* __restrict__ gb2,
                                float gate_override, const float* __restrict__ M,
                                const float* __restrict__ bst, int q_len, int d_mem, int gh,
-                               int kvw, bool round_bf16, float* __restrict__ res) {
+                               int kvw, int round_mode, float* __restrict__ res) {
   __shared__ float4 s_w[kMemCWarps][32];
   __shared__ float s_wden[kMemCWarps];
   __shared__ float4 s_cta[32];  // this CTA's sum over its rows, read by rank 0
@@ -291,7 +316,7 @@ __global__ void __cluster_dims__(1, kMemCluster, 1) __launch_bounds__(kMemCWarps
   s_w[warp][lane] = acc;
   if (lane == 0) s_wden[warp] = den;
   if (rank == 0 && warp == kMemCWarps - 1 && lane == 0)
-    s_g = gate_override >= 0.f ? gate_override : 1.0f / (1.0f + expf(-(gl + gb2[0])));
+    s_g = learned_gate(gate_override) ? 1.0f / (1.0f + expf(-(gl + gb2[0]))) : gate_override;
   __syncthreads();
   if (warp == 0) {
     float4 v = s_w[0][lane];
@@ -323,15 +348,12 @@ __global__ void __cluster_dims__(1, kMemCluster, 1) __launch_bounds__(kMemCWarps
       m.x += u[k].x; m.y += u[k].y; m.z += u[k].z; m.w += u[k].w;
       dd += dv[k];
     }
-    const float sc = 1.0f / sqrtf(dd + 1e-8f), g = s_g;
+    const float sq = sqrtf(dd + 1e-8f), g = s_g;
     float4 o;
-    o.x = g * (m.x * sc);
-    o.y = g * (m.y * sc);
-    o.z = g * (m.z * sc);
-    o.w = g * (m.w * sc);
-    if (round_bf16) {
-      o.x = bf16_round(o.x); o.y = bf16_round(o.y); o.z = bf16_round(o.z); o.w = bf16_round(o.w);
-    }
+    o.x = round_to(g * __fdiv_rn(m.x, sq), round_mode);
+    o.y = round_to(g * __fdiv_rn(m.y, sq), round_mode);
+    o.z = round_to(g * __fdiv_rn(m.z, sq), round_mode);
+    o.w = round_to(g * __fdiv_rn(m.w, sq), round_mode);
     *reinterpret_cast<float4*>(res + (long long)z * kvw + c) = o;
   }
   cluster.sync();  // rank 0 has read every CTA's shared memory
@@ -443,6 +465,13 @@ using namespace core::misc;
 extern "C" int core_compact_kv(const core_dims_t* d, const void* k, const void* v,
                                const int32_t* keep_idx, int32_t n_kept, void* out_k, void* out_v,
                                void* stream) {
+  // the gather moves raw 16-byte pieces: fp16 rows travel like bf16 ones
+  core_dims_t dd;
+  if (d != nullptr) {
+    dd = *d;
+    if (dd.dtype == CORE_DTYPE_F16) dd.dtype = CORE_DTYPE_BF16;
+    d = &dd;
+  }
   int rc = check_dims(d, "core_compact_kv", true);
   if (rc != CORE_OK) return rc;
   if (k == nullptr || v == nullptr || keep_idx == nullptr || out_k == nullptr || out_v == nullptr)
@@ -483,6 +512,97 @@ extern "C" size_t core_memory_readout_workspace_bytes(const core_dims_t* d, int3
   return z.used;
 }
 
+namespace {
+
+// The three readout stages for queries and attention output of type T
+// (bf16, fp16 or f32); proj / gpre / res are the workspace carves.
+template <typename T>
+int readout_launch(const core_dims_t* d, int32_t q_len, const T* q, const float* theta,
+                   const float* gate_w1, const float* gate_b1, const float* gate_w2,
+                   const float* gate_b2, int32_t d_mem, int gh, float gate_override,
+                   const float* M, const float* b_state, const float* o_fold, int32_t hidden,
+                   T* attn_out, float* proj, float* gpre, float* res, cudaStream_t s) {
+  using namespace core::misc;
+  constexpr bool kF32 = std::is_same<T, float>::value;
+  const int round_mode = kF32 ? kRoundNone
+                         : std::is_same<T, __half>::value ? kRoundF16 : kRoundBf16;
+  const int dm = d->n_q_heads * kD, kvw = d->n_kv_heads * kD;
+  cudaError_t e;
+  const int sms = sm_count();
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  // register paths: 16-byte weight rows and 8-byte (16-bit types) or 16-byte (f32) q groups
+  const bool q_al = (reinterpret_cast<uintptr_t>(q) & (kF32 ? 15 : 7)) == 0;
+  const int pv = d->n_q_heads / kProjSplit;
+  const bool proj_reg = d->n_q_heads % kProjSplit == 0 && pv <= 16 && q_al && al16(theta) &&
+                        (gh == 0 || al16(gate_w1));
+  if (proj_reg) {
+    const dim3 grid((d_mem + gh + kProjRowsPerBlock - 1) / kProjRowsPerBlock, d->batch);
+    const int threads = kProjSplit * kProjRowsPerBlock * 32;
+    if (pv <= 8)
+      readout_proj_reg_kernel<T, 8><<<grid, threads, 0, s>>>(q, d->n_q_heads, q_len, theta,
+                                                              gate_w1, gate_b1, d_mem, gh, proj,
+                                                              gpre);
+    else
+      readout_proj_reg_kernel<T, 16><<<grid, threads, 0, s>>>(q, d->n_q_heads, q_len, theta,
+                                                               gate_w1, gate_b1, d_mem, gh, proj,
+                                                               gpre);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_proj launch");
+  } else {
+    const size_t smem = (size_t)q_len * dm * 4;
+    e = cudaFuncSetAttribute(readout_proj_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return cuda_error(e, "readout_proj attribute");
+    const int rows = d_mem + gh;
+    int bx = (rows + kProjWarps / 2 - 1) / (kProjWarps / 2);  // two warps per weight row
+    if (bx > sms) bx = sms;
+    readout_proj_kernel<T><<<dim3(bx, d->batch), kProjWarps * 32, smem, s>>>(
+        q, d->n_q_heads, q_len, theta, gate_w1, gate_b1, d_mem, gh, proj, gpre);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_proj launch");
+  }
+  if (d_mem <= 64 * 16 && al16(M) && (long long)d->batch * q_len <= 65535) {
+    const dim3 grid(kvw / 128, kMemCluster, d->batch * q_len);
+    if (d_mem <= 64 * 8)
+      readout_mem_cluster_kernel<8><<<grid, kMemCWarps * 32, 0, s>>>(
+          proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw,
+          round_mode, res);
+    else
+      readout_mem_cluster_kernel<16><<<grid, kMemCWarps * 32, 0, s>>>(
+          proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw,
+          round_mode, res);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_mem launch");
+  } else {
+    const size_t smem = (size_t)d_mem * 4;
+    readout_mem_kernel<<<dim3((kvw + 31) / 32, d->batch, q_len), kMemWarps * 32, smem, s>>>(
+        proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw,
+        round_mode, res);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_mem launch");
+  }
+  if (kvw <= 128 * 16 && al16(o_fold)) {
+    const int rpw = kvw <= 128 * 8 ? 2 : 1;  // rows per warp
+    const dim3 grid((hidden + kOutWarps * rpw - 1) / (kOutWarps * rpw), d->batch);
+    if (rpw == 2)
+      readout_out_reg_kernel<T, 2, 8><<<grid, kOutWarps * 32, 0, s>>>(res, o_fold, q_len, kvw,
+                                                                      hidden, attn_out);
+    else
+      readout_out_reg_kernel<T, 1, 16><<<grid, kOutWarps * 32, 0, s>>>(res, o_fold, q_len, kvw,
+                                                                       hidden, attn_out);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_out launch");
+  } else {
+    const size_t smem = (size_t)q_len * kvw * 4;
+    e = cudaFuncSetAttribute(readout_out_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return cuda_error(e, "readout_out attribute");
+    int bx = (hidden + 7) / 8;
+    if (bx > sms) bx = sms;
+    readout_out_kernel<T><<<dim3(bx, d->batch), 256, smem, s>>>(res, o_fold, q_len, kvw, hidden,
+                                                                attn_out);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_out launch");
+  }
+  return CORE_OK;
+}
+
+}  // namespace
+
 extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const void* q,
                                    const float* theta, const float* gate_w1, const float* gate_b1,
                                    const float* gate_w2, const float* gate_b2, int32_t d_mem,
@@ -492,15 +612,17 @@ extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const vo
                                    void* stream) {
   if (d == nullptr || d->batch <= 0 || d->n_q_heads <= 0 || d->n_kv_heads <= 0 || d->head_dim != kD)
     return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout: bad dims");
+  const bool learned = gate_override != gate_override;  // NaN: the learned gate
   if (q == nullptr || theta == nullptr || M == nullptr || b_state == nullptr || o_fold == nullptr ||
-      attn_out == nullptr || (gate_override < 0.f && (gate_w1 == nullptr || gate_b1 == nullptr ||
-                                                      gate_w2 == nullptr || gate_b2 == nullptr)))
+      attn_out == nullptr || (learned && (gate_w1 == nullptr || gate_b1 == nullptr ||
+                                          gate_w2 == nullptr || gate_b2 == nullptr)))
     return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout: NULL tensor");
+  if (!learned && !std::isfinite(gate_override))
+    return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout: gate_override must be finite or NaN");
   if (q_len <= 0 || d_mem <= 0 || hidden <= 0 || gate_hidden < 0)
     return set_error(CORE_ERR_INVALID_ARG, "core_memory_readout: bad sizes");
-  if (d->dtype != CORE_DTYPE_BF16 && d->dtype != CORE_DTYPE_F32)
-    return set_error(CORE_ERR_UNSUPPORTED, "core_memory_readout: dtype must be bf16 or f32");
-  const bool f32 = d->dtype == CORE_DTYPE_F32;
+  if (d->dtype != CORE_DTYPE_BF16 && d->dtype != CORE_DTYPE_F32 && d->dtype != CORE_DTYPE_F16)
+    return set_error(CORE_ERR_UNSUPPORTED, "core_memory_readout: dtype must be bf16, f16 or f32");
   const int dm = d->n_q_heads * kD, kvw = d->n_kv_heads * kD;
   if ((size_t)q_len * dm * 4 > 200 * 1024 || (size_t)q_len * kvw * 4 > 200 * 1024)
     return set_error(CORE_ERR_UNSUPPORTED, "core_memory_readout: q_len too large for one call");
@@ -510,107 +632,24 @@ extern "C" int core_memory_readout(const core_dims_t* d, int32_t q_len, const vo
   float* res = cv.take<float>((size_t)d->batch * q_len * kvw);
   if (cv.overflow) return set_error(CORE_ERR_WORKSPACE, "core_memory_readout: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e;
-  const int sms = sm_count();
-  const int gh = gate_override >= 0.f ? 0 : gate_hidden;
-  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  // register paths: 16-byte weight rows and 8-byte (bf16) or 16-byte (f32) q groups
-  const bool q_al = (reinterpret_cast<uintptr_t>(q) & (f32 ? 15 : 7)) == 0;
-  const int pv = d->n_q_heads / kProjSplit;
-  const bool proj_reg = d->n_q_heads % kProjSplit == 0 && pv <= 16 && q_al && al16(theta) &&
-                        (gh == 0 || al16(gate_w1));
-  if (proj_reg) {
-    const dim3 grid((d_mem + gh + kProjRowsPerBlock - 1) / kProjRowsPerBlock, d->batch);
-    const int threads = kProjSplit * kProjRowsPerBlock * 32;
-    if (f32 && pv <= 8)
-      readout_proj_reg_kernel<float, 8><<<grid, threads, 0, s>>>(
-          static_cast<const float*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1, d_mem, gh,
-          proj, gpre);
-    else if (f32)
-      readout_proj_reg_kernel<float, 16><<<grid, threads, 0, s>>>(
-          static_cast<const float*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1, d_mem, gh,
-          proj, gpre);
-    else if (pv <= 8)
-      readout_proj_reg_kernel<__nv_bfloat16, 8><<<grid, threads, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1,
-          d_mem, gh, proj, gpre);
-    else
-      readout_proj_reg_kernel<__nv_bfloat16, 16><<<grid, threads, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1,
-          d_mem, gh, proj, gpre);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_proj launch");
-  } else {
-    const size_t smem = (size_t)q_len * dm * 4;
-    e = f32 ? cudaFuncSetAttribute(readout_proj_kernel<float>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-            : cudaFuncSetAttribute(readout_proj_kernel<__nv_bfloat16>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_error(e, "readout_proj attribute");
-    const int rows = d_mem + gh;
-    int bx = (rows + kProjWarps / 2 - 1) / (kProjWarps / 2);  // two warps per weight row
-    if (bx > sms) bx = sms;
-    const dim3 grid(bx, d->batch);
-    if (f32)
-      readout_proj_kernel<float><<<grid, kProjWarps * 32, smem, s>>>(
-          static_cast<const float*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1, d_mem, gh,
-          proj, gpre);
-    else
-      readout_proj_kernel<__nv_bfloat16><<<grid, kProjWarps * 32, smem, s>>>(
-          static_cast<const __nv_bfloat16*>(q), d->n_q_heads, q_len, theta, gate_w1, gate_b1,
-          d_mem, gh, proj, gpre);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_proj launch");
+  const int gh = learned ? gate_hidden : 0;
+  switch (d->dtype) {
+    case CORE_DTYPE_F32:
+      return readout_launch<float>(d, q_len, static_cast<const float*>(q), theta, gate_w1, gate_b1,
+                                   gate_w2, gate_b2, d_mem, gh, gate_override, M, b_state, o_fold,
+                                   hidden, static_cast<float*>(attn_out), proj, gpre, res, s);
+    case CORE_DTYPE_F16:
+      return readout_launch<__half>(d, q_len, static_cast<const __half*>(q), theta, gate_w1,
+                                    gate_b1, gate_w2, gate_b2, d_mem, gh, gate_override, M,
+                                    b_state, o_fold, hidden, static_cast<__half*>(attn_out), proj,
+                                    gpre, res, s);
+    default:
+      return readout_launch<__nv_bfloat16>(d, q_len, static_cast<const __nv_bfloat16*>(q), theta,
+                                           gate_w1, gate_b1, gate_w2, gate_b2, d_mem, gh,
+                                           gate_override, M, b_state, o_fold, hidden,
+                                           static_cast<__nv_bfloat16*>(attn_out), proj, gpre, res,
+                                           s);
   }
-  if (d_mem <= 64 * 16 && al16(M) && (long long)d->batch * q_len <= 65535) {
-    const dim3 grid(kvw / 128, kMemCluster, d->batch * q_len);
-    if (d_mem <= 64 * 8)
-      readout_mem_cluster_kernel<8><<<grid, kMemCWarps * 32, 0, s>>>(
-          proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, !f32,
-          res);
-    else
-      readout_mem_cluster_kernel<16><<<grid, kMemCWarps * 32, 0, s>>>(
-          proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, !f32,
-          res);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_mem launch");
-  } else {
-    const size_t smem = (size_t)d_mem * 4;
-    readout_mem_kernel<<<dim3((kvw + 31) / 32, d->batch, q_len), kMemWarps * 32, smem, s>>>(
-        proj, gpre, gate_w2, gate_b2, gate_override, M, b_state, q_len, d_mem, gh, kvw, !f32, res);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_mem launch");
-  }
-  if (kvw <= 128 * 16 && al16(o_fold)) {
-    const int rpw = kvw <= 128 * 8 ? 2 : 1;  // rows per warp
-    const dim3 grid((hidden + kOutWarps * rpw - 1) / (kOutWarps * rpw), d->batch);
-    if (f32 && rpw == 2)
-      readout_out_reg_kernel<float, 2, 8><<<grid, kOutWarps * 32, 0, s>>>(
-          res, o_fold, q_len, kvw, hidden, static_cast<float*>(attn_out));
-    else if (f32)
-      readout_out_reg_kernel<float, 1, 16><<<grid, kOutWarps * 32, 0, s>>>(
-          res, o_fold, q_len, kvw, hidden, static_cast<float*>(attn_out));
-    else if (rpw == 2)
-      readout_out_reg_kernel<__nv_bfloat16, 2, 8><<<grid, kOutWarps * 32, 0, s>>>(
-          res, o_fold, q_len, kvw, hidden, static_cast<__nv_bfloat16*>(attn_out));
-    else
-      readout_out_reg_kernel<__nv_bfloat16, 1, 16><<<grid, kOutWarps * 32, 0, s>>>(
-          res, o_fold, q_len, kvw, hidden, static_cast<__nv_bfloat16*>(attn_out));
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_out launch");
-  } else {
-    const size_t smem = (size_t)q_len * kvw * 4;
-    e = f32 ? cudaFuncSetAttribute(readout_out_kernel<float>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
-            : cudaFuncSetAttribute(readout_out_kernel<__nv_bfloat16>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_error(e, "readout_out attribute");
-    int bx = (hidden + 7) / 8;
-    if (bx > sms) bx = sms;
-    if (f32)
-      readout_out_kernel<float><<<dim3(bx, d->batch), 256, smem, s>>>(
-          res, o_fold, q_len, kvw, hidden, static_cast<float*>(attn_out));
-    else
-      readout_out_kernel<__nv_bfloat16><<<dim3(bx, d->batch), 256, smem, s>>>(
-          res, o_fold, q_len, kvw, hidden, static_cast<__nv_bfloat16*>(attn_out));
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "readout_out launch");
-  }
-  return CORE_OK;
 }
 
 // ---------------------------------------------------------------------------

@@ -8,6 +8,7 @@ the current torch stream.  There is no CPU path: inputs must be CUDA tensors.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -40,6 +41,21 @@ def _dtype_code(dtype: torch.dtype) -> int:
     if dtype not in _DTYPES:
         raise TypeError(f"core_b200 takes bfloat16 or float32 caches; got {dtype}")
     return _DTYPES[dtype]
+
+
+_READOUT_DTYPES = {torch.bfloat16: _lib.CORE_DTYPE_BF16, torch.float16: _lib.CORE_DTYPE_F16,
+                   torch.float32: _lib.CORE_DTYPE_F32}
+
+
+def gate_value(gate_override) -> float:
+    """The C-ABI gate argument: NaN selects the learned gate, a finite value
+    is the constant gate (negative values included, as in the reference)."""
+    if gate_override is None:
+        return float("nan")
+    g = float(gate_override)
+    if not math.isfinite(g):
+        raise ValueError(f"memory_gate_override must be finite, got {gate_override!r}")
+    return g
 
 
 def _dims(keys: torch.Tensor, n_q_heads: int, n_queries: int) -> CoreDims:
@@ -224,13 +240,17 @@ def memory_write(k: torch.Tensor, v: torch.Tensor, scores_cal: torch.Tensor,
 
 
 def compact_kv(k: torch.Tensor, v: torch.Tensor, keep: torch.Tensor):
-    """Gather the kept rows: (B, Hkv, n_kept, d) keys and values."""
+    """Gather the kept rows: (B, Hkv, n_kept, d) keys and values (bf16, fp16
+    or f32 caches: the rows are copied bit for bit)."""
     _require_cuda(k, v, keep)
     k = k.contiguous()
     v = v.contiguous()
     B, hkv, L, d = k.shape
     n_kept = keep.shape[1]
-    dims = _dims(k, hkv, 0)
+    if k.dtype == torch.float16:
+        dims = CoreDims(B, hkv, hkv, d, 0, L, _lib.CORE_DTYPE_F16)
+    else:
+        dims = _dims(k, hkv, 0)
     ok = torch.empty(B, hkv, n_kept, d, dtype=k.dtype, device=k.device)
     ov = torch.empty_like(ok)
     check(_lib.load().core_compact_kv(ctypes.byref(dims), _ptr(k), _ptr(v),
@@ -244,14 +264,17 @@ def memory_readout(q: torch.Tensor, theta: torch.Tensor, gate, M: torch.Tensor,
                    *, n_kv_heads: int, gate_override: float | None = None,
                    workspace: torch.Tensor | None = None) -> torch.Tensor:
     """attn_out (B, q_len, hidden) += o_fold(g(q) m(q)); updated in place and returned.
-    attn_out's dtype (bf16 or f32) selects the arithmetic; q is cast to it.
+    attn_out's dtype (bf16, fp16 or f32) selects the arithmetic; q is cast to it.
+    ``gate_override``: None for the learned gate, else any finite constant gate.
 
     gate = (w1 (gh, Hq*d), b1 (gh), w2 (gh), b2 (1)) f32 tensors.  ``workspace``:
     an optional uint8 device buffer of at least ``core_memory_readout_workspace_bytes``
     (allocated here when absent or too small).
     """
     _require_cuda(q, theta, M, b_state, o_fold, attn_out)
-    code = _dtype_code(attn_out.dtype)
+    code = _READOUT_DTYPES.get(attn_out.dtype)
+    if code is None:
+        raise TypeError(f"memory_readout takes bf16, fp16 or f32 outputs; got {attn_out.dtype}")
     q = q.to(attn_out.dtype).contiguous()
     B, Hq, q_len, d = q.shape
     dims = CoreDims(B, Hq, n_kv_heads, d, q_len, max(q_len, 1), code)
@@ -264,12 +287,62 @@ def memory_readout(q: torch.Tensor, theta: torch.Tensor, gate, M: torch.Tensor,
     lib = _lib.load()
     need = lib.core_memory_readout_workspace_bytes(ctypes.byref(dims), q_len, d_mem, gh)
     ws = workspace if workspace is not None and workspace.numel() >= need else _workspace(need, q.device)
-    go = -1.0 if gate_override is None else float(gate_override)
+    go = gate_value(gate_override)
     check(lib.core_memory_readout(
         ctypes.byref(dims), q_len, _ptr(q), _ptr(theta), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2),
         d_mem, gh, go, _ptr(M), _ptr(b_state), _ptr(o_fold), hidden, _ptr(attn_out), _ptr(ws),
         ws.numel(), _stream(q.device)))
     return attn_out
+
+
+_ROPE_DTYPES = _READOUT_DTYPES
+
+
+def rope_queries(q_proj: torch.Tensor, n_q_heads: int, *, positions: torch.Tensor | None = None,
+                 inv_freq: torch.Tensor | None = None, attention_scaling: float = 1.0,
+                 cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Post-RoPE queries (B, Hq, T, d) from q_proj rows (B, T, Hq*d).
+
+    Either ``positions`` (B or 1, T) int64 with the rotary ``inv_freq`` (d/2)
+    and ``attention_scaling`` of a LlamaRotaryEmbedding, or the (cos, sin)
+    position embeddings (B or 1, T, d) a model computed.  Roundings are those
+    of transformers' apply_rotary_pos_emb in q_proj's dtype.
+    """
+    _require_cuda(q_proj, positions, inv_freq, cos, sin)
+    if q_proj.dim() != 3 or q_proj.stride(-1) != 1:
+        raise ValueError("q_proj must be (B, T, Hq*d) with unit inner stride")
+    code = _ROPE_DTYPES.get(q_proj.dtype)
+    if code is None:
+        raise TypeError(f"rope_queries takes bf16, fp16 or f32; got {q_proj.dtype}")
+    B, T, width = q_proj.shape
+    if width % n_q_heads:
+        raise ValueError("q_proj width must be a multiple of n_q_heads")
+    d = width // n_q_heads
+    if q_proj.stride(0) != T * q_proj.stride(1):
+        q_proj = q_proj.contiguous()
+    row_stride = q_proj.stride(1)
+    if out is None:
+        out = torch.empty(B, n_q_heads, T, d, dtype=q_proj.dtype, device=q_proj.device)
+    pos = inv = c = s = None
+    cb = 1
+    if cos is not None:
+        c = cos.to(q_proj.dtype).reshape(-1, T, d).contiguous()
+        s = sin.to(q_proj.dtype).reshape(-1, T, d).contiguous()
+        cb = c.shape[0]
+        if cb not in (1, B) or s.shape != c.shape:
+            raise ValueError("cos/sin must be (1 or B, T, d)")
+    else:
+        if positions is None or inv_freq is None:
+            raise ValueError("rope_queries needs positions and inv_freq, or cos and sin")
+        pos = positions.to(torch.int64).reshape(-1, T).expand(B, T).contiguous()
+        inv = inv_freq.to(torch.float32).contiguous()
+        if inv.numel() != d // 2:
+            raise ValueError("inv_freq must hold head_dim/2 frequencies")
+    check(_lib.load().core_rope_queries(B, T, n_q_heads, d, code, _ptr(q_proj), row_stride,
+                                        _ptr(pos), _ptr(inv), float(attention_scaling), _ptr(c),
+                                        _ptr(s), cb, _ptr(out), _stream(q_proj.device)))
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -1,12 +1,26 @@
 """KVPress-compatible CORE presses running on the B200 CUDA library.
 
-Drop-in counterparts of the reference presses (``core/kvpress_adapter.py``)
-and of the KVPress hook machinery they plug into
-(``kvpress/kvpress/presses/{base,scorer,decoding,prefill_decoding}_press.py``):
-same class names, dataclass fields, methods, factories and hook protocol.
-The compression step itself (features, scores, Top-B, memory write, gather)
-and the memory readout run in the CUDA library; the classes here keep the
-per-sequence host state (cache metadata, memory state, decode buffers).
+The classes keep the reference's public surface -- class names, dataclass
+fields, methods, factories, the ``"core_full"`` registry key and the forward
+hook contract ``compress(module, hidden_states, keys, values, attentions,
+kwargs) -> (keys, values)`` (kvpress/kvpress/presses/base_press.py:55-93) --
+so that an evaluator which builds the reference press can build this one
+instead (core/kvpress_adapter.py:56-1832 and the kvpress base presses it
+extends).
+
+What runs where:
+  * the compression step of one layer (features, indexer scores, Top-B with
+    sinks, memory write, retained-KV gather) is one call into the CUDA
+    library (``engine.compress_layer``);
+  * the memory readout of a decode step is one library call
+    (``ops.memory_readout``);
+  * decode-time queries are rebuilt from a device window of buffered hidden
+    states by the q_proj GEMM plus the library's RoPE kernel
+    (``queries.post_rope_queries``);
+  * the original-position journal of the compacted cache stays on the device
+    (``journal.CacheMetadata``).
+The host side is a small state machine per press: which phase a forward is
+in, when a decode interval is complete, which per-layer state to update.
 
 Not thread-safe: one sequence per press instance, as in the reference.
 """
@@ -14,7 +28,6 @@ Not thread-safe: one sequence per press instance, as in the reference.
 from __future__ import annotations
 
 import logging
-from collections import defaultdict
 from contextlib import contextmanager
 from dataclasses import dataclass, field
 from typing import Optional
@@ -24,150 +37,191 @@ from torch import nn
 
 from . import engine, ops
 from .checkpoint import FeatureGeometry, IndexerStack, MemoryStack, load_checkpoint
+from .journal import CacheMetadata
+from .queries import HiddenStateWindow, decode_positions, post_rope_queries
 
 logger = logging.getLogger(__name__)
 
-
-# ===========================================================================
-# Cache metadata: original positions / token ids of the compacted slots
-# (core/cache_metadata.py:6-54)
-# ===========================================================================
-class CacheMetadata:
-    def __init__(self):
-        self.reset()
-
-    def reset(self):
-        self.token_ids = None
-        self.positions = {}
-        self.next_position = {}
-
-    def record(self, input_ids, position_ids=None):
-        if input_ids is None:
-            raise ValueError("CORE token metadata requires input_ids")
-        if position_ids is None:
-            start = 0 if self.token_ids is None else self.token_ids.shape[1]
-            position_ids = torch.arange(start, start + input_ids.shape[1], device=input_ids.device)[None]
-        position_ids = position_ids.expand(input_ids.shape[0], -1).long()
-        size = int(position_ids.max()) + 1
-        previous = self.token_ids
-        if previous is not None:
-            if previous.shape[0] != input_ids.shape[0]:
-                raise ValueError("Batch changed without a sequence reset")
-            size = max(size, previous.shape[1])
-        ids = input_ids.new_full((input_ids.shape[0], size), -1)
-        if previous is not None:
-            ids[:, :previous.shape[1]] = previous.to(ids.device)
-        ids.scatter_(1, position_ids, input_ids)
-        self.token_ids = ids
-
-    def align(self, layer_idx, batch_size, cache_length, device):
-        previous = self.positions.get(layer_idx)
-        old_length = 0 if previous is None else previous.shape[1]
-        if cache_length < old_length:
-            raise RuntimeError("KV metadata was not pruned with the cache; reset at new sample boundaries")
-        start = self.next_position.get(layer_idx, 0)
-        added = cache_length - old_length
-        tail = torch.arange(start, start + added, device=device)[None].expand(batch_size, -1)
-        positions = tail if previous is None else torch.cat((previous.to(device), tail), dim=1)
-        self.positions[layer_idx] = positions
-        self.next_position[layer_idx] = start + added
-        ids = positions.new_full(positions.shape, -1)
-        if self.token_ids is not None:
-            journal = self.token_ids.to(device)
-            if positions.numel() and int(positions.max()) >= journal.shape[1]:
-                raise RuntimeError("Missing input token IDs for newly appended KV entries")
-            ids = journal.gather(1, positions)
-        return positions, ids, self.next_position[layer_idx]
-
-    def retain(self, layer_idx, indices):
-        self.positions[layer_idx] = self.positions[layer_idx].gather(1, indices.long()).contiguous()
+__all__ = ["BasePress", "ScorerPress", "DecodingPress", "PrefillDecodingPress", "CacheMetadata",
+           "COREScorerPress", "COREMemoryPress", "COREIndexerPress", "COREDecodingPress",
+           "COREPrefillDecodingPress", "retained_budget", "load_core_scorer_press",
+           "load_core_indexer_press", "load_core_memory_press",
+           "load_core_prefill_decoding_press", "PRESS_REGISTRY"]
 
 
-def retained_budget(length, ratio, sinks=4):
-    """Decode target size (core/paper_protocol.py:17-20)."""
-    if not 0 <= ratio < 1 or length < 1:
-        raise ValueError("Expected a nonempty sequence and 0 <= eviction ratio < 1")
+def retained_budget(length: int, ratio: float, sinks: int = 4) -> int:
+    """Tokens a sequence of ``length`` keeps at eviction ratio ``ratio``, never
+    fewer than the sinks (core/paper_protocol.py:17-20)."""
+    if length < 1 or not 0.0 <= ratio < 1.0:
+        raise ValueError("retained_budget needs length >= 1 and 0 <= ratio < 1")
     return max(min(sinks, length), int(length * (1 - ratio)))
 
 
+def ratio_for_kept_count(length: int, target: int) -> float:
+    """An eviction ratio r with int(length * (1 - r)) == target (0 when nothing
+    has to go).  The decoding press hands r to its base press, which keeps
+    int(length * (1 - r)) tokens (kvpress decoding_press.py:203-245 searches
+    for the same r by bisection).  The plain quotient is tried first; when
+    floating point puts it one token short, the middle of the interval of
+    valid ratios is exact."""
+    if length <= target:
+        return 0.0
+    r = 1.0 - target / length
+    if int(length * (1 - r)) == target:
+        return r
+    r = 1.0 - (target + 0.5) / length
+    if int(length * (1 - r)) != target:
+        logger.warning("no eviction ratio keeps exactly %d of %d tokens", target, length)
+    return r
+
+
 # ===========================================================================
-# KVPress hook machinery (kvpress/kvpress/presses/*.py)
+# Hook plumbing
 # ===========================================================================
-def _extract_keys_and_values(cache, layer_idx):
+def _is_quantized(cache) -> bool:
+    try:
+        from transformers.cache_utils import QuantizedCache
+    except ImportError:  # pragma: no cover
+        return False
+    return isinstance(cache, QuantizedCache)
+
+
+def read_cache_layer(cache, layer_idx: int):
+    """(keys, values) of one cache layer, dequantized for a quantized cache
+    (kvpress utils.py:98-114: the quantized part only)."""
     layer = cache.layers[layer_idx]
-    if hasattr(layer, "_quantized_keys") and getattr(layer, "keys", None) is not None \
-            and layer.keys.numel() == 0:
-        raise NotImplementedError("quantized KV caches are not supported by core_b200")
+    if _is_quantized(cache):
+        return layer._dequantize(layer._quantized_keys), layer._dequantize(layer._quantized_values)
     return layer.keys, layer.values
 
 
-def _write_back(cache, layer_idx, keys, values):
+def write_cache_layer(cache, layer_idx: int, keys: torch.Tensor, values: torch.Tensor) -> None:
+    """Store compressed keys/values back into the cache layer; a quantized
+    cache re-quantizes them and empties its full-precision residual
+    (kvpress base_press.py:146-155)."""
     layer = cache.layers[layer_idx]
-    layer.keys = keys
-    layer.values = values
+    if _is_quantized(cache):
+        layer._quantized_keys = layer._quantize(keys, axis=layer.axis_key)
+        layer._quantized_values = layer._quantize(values, axis=layer.axis_value)
+        layer.keys = keys.new_zeros(0)
+        layer.values = values.new_zeros(0)
+        layer.cumulative_length = keys.shape[2]
+    else:
+        layer.keys = keys
+        layer.values = values
+
+
+class _LastCachePosition:
+    """The last entry of a forward's ``cache_position``.  Every layer of a
+    model forward gets the same tensor, so its value is read from the device
+    once per forward (and again only if the tensor is modified in place)."""
+
+    def __init__(self):
+        self._tensor = None
+        self._version = -1
+        self._value = 0
+
+    def __call__(self, cache_position) -> int:
+        if cache_position is not self._tensor or cache_position._version != self._version:
+            self._value = int(cache_position[-1])
+            self._tensor = cache_position
+            self._version = cache_position._version
+        return self._value
+
+
+_LAST_POSITION = _LastCachePosition()
+
+
+def _phase_is_prefill(kwargs, q_len: int) -> bool:
+    """A forward is a prefill when its last cache position lies within its own
+    length (kvpress base_press.py:135-138)."""
+    return _LAST_POSITION(kwargs["cache_position"]) <= q_len
+
+
+_TEMPORARIES = ("_core_cached_query_states", "_core_cached_key_states", "_core_cached_softmax_lse")
+
+
+def _drop_temporaries(module, args, output):
+    """Forget the per-forward tensors the CORE attention adapter attached to
+    the module (kvpress base_press.py:198-204)."""
+    for name in _TEMPORARIES:
+        if hasattr(module, name):
+            delattr(module, name)
+
+
+def _language_model(model):
+    return model.model.language_model if hasattr(model.model, "language_model") else model.model
 
 
 @dataclass
 class BasePress:
-    """Hook-based press: compress the cache after each attention layer's prefill
-    forward (``base_press.py:95-156``)."""
+    """A press compresses a layer's cache from a forward hook on its attention
+    module.  This base runs ``compress`` once per layer at prefill and leaves
+    decode forwards alone (kvpress base_press.py:95-156)."""
 
     def post_init_from_model(self, model):
         pass
 
     def compress(self, module, hidden_states, keys, values, attentions, kwargs):
-        raise NotImplementedError("compress method must be implemented in subclass")
+        raise NotImplementedError(f"{type(self).__name__} must implement compress()")
+
+    def _compress_cache_layer(self, module, hidden_states, kwargs, attentions) -> None:
+        cache = kwargs["past_key_values"]
+        keys, values = read_cache_layer(cache, module.layer_idx)
+        keys, values = self.compress(module, hidden_states, keys, values, attentions, kwargs)
+        write_cache_layer(cache, module.layer_idx, keys, values)
 
     def forward_hook(self, module: nn.Module, input, kwargs: dict, output):
-        hidden_states = kwargs["hidden_states"]
-        cache = kwargs["past_key_values"]
-        q_len = hidden_states.shape[1]
-        if kwargs["cache_position"][-1] > q_len:
-            return output
-        keys, values = _extract_keys_and_values(cache, module.layer_idx)
-        keys, values = self.compress(module, hidden_states, keys, values, output[1], kwargs)
-        _write_back(cache, module.layer_idx, keys, values)
+        if _phase_is_prefill(kwargs, kwargs["hidden_states"].shape[1]):
+            self._compress_cache_layer(module, kwargs["hidden_states"], kwargs, output[1])
         return output
 
     @contextmanager
     def __call__(self, model):
+        """Hook every attention layer of ``model`` for the duration of the block."""
         self.post_init_from_model(model)
-        hooks = []
+        handles = []
         try:
-            lm = model.model.language_model if hasattr(model.model, "language_model") else model.model
+            lm = _language_model(model)
             for layer in lm.layers:
-                layer.self_attn.rotary_emb = lm.rotary_emb
-                hooks.append(layer.self_attn.register_forward_hook(self.forward_hook, with_kwargs=True))
-
-                def release_core_temporaries(module, args, output):
-                    for name in ("_core_cached_query_states", "_core_cached_key_states",
-                                 "_core_cached_softmax_lse"):
-                        if hasattr(module, name):
-                            delattr(module, name)
-                hooks.append(layer.self_attn.register_forward_hook(release_core_temporaries,
-                                                                   always_call=True))
+                attn = layer.self_attn
+                attn.rotary_emb = lm.rotary_emb
+                handles.append(attn.register_forward_hook(self.forward_hook, with_kwargs=True))
+                handles.append(attn.register_forward_hook(_drop_temporaries, always_call=True))
             yield
         finally:
-            for h in hooks:
+            for h in handles:
                 h.remove()
 
 
 @dataclass
 class ScorerPress(BasePress):
-    """Score-based press (``scorer_press.py:16-106``)."""
+    """A press that scores tokens and keeps the best (kvpress scorer_press.py)."""
 
     compression_ratio: float = 0.0
 
     def __post_init__(self):
-        assert 0 <= self.compression_ratio < 1, "Compression ratio must be between 0 and 1"
+        if not 0 <= self.compression_ratio < 1:
+            raise ValueError("compression_ratio must lie in [0, 1)")
 
     def score(self, module, hidden_states, keys, values, attentions, kwargs):
-        raise NotImplementedError
+        raise NotImplementedError(f"{type(self).__name__} must implement score()")
 
 
 @dataclass
 class DecodingPress(BasePress):
-    """Periodic decode-time compression with a hidden-state buffer (``decoding_press.py:22-248``)."""
+    """Recompress a layer's cache every ``compression_interval`` decode
+    forwards, scoring with the hidden states buffered since the last
+    compression (kvpress decoding_press.py:22-248).
+
+    Per layer the press keeps a step counter and a ``HiddenStateWindow`` of
+    the last ``hidden_states_buffer_size`` forwards.  A decode forward first
+    applies the base press's memory readout (when it has one), then buffers
+    its hidden states; when the interval is complete (or the forward alone
+    reaches ``target_size`` tokens) the cache is compressed to
+    ``target_size`` tokens with every buffered query, and the window is
+    emptied.
+    """
 
     base_press: BasePress = None  # type: ignore[assignment]
     compression_interval: int = 512
@@ -175,56 +229,78 @@ class DecodingPress(BasePress):
     hidden_states_buffer_size: int = 256
 
     def __post_init__(self):
-        assert hasattr(self.base_press, "compress") and hasattr(self.base_press, "compression_ratio"), \
-            "DecodingPress requires a compressible press with compression_ratio"
-        self.hidden_states_buffer = defaultdict(list)
-        self.layer_step_counts = defaultdict(int)
-        assert self.compression_interval > 0, "compression_interval must be greater than 0"
-        assert self.target_size > 0, "target_size must be greater than 0"
+        if not (hasattr(self.base_press, "compress") and hasattr(self.base_press, "compression_ratio")):
+            raise ValueError("DecodingPress needs a base press with compress() and compression_ratio")
+        self._check_sizes()
+        self.reset()
+
+    def _check_sizes(self):
+        if self.compression_interval <= 0:
+            raise ValueError("compression_interval must be positive")
+        if self.target_size <= 0:
+            raise ValueError("target_size must be positive")
+
+    def reset(self):
+        """Drop the buffered hidden states and step counts of every layer."""
+        self._windows: dict = {}
+        self._steps: dict = {}
+
+    # the reference's per-layer bookkeeping, readable for inspection
+    @property
+    def layer_step_counts(self) -> dict:
+        return dict(self._steps)
+
+    @property
+    def hidden_states_buffer(self) -> dict:
+        return {k: w.view() for k, w in self._windows.items() if w.n_entries}
+
+    def _window(self, layer_idx: int) -> HiddenStateWindow:
+        w = self._windows.get(layer_idx)
+        if w is None:
+            w = self._windows[layer_idx] = HiddenStateWindow(self.hidden_states_buffer_size)
+        return w
 
     def post_init_from_model(self, model):
         self.base_press.post_init_from_model(model)
 
+    def _resolve_target_size(self, kwargs) -> int:
+        return self.target_size
+
+    def _find_target_compression_ratio(self, q_len: int, target_tokens: int) -> float:
+        return ratio_for_kept_count(q_len, target_tokens)
+
     def compress(self, module, hidden_states, keys, values, attentions, kwargs):
-        k_len = keys.shape[2]
-        target_size = self._resolve_target_size(kwargs)
-        ratio = self._find_target_compression_ratio(k_len, target_size)
-        original = self.base_press.compression_ratio
+        """Compress to ``target_size`` tokens through the base press, at the
+        ratio that keeps exactly that many."""
+        ratio = ratio_for_kept_count(keys.shape[2], self._resolve_target_size(kwargs))
+        saved = self.base_press.compression_ratio
         self.base_press.compression_ratio = ratio
         try:
             return self.base_press.compress(module, hidden_states, keys, values, attentions, kwargs)
         finally:
-            self.base_press.compression_ratio = original
+            self.base_press.compression_ratio = saved
 
-    def forward_hook(self, module, input, kwargs, output):
-        hidden_states = kwargs["hidden_states"]
-        cache = kwargs["past_key_values"]
-        q_len = hidden_states.shape[1]
-        layer_idx = module.layer_idx
-        if kwargs["cache_position"][-1] <= q_len:
+    def forward_hook(self, module: nn.Module, input, kwargs: dict, output):
+        hs = kwargs["hidden_states"]
+        if _phase_is_prefill(kwargs, hs.shape[1]):
             return output
-        # Read memory written by previous compressions before this step writes.
-        if hasattr(self.base_press, "apply_memory_readout"):
-            output = self.base_press.apply_memory_readout(module, kwargs, output)
-        self.hidden_states_buffer[layer_idx].append(hidden_states.detach().clone())
-        self.layer_step_counts[layer_idx] += 1
-        target_size = self._resolve_target_size(kwargs)
-        if self.layer_step_counts[layer_idx] >= self.compression_interval or q_len >= target_size:
-            keys, values = _extract_keys_and_values(cache, module.layer_idx)
-            attentions = output[1] if len(output) > 1 and output[1] is not None else None
-            buffered = torch.cat(self.hidden_states_buffer[layer_idx], dim=1)
-            keys, values = self.compress(module, buffered, keys, values, attentions, kwargs)
-            _write_back(cache, module.layer_idx, keys, values)
-            self.layer_step_counts[layer_idx] = 0
-            self.hidden_states_buffer[layer_idx] = []
-        self.hidden_states_buffer[layer_idx] = (
-            self.hidden_states_buffer[layer_idx][-self.hidden_states_buffer_size:]
-            if self.hidden_states_buffer_size > 0 else [])
+        # memory written by earlier compressions is read before this step writes
+        readout = getattr(self.base_press, "apply_memory_readout", None)
+        if readout is not None:
+            output = readout(module, kwargs, output)
+        layer = module.layer_idx
+        window = self._window(layer)
+        window.append(hs)
+        self._steps[layer] = self._steps.get(layer, 0) + 1
+        due = (self._steps[layer] >= self.compression_interval
+               or hs.shape[1] >= self._resolve_target_size(kwargs))
+        if due:
+            attn = output[1] if len(output) > 1 else None
+            self._compress_cache_layer(module, window.view(), kwargs, attn)
+            self._steps[layer] = 0
+            window.clear()  # the cache no longer matches the buffered queries
+        window.trim()
         return output
-
-    def reset(self):
-        self.hidden_states_buffer = defaultdict(list)
-        self.layer_step_counts = defaultdict(int)
 
     @contextmanager
     def __call__(self, model):
@@ -234,76 +310,53 @@ class DecodingPress(BasePress):
         finally:
             self.reset()
 
-    def _find_target_compression_ratio(self, q_len: int, target_tokens: int) -> float:
-        """Ratio r with int(q_len * (1 - r)) == target (``decoding_press.py:203-245``)."""
-        if q_len <= target_tokens:
-            return 0.0
-        ratio = 1.0 - (target_tokens / q_len)
-        low, high = 0.0, 1.0
-        for _ in range(20):
-            n_kept = int(q_len * (1 - ratio))
-            if n_kept == target_tokens:
-                break
-            if n_kept > target_tokens:
-                low = ratio
-                ratio = (ratio + high) / 2
-            else:
-                high = ratio
-                ratio = (low + ratio) / 2
-        if int(q_len * (1 - ratio)) != target_tokens:
-            logger.warning("Binary search failed: q_len=%d, target=%d", q_len, target_tokens)
-        return ratio
-
-    def _resolve_target_size(self, kwargs) -> int:
-        return self.target_size
-
 
 @dataclass
 class PrefillDecodingPress(BasePress):
-    """Prefill press + decoding press behind one hook (``prefill_decoding_press.py:19-113``)."""
+    """One press for both phases: prefill forwards go to ``prefilling_press``,
+    decode forwards to ``decoding_press`` (kvpress prefill_decoding_press.py)."""
 
     prefilling_press: Optional[BasePress] = None
     decoding_press: Optional[DecodingPress] = None
     query_aware_prefill: bool = False
 
+    def _target(self, kwargs, q_len: int):
+        if self.prefilling_press is not None and _phase_is_prefill(kwargs, q_len):
+            return self.prefilling_press
+        return self.decoding_press
+
     def post_init_from_model(self, model):
-        if self.prefilling_press is not None:
-            self.prefilling_press.post_init_from_model(model)
-        if self.decoding_press is not None:
-            self.decoding_press.post_init_from_model(model)
+        for p in (self.prefilling_press, self.decoding_press):
+            if p is not None:
+                p.post_init_from_model(model)
 
     def set_token_ids(self, token_ids, special_token_ids=None):
-        if self.prefilling_press is not None and hasattr(self.prefilling_press, "set_token_ids"):
-            self.prefilling_press.set_token_ids(token_ids, special_token_ids)
+        fn = getattr(self.prefilling_press, "set_token_ids", None)
+        if fn is not None:
+            fn(token_ids, special_token_ids)
 
     def set_query_boundary(self, query_start: int):
-        if self.prefilling_press is not None and hasattr(self.prefilling_press, "set_query_boundary"):
-            self.prefilling_press.set_query_boundary(query_start)
+        fn = getattr(self.prefilling_press, "set_query_boundary", None)
+        if fn is not None:
+            fn(query_start)
 
     def reset_cache(self):
-        seen = set()
-        for press in (self.prefilling_press, getattr(self.decoding_press, "base_press", None)):
-            if press is not None and id(press) not in seen and hasattr(press, "reset_cache"):
-                press.reset_cache()
-                seen.add(id(press))
+        inner = [self.prefilling_press, getattr(self.decoding_press, "base_press", None)]
+        for p in {id(p): p for p in inner if p is not None}.values():
+            if hasattr(p, "reset_cache"):
+                p.reset_cache()
         if self.decoding_press is not None:
             self.decoding_press.reset()
 
     def compress(self, module, hidden_states, keys, values, attentions, kwargs):
-        q_len = hidden_states.shape[1]
-        if kwargs["cache_position"][-1] <= q_len and self.prefilling_press is not None:
-            return self.prefilling_press.compress(module, hidden_states, keys, values, attentions, kwargs)
-        if self.decoding_press is not None:
-            return self.decoding_press.compress(module, hidden_states, keys, values, attentions, kwargs)
-        return keys, values
+        target = self._target(kwargs, hidden_states.shape[1])
+        if target is None:
+            return keys, values
+        return target.compress(module, hidden_states, keys, values, attentions, kwargs)
 
     def forward_hook(self, module, input, kwargs, output):
-        q_len = kwargs["hidden_states"].shape[1]
-        if kwargs["cache_position"][-1] <= q_len and self.prefilling_press is not None:
-            return self.prefilling_press.forward_hook(module, input, kwargs, output)
-        if self.decoding_press is not None:
-            return self.decoding_press.forward_hook(module, input, kwargs, output)
-        return output
+        target = self._target(kwargs, kwargs["hidden_states"].shape[1])
+        return output if target is None else target.forward_hook(module, input, kwargs, output)
 
     @contextmanager
     def __call__(self, model):
@@ -316,46 +369,41 @@ class PrefillDecodingPress(BasePress):
 
 
 # ===========================================================================
-# Post-RoPE query reconstruction (core/collector.py:135-201)
+# CORE presses
 # ===========================================================================
-def recompute_post_rope_queries(attn_module, hidden_states, position_ids, position_embeddings=None):
-    """q = RoPE(q_proj(h)) for the given absolute positions; (B, Hq, q_len, d) or None."""
-    from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
-
-    bsz, q_len, _ = hidden_states.shape
-    if not hasattr(attn_module, "q_proj"):
-        return None
-    cfg = attn_module.config
-    num_heads = getattr(attn_module, "num_heads", cfg.num_attention_heads)
-    head_dim = getattr(attn_module, "head_dim", cfg.hidden_size // cfg.num_attention_heads)
-    q = attn_module.q_proj(hidden_states).view(bsz, q_len, num_heads, head_dim)
-    if hasattr(attn_module, "q_norm"):
-        q = attn_module.q_norm(q)
-    q = q.transpose(1, 2)
-    if position_embeddings is not None:
-        cos, sin = position_embeddings
-        q, _ = apply_rotary_pos_emb(q, q, cos, sin)
-    else:
-        rotary_emb = getattr(attn_module, "rotary_emb", None)
-        if rotary_emb is None:
-            return None
-        if position_ids is None:
-            position_ids = torch.arange(q_len, device=q.device, dtype=torch.long)[None].expand(bsz, -1)
-        try:
-            cos, sin = rotary_emb(q, position_ids)
-            q, _ = apply_rotary_pos_emb(q, q, cos, sin)
-        except (TypeError, ValueError):
-            return None
-    return q.detach()
+def _score_dtype(fe) -> torch.dtype:
+    """Arithmetic of the features: the feature extractor's configured dtype
+    (the reference casts Q, K and V to it before scoring,
+    core/kvpress_adapter.py:334,420-470)."""
+    name = str(getattr(getattr(fe, "config", None), "dtype", "bfloat16")).replace("torch.", "")
+    if name in ("float32", "float"):
+        return torch.float32
+    if name in ("bfloat16",):
+        return torch.bfloat16
+    raise NotImplementedError(f"core_b200 scores in bfloat16 or float32, not {name}")
 
 
-# ===========================================================================
-# CORE presses (core/kvpress_adapter.py)
-# ===========================================================================
+@dataclass
+class _SelectionMemo:
+    """Scores of the last scoring layer, reused by the layers that do not
+    score (stride mode) and by the memory write; forgotten when the cache
+    length changes (core/kvpress_adapter.py:735-797)."""
+
+    seq_len: int = 0
+    selection: Optional[torch.Tensor] = None   # (B, L), sinks saturated
+    calibrated: Optional[torch.Tensor] = None  # (B, L), as the indexer produced them
+    kept: Optional[torch.Tensor] = None        # (B, n_kept) top-k of selection (diagnostics)
+
+    def follow(self, seq_len: int) -> None:
+        if seq_len != self.seq_len:
+            self.selection = self.calibrated = self.kept = None
+            self.seq_len = seq_len
+
+
 @dataclass
 class COREScorerPress(ScorerPress):
-    """CORE scorer (``kvpress_adapter.py:130-811``): 14-D token features and the
-    per-layer indexer MLP, computed by the CUDA library."""
+    """CORE scorer (core/kvpress_adapter.py:130-811): 14-D token features and
+    the per-layer indexer MLP, computed by the CUDA library."""
 
     indexer: object = None
     feature_extractor: Optional[FeatureGeometry] = None
@@ -387,31 +435,55 @@ class COREScorerPress(ScorerPress):
         super().__post_init__()
         if self.feature_extractor is None:
             raise ValueError("feature_extractor must be provided")
-        self._cached_kept_indices = None
-        self._cached_scores = None
-        self._cached_memory_scores = None
+        self._memo = _SelectionMemo()
         self._latest_query_feature = None
-        self._cached_original_seq_len = 0
         self.cache_metadata = CacheMetadata()
         self.diagnostic_keep_indices: dict = {}
         self.diagnostic_scores: dict = {}
         self.diagnostic_features: dict = {}
         self._weights: dict = {}
 
-    # ---- configuration / per-sequence state ----
+    # the reference's names for the memo's fields
+    @property
+    def _cached_scores(self):
+        return self._memo.selection
+
+    @_cached_scores.setter
+    def _cached_scores(self, v):
+        self._memo.selection = v
+
+    @property
+    def _cached_memory_scores(self):
+        return self._memo.calibrated
+
+    @_cached_memory_scores.setter
+    def _cached_memory_scores(self, v):
+        self._memo.calibrated = v
+
+    @property
+    def _cached_kept_indices(self):
+        return self._memo.kept
+
+    @property
+    def _cached_original_seq_len(self):
+        return self._memo.seq_len
+
+    # ---- configuration and per-sequence state ----
     def post_init_from_model(self, model):
-        device = next(model.parameters()).device
-        self._ensure_device(device)
-        lm = model.model.language_model if hasattr(model.model, "language_model") else model.model
-        n_model = len(lm.layers)
-        expected = int(getattr(self.indexer, "n_layers", n_model))
-        if self.use_indexer_stack and expected != n_model:
-            raise ValueError(f"CORE checkpoint/model layer mismatch: checkpoint has {expected} "
-                             f"indexer layers, model has {n_model}.")
+        self._ensure_device(next(model.parameters()).device)
+        n_model = len(_language_model(model).layers)
+        n_ckpt = int(getattr(self.indexer, "n_layers", n_model))
+        if self.use_indexer_stack and n_ckpt != n_model:
+            raise ValueError(f"CORE checkpoint/model layer mismatch: the checkpoint has {n_ckpt} "
+                             f"indexer layers, the model {n_model}")
+        want = getattr(getattr(self.feature_extractor, "config", None), "hidden_size", None)
+        have = getattr(getattr(model, "config", None), "hidden_size", None)
+        if want is not None and have is not None and int(want) != int(have):
+            raise ValueError(f"CORE checkpoint/model hidden-size mismatch: {want} vs {have}")
         if self.scoring_layer_idx is None:
-            self.scoring_layer_idx = -1 if self.scoring_stride <= 1 else 0
+            self.scoring_layer_idx = 0 if self.scoring_stride > 1 else -1
         if self.scoring_stride > 1 and self.scoring_layer_idx >= 0:
-            self.scoring_layer_idx = self.scoring_layer_idx // self.scoring_stride * self.scoring_stride
+            self.scoring_layer_idx -= self.scoring_layer_idx % self.scoring_stride
 
     def _ensure_device(self, device):
         device = torch.device(device)
@@ -420,11 +492,9 @@ class COREScorerPress(ScorerPress):
         fe = self.feature_extractor
         if isinstance(fe, FeatureGeometry) and fe.weight.device != device:
             fe.to(device)
-        if isinstance(self.indexer, IndexerStack):
-            first = self.indexer.modules[0][0]
-            if first.device != device:
-                self.indexer.to(device)
-                self._weights.clear()
+        if isinstance(self.indexer, IndexerStack) and self.indexer.modules[0][0].device != device:
+            self.indexer.to(device)
+            self._weights.clear()
 
     def set_token_ids(self, token_ids, special_token_ids=None):
         self._token_ids = token_ids.detach()
@@ -442,29 +512,22 @@ class COREScorerPress(ScorerPress):
         self.cache_metadata.retain(layer_idx, indices)
 
     def reset_cache(self):
-        self._cached_kept_indices = None
-        self._cached_scores = None
-        self._cached_memory_scores = None
+        self._memo = _SelectionMemo()
         self._latest_query_feature = None
-        self._cached_original_seq_len = 0
         self._token_ids = None
-        self.cache_metadata.reset()
         self._query_start = None
-        self.diagnostic_keep_indices.clear()
-        self.diagnostic_scores.clear()
-        self.diagnostic_features.clear()
+        self.cache_metadata.reset()
+        for d in (self.diagnostic_keep_indices, self.diagnostic_scores, self.diagnostic_features):
+            d.clear()
 
-    # ---- weights in kernel formats, prepared once per layer ----
+    # ---- weights in the kernels' formats, prepared once per layer ----
     def layer_weights(self, layer_idx: int, device) -> engine.LayerWeights:
         key = (int(layer_idx), str(device))
         lw = self._weights.get(key)
         if lw is None:
             fe = self.feature_extractor
             cfg = fe.config
-            if self.use_indexer_stack:
-                mlp = self.indexer.params(layer_idx)
-            else:
-                mlp = self.indexer.params(0)
+            mlp = self.indexer.params(layer_idx if self.use_indexer_stack else 0)
             lw = engine.LayerWeights.prepare(
                 geometry=fe.weight[int(layer_idx)], prototypes=fe.prototypes_for(layer_idx),
                 hadamard=fe.hadamard, mlp_params=mlp, n_kv_heads=int(cfg.n_kv_heads),
@@ -473,6 +536,8 @@ class COREScorerPress(ScorerPress):
         return lw
 
     def _check_policy(self):
+        """Only the tokenwise policy the paper protocol requires is built
+        (kvpress/evaluation/evaluate.py:743-754)."""
         if (int(self.span_block_size) > 1 or self.query_feature_weight != 0.0
                 or self.lexical_overlap_weight != 0.0 or self.protect_query_tokens):
             raise NotImplementedError(
@@ -484,168 +549,188 @@ class COREScorerPress(ScorerPress):
         if not getattr(cfg, "center_prototype_features", True):
             raise NotImplementedError("center_prototype_features=False is not supported")
 
-    # ---- queries of the scoring window ----
+    # ---- the scoring queries ----
+    def _prefill_queries(self, module, hidden_states, kwargs):
+        """Post-RoPE queries of a prefill and the matching row LSE if the
+        attention adapter exported one (core/kvpress_adapter.py:357-439)."""
+        q = getattr(module, "_core_cached_query_states", None)
+        if q is None:
+            q = post_rope_queries(module, hidden_states, kwargs.get("position_ids"),
+                                  kwargs.get("position_embeddings"))
+        if q is None or q.shape[-2] == 0:
+            raise RuntimeError("CORE failed to compute prefill QK relation features: no "
+                               "post-RoPE queries (set _core_cached_query_states or q_proj)")
+        if q.ndim == 3:
+            q = q[None]
+        first = 0
+        if self.prefill_qk_scope == "question":
+            if self._query_start is None:
+                raise RuntimeError("CORE prefill_qk_scope='question' requires "
+                                   "set_query_boundary() before prefill.")
+            first = int(self._query_start)
+            if not 0 <= first < q.shape[2]:
+                raise RuntimeError(f"Invalid CORE query boundary: query_start={first}, "
+                                   f"seq_len={q.shape[2]}")
+            q = q[:, :, first:]
+        elif self.prefill_qk_scope != "all":
+            raise ValueError(f"prefill_qk_scope must be 'all' or 'question', got "
+                             f"{self.prefill_qk_scope!r}")
+        lse = getattr(module, "_core_cached_softmax_lse", None)
+        if lse is not None:
+            lse = lse[:, :, first:] if lse.ndim == 3 else None
+            if lse is not None and lse.shape[-1] != q.shape[2]:
+                lse = None
+        return q, lse
+
+    def _decode_queries(self, module, hidden_states, kwargs):
+        """Queries of every buffered decode token: the adapter's own if they
+        cover the buffer, else rebuilt at their absolute positions
+        (core/kvpress_adapter.py:469-519)."""
+        q = getattr(module, "_core_cached_query_states", None)
+        t = hidden_states.shape[1]
+        if q is None or q.shape[-2] != t:
+            pos = emb = None
+            if t > 1:
+                pos = decode_positions(kwargs, t, hidden_states.device)
+            if pos is None:
+                pos, emb = kwargs.get("position_ids"), kwargs.get("position_embeddings")
+            q = post_rope_queries(module, hidden_states, pos, emb)
+        if q is None or q.shape[-2] == 0:
+            raise RuntimeError("CORE failed to reconstruct decode QK features; refusing to "
+                               "replace the paper features with zeros")
+        return (q[None] if q.ndim == 3 else q), None
+
     def _scoring_queries(self, module, hidden_states, keys, is_prefill, kwargs):
-        """Post-RoPE queries (B, Hq, nq, d) as ``_compute_scores_from_features``
-        selects them (kvpress_adapter.py:357-519), plus an optional row LSE."""
-        B, _, L, _ = keys.shape
-        lse = None
-        if is_prefill:
-            q = getattr(module, "_core_cached_query_states", None)
-            if q is None:
-                q = recompute_post_rope_queries(module, hidden_states, kwargs.get("position_ids"),
-                                                kwargs.get("position_embeddings"))
-            if q is None or q.shape[-2] == 0:
-                raise RuntimeError("CORE failed to compute prefill QK relation features: no "
-                                   "post-RoPE queries (set _core_cached_query_states or q_proj)")
-            if q.ndim == 3:
-                q = q[None]
-            query_start = 0
-            if self.prefill_qk_scope == "question":
-                if self._query_start is None:
-                    raise RuntimeError("CORE prefill_qk_scope='question' requires set_query_boundary() "
-                                       "before prefill.")
-                query_start = int(self._query_start)
-                if not 0 <= query_start < q.shape[2]:
-                    raise RuntimeError(f"Invalid CORE query boundary: query_start={query_start}, "
-                                       f"seq_len={q.shape[2]}")
-                q = q[:, :, query_start:]
-            elif self.prefill_qk_scope != "all":
-                raise ValueError(f"prefill_qk_scope must be 'all' or 'question', got {self.prefill_qk_scope!r}")
-            sl = getattr(module, "_core_cached_softmax_lse", None)
-            if sl is not None and sl.ndim == 3:
-                sl = sl[:, :, query_start:]
-                if sl.shape[-1] == q.shape[2]:
-                    lse = sl
-        else:
-            hs = hidden_states
-            pos_ids = kwargs.get("position_ids")
-            pos_emb = kwargs.get("position_embeddings")
-            if hs.shape[1] > 1 and kwargs.get("cache_position") is not None:
-                cur = kwargs.get("position_ids")
-                end = int(cur[0, -1].item()) if cur is not None else int(kwargs["cache_position"][-1].item())
-                pos_ids = torch.arange(end - hs.shape[1] + 1, end + 1, device=hs.device,
-                                       dtype=torch.long)[None]
-                pos_emb = None
-            q = getattr(module, "_core_cached_query_states", None)
-            if q is None or q.shape[-2] != hs.shape[1]:
-                q = recompute_post_rope_queries(module, hs, pos_ids, pos_emb)
-            if q is None or q.shape[-2] == 0:
-                raise RuntimeError("CORE failed to reconstruct decode QK features; refusing to "
-                                   "replace the paper features with zeros")
-            if q.ndim == 3:
-                q = q[None]
-        if q.shape[0] != B:
-            q = q.expand(B, -1, -1, -1)
-        return q.to(engine.cache_dtype(keys.dtype)).contiguous(), lse
+        """(B, Hq, nq, d) post-RoPE queries in the scoring dtype, plus an
+        optional exported row LSE."""
+        pick = self._prefill_queries if is_prefill else self._decode_queries
+        q, lse = pick(module, hidden_states, kwargs)
+        if q.shape[0] != keys.shape[0]:
+            q = q.expand(keys.shape[0], -1, -1, -1)
+        return q.to(_score_dtype(self.feature_extractor)).contiguous(), lse
 
     def _special_mask(self, ids):
-        fe = self.feature_extractor
-        sp = tuple(getattr(fe.config, "special_token_ids", ()) or ())
-        if not sp or ids is None:
+        special = tuple(getattr(self.feature_extractor.config, "special_token_ids", ()) or ())
+        if not special or ids is None:
             return None
-        t = torch.tensor(sp, device=ids.device, dtype=ids.dtype)
-        return torch.isin(ids, t)
+        return torch.isin(ids, torch.tensor(special, device=ids.device, dtype=ids.dtype))
 
     def _scores_and_features(self, module, hidden_states, keys, values, kwargs, layer_idx):
-        """Calibrated scores (B, L) and features (B, L, 14) on the CUDA path."""
+        """Calibrated scores (B, L) and features (B, L, 14) through the
+        library's feature and indexer entry points."""
         self._check_policy()
-        B, hkv, L, d = keys.shape
+        B, _, L, _ = keys.shape
         is_prefill = hidden_states.shape[1] >= L
-        positions, ids, original_length = self.cache_metadata.align(layer_idx, B, L, keys.device)
+        positions, ids, extent = self.cache_metadata.align(layer_idx, B, L, keys.device)
         q, lse = self._scoring_queries(module, hidden_states, keys, is_prefill, kwargs)
         cfg = self.feature_extractor.config
         lw = self.layer_weights(layer_idx, keys.device)
-        dt = engine.cache_dtype(keys.dtype)
-        k = keys.to(dt).contiguous()
-        v = values.to(dt).contiguous()
+        sdt = _score_dtype(self.feature_extractor)
+        k = keys.to(sdt).contiguous()
+        v = values.to(sdt).contiguous()
         feats = torch.empty(B, L, 14, dtype=torch.float32, device=keys.device)
         ops.qk_features(q, k, topk_qk=int(cfg.topk_qk), n_recent_queries=int(cfg.n_recent_queries),
                         lse=lse, features=feats)
         ops.coverage_features(k, lw.geometry_ext, lw.prototypes,
                               shrinkage_rho=float(cfg.shrinkage_rho), features=feats, col0=6)
-        scores = ops.indexer_scores(v, positions, feats, lw.mlp, original_length=int(original_length),
+        scores = ops.indexer_scores(v, positions, feats, lw.mlp, original_length=int(extent),
                                     is_prefill=is_prefill, n_sink=int(cfg.n_sink),
                                     special=self._special_mask(ids))
+        self._note_features(layer_idx, feats)
+        return scores, feats
+
+    def _note_features(self, layer_idx, feats):
         self._latest_query_feature = feats[:, :, 3]
         if self.capture_diagnostics:
             self.diagnostic_features[int(layer_idx)] = feats[0].detach().float().cpu()
-        return scores, feats
 
     def _compute_scores_from_features(self, module, hidden_states, keys, values, attentions,
                                       is_prefill, kwargs=None, layer_idx=0):
-        """(B, Hkv, L) calibrated scores broadcast over KV heads (kvpress_adapter.py:312-558)."""
+        """(B, Hkv, L) calibrated scores, the same for every KV head
+        (core/kvpress_adapter.py:312-558)."""
         scores, _ = self._scores_and_features(module, hidden_states, keys, values, kwargs or {},
                                               layer_idx)
         return scores[:, None, :].expand(-1, keys.shape[1], -1).contiguous()
 
-    def _is_scoring_layer(self, layer_idx):
-        if self.scoring_stride > 1 and (self.scoring_layer_idx or 0) >= 0:
-            return layer_idx is None or layer_idx % self.scoring_stride == \
-                (self.scoring_layer_idx or 0) % self.scoring_stride
-        return self.scoring_layer_idx in (-1, None) or layer_idx == self.scoring_layer_idx \
-            or layer_idx is None
+    # ---- the selection policy around the indexer scores ----
+    def _is_scoring_layer(self, layer_idx) -> bool:
+        if layer_idx is None:
+            return True
+        every = self.scoring_layer_idx if self.scoring_layer_idx is not None else -1
+        if self.scoring_stride > 1 and every >= 0:
+            return layer_idx % self.scoring_stride == every % self.scoring_stride
+        return every == -1 or layer_idx == every
+
+    def _budget(self, seq_len: int) -> int:
+        return max(min(self.n_sink_protect, seq_len), int(seq_len * (1 - self.compression_ratio)))
 
     def _recency(self, scores: torch.Tensor) -> torch.Tensor:
-        seq_len = scores.shape[-1]
-        if self.recency_alpha > 0.0 and seq_len > 1:
-            pos = torch.arange(seq_len, device=scores.device, dtype=scores.dtype)
-            bonus = self.recency_alpha * torch.exp(-(seq_len - 1 - pos) / max(1, self.recency_window))
-            scores = scores + bonus.view(*([1] * (scores.ndim - 1)), -1)
-        return scores
+        """Add alpha * exp(-(age) / window) when the recency bonus is on."""
+        n = scores.shape[-1]
+        if self.recency_alpha <= 0.0 or n <= 1:
+            return scores
+        age = (n - 1) - torch.arange(n, device=scores.device, dtype=scores.dtype)
+        bonus = self.recency_alpha * torch.exp(-age / max(1, self.recency_window))
+        return scores + bonus
+
+    def _protect_sinks(self, scores: torch.Tensor, seq_len: int) -> torch.Tensor:
+        """Selection copy with the first n_sink_protect tokens lifted above
+        every other score; the calibrated scores stay as they are."""
+        s = self.n_sink_protect
+        if not 0 < s < seq_len:
+            return scores
+        lifted = scores.clone()
+        lifted[..., :s] = scores.max().detach() + 1.0
+        return lifted
+
+    def _remember(self, selection, calibrated, budget, layer_idx):
+        self._memo.selection = selection.detach().clone()
+        self._memo.calibrated = calibrated.detach().clone()
+        if self.capture_diagnostics:
+            dl = int(layer_idx if layer_idx is not None else -1)
+            self._memo.kept = selection.topk(budget, dim=-1).indices
+            self.diagnostic_scores[dl] = calibrated.detach().float().cpu()
+            self.diagnostic_keep_indices[dl] = self._memo.kept.detach().cpu()
 
     @torch.no_grad()
     def score(self, module, hidden_states, keys, values, attentions, kwargs):
-        """Selection scores (B, Hkv, L) with sinks saturated (kvpress_adapter.py:690-797)."""
+        """Selection scores (B, Hkv, L), sinks saturated (core/kvpress_adapter.py:690-797)."""
         self._ensure_device(hidden_states.device)
-        batch_size, num_kv_heads, seq_len, _ = keys.shape
-        is_prefill = hidden_states.shape[1] >= seq_len
-        layer_idx = getattr(module, "layer_idx", None)
-        if seq_len != self._cached_original_seq_len:
-            self._cached_kept_indices = None
-            self._cached_scores = None
-            self._cached_memory_scores = None
-            self._cached_original_seq_len = seq_len
-        if not self._is_scoring_layer(layer_idx) and self._cached_scores is not None:
-            return self._cached_scores.to(device=keys.device, dtype=keys.dtype).unsqueeze(1) \
-                .expand(-1, num_kv_heads, -1).contiguous()
-        scores = self._compute_scores_from_features(module, hidden_states, keys, values, attentions,
-                                                    is_prefill, kwargs,
-                                                    layer_idx=layer_idx if layer_idx is not None else 0)
-        scores = self._recency(scores)
-        calibrated = scores
-        n_kept = max(min(self.n_sink_protect, seq_len), int(seq_len * (1 - self.compression_ratio)))
-        if 0 < self.n_sink_protect < seq_len:
-            scores = scores.clone()
-            scores[:, :, : self.n_sink_protect] = scores.max().detach() + 1.0
-        if 0 < n_kept < seq_len:
-            self._cached_scores = scores[:, 0].detach().clone()
-            self._cached_memory_scores = calibrated[:, 0].detach().clone()
-            if self.capture_diagnostics:
-                dl = int(layer_idx if layer_idx is not None else -1)
-                self.diagnostic_scores[dl] = calibrated[:, 0].detach().float().cpu()
-                self._cached_kept_indices = scores[:, 0].topk(n_kept, dim=-1).indices
-                self.diagnostic_keep_indices[dl] = self._cached_kept_indices.detach().cpu()
-        return scores
+        B, H, L, _ = keys.shape
+        layer = getattr(module, "layer_idx", None)
+        self._memo.follow(L)
+        if not self._is_scoring_layer(layer) and self._memo.selection is not None:
+            reuse = self._memo.selection.to(device=keys.device, dtype=keys.dtype)
+            return reuse[:, None, :].expand(-1, H, -1).contiguous()
+        calibrated = self._recency(self._compute_scores_from_features(
+            module, hidden_states, keys, values, attentions, hidden_states.shape[1] >= L, kwargs,
+            layer_idx=layer if layer is not None else 0))
+        selection = self._protect_sinks(calibrated, L)
+        budget = self._budget(L)
+        if 0 < budget < L:
+            self._remember(selection[:, 0], calibrated[:, 0], budget, layer)
+        return selection
 
     def compress(self, module, hidden_states, keys, values, attentions, kwargs):
-        """Per-token Top-B and gather (kvpress_adapter.py:299-310)."""
+        """Keep the Top-B of the selection scores and gather them (core/kvpress_adapter.py:299-310)."""
         if self.compression_ratio == 0:
             return keys, values
         scores = self.score(module, hidden_states, keys, values, attentions, kwargs)
-        count = max(min(self.n_sink_protect, keys.shape[2]), int(keys.shape[2] * (1 - self.compression_ratio)))
-        if count >= keys.shape[2]:
-            self.cache_metadata.align(int(module.layer_idx), keys.shape[0], keys.shape[2], keys.device)
+        layer = int(module.layer_idx)
+        budget = self._budget(keys.shape[2])
+        self.cache_metadata.align(layer, keys.shape[0], keys.shape[2], keys.device)
+        if budget >= keys.shape[2]:
             return keys, values
-        keep, _ = ops.topb_select(scores[:, 0].float(), count, 0)
-        self.cache_metadata.align(int(module.layer_idx), keys.shape[0], keys.shape[2], keys.device)
-        self.retain_metadata(int(module.layer_idx), keep)
+        keep, _ = ops.topb_select(scores[:, 0].float(), budget, 0)
+        self.retain_metadata(layer, keep)
         return ops.compact_kv(keys.contiguous(), values.contiguous(), keep)
 
 
 @dataclass
 class COREMemoryPress(BasePress):
-    """Eviction with latent-memory writing and gated readout (kvpress_adapter.py:814-1382)."""
+    """Eviction with latent-memory writing and the gated readout
+    (core/kvpress_adapter.py:814-1382).  The memory state of layer l is
+    ``_M[l]`` (B, d_mem, Hkv*d), ``_b[l]`` (B, d_mem), ``_Z[l]`` (B,)."""
 
     base_press: COREScorerPress = None  # type: ignore[assignment]
     memory_module: Optional[MemoryStack] = None
@@ -660,12 +745,12 @@ class COREMemoryPress(BasePress):
     requires_decoding_hook: bool = field(default=True, init=False, repr=False)
 
     def __post_init__(self):
-        assert self.base_press is not None, "base_press (COREScorerPress) is required"
+        if self.base_press is None:
+            raise ValueError("COREMemoryPress needs a COREScorerPress as base_press")
         self._M: dict = {}
         self._b: dict = {}
         self._Z: dict = {}
-        self._folded_theta: dict = {}
-        self._folded_o_proj: dict = {}
+        self._write_theta: dict = {}   # folded memory projection per (module, layout)
         self._readout_weights: dict = {}
 
     @property
@@ -694,21 +779,23 @@ class COREMemoryPress(BasePress):
 
     def _ensure_device(self, device):
         self.base_press._ensure_device(device)
-        if self.memory_module is not None and torch.device(device).type == "cuda":
-            if self.memory_module.modules[0][0].device != torch.device(device):
-                self.memory_module.to(device)
-                self._folded_theta.clear()
-                self._readout_weights.clear()
+        mm = self.memory_module
+        if mm is not None and torch.device(device).type == "cuda" \
+                and mm.modules[0][0].device != torch.device(device):
+            mm.to(device)
+            self._write_theta.clear()
+            self._readout_weights.clear()
 
     def reset_cache(self):
         self.base_press.reset_cache()
-        self._M.clear(); self._b.clear(); self._Z.clear()
+        self.reset_memory()
 
     def reset_memory(self, layer_idx: Optional[int] = None):
-        if layer_idx is None:
-            self._M.clear(); self._b.clear(); self._Z.clear()
-        else:
-            self._M.pop(layer_idx, None); self._b.pop(layer_idx, None); self._Z.pop(layer_idx, None)
+        for state in (self._M, self._b, self._Z):
+            if layer_idx is None:
+                state.clear()
+            else:
+                state.pop(layer_idx, None)
 
     def _check_spaces(self):
         if self.memory_value_space != "pre_o_proj":
@@ -718,234 +805,234 @@ class COREMemoryPress(BasePress):
         if self.memory_uniform_fraction != 0.0:
             raise NotImplementedError("memory_uniform_fraction != 0 is not supported by core_b200")
 
-    def _theta_split(self, layer_idx, num_kv_heads, num_groups, head_dim, device, dtype):
-        """Folded memory-write projection in the form caches of ``dtype`` take:
-        bf16 hi/lo terms, or the f32 fold itself for f32 caches."""
-        f32 = engine.cache_dtype(dtype) == torch.float32
-        key = (self.memory_module.module_index(layer_idx), num_kv_heads, num_groups, str(device),
-               f32)
-        ts = self._folded_theta.get(key)
-        if ts is None:
-            theta = self.memory_module.params(layer_idx)[0].to(device)
-            fold = engine.fold_groups(theta, num_kv_heads, num_groups, head_dim)
-            ts = fold if f32 else ops.split_bf16(fold, 2)
-            self._folded_theta[key] = ts
-        return ts
+    def _theta_for(self, layer_idx, n_kv, groups, head_dim, device, f32: bool):
+        """The group-folded memory projection (core/kvpress_adapter.py:916-940):
+        its f32 fold for the f32 kernels, its two bf16 terms for the tensor-core ones."""
+        key = (self.memory_module.module_index(layer_idx), n_kv, groups, str(device), f32)
+        t = self._write_theta.get(key)
+        if t is None:
+            fold = engine.fold_groups(self.memory_module.params(layer_idx)[0].to(device), n_kv,
+                                      groups, head_dim)
+            t = self._write_theta[key] = fold if f32 else ops.split_bf16(fold, 2)
+        return t
 
-    def _state(self, layer_idx, B, d_mem, kvw, device):
+    def _memory_state(self, layer_idx, B, d_mem, width, device) -> engine.MemoryState:
         M = self._M.get(layer_idx)
-        if M is None or M.shape != (B, d_mem, kvw) or M.device != torch.device(device):
-            self._M[layer_idx] = torch.zeros(B, d_mem, kvw, device=device)
+        if M is None or M.shape != (B, d_mem, width) or M.device != torch.device(device):
+            self._M[layer_idx] = torch.zeros(B, d_mem, width, device=device)
             self._b[layer_idx] = torch.zeros(B, d_mem, device=device)
+        if self._Z.get(layer_idx) is None or self._Z[layer_idx].shape != (B,):
             self._Z[layer_idx] = torch.zeros(B, device=device)
-        Z = self._Z.get(layer_idx)
-        if Z is None or Z.shape != (B,):
-            self._Z[layer_idx] = torch.zeros(B, device=device)
-        return self._M[layer_idx], self._b[layer_idx], self._Z[layer_idx]
+        return engine.MemoryState(self._M[layer_idx], self._b[layer_idx], self._Z[layer_idx])
 
     @torch.no_grad()
     def compress(self, module, hidden_states, keys, values, attentions, kwargs):
-        """Select retained tokens, write the evicted ones to memory, prune K/V
-        (kvpress_adapter.py:968-1210)."""
+        """Select the retained tokens, fold the evicted ones into the layer's
+        memory state, return the retained K/V (core/kvpress_adapter.py:968-1210)."""
         self._ensure_device(hidden_states.device)
         if self.compression_ratio == 0:
             return keys, values
-        bp = self.base_press
-        layer_idx = int(getattr(module, "layer_idx", 0))
-        bsz, num_kv_heads, k_len, head_dim = keys.shape
-        num_groups = bp.feature_extractor.n_q_heads // num_kv_heads
-        if k_len != bp._cached_original_seq_len:
-            bp._cached_scores = None
-            bp._cached_memory_scores = None
-            bp._cached_original_seq_len = k_len
-        n_sink = int(bp.n_sink_protect)
-        n_kept = engine.n_kept_for(k_len, self.compression_ratio, n_sink)
-        if n_kept >= k_len:
-            bp.cache_metadata.align(layer_idx, bsz, k_len, keys.device)
+        sp = self.base_press
+        layer = int(getattr(module, "layer_idx", 0))
+        B, n_kv, L, head_dim = keys.shape
+        sp._memo.follow(L)
+        n_sink = int(sp.n_sink_protect)
+        n_kept = engine.n_kept_for(L, self.compression_ratio, n_sink)
+        if n_kept >= L:
+            sp.cache_metadata.align(layer, B, L, keys.device)
             return keys, values
         write = self.enable_memory_writing and self.memory_module is not None
         if write:
             self._check_spaces()
-        dt = engine.cache_dtype(keys.dtype)
-        k = keys.to(dt).contiguous()
-        v = values.to(dt).contiguous()
-        state = None
-        ts = None
+        sdt = _score_dtype(sp.feature_extractor)
+        # the memory write and the gather see the cache's own values; the
+        # features see them in the scoring dtype
+        mdt = torch.float32 if keys.dtype != torch.bfloat16 else torch.bfloat16
+        fused = keys.dtype == sdt and mdt == sdt
+        state = theta = None
         if write:
-            d_mem = self.memory_module.d_mem
-            M, b, Z = self._state(layer_idx, bsz, d_mem, num_kv_heads * head_dim, keys.device)
-            state = engine.MemoryState(M, b, Z)
-            ts = self._theta_split(layer_idx, num_kv_heads, num_groups, head_dim, keys.device,
-                                   keys.dtype)
-        reuse = (not bp._is_scoring_layer(layer_idx)) and bp._cached_memory_scores is not None
-        if reuse or bp.recency_alpha > 0.0:
-            # scores first (reused across layers, or adjusted by the recency bonus)
-            if reuse:
-                bp.cache_metadata.align(layer_idx, bsz, k_len, keys.device)
-                calibrated = bp._cached_memory_scores
-            else:
-                calibrated = bp._recency(bp._scores_and_features(module, hidden_states, keys,
-                                                                 values, kwargs or {}, layer_idx)[0])
-            keep, evict = ops.topb_select(calibrated, n_kept, n_sink)
+            state = self._memory_state(layer, B, self.memory_module.d_mem, n_kv * head_dim,
+                                       keys.device)
+            theta = self._theta_for(layer, n_kv, sp.feature_extractor.n_q_heads // n_kv,
+                                    head_dim, keys.device, f32=mdt == torch.float32)
+        reuse = (not sp._is_scoring_layer(layer)) and sp._memo.calibrated is not None
+        if reuse or sp.recency_alpha > 0.0 or not fused:
+            calibrated, keep, evict = self._select_outside(module, hidden_states, keys, values,
+                                                           kwargs, layer, n_kept, reuse)
             if write and evict.shape[1] > 0:
-                ops.memory_write(k, v, calibrated, evict, ts, state.M, state.b, state.Z,
+                ops.memory_write(keys.to(mdt).contiguous(), values.to(mdt).contiguous(),
+                                 calibrated, evict, theta, state.M, state.b, state.Z,
                                  gamma=self.memory_decay, eta=self.memory_write_eta,
                                  student_temp=self.student_temp)
-            out_k, out_v = ops.compact_kv(k, v, keep)
+            out_k, out_v = ops.compact_kv(keys.contiguous(), values.contiguous(), keep)
         else:
-            bp._check_policy()
-            is_prefill = hidden_states.shape[1] >= k_len
-            positions, ids, original_length = bp.cache_metadata.align(layer_idx, bsz, k_len,
-                                                                       keys.device)
-            q, lse = bp._scoring_queries(module, hidden_states, keys, is_prefill, kwargs or {})
-            cfg = bp.feature_extractor.config
-            lw = bp.layer_weights(layer_idx, keys.device)
-            if dt == torch.float32:
-                lw.theta_fold = ts
-            else:
-                lw.theta_split = ts
-            out = engine.compress_layer(
-                q, k, v, lw, n_kept=n_kept, positions=positions, original_length=int(original_length),
-                is_prefill=is_prefill, n_sink=n_sink, topk_qk=int(cfg.topk_qk),
-                n_recent_queries=int(cfg.n_recent_queries), shrinkage_rho=float(cfg.shrinkage_rho),
-                memory=state, gamma=self.memory_decay, eta=self.memory_write_eta,
-                student_temp=self.student_temp, special=bp._special_mask(ids), lse=lse)
-            calibrated, keep, out_k, out_v = out["scores"], out["keep"], out["keys"], out["values"]
-            bp._latest_query_feature = out["features"][:, :, 3]
-            if bp.capture_diagnostics:
-                bp.diagnostic_features[layer_idx] = out["features"][0].detach().float().cpu()
-        bp._cached_memory_scores = calibrated
-        sel = calibrated.clone()
-        if 0 < n_sink < k_len:
-            sel[:, :n_sink] = sel.max() + 1.0
-        bp._cached_scores = sel
-        if bp.capture_diagnostics:
-            bp.diagnostic_scores[layer_idx] = calibrated.detach().float().cpu()
-            bp.diagnostic_keep_indices[layer_idx] = keep.detach().long().cpu()
-        bp.retain_metadata(layer_idx, keep)
-        return out_k.to(keys.dtype), out_v.to(values.dtype)
+            calibrated, keep, out_k, out_v = self._select_fused(
+                module, hidden_states, keys, values, kwargs, layer, n_kept, n_sink, state, theta)
+        self._remember_layer(layer, calibrated, keep, L)
+        return out_k, out_v
 
-    def _readout_params(self, module, layer_idx, num_kv_heads, num_groups, head_dim, device):
+    def _select_fused(self, module, hidden_states, keys, values, kwargs, layer, n_kept, n_sink,
+                      state, theta):
+        """The whole layer step in one library call (features, scores, Top-B,
+        memory write, gather) on caches already in the scoring dtype."""
+        sp = self.base_press
+        sp._check_policy()
+        B, _, L, _ = keys.shape
+        is_prefill = hidden_states.shape[1] >= L
+        positions, ids, extent = sp.cache_metadata.align(layer, B, L, keys.device)
+        q, lse = sp._scoring_queries(module, hidden_states, keys, is_prefill, kwargs or {})
+        cfg = sp.feature_extractor.config
+        lw = sp.layer_weights(layer, keys.device)
+        if theta is not None:
+            if keys.dtype == torch.float32:
+                lw.theta_fold = theta
+            else:
+                lw.theta_split = theta
+        out = engine.compress_layer(
+            q, keys, values, lw, n_kept=n_kept, positions=positions, original_length=int(extent),
+            is_prefill=is_prefill, n_sink=n_sink, topk_qk=int(cfg.topk_qk),
+            n_recent_queries=int(cfg.n_recent_queries), shrinkage_rho=float(cfg.shrinkage_rho),
+            memory=state, gamma=self.memory_decay, eta=self.memory_write_eta,
+            student_temp=self.student_temp, special=sp._special_mask(ids), lse=lse)
+        sp._note_features(layer, out["features"])
+        return out["scores"], out["keep"], out["keys"], out["values"]
+
+    def _select_outside(self, module, hidden_states, keys, values, kwargs, layer, n_kept, reuse):
+        """Scores (reused from the scoring layer, or computed in the scoring
+        dtype and adjusted by the recency bonus) and the Top-B split."""
+        sp = self.base_press
+        if reuse:
+            sp.cache_metadata.align(layer, keys.shape[0], keys.shape[2], keys.device)
+            calibrated = sp._memo.calibrated
+        else:
+            calibrated = sp._recency(sp._scores_and_features(module, hidden_states, keys, values,
+                                                             kwargs or {}, layer)[0])
+        keep, evict = ops.topb_select(calibrated, n_kept, int(sp.n_sink_protect))
+        return calibrated, keep, evict
+
+    def _remember_layer(self, layer, calibrated, keep, L):
+        sp = self.base_press
+        sp._memo.seq_len = L
+        sp._memo.calibrated = calibrated
+        sp._memo.selection = sp._protect_sinks(calibrated, L)
+        if sp.capture_diagnostics:
+            sp.diagnostic_scores[layer] = calibrated.detach().float().cpu()
+            sp.diagnostic_keep_indices[layer] = keep.detach().long().cpu()
+        sp.retain_metadata(layer, keep)
+
+    # ---- decode-step readout ----
+    def _readout_params(self, module, layer_idx, n_kv, groups, head_dim, device):
         key = (layer_idx, str(device))
         rp = self._readout_weights.get(key)
         if rp is None:
             th, gw1, gb1, gw2, gb2 = self.memory_module.params(layer_idx)
-            o_fold = engine.fold_groups(module.o_proj.weight.to(device), num_kv_heads, num_groups,
-                                        head_dim)
-            rp = (th.to(device).float().contiguous(),
-                  (gw1.to(device).float().contiguous(), gb1.to(device).float().contiguous(),
-                   gw2.to(device).float().reshape(-1).contiguous(),
-                   gb2.to(device).float().reshape(-1).contiguous()),
-                  o_fold)
+            f32 = lambda t: t.to(device).float().contiguous()  # noqa: E731
+            rp = (f32(th), (f32(gw1), f32(gb1), f32(gw2).reshape(-1), f32(gb2).reshape(-1)),
+                  engine.fold_groups(module.o_proj.weight.to(device), n_kv, groups, head_dim))
             self._readout_weights[key] = rp
         return rp
 
+    def _readout_queries(self, module, kwargs):
+        hidden = kwargs["hidden_states"]
+        q = getattr(module, "_core_cached_query_states", None)
+        if q is not None and q.ndim == 4 and q.shape[0] == hidden.shape[0] \
+                and q.shape[-2] == hidden.shape[1]:
+            return q
+        return post_rope_queries(module, hidden, kwargs.get("position_ids"),
+                                 kwargs.get("position_embeddings"))
+
     @torch.no_grad()
     def apply_memory_readout(self, module, kwargs, output):
-        """attention output += folded o_proj(g(q) m(q)) (kvpress_adapter.py:1212-1352)."""
+        """attention output += folded o_proj(g(q) m(q)) for this layer's memory
+        (core/kvpress_adapter.py:1212-1352)."""
         if not self.enable_memory_writing or self.memory_module is None:
             return output
-        layer_idx = int(getattr(module, "layer_idx", 0))
-        M = self._M.get(layer_idx)
-        b = self._b.get(layer_idx)
-        if M is None or b is None:
+        layer = int(getattr(module, "layer_idx", 0))
+        if self._M.get(layer) is None or self._b.get(layer) is None:
             return output
         self._check_spaces()
-        hidden = kwargs["hidden_states"]
-        batch_size, q_len, _ = hidden.shape
-        q = getattr(module, "_core_cached_query_states", None)
-        if q is None or q.ndim != 4 or q.shape[0] != batch_size or q.shape[-2] != q_len:
-            q = recompute_post_rope_queries(module, hidden, kwargs.get("position_ids"),
-                                            kwargs.get("position_embeddings"))
+        q = self._readout_queries(module, kwargs)
         if q is None:
             raise RuntimeError("CORE memory readout could not reconstruct post-RoPE queries; "
                                "refusing to mix hidden-state queries with post-RoPE memory keys.")
-        n_q_heads = int(module.config.num_attention_heads)
-        n_kv_heads = int(module.config.num_key_value_heads)
-        head_dim = q.shape[-1]
-        theta, gate, o_fold = self._readout_params(module, layer_idx, n_kv_heads,
-                                                   n_q_heads // n_kv_heads, head_dim, hidden.device)
-        attn = output[0].to(engine.cache_dtype(output[0].dtype)).contiguous().clone()
-        ops.memory_readout(q, theta, gate, M, b, o_fold, attn, n_kv_heads=n_kv_heads,
-                           gate_override=self.memory_gate_override)
-        new_attn = attn.to(output[0].dtype)
+        n_q = int(module.config.num_attention_heads)
+        n_kv = int(module.config.num_key_value_heads)
+        theta, gate, o_fold = self._readout_params(module, layer, n_kv, n_q // n_kv, q.shape[-1],
+                                                   q.device)
+        attn = output[0] if isinstance(output, (list, tuple)) else output
+        out = attn.contiguous().clone()
+        ops.memory_readout(q, theta, gate, self._M[layer], self._b[layer], o_fold, out,
+                           n_kv_heads=n_kv, gate_override=self.memory_gate_override)
         if isinstance(output, (list, tuple)):
-            return type(output)([new_attn] + list(output[1:]))
-        return new_attn
+            return type(output)([out, *output[1:]])
+        return out
 
     def forward_hook(self, module, input, kwargs, output):
-        q_len = kwargs["hidden_states"].shape[1]
-        if kwargs["cache_position"][-1] <= q_len:
+        """Prefill: compress (the base hook); decode: add the memory readout."""
+        if _phase_is_prefill(kwargs, kwargs["hidden_states"].shape[1]):
             return super().forward_hook(module, input, kwargs, output)
         return self.apply_memory_readout(module, kwargs, output)
 
 
 @dataclass
 class COREIndexerPress(COREScorerPress):
-    """Backward-compatible press with an optional absolute budget (kvpress_adapter.py:1385-1436)."""
+    """Scorer press with an optional absolute budget (core/kvpress_adapter.py:1385-1436)."""
 
     budget: Optional[int] = None
 
     def compress(self, module, hidden_states, keys, values, attentions, kwargs):
-        if keys.shape[2] <= 1:
+        L = keys.shape[2]
+        if L <= 1:
             return keys, values
         self._ensure_device(hidden_states.device)
-        seq_len = keys.shape[2]
-        if self.budget is not None:
-            n_kept = max(1, min(self.n_sink_protect, seq_len), min(self.budget, seq_len))
-        else:
-            n_kept = max(1, min(self.n_sink_protect, seq_len), int(seq_len * (1 - self.compression_ratio)))
-        if n_kept >= seq_len:
+        want = self.budget if self.budget is not None else int(L * (1 - self.compression_ratio))
+        n_kept = max(1, min(self.n_sink_protect, L), min(want, L))
+        if n_kept >= L:
             return keys, values
-        original = self.compression_ratio
-        self.compression_ratio = 1.0 - (n_kept / seq_len)
+        saved = self.compression_ratio
+        self.compression_ratio = 1.0 - n_kept / L
         try:
             return super().compress(module, hidden_states, keys, values, attentions, kwargs)
         finally:
-            self.compression_ratio = original
+            self.compression_ratio = saved
 
 
 @dataclass
 class COREDecodingPress(DecodingPress):
-    """DecodingPress accepting the memory press (kvpress_adapter.py:92-122)."""
+    """Decoding press over the CORE memory press (core/kvpress_adapter.py:92-122):
+    the buffer defaults to, and may not be shorter than, one compression
+    interval, since every query of the interval scores the recompression."""
 
     hidden_states_buffer_size: Optional[int] = None
 
     def __post_init__(self):
-        assert hasattr(self.base_press, "compress"), "CORE decoding press requires a compress-capable base press"
-        self.hidden_states_buffer = defaultdict(list)
-        self.layer_step_counts = defaultdict(int)
-        assert self.compression_interval > 0
-        assert self.target_size > 0
+        if not hasattr(self.base_press, "compress"):
+            raise ValueError("CORE decoding press requires a compress-capable base press")
+        self._check_sizes()
         if self.hidden_states_buffer_size is None:
             self.hidden_states_buffer_size = self.compression_interval
         if self.hidden_states_buffer_size < self.compression_interval:
             raise ValueError("CORE requires queries from the entire compression interval; "
                              "hidden_states_buffer_size must be >= compression_interval")
+        self.reset()
 
 
 @dataclass
 class COREPrefillDecodingPress(PrefillDecodingPress):
-    """CORE token metadata and prefill/decode budgets (kvpress_adapter.py:56-89)."""
+    """CORE token metadata and matched prefill/decode budgets
+    (core/kvpress_adapter.py:56-89)."""
 
     query_aware_prefill: bool = False
     match_prefill_budget: bool = True
 
     def begin_sequence(self, context_length):
+        """Decode recompressions return the cache to the prefill's budget."""
         if self.match_prefill_budget:
             self.decoding_press.target_size = retained_budget(
                 context_length, self.prefilling_press.compression_ratio)
 
-    def set_token_ids(self, token_ids, special_token_ids=None):
-        if self.prefilling_press is not None and hasattr(self.prefilling_press, "set_token_ids"):
-            self.prefilling_press.set_token_ids(token_ids, special_token_ids)
-
     def record_input_tokens(self, input_ids, position_ids=None):
         self.prefilling_press.record_input_tokens(input_ids, position_ids)
-
-    def set_query_boundary(self, query_start: int):
-        if self.prefilling_press is not None and hasattr(self.prefilling_press, "set_query_boundary"):
-            self.prefilling_press.set_query_boundary(query_start)
 
     def reset_cache(self):
         if self.decoding_press is not None:
@@ -955,41 +1042,44 @@ class COREPrefillDecodingPress(PrefillDecodingPress):
 
 
 # ===========================================================================
-# Factories (kvpress_adapter.py:1444-1832)
+# Factories (core/kvpress_adapter.py:1444-1832)
 # ===========================================================================
-def _check_compression_ratio(requested, cfg, checkpoint_path) -> float:
-    train_cr = float(cfg.compression_ratio)
-    effective = train_cr if requested is None else float(requested)
-    if not 0.0 < effective < 1.0:
-        raise ValueError(f"compression_ratio must lie in (0, 1), received {effective}")
-    return effective
+def _effective_ratio(requested, cfg) -> float:
+    r = float(cfg.compression_ratio) if requested is None else float(requested)
+    if not 0.0 < r < 1.0:
+        raise ValueError(f"compression_ratio must lie in (0, 1), received {r}")
+    return r
 
 
-def _apply_protection_fields(press: COREScorerPress, cfg) -> None:
-    press.n_sink_protect = cfg.get("n_sink_protect", 0)
-    press.recency_alpha = cfg.get("recency_alpha", 0.0)
-    press.recency_window = cfg.get("recency_window", 64)
-    press.scoring_stride = cfg.get("scoring_stride", 1)
-    press.span_block_size = cfg.get("span_block_size", 1)
-    press.span_pool_beta = cfg.get("span_pool_beta", 5.0)
-    press.span_selection_mode = cfg.get("span_selection_mode", "sliding_max")
-    press.coverage_fraction = cfg.get("coverage_fraction", 0.25)
-    press.query_feature_weight = cfg.get("query_feature_weight", 0.0)
-    press.lexical_overlap_weight = cfg.get("lexical_overlap_weight", 0.0)
-    press.identifier_lexical_weight = cfg.get("identifier_lexical_weight", 0.0)
-    press.identifier_min_match_tokens = cfg.get("identifier_min_match_tokens", 20)
-    press.identifier_context_skip = cfg.get("identifier_context_skip", 64)
-    press.identifier_span_size = cfg.get("identifier_span_size", 32)
-    press.protect_query_tokens = cfg.get("protect_query_tokens", False)
-    press.prefill_qk_scope = cfg.get("prefill_qk_scope", "all")
+# checkpoint config key -> (press field, default when absent)
+_POLICY_FIELDS = {
+    "n_sink_protect": 0, "recency_alpha": 0.0, "recency_window": 64, "scoring_stride": 1,
+    "span_block_size": 1, "span_pool_beta": 5.0, "span_selection_mode": "sliding_max",
+    "coverage_fraction": 0.25, "query_feature_weight": 0.0, "lexical_overlap_weight": 0.0,
+    "identifier_lexical_weight": 0.0, "identifier_min_match_tokens": 20,
+    "identifier_context_skip": 64, "identifier_span_size": 32, "protect_query_tokens": False,
+    "prefill_qk_scope": "all",
+}
 
 
-def _load(checkpoint_path, device):
+def _apply_policy(press: COREScorerPress, cfg) -> None:
+    for name, default in _POLICY_FIELDS.items():
+        setattr(press, name, cfg.get(name, default))
+
+
+def _scorer(cls, checkpoint_path, device, compression_ratio, **extra):
     parts = load_checkpoint(checkpoint_path, device=device)
-    return parts["indexer"], parts["config"], parts["geometry"], parts["use_stack"], parts["memory"]
+    cfg = parts["config"]
+    press = cls(indexer=parts["indexer"], feature_extractor=parts["geometry"],
+                compression_ratio=_effective_ratio(compression_ratio, cfg),
+                student_temp=cfg.student_temp, use_indexer_stack=parts["use_stack"],
+                **{k: v(cfg) for k, v in extra.items()})
+    _apply_policy(press, cfg)
+    return press, parts
 
 
-def _required_memory(memory, cfg, checkpoint_path):
+def _memory_of(parts, checkpoint_path):
+    memory, cfg = parts["memory"], parts["config"]
     if memory is None:
         raise ValueError("CORE memory evaluation requires a joint checkpoint containing a compatible "
                          f"memory_state_dict. Checkpoint: {checkpoint_path}")
@@ -1003,27 +1093,7 @@ def _required_memory(memory, cfg, checkpoint_path):
     return memory
 
 
-def load_core_scorer_press(checkpoint_path: str, device: str = "cuda:0",
-                           compression_ratio: float = 0.5) -> COREScorerPress:
-    indexer, cfg, fe, use_stack, _ = _load(checkpoint_path, device)
-    press = COREScorerPress(indexer=indexer, feature_extractor=fe,
-                            compression_ratio=_check_compression_ratio(compression_ratio, cfg, checkpoint_path),
-                            student_temp=cfg.student_temp, use_indexer_stack=use_stack)
-    _apply_protection_fields(press, cfg)
-    return press
-
-
-def load_core_indexer_press(checkpoint_path: str, device: str = "cuda:0",
-                            compression_ratio: Optional[float] = None) -> COREIndexerPress:
-    indexer, cfg, fe, use_stack, _ = _load(checkpoint_path, device)
-    press = COREIndexerPress(indexer=indexer, feature_extractor=fe,
-                             compression_ratio=_check_compression_ratio(compression_ratio, cfg, checkpoint_path),
-                             budget=cfg.budget, student_temp=cfg.student_temp, use_indexer_stack=use_stack)
-    _apply_protection_fields(press, cfg)
-    return press
-
-
-def _memory_press(base, memory, cfg):
+def _with_memory(base, memory, cfg) -> COREMemoryPress:
     return COREMemoryPress(base_press=base, memory_module=memory, memory_decay=cfg.memory_decay,
                            memory_write_eta=cfg.memory_write_eta,
                            memory_uniform_fraction=cfg.memory_uniform_fraction,
@@ -1032,14 +1102,21 @@ def _memory_press(base, memory, cfg):
                            memory_value_space=cfg.memory_value_space)
 
 
+def load_core_scorer_press(checkpoint_path: str, device: str = "cuda:0",
+                           compression_ratio: float = 0.5) -> COREScorerPress:
+    return _scorer(COREScorerPress, checkpoint_path, device, compression_ratio)[0]
+
+
+def load_core_indexer_press(checkpoint_path: str, device: str = "cuda:0",
+                            compression_ratio: Optional[float] = None) -> COREIndexerPress:
+    return _scorer(COREIndexerPress, checkpoint_path, device, compression_ratio,
+                   budget=lambda cfg: cfg.budget)[0]
+
+
 def load_core_memory_press(checkpoint_path: str, device: str = "cuda:0",
                            compression_ratio: Optional[float] = None) -> COREMemoryPress:
-    indexer, cfg, fe, use_stack, memory = _load(checkpoint_path, device)
-    base = COREScorerPress(indexer=indexer, feature_extractor=fe,
-                           compression_ratio=_check_compression_ratio(compression_ratio, cfg, checkpoint_path),
-                           student_temp=cfg.student_temp, use_indexer_stack=use_stack)
-    _apply_protection_fields(base, cfg)
-    return _memory_press(base, _required_memory(memory, cfg, checkpoint_path), cfg)
+    base, parts = _scorer(COREScorerPress, checkpoint_path, device, compression_ratio)
+    return _with_memory(base, _memory_of(parts, checkpoint_path), parts["config"])
 
 
 def load_core_prefill_decoding_press(checkpoint_path: str, device: str = "cuda:0",
@@ -1048,17 +1125,16 @@ def load_core_prefill_decoding_press(checkpoint_path: str, device: str = "cuda:0
                                      decoding_target_size: Optional[int] = None,
                                      decoding_hidden_states_buffer_size: Optional[int] = None
                                      ) -> COREPrefillDecodingPress:
-    indexer, cfg, fe, use_stack, memory = _load(checkpoint_path, device)
-    base = COREScorerPress(indexer=indexer, feature_extractor=fe,
-                           compression_ratio=_check_compression_ratio(compression_ratio, cfg, checkpoint_path),
-                           student_temp=cfg.student_temp, use_indexer_stack=use_stack)
-    _apply_protection_fields(base, cfg)
-    shared = _memory_press(base, _required_memory(memory, cfg, checkpoint_path), cfg)
+    """The ``core_full`` press: one memory press shared by the prefill and the
+    decoding press, decode recompression back to the prefill budget unless a
+    target size is given."""
+    base, parts = _scorer(COREScorerPress, checkpoint_path, device, compression_ratio)
+    shared = _with_memory(base, _memory_of(parts, checkpoint_path), parts["config"])
     decoding = COREDecodingPress(base_press=shared, compression_interval=decoding_compression_interval,
                                  target_size=decoding_target_size or 1,
                                  hidden_states_buffer_size=decoding_hidden_states_buffer_size)
-    return COREPrefillDecodingPress(match_prefill_budget=decoding_target_size is None,
-                                    prefilling_press=shared, decoding_press=decoding,
+    return COREPrefillDecodingPress(prefilling_press=shared, decoding_press=decoding,
+                                    match_prefill_budget=decoding_target_size is None,
                                     query_aware_prefill=False)
 
 

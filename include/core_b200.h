@@ -47,6 +47,7 @@ extern "C" {
 /* ---- dtypes ---- */
 #define CORE_DTYPE_BF16 1
 #define CORE_DTYPE_F32 2
+#define CORE_DTYPE_F16 3 /* core_rope_queries and core_compact_kv only */
 
 typedef struct core_dims {
   int32_t batch;      /* B   */
@@ -187,16 +188,20 @@ int core_compact_kv(const core_dims_t* dims, const void* k, const void* v,
  * Replaces MemoryModule.readout (core/indexer.py:165-207) and the folded
  * o_proj projection of COREMemoryPress.apply_memory_readout
  * (core/kvpress_adapter.py:1302-1352).
- *   q        : (B, Hq, q_len, d) post-RoPE queries (dims.dtype)
+ *   q        : (B, Hq, q_len, d) post-RoPE queries (dims.dtype: CORE_DTYPE_BF16,
+ *              _F16 or _F32)
  *   theta    : (d_mem, Hq*d) f32;  gate_w1 : (gh, Hq*d) f32; gate_b1 : (gh)
  *   gate_w2  : (gh) f32; gate_b2 : scalar f32 (pointer)
  *   M, b     : layer fast state (B, d_mem, Hkv*d), (B, d_mem) f32
  *   o_fold   : (hidden, Hkv*d) f32 group-folded o_proj
- *   attn_out : (B, q_len, hidden) of dims.dtype, updated in place (bf16:
- *              the residual and the o_proj product are rounded to bf16)
- * gate_override < 0 uses the learned gate, otherwise the constant gate.
+ *   attn_out : (B, q_len, hidden) of dims.dtype, updated in place (bf16 and
+ *              fp16: the residual and the o_proj product are rounded to that
+ *              dtype before the sum, as the reference's .to(dtype) casts)
+ * gate_override NaN uses the learned gate; any finite value is the constant
+ * gate (MemoryModule.readout's gate_override, negative values included);
+ * infinities are rejected.
  * Any alignment is accepted; 16-byte aligned theta, gate_w1, M and o_fold
- * (and q aligned to 8 bytes for bf16, 16 for f32) take the faster kernels.
+ * (and q aligned to 8 bytes for 16-bit types, 16 for f32) take the faster kernels.
  * ------------------------------------------------------------------------- */
 size_t core_memory_readout_workspace_bytes(const core_dims_t* dims, int32_t q_len,
                                            int32_t d_mem, int32_t gate_hidden);
@@ -214,7 +219,8 @@ int core_memory_readout(const core_dims_t* dims, int32_t q_len, const void* q, c
  * rounded up to 256 bytes, must fit in 256 KB; larger calls return
  * CORE_ERR_INVALID_ARG.  The first call on a device, with that device current,
  * resolves the scratch address (cudaGetSymbolAddress) and should precede any
- * stream capture.  Nothing in the scratch needs to start at zero.  There is one
+ * stream capture.  The resolved address is kept for the life of the process:
+ * it does not survive cudaDeviceReset or a re-created primary context.  Nothing in the scratch needs to start at zero.  There is one
  * scratch per device: calls that overlap on one device (other streams or host
  * threads) race on it and must be serialised by the caller. */
 int core_memory_readout_noalloc(const core_dims_t* dims, int32_t q_len, const void* q,
@@ -374,6 +380,28 @@ int core_memory_write_gathered(const core_dims_t* dims, const void* k_ev, const 
                                const void* theta_split, int32_t d_mem, float gamma, float eta,
                                float student_temp, float* M, float* b_state, float* Z,
                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Post-RoPE queries of buffered hidden states.
+ * Replaces the rotary part of BackboneStatsCollector._recompute_post_rope_queries
+ * (core/collector.py:163-192): transformers' LlamaRotaryEmbedding.forward and
+ * apply_rotary_pos_emb, fused with the transpose to the QK kernels' layout.
+ * The q_proj GEMM before it is the caller's (a library GEMM).
+ *   q_proj    : (B, T, Hq*head_dim) rows of `dtype` (CORE_DTYPE_BF16, _F16 or
+ *               _F32), row r at q_proj + r * row_stride elements
+ *   positions : (B, T) int64 absolute positions   } used when cos/sin are NULL:
+ *   inv_freq  : (head_dim/2) f32                  } angle = inv_freq[j] * pos,
+ *               c = dtype(cosf(angle) * attention_scaling), likewise s
+ *   cos, sin  : (cos_batch, T, head_dim) of `dtype`, a model's precomputed
+ *               position embeddings (cos_batch 1 or B), or NULL
+ *   q_out     : (B, Hq, T, head_dim) of `dtype`
+ * Every product and sum rounds to `dtype` as the torch ops do.
+ * ------------------------------------------------------------------------- */
+int core_rope_queries(int32_t batch, int32_t n_tokens, int32_t n_q_heads, int32_t head_dim,
+                      int32_t dtype, const void* q_proj, int64_t row_stride,
+                      const int64_t* positions, const float* inv_freq, float attention_scaling,
+                      const void* cos, const void* sin, int32_t cos_batch, void* q_out,
+                      void* stream);
 
 #ifdef __cplusplus
 }

@@ -427,16 +427,27 @@ def memory_write(k, v, scores_cal, evict, theta, *, groups: int, M=None, b=None,
     return M_t, b_t, zt
 
 
+def f16_round(x) -> np.ndarray:
+    """Round float32 to IEEE half (round-to-nearest-even) and back."""
+    return np.asarray(x, np.float32).astype(np.float16).astype(np.float32)
+
+
 def memory_readout(q_full, theta, gate_w1, gate_b1, gate_w2, gate_b2, M, b, o_fold,
                    attn_out, *, eps: float = 1e-8, gate_override=None,
-                   out_bf16: bool = True):
+                   out_bf16: bool = True, out_dtype: str | None = None):
     """``MemoryModule.readout`` (``core/indexer.py:165-207``) and the output
     projection of ``apply_memory_readout`` (``core/kvpress_adapter.py:1302-1352``).
 
     ``q_full`` is (q_len, Hq*d) post-RoPE queries (head-major columns),
     ``o_fold`` the group-folded o_proj (hidden, Hkv*d); ``attn_out`` is
-    (q_len, hidden).  Returns the new attention output.
+    (q_len, hidden).  Returns the new attention output.  ``out_dtype``
+    ("bf16", "f16" or "f32"; default from ``out_bf16``) is the attention
+    output's dtype: the residual and its o_proj product are rounded to it
+    before the sum (``kvpress_adapter.py:1320-1343``).
     """
+    if out_dtype is None:
+        out_dtype = "bf16" if out_bf16 else "f32"
+    rnd = {"bf16": bf16_round, "f16": f16_round, "f32": None}[out_dtype]
     q = _f32(q_full).astype(np.float64)
     proj = (q @ theta.astype(np.float64).T).astype(np.float32).astype(np.float64)
     num = proj @ M.astype(np.float64)
@@ -449,12 +460,11 @@ def memory_readout(q_full, theta, gate_w1, gate_b1, gate_w2, gate_b2, M, b, o_fo
     else:
         g = np.full(q.shape[0], float(gate_override))
     res = (g[:, None] * m).astype(np.float32)
-    if out_bf16:
-        res = bf16_round(res)
+    if rnd is not None:
+        res = rnd(res)
     res = (res.astype(np.float64) @ o_fold.astype(np.float64).T).astype(np.float32)
-    if out_bf16:
-        res = bf16_round(res)
-        return bf16_round(_f32(attn_out) + res)
+    if rnd is not None:
+        return rnd(_f32(attn_out) + rnd(res))
     return (_f32(attn_out) + res).astype(np.float32)
 
 

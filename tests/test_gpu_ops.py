@@ -5,21 +5,19 @@ import numpy as np
 import pytest
 import torch
 
-from helpers import (SINGLE_STEP_CASES, TWO_STEP_CASE, f3_flip_consistent, layer_weights,
-                     load_case, rel_err)
+from helpers import (SINGLE_STEP_CASES, TWO_STEP_CASE, check_qk_features_bounded,
+                     check_scores_explained, flip_bound, layer_weights, load_case, rel_err)
 from oracle import core_oracle as O
 
 pytestmark = pytest.mark.gpu
 
 BF16_CASES = [c for c in SINGLE_STEP_CASES if c.startswith("bf16")]
-# Tolerances (bf16 compute): relative, floored at 1e-3 absolute scale.  Logits
-# are rounded to bf16 after an f32 dot product whose summation order differs
-# between the tensor cores and the oracle, so a rare logit lands one bf16 ulp
-# away; when that flips the sign of a near-zero relation value, f3 (mean of
-# the positive values) moves by about 1/count.  FEATURE_TOL bounds 99.9 % of
-# the keys, FLIP_TOL the rest.
+# Tolerances (bf16 compute): relative, floored at 1e-3 absolute scale, on
+# every key.  Logits are rounded to bf16 after an f32 dot product whose
+# summation order differs between the tensor cores and the oracle, so a rare
+# logit lands one bf16 ulp away; a key outside FEATURE_TOL must be explained
+# by such flips (helpers.check_qk_features_bounded counts and bounds them).
 FEATURE_TOL = 2e-3
-FLIP_TOL = 1e-2
 LSE_TOL = 2e-5
 
 
@@ -37,22 +35,16 @@ def _f32(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
 
 
-def _check_qk_features(got, ref, R):
-    err = rel_err(got[:, :4], ref[:, :4])
-    # f1, f2, f4: maxima and top-k means, continuous in the relation values
-    assert np.quantile(err[:, [0, 1, 3]], 0.999) < FEATURE_TOL, err.max(0)
-    assert err[:, [0, 1, 3]].max() < FLIP_TOL, err.max(0)
-    # f3: exact up to sign flips of relation values at 0
-    bad = np.nonzero(err[:, 2] > FEATURE_TOL)[0]
-    assert len(bad) <= max(2, 0.005 * len(err)), len(bad)
-    ok, k = f3_flip_consistent(got[:, 2], R, bad, rtol=FEATURE_TOL)
-    assert ok, (k, got[k, 2], ref[k, 2])
-
-
 def _discrete_mismatch(a, b, step):
     """Fraction of entries that differ, and the largest difference in units of step."""
     d = np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64))
     return float((d > 1e-6).mean()), float(d.max() / step)
+
+
+def _check_qk(q, k, got, ref, lse, ref_lse, R):
+    lse_err = float(np.abs(lse - ref_lse).max())
+    assert lse_err <= LSE_TOL * np.abs(ref_lse).max()
+    return check_qk_features_bounded(got, ref, R, flip_bound(q, k, lse_err), rtol=FEATURE_TOL)
 
 
 @pytest.mark.parametrize("name", BF16_CASES)
@@ -65,14 +57,7 @@ def test_qk_features_match_oracle(name):
     feats, lse = ops.qk_features(q, k)
     ops.status()
     ref, ref_lse, R = O.qk_features(d["q"], d["k"], groups=m["hq"] // m["hkv"], round_bf16=True)
-    got = feats[0].cpu().numpy()
-    assert np.abs(lse[0].cpu().numpy() - ref_lse).max() <= LSE_TOL * np.abs(ref_lse).max()
-    _check_qk_features(got, ref, R)
-    nq, hkv = m["nq"], m["hkv"]
-    f5_frac, f5_steps = _discrete_mismatch(got[:, 4], ref[:, 4], 1.0 / nq)
-    f6_frac, f6_steps = _discrete_mismatch(got[:, 5], ref[:, 5], 1.0 / hkv)
-    assert f5_frac <= 0.005 and f5_steps <= 1.01, (f5_frac, f5_steps)
-    assert f6_frac <= 0.005 and f6_steps <= 1.01, (f6_frac, f6_steps)
+    _check_qk(d["q"], d["k"], feats[0].cpu().numpy(), ref, lse[0].cpu().numpy(), ref_lse, R)
 
 
 def test_qk_features_llama_shapes_4096():
@@ -85,12 +70,7 @@ def test_qk_features_llama_shapes_4096():
     qn = q[0].float().cpu().numpy()
     kn = k[0].float().cpu().numpy()
     ref, ref_lse, R = O.qk_features(qn, kn, groups=4, round_bf16=True)
-    got = feats[0].cpu().numpy()
-    assert np.abs(lse[0].cpu().numpy() - ref_lse).max() <= LSE_TOL * np.abs(ref_lse).max()
-    _check_qk_features(got, ref, R)
-    f5_frac, _ = _discrete_mismatch(got[:, 4], ref[:, 4], 1 / 128)
-    f6_frac, _ = _discrete_mismatch(got[:, 5], ref[:, 5], 1 / 8)
-    assert f5_frac <= 0.005 and f6_frac <= 0.005, (f5_frac, f6_frac)
+    _check_qk(qn, kn, feats[0].cpu().numpy(), ref, lse[0].cpu().numpy(), ref_lse, R)
 
 
 def test_qk_features_full_scope_prefill_2048():
@@ -106,12 +86,21 @@ def test_qk_features_full_scope_prefill_2048():
     qn = q[0].float().cpu().numpy()
     kn = k[0].float().cpu().numpy()
     ref, ref_lse, R = O.qk_features(qn, kn, groups=4, round_bf16=True)
-    got = feats[0].cpu().numpy()
-    assert np.abs(lse[0].cpu().numpy() - ref_lse).max() <= LSE_TOL * np.abs(ref_lse).max()
-    _check_qk_features(got, ref, R)
-    f5_frac, _ = _discrete_mismatch(got[:, 4], ref[:, 4], 1 / L)
-    f6_frac, _ = _discrete_mismatch(got[:, 5], ref[:, 5], 1 / 4)
-    assert f5_frac <= 0.005 and f6_frac <= 0.005, (f5_frac, f6_frac)
+    _check_qk(qn, kn, feats[0].cpu().numpy(), ref, lse[0].cpu().numpy(), ref_lse, R)
+
+
+def test_qk_features_q512_L32768():
+    """The long-context query buffer (512 queries) over 32768 cached keys."""
+    from core_b200 import ops, synthetic
+    dev = _dev()
+    q, k, _ = synthetic.make_layer_inputs(seed=13, batch=1, n_kv_heads=2, n_q_heads=8,
+                                          seq_len=32768, n_queries=512, device=dev)
+    feats, lse = ops.qk_features(q, k)
+    ops.status()
+    qn = q[0].float().cpu().numpy()
+    kn = k[0].float().cpu().numpy()
+    ref, ref_lse, R = O.qk_features(qn, kn, groups=4, round_bf16=True)
+    _check_qk(qn, kn, feats[0].cpu().numpy(), ref, lse[0].cpu().numpy(), ref_lse, R)
 
 
 def test_qk_features_batch_rows_are_independent():
@@ -190,11 +179,22 @@ def test_coverage_matches_oracle(name):
     ops.status()
     got = cov[0].cpu().numpy()
     ref = O.coverage_features(d["k"], d["geometry"], d["prototypes"], d["hadamard"])
-    # occupancy is discrete: allow a handful of prototype reassignments
-    occ_frac = float((np.abs(got[:, 0] - ref[:, 0]) > 1e-5).mean())
-    assert occ_frac <= 0.01, occ_frac
-    err = rel_err(got[:, 1:], ref[:, 1:])
-    assert np.quantile(err, 0.999) < FEATURE_TOL, err.max(0)
+    check_coverage(got, ref)
+
+
+def check_coverage(got, ref, cos_err=2e-5):
+    """d_proto and delta_proto are (differences of) cosines computed to f32
+    accuracy: within FEATURE_TOL relative or ``cos_err`` absolute.  g within
+    FEATURE_TOL.  Occupancy counts change only when some key's top two
+    prototypes tie within ``cos_err`` (a reassignment moves two counts)."""
+    err = rel_err(got[:, 1:3], ref[:, 1:3])
+    absd = np.abs(got[:, 1:3] - ref[:, 1:3])
+    assert np.all((err <= FEATURE_TOL) | (absd <= cos_err)), (err.max(0), absd.max(0))
+    assert rel_err(got[:, 3], ref[:, 3]).max() <= FEATURE_TOL
+    occ = np.abs(got[:, 0] - ref[:, 0]) > 1e-5
+    assert occ.mean() <= 0.01, occ.mean()
+    if occ.any():
+        assert (ref[:, 2] <= cos_err).any(), "occupancy changed without a near tie"
 
 
 @pytest.mark.parametrize("name", BF16_CASES)
@@ -456,8 +456,15 @@ def test_compress_layer_keep_set_matches_reference(name):
     ops.status()
     got_scores = out["scores"][0].cpu().numpy()
     ref_scores = d["scores"]
-    err = np.abs(got_scores - ref_scores) / np.maximum(np.abs(ref_scores), 1e-3)
-    assert np.quantile(err, 0.995) < 2e-3, err.max()
+    # every score within 2e-3, or (a counted few) explained by its own features,
+    # which are checked against the reference's with the flip bound
+    n_expl = check_scores_explained(got_scores, ref_scores, out["features"][0].cpu().numpy(),
+                                    w.mlp)
+    assert n_expl <= max(2, 0.01 * L), n_expl
+    _, ref_lse, R = O.qk_features(d["q"], d["k"], groups=m["hq"] // m["hkv"], round_bf16=True)
+    gf = out["features"][0].cpu().numpy()
+    check_qk_features_bounded(gf[:, :6], d["features"][:, :6], R,
+                              flip_bound(d["q"], d["k"], LSE_TOL * np.abs(ref_lse).max()))
     if n_kept >= L:
         return
     keep = out["keep"][0].cpu().numpy()
@@ -571,3 +578,60 @@ def test_memory_readout_sees_writes_of_the_kernels_just_before_it():
         ops.status()
         assert torch.equal(got, want)
 
+
+
+def test_compress_layer_headline_shape():
+    """One layer at the benchmark's shape (bf16, 8 KV / 32 query heads,
+    L = 16384, 128 scoring queries in the prefill's question scope,
+    r = 0.75, d_mem = 512) through the fused layer step, against the
+    oracle: keep set (boundary band only), every score, the features, the
+    retained K/V bit for bit and the memory state."""
+    from core_b200 import engine, ops, synthetic
+    dev = _dev()
+    L, nq, hkv, hq, dm = 16384, 128, 8, 32, 512
+    q, k, v = synthetic.make_layer_inputs(seed=31, batch=1, n_kv_heads=hkv, n_q_heads=hq,
+                                          seq_len=L, n_queries=nq, device=dev)
+    w = synthetic.make_layer_weights(seed=32, n_kv_heads=hkv, n_q_heads=hq, d_mem=dm)
+    lw = engine.LayerWeights.prepare(geometry=w["geometry"], prototypes=w["prototypes"],
+                                     hadamard=w["hadamard"], mlp_params=w["mlp"], theta=w["theta"],
+                                     n_kv_heads=hkv, n_q_heads=hq, device=dev)
+    mem = engine.MemoryState.zeros(1, dm, hkv * 128, dev)
+    n_kept = engine.n_kept_for(L, 0.75, 4)
+    out = engine.compress_layer(q, k, v, lw, n_kept=n_kept, positions=torch.arange(L, device=dev)[None],
+                                original_length=L, is_prefill=True, memory=mem)
+    ops.status()
+    qn, kn, vn = (t[0].float().cpu().numpy() for t in (q, k, v))
+    ow = O.LayerWeights(mlp=tuple(t.numpy() for t in w["mlp"]), geometry=w["geometry"].numpy(),
+                        prototypes=w["prototypes"].numpy(), hadamard=w["hadamard"].numpy(),
+                        theta=w["theta"].numpy())
+    ref = O.compress_layer(qn, kn, vn, ow, compression_ratio=0.75, is_prefill=True,
+                           round_bf16=True)
+    gf = out["features"][0].cpu().numpy()
+    _, ref_lse, R = O.qk_features(qn, kn, groups=4, round_bf16=True)
+    n_qk = check_qk_features_bounded(gf[:, :6], ref["features"][:, :6], R,
+                                     flip_bound(qn, kn, LSE_TOL * np.abs(ref_lse).max()))
+    check_coverage(gf[:, 6:10], ref["features"][:, 6:10])
+    np.testing.assert_allclose(gf[:, 10:], ref["features"][:, 10:], rtol=1e-6, atol=1e-7)
+    gs = out["scores"][0].cpu().numpy()
+    n_sc = check_scores_explained(gs, ref["scores"], gf, ow.mlp)
+    assert n_sc <= 0.01 * L, (n_qk, n_sc)
+    keep = out["keep"][0].cpu().numpy()
+    s = ref["scores"].astype(np.float64).copy()
+    s[:4] = s.max() + 1
+    boundary = np.sort(s)[::-1][n_kept - 1]
+    near = np.abs(s - boundary) <= 1e-3 * abs(boundary)
+    diff = np.setxor1d(keep, ref["keep"])
+    assert np.all(near[diff]), (diff, boundary)
+    idx = out["keep"].long()[:, None, :, None].expand(-1, hkv, -1, 128)
+    assert torch.equal(out["keys"], k.gather(2, idx)) and torch.equal(out["values"], v.gather(2, idx))
+    # the memory write of the evicted set this path chose (the reference's
+    # unless a boundary key flipped)
+    M_ref, b_ref, Z_ref = ref["M"], ref["b"], ref["Z"]
+    if diff.size:
+        evict = np.ones(L, bool)
+        evict[keep] = False
+        M_ref, b_ref, Z_ref = O.memory_write(kn, vn, ref["scores"], evict, ow.theta, groups=4)
+    for got, want in ((mem.M[0], M_ref), (mem.b[0], b_ref)):
+        g = got.cpu().numpy()
+        assert np.abs(g - want).max() <= 2e-3 * np.abs(want).max()
+    assert abs(float(mem.Z[0]) - float(Z_ref)) <= 1e-6

@@ -36,7 +36,7 @@ def test_default_buffer_covers_entire_compression_interval(interval):
     keys = torch.zeros(1, 1, 4097, 1)
     cache = SimpleNamespace(layers=[SimpleNamespace(keys=keys, values=keys)])
     with patch.object(press, "compress", return_value=(keys, keys)) as compress, patch(
-            "core_b200.press._extract_keys_and_values", return_value=(keys, keys)):
+            "core_b200.press.read_cache_layer", return_value=(keys, keys)):
         for token in range(interval):
             press.forward_hook(SimpleNamespace(layer_idx=0), [], {
                 "hidden_states": torch.tensor([[[float(token)]]]),

@@ -46,7 +46,7 @@ def _call(lib, name, q, w, attn, hkv, ws=None):
     dims = _lib.CoreDims(B, hq, hkv, d, q_len, q_len, _lib.CORE_DTYPE_BF16)
     d_mem, gh, hidden = w["theta"].shape[0], w["w1"].shape[0], w["ofold"].shape[0]
     args = [ctypes.byref(dims), q_len, q.data_ptr(), w["theta"].data_ptr(), w["w1"].data_ptr(),
-            w["b1"].data_ptr(), w["w2"].data_ptr(), w["b2"].data_ptr(), d_mem, gh, -1.0,
+            w["b1"].data_ptr(), w["w2"].data_ptr(), w["b2"].data_ptr(), d_mem, gh, float("nan"),
             w["M"].data_ptr(), w["b"].data_ptr(), w["ofold"].data_ptr(), hidden, attn.data_ptr()]
     if ws is not None:
         args += [ws.data_ptr(), ws.numel()]
@@ -94,7 +94,7 @@ def test_noalloc_readout_rejects_oversized_call():
     rc = lib.core_memory_readout_noalloc(
         ctypes.byref(dims), q_len, big_q.data_ptr(), w["theta"].data_ptr(), w["w1"].data_ptr(),
         w["b1"].data_ptr(), w["w2"].data_ptr(), w["b2"].data_ptr(), w["theta"].shape[0],
-        w["w1"].shape[0], -1.0, w["M"].data_ptr(), w["b"].data_ptr(), w["ofold"].data_ptr(),
+        w["w1"].shape[0], float("nan"), w["M"].data_ptr(), w["b"].data_ptr(), w["ofold"].data_ptr(),
         w["ofold"].shape[0], big_attn.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
     assert rc == -1  # CORE_ERR_INVALID_ARG, before any launch
     assert "static scratch" in _lib.last_error()
