@@ -363,4 +363,34 @@ __device__ __forceinline__ void top4_insert(float (&t)[4], float v) {
   t[0] = fmaxf(t[0], v);
 }
 
+// Merge a pair {a, b} into a descending top-4 list: the k-th largest of the
+// union is the largest min(t_i, pair_j) with i + j = k (pair sorted).
+__device__ __forceinline__ void top4_insert2(float (&t)[4], float a, float b) {
+  const float hi = fmaxf(a, b), lo = fminf(a, b);
+  t[3] = fmax3(t[3], fminf(t[2], hi), fminf(t[1], lo));
+  t[2] = fmax3(t[2], fminf(t[1], hi), fminf(t[0], lo));
+  t[1] = fmax3(t[1], fminf(t[0], hi), lo);
+  t[0] = fmaxf(t[0], hi);
+}
+
+// Top-4 of the union of two descending top-4 lists: max(t_i, o_{3-i}) are the
+// four largest (a bitonic sequence), then two compare-exchange stages sort them.
+__device__ __forceinline__ void cex_desc(float& a, float& b) {
+  const float hi = fmaxf(a, b), lo = fminf(a, b);
+  a = hi;
+  b = lo;
+}
+__device__ __forceinline__ void top4_merge(float (&t)[4], const float (&o)[4]) {
+  float d0 = fmaxf(t[0], o[3]), d1 = fmaxf(t[1], o[2]), d2 = fmaxf(t[2], o[1]),
+        d3 = fmaxf(t[3], o[0]);
+  cex_desc(d0, d2);
+  cex_desc(d1, d3);
+  cex_desc(d0, d1);
+  cex_desc(d2, d3);
+  t[0] = d0;
+  t[1] = d1;
+  t[2] = d2;
+  t[3] = d3;
+}
+
 }  // namespace core

@@ -34,6 +34,7 @@ constexpr int kRelQ = 64 / kRelTeams;        // queries per thread per half (one
 constexpr int kEpiThreads = 128 * kRelTeams;
 constexpr int kThreads = 64 + kEpiThreads;   // warp 0 TMA, warp 1 MMA, 16 epilogue warps
 static_assert(kRelTeams == 4, "the team merge packs two 16-query masks per record word");
+static_assert(kRelQ == 16, "one 16-query chunk per thread and half");
 constexpr int kLseTeams = 4;                       // LSE epilogue: 16-key quarters of a sub-tile
 constexpr int kLseEpiThreads = 128 * kLseTeams;
 constexpr int kLseThreads = 64 + kLseEpiThreads;  // warp 0 TMA, warp 1 MMA, 16 epilogue warps
@@ -352,25 +353,60 @@ struct RelSmem {
   static constexpr uint32_t kKOff = kQOff + kQBytes;
   static constexpr uint32_t kLseOff = kKOff + kKStages * kKTileBytes;  // float2 [G][128]: (-lse, log|C|)
   static constexpr uint32_t kCcOff = kLseOff + G * kTile * 8;          // unused
-  static constexpr uint32_t kXchOff = kCcOff + kTile * 4;  // uint32 [teams - 1][128][16]
+  static constexpr uint32_t kXchOff = kCcOff + kTile * 4;  // uint32 [3 slots][16 words][128 rows]
   static constexpr uint32_t kBarOff = kXchOff + (kRelTeams - 1) * kTile * 16 * 4;
   static constexpr uint32_t kTotal = kBarOff + 256;
 };
 
+// Running statistics of one key over one thread's queries of a unit.
 struct KeyStats {
   float top[4], rtop[4];
-  float psum, mxnp;
+  float psum, mxnp, nsum;  // sum of the positive R, max and sum of the non-positive R
   uint32_t pcnt;
-  uint32_t mask[2];
+  uint32_t mask0, mask1;   // positive-R bits of the thread's queries, per half
   __device__ __forceinline__ void init() {
 #pragma unroll
     for (int i = 0; i < 4; ++i) top[i] = rtop[i] = -INFINITY;
     psum = 0.f;
     mxnp = -INFINITY;
+    nsum = 0.f;
     pcnt = 0;
-    mask[0] = mask[1] = 0;
+    mask0 = mask1 = 0;
   }
 };
+
+// Team exchange slot (word-major: word i of key row r at x[i * kTile + r]).
+__device__ __forceinline__ void xch_put(uint32_t* x, const KeyStats& st, uint32_t w0,
+                                        uint32_t w1) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[i * kTile] = __float_as_uint(st.top[i]);
+    x[(4 + i) * kTile] = __float_as_uint(st.rtop[i]);
+  }
+  x[8 * kTile] = __float_as_uint(st.psum);
+  x[9 * kTile] = st.pcnt;
+  x[10 * kTile] = w0;
+  x[11 * kTile] = w1;
+  x[12 * kTile] = __float_as_uint(st.mxnp);
+  x[13 * kTile] = __float_as_uint(st.nsum);
+}
+__device__ __forceinline__ void xch_take(const uint32_t* x, KeyStats& st, uint32_t& w0,
+                                         uint32_t& w1) {
+  float o[4], ro[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    o[i] = __uint_as_float(x[i * kTile]);
+    ro[i] = __uint_as_float(x[(4 + i) * kTile]);
+  }
+  top4_merge(st.top, o);
+  top4_merge(st.rtop, ro);
+  st.psum += __uint_as_float(x[8 * kTile]);
+  st.pcnt += x[9 * kTile];
+  w0 = x[10 * kTile];
+  w1 = x[11 * kTile];
+  st.mxnp = fmaxf(st.mxnp, __uint_as_float(x[12 * kTile]));
+  st.nsum += __uint_as_float(x[13 * kTile]);
+}
 
 // 18 warps: five share one scheduler's 16K registers, so 96 registers a thread
 template <int G, bool kLoo>
@@ -440,13 +476,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (t.grp != cur) {
           if (gcount > 0 && !wait(bar_q_empty, (gcount - 1) & 1, 201)) break;
           mbar_arrive_expect_tx(bar_q_full, S::kQBytes);
+          // rows of a half ordered [team][head][16 queries], so that one
+          // epilogue thread's queries of all G heads are G*16 adjacent TMEM columns
           for (int ka = 0; ka < 2; ++ka)
             for (int hf = 0; hf < 2; ++hf)
-              for (int g = 0; g < G; ++g)
-                tma_load_3d(sQ + (uint32_t)ka * 2u * kQHalf + (uint32_t)hf * kQHalf +
-                                (uint32_t)g * 64u * 128u,
-                            &tmQ, bar_q_full, ka * 64, t.qb * kTile + hf * 64,
-                            t.b * p.Hq + t.h * G + g);
+              for (int tm = 0; tm < kRelTeams; ++tm)
+                for (int g = 0; g < G; ++g)
+                  tma_load_3d(sQ + (uint32_t)ka * 2u * kQHalf + (uint32_t)hf * kQHalf +
+                                  (uint32_t)(tm * G + g) * 16u * 128u,
+                              &tmQ, bar_q_full, ka * 64, t.qb * kTile + hf * 64 + tm * kRelQ,
+                              t.b * p.Hq + t.h * G + g);
           cur = t.grp;
           ++gcount;
         }
@@ -533,28 +572,96 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int key = t.kt * kTile + krow;
       KeyStats st;
       st.init();
-      // units whose keys are all visible to all valid queries and in range
       const int qb_first_pos = p.q_start + t.qb * kTile;
       const int qb_valid = min(kTile, p.nq - t.qb * kTile);
+      // every key of the tile visible to every query of the block, and in range
+      const bool keys_full = (t.kt * kTile + kTile - 1 <= qb_first_pos) && (t.kt * kTile + kTile <= p.L);
+      // Full units keep their statistics on the unscaled head sum S = head_topk * R:
+      // 1/head_topk is a power of two here, so scaling the finished statistics
+      // (maxima, top-4, positive sum) is exact and the signs are unchanged.
+      const bool sspace = !kLoo && !exact_div && keys_full && qb_valid == kTile;
       for (int hf = 0; hf < 2; ++hf) {
         const int buf = sub & 1, n = sub >> 1;
         if (!(ok = wait(bar_t_full(buf), n & 1, 206))) break;
         tc_fence_after();
         const int tl0 = hf * 64 + team * kRelQ;  // query index within the block of j = 0
-        const bool full = (t.kt * kTile + kTile - 1 <= qb_first_pos) &&
-                          (t.kt * kTile + kTile <= p.L) && (tl0 + kRelQ <= qb_valid);
+        const bool full = keys_full && (tl0 + kRelQ <= qb_valid);
+        // this thread's G * 16 columns: head g's 16 queries at tcol + 16 g
+        const uint32_t tcol = tmem + ((uint32_t)(wq * 32) << 16) + (uint32_t)(buf * kN + team * G * kRelQ);
         // kRelQ queries per thread, in chunks of 16 to bound registers
         uint32_t msk = 0;
 #pragma unroll 1
         for (int ch = 0; ch < kRelQ / 16; ++ch) {
           const int c0 = tl0 + ch * 16;  // query index within the block of element 0
+          const int tabs0 = t.qb * kTile + c0;  // absolute query index of element 0
+          const bool recent_chunk = tabs0 + 15 >= p.nq - p.n_recent;
+          bool done = false;
+          if (sspace) {
+            // S = sum over the group's heads of fma(s, bf16(x), -lse + log|C|) in
+            // f32x2, with the floor clamp left out: exact when every r of the
+            // chunk lies at least 16 above the floor (then logaddexp(r, floor)
+            // is r); otherwise the chunk is redone below
+            unsigned long long S2[8];
+            float rmin = INFINITY;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+              float v[16];
+              tmem_ld16(tcol + (uint32_t)(g * 16), v);
+              const float4* nc4 = reinterpret_cast<const float4*>(s_nc + g * kTile + c0);
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) {
+                const float4 c = nc4[q4];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const int j = q4 * 4 + e * 2;
+                  bf16_round2(v[j], v[j + 1]);
+                  const unsigned long long r2 =
+                      f2_fma(f2_pack(v[j], v[j + 1]), sc2, e ? f2_pack(c.z, c.w) : f2_pack(c.x, c.y));
+                  rmin = fmin3(rmin, f2_lo(r2), f2_hi(r2));
+                  S2[j >> 1] = (g == 0) ? r2 : f2_add(S2[j >> 1], r2);
+                }
+              }
+            }
+            if (!__any_sync(0xffffffffu, rmin < kLogFloor + 16.0f)) {
+              done = true;
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                const float a = f2_lo(S2[jj]), b = f2_hi(S2[jj]);
+                top4_insert2(st.top, a, b);
+                const bool pa = a > 0.f, pb = b > 0.f;
+                if (pa) {
+                  st.psum += a;
+                } else {
+                  st.mxnp = fmaxf(st.mxnp, a);
+                  st.nsum += a;
+                }
+                if (pb) {
+                  st.psum += b;
+                } else {
+                  st.mxnp = fmaxf(st.mxnp, b);
+                  st.nsum += b;
+                }
+                msk |= ((pa ? 1u : 0u) | (pb ? 2u : 0u)) << (ch * 16 + 2 * jj);
+              }
+              if (recent_chunk) {
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                  const int r0 = p.nq - p.n_recent - tabs0;  // first recent element
+                  if (2 * jj >= r0) top4_insert(st.rtop, f2_lo(S2[jj]));
+                  if (2 * jj + 1 >= r0) top4_insert(st.rtop, f2_hi(S2[jj]));
+                }
+              }
+            }
+          }
+          if (done) continue;
+          // general path: exact logaddexp with the floor where needed, causal and
+          // ragged masks, leave-one-out TopMean
           float acc[16];
           float mn[kLoo ? 16 : 1];
 #pragma unroll 1
           for (int g = 0; g < G; ++g) {
             float v[16];
-            tmem_ld16(tmem + ((uint32_t)(wq * 32) << 16) +
-                          (uint32_t)(buf * kN + g * 64 + team * kRelQ + ch * 16), v);
+            tmem_ld16(tcol + (uint32_t)(g * 16), v);
             const float* ncp = s_nc + g * kTile + c0;
             float rmin = INFINITY;
             // r for pairs of queries in packed f32x2 arithmetic (each lane rounds as the
@@ -594,13 +701,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          const int tabs0 = t.qb * kTile + c0;  // absolute query index of element 0
-          const bool recent_chunk = tabs0 + 15 >= p.nq - p.n_recent;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float R;
             if (kLoo) {
               R = __fdiv_rn(acc[j] - mn[kLoo ? j : 0], (float)p.head_topk);
+            } else if (sspace) {
+              R = acc[j];
             } else {
               R = exact_div ? __fdiv_rn(acc[j], (float)p.head_topk) : acc[j] * inv_ht;
             }
@@ -612,6 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (recent_chunk && tabs0 + j >= p.nq - p.n_recent) top4_insert(st.rtop, R);
             const bool pz = R > 0.f;
             st.psum += fmaxf(R, 0.f);  // adds R when positive, +0 otherwise (NaN: +0)
+            if (R > -INFINITY) st.nsum += fminf(R, 0.f);  // masked entries are not queries
             msk |= (pz ? 1u : 0u) << (ch * 16 + j);
             st.mxnp = fmaxf(st.mxnp, pz ? -INFINITY : R);
           }
@@ -620,42 +728,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_t_empty(buf));
         ++sub;
-        st.mask[hf] = msk;
+        if (hf == 0) st.mask0 = msk; else st.mask1 = msk;
       }
       if (!ok) break;
-      st.pcnt = (uint32_t)(__popc(st.mask[0]) + __popc(st.mask[1]));  // positive relations
-      // merge the teams (same key, different query quarters) into team 0 and store
-      if (team > 0) {
-        uint32_t* x = s_xch + ((team - 1) * kTile + krow) * 16;
+      if (sspace) {  // back to R = S / head_topk (exact)
+#pragma unroll
         for (int i = 0; i < 4; ++i) {
-          x[i] = __float_as_uint(st.top[i]);
-          x[4 + i] = __float_as_uint(st.rtop[i]);
+          st.top[i] *= inv_ht;
+          st.rtop[i] *= inv_ht;
         }
-        x[8] = __float_as_uint(st.psum);
-        x[9] = st.pcnt;
-        x[10] = st.mask[0];
-        x[11] = st.mask[1];
-        x[12] = __float_as_uint(st.mxnp);
+        st.psum *= inv_ht;
+        st.mxnp *= inv_ht;
+        st.nsum *= inv_ht;
+      }
+      st.pcnt = (uint32_t)(__popc(st.mask0) + __popc(st.mask1));  // positive relations
+      // Merge the four teams (same key, different query quarters) as a tree:
+      // 1 -> 0 and 3 -> 2, then 2 -> 0, which stores the record.  Exchange
+      // slots are word-major (word i of key row r at [i * kTile + r]), so a
+      // warp's 32 rows fall in 32 banks.  Slot 0 and 1 are written before the
+      // first barrier and read before the second; slot 2 between them and read
+      // after the second, so two barriers per unit suffice.
+      // query bits: record word 2 hf + (team >> 1) holds teams 2 (team >> 1) and
+      // 2 (team >> 1) + 1 of half hf, the odd team in the upper 16 bits
+      uint32_t* xrow = s_xch + krow;
+      if (team & 1) xch_put(xrow + (team >> 1) * 16 * kTile, st, st.mask0, st.mask1);
+      named_barrier(2, kEpiThreads);
+      uint32_t wa = 0, wb = 0;
+      if (!(team & 1)) {
+        uint32_t o0, o1;
+        xch_take(xrow + (team >> 1) * 16 * kTile, st, o0, o1);
+        wa = st.mask0 | (o0 << kRelQ);
+        wb = st.mask1 | (o1 << kRelQ);
+        if (team == 2) xch_put(xrow + 2 * 16 * kTile, st, wa, wb);
       }
       named_barrier(2, kEpiThreads);
       if (team == 0) {
-        // query word w (32 queries) of half hf holds teams 2 (w % 2) and 2 (w % 2) + 1
-        uint32_t qw[4] = {st.mask[0], 0u, st.mask[1], 0u};
-        float psum = st.psum, mxnp = st.mxnp;
-        uint32_t pcnt = st.pcnt;
-        for (int tm = 1; tm < kRelTeams; ++tm) {
-          const uint32_t* x = s_xch + ((tm - 1) * kTile + krow) * 16;
-          for (int i = 0; i < 4; ++i) {
-            top4_insert(st.top, __uint_as_float(x[i]));
-            top4_insert(st.rtop, __uint_as_float(x[4 + i]));
-          }
-          psum += __uint_as_float(x[8]);
-          pcnt += x[9];
-          mxnp = fmaxf(mxnp, __uint_as_float(x[12]));
-          const int w = tm >> 1, sh = (tm & 1) * kRelQ;
-          qw[w] |= x[10] << sh;
-          qw[2 + w] |= x[11] << sh;
-        }
+        uint32_t w1, w3;
+        xch_take(xrow + 2 * 16 * kTile, st, w1, w3);
         if (key < p.L) {
           uint4* dst = reinterpret_cast<uint4*>(
               p.rec + ((((long long)t.b * p.L + key) * p.Hkv + t.h) * p.n_qb + t.qb) * kRecWords);
@@ -663,11 +772,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                               __float_as_uint(st.top[2]), __float_as_uint(st.top[3]));
           dst[1] = make_uint4(__float_as_uint(st.rtop[0]), __float_as_uint(st.rtop[1]),
                               __float_as_uint(st.rtop[2]), __float_as_uint(st.rtop[3]));
-          dst[2] = make_uint4(__float_as_uint(psum), pcnt, qw[0], qw[1]);
-          dst[3] = make_uint4(qw[2], qw[3], __float_as_uint(mxnp), 0u);
+          dst[2] = make_uint4(__float_as_uint(st.psum), st.pcnt, wa, w1);
+          dst[3] = make_uint4(wb, w3, __float_as_uint(st.mxnp), __float_as_uint(st.nsum));
         }
       }
-      named_barrier(2, kEpiThreads);
     }
   }
 
@@ -843,7 +951,7 @@ __global__ void __launch_bounds__(kMergeThreads)
 
   float top[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   float rtop[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-  float hs = 0.f, mx = -INFINITY;
+  float hs = 0.f, mx = -INFINITY, ns = 0.f;
   unsigned int hc = 0;
   int f5cnt = 0;
   uint32_t* sum_out = (p.summary != nullptr && live) ? p.summary + gi * p.sum_words : nullptr;
@@ -862,6 +970,7 @@ __global__ void __launch_bounds__(kMergeThreads)
     hs += __uint_as_float(r2.x);
     hc += r2.y;
     mx = fmaxf(mx, __uint_as_float(r3.z));
+    ns += __uint_as_float(r3.w);
     // f5: OR over the heads of the positive-query bits of this block
     const uint32_t w0 = lanes_or<kLanes>(r2.z), w1 = lanes_or<kLanes>(r2.w);
     const uint32_t w2 = lanes_or<kLanes>(r3.x), w3 = lanes_or<kLanes>(r3.y);
@@ -874,9 +983,13 @@ __global__ void __launch_bounds__(kMergeThreads)
   if ((int)hc >= kf) {
     f6pos = 1;
   } else if (hc > 0) {
+    // the top kf are the hc positive values and the largest rem non-positive
+    // ones: those lie at or below mx, and their mean is at least the mean of
+    // all valid - hc non-positive values (ns / (valid - hc)), as rem <= valid - hc
     const float rem = (float)(kf - (int)hc);
-    const float hi = hs + rem * mx;                       // remaining values <= mx
-    const float lo = hs + rem * (kLogFloor * 1.0001f);    // and >= the floor
+    const float mean_np = ns / (float)(valid - (int)hc);
+    const float hi = hs + rem * mx;
+    const float lo = hs + rem * fmaxf(mean_np, kLogFloor * 1.0001f);
     const float tol = 1e-5f * (fabsf(hs) + rem * fabsf(kLogFloor));
     if (hi < -tol) {
       // definitely not positive
@@ -1219,7 +1332,7 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
     uint64_t dims[3] = {128, (uint64_t)p.nq, (uint64_t)p.B * p.Hq};
     uint64_t str[2] = {256, (uint64_t)p.nq * 256};
     uint32_t box_lse[3] = {64, 128, 1};
-    uint32_t box_rel[3] = {64, 64, 1};
+    uint32_t box_rel[3] = {64, (uint32_t)kRelQ, 1};
     if ((rc = make_tmap_bf16(&tmQ_lse, q, 3, dims, str, box_lse, true)) != CORE_OK) return rc;
     if ((rc = make_tmap_bf16(&tmQ_rel, q, 3, dims, str, box_rel, true)) != CORE_OK) return rc;
   }

@@ -18,7 +18,7 @@ constexpr float kLn2 = 0.6931471805599453f;
 //   [4..7]  top-4 R over the block's recent queries
 //   [8]     sum of the positive R          [9]  count of the positive R
 //   [10..13] positive-R bits, query 32 w + b of the block in word w, bit b
-//   [14]    max of the non-positive R      [15] unused
+//   [14]    max of the non-positive R      [15] sum of the non-positive R
 constexpr int kRecWords = 16;
 // Per-key summary of one rank's KV heads (head-sharded caches), sum_words =
 // kSumHead + 4 n_qb words: 0-3 top-4 relation values (descending), 4-7 top-4

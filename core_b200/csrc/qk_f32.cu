@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kThreads)
   // ---- per-key statistics over this thread's 32 queries ----
   float top[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   float rtop[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-  float psum = 0.f, mxnp = -INFINITY;
+  float psum = 0.f, mxnp = -INFINITY, nsum = 0.f;
   uint32_t word = 0;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
@@ -230,6 +230,7 @@ __global__ void __launch_bounds__(kThreads)
     if (tq0 + t >= p.nq - p.n_recent) top4_insert(rtop, R);
     const bool pz = R > 0.f;
     psum += fmaxf(R, 0.f);
+    if (R > -INFINITY) nsum += fminf(R, 0.f);  // masked entries are not queries
     word |= (pz ? 1u : 0u) << j;
     mxnp = fmaxf(mxnp, pz ? -INFINITY : R);
   }
@@ -240,6 +241,8 @@ __global__ void __launch_bounds__(kThreads)
   merge_top4(rtop, 2);
   psum += __shfl_xor_sync(0xffffffffu, psum, 1);
   psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+  nsum += __shfl_xor_sync(0xffffffffu, nsum, 1);
+  nsum += __shfl_xor_sync(0xffffffffu, nsum, 2);
   mxnp = fmaxf(mxnp, __shfl_xor_sync(0xffffffffu, mxnp, 1));
   mxnp = fmaxf(mxnp, __shfl_xor_sync(0xffffffffu, mxnp, 2));
   uint32_t cnt = __popc(word);
@@ -257,7 +260,7 @@ __global__ void __launch_bounds__(kThreads)
       dst[8] = __float_as_uint(psum);
       dst[9] = cnt;
       dst[14] = __float_as_uint(mxnp);
-      dst[15] = 0u;
+      dst[15] = __float_as_uint(nsum);
     }
   }
 }

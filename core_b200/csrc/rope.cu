@@ -46,9 +46,8 @@ struct Round<float> {
   static __device__ __forceinline__ void store(float* p, float x) { *p = x; }
 };
 
-// One thread per rotation pair (j, j + d/2) of one (b, t, head); the block
-// covers kRows (b, t) rows of all heads for a run of pairs, so the cos / sin
-// of a (b, t, j) are computed once per thread and reused over the heads.
+// One thread per rotation pair (j, j + d/2) of one (b, t): it computes (or
+// reads) that pair's cos / sin once and rotates the pair in every head.
 constexpr int kThreads = 256;
 
 template <typename T>
@@ -100,7 +99,8 @@ int launch(int B, int Tn, int Hq, int d, const void* qp, long long row_stride, c
   rope_queries_kernel<T><<<blocks, kThreads, 0, st>>>(
       B, Tn, Hq, d, static_cast<const T*>(qp), row_stride, pos, inv_freq, scaling,
       static_cast<const T*>(cosv), static_cast<const T*>(sinv), cs_batch, static_cast<T*>(out));
-  return cuda_error(cudaGetLastError(), "rope_queries_kernel");
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "rope_queries_kernel launch");
 }
 
 }  // namespace rope
