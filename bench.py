@@ -70,6 +70,10 @@ def parse():
     p.add_argument("--graph", action=argparse.BooleanOptionalAction, default=True,
                    help="replay the whole step (all layers' kernels and, head-sharded, the "
                         "NCCL collectives) as one CUDA graph (--no-graph: issue it eagerly)")
+    p.add_argument("--long-steps", type=int, default=5,
+                   help="timed steps of the long-context step (131072 tokens, 512 queries, r=0.9; "
+                        "head-sharded over the ranks) reported as long_context in the headline "
+                        "line; 0 leaves it out")
     p.add_argument("--sm-reserve", type=int, default=2,
                    help="SMs the persistent grids leave free for the other streams' kernels")
     a = p.parse_args()
@@ -214,7 +218,25 @@ def cpu_baseline(a):
             "kind": "port",
             "sample": f"1 of {a.layers} layers ({_sample_note(a)}, nq={a.n_queries}, "
                       f"r={a.ratio}, bf16-rounded inputs) through oracle.core_oracle.compress_layer "
-                      f"in {t:.2f} s, scaled by 1/{a.layers}; numpy/BLAS threads = host cores"}
+                      f"in {t:.2f} s, extrapolated x{a.layers} to the {a.layers}-layer step; "
+                      f"numpy/BLAS threads = host cores",
+            "extrapolated_layers": a.layers,
+            "reference_torch_cpu": reference_torch_timing()}
+
+
+REF_LAYERS_PER_STEP = 4  # layers the CPU arm computes per step (each its own seed)
+
+
+def reference_torch_timing():
+    """The reference's own torch CPU path, one layer of the headline workload,
+    measured where the reference imports (oracle/time_reference_cpu.py)."""
+    path = os.path.join(ROOT, "oracle", "reference_cpu_timing.json")
+    if not os.path.exists(path):
+        return None
+    rec = json.load(open(path))
+    return {"s_per_layer": rec["s_per_layer"], "threads": rec["threads"],
+            "where": "build container with the reference importable (not this host); "
+                     "oracle/time_reference_cpu.py", "workload": rec["workload"]}
 
 
 def run_reference(a, rank):
@@ -222,16 +244,19 @@ def run_reference(a, rank):
         return
     steps = max(1, min(a.steps, 3))
     warm = min(a.warmup, 1)
+    per = min(REF_LAYERS_PER_STEP, a.layers)
     for _ in range(warm):
         cpu_layer_sample(a, seed=1)
-    times = [cpu_layer_sample(a, seed=2 + i) for i in range(steps)]
-    t = statistics.median(times)
+    step_s = [sum(cpu_layer_sample(a, seed=2 + per * i + j) for j in range(per))
+              for i in range(steps)]
+    t = statistics.median(step_s) / per  # seconds per layer
     Ls = min(a.seq_len, CPU_SAMPLE_MAX_LEN)
     value = Ls / (t * a.layers)
-    sample = (f"{steps} timed samples (+{warm} warm-up) of 1 of {a.layers} layers each "
-              f"({_sample_note(a)}, nq={a.n_queries}, r={a.ratio}) through "
-              f"oracle.core_oracle.compress_layer, median {t:.2f} s per layer, scaled by "
-              f"1/{a.layers}")
+    sample = (f"{steps} timed steps (+{warm} warm-up layer), each {per} of the {a.layers} "
+              f"layers ({_sample_note(a)}, nq={a.n_queries}, r={a.ratio}, each layer its own "
+              f"seed) through oracle.core_oracle.compress_layer (the numpy restatement; the "
+              f"reference's torch code is not on this host), median {t:.2f} s per layer; "
+              f"value and ms_per_step scale the {per} layers to {a.layers} (x{a.layers / per:g})")
     long = a.workload == "long"
     line = {"metric": LONG_METRIC if long else METRIC, "value": value, "unit": UNIT,
             "impl": "reference", "n_gpus": a.gpus,
@@ -240,8 +265,10 @@ def run_reference(a, rank):
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic", "config": long_config(a, 1) if long else config_dict(a, 1),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                             "sample": sample},
+                             "sample": sample, "extrapolated_layers": a.layers / per,
+                             "reference_torch_cpu": reference_torch_timing()},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    line["config"]["cpu_sample"] = f"{per} of {a.layers} layers per step, scaled x{a.layers / per:g}"
     print(json.dumps(line), flush=True)
 
 
@@ -411,12 +438,31 @@ def main():
     # ---- end to end through the press API with host buffers ----
     e2e = run_e2e(a, dev, parts, layers, dist) if a.e2e_steps > 0 else None
 
+    # ---- the long-context configuration on the same ranks ----
+    long_context = None
+    if a.long_steps > 0:
+        del layers, parts, ws
+        torch.cuda.empty_cache()
+        la = argparse.Namespace(**vars(a))
+        la.workload, la.seq_len, la.n_queries, la.ratio = "long", 131072, 512, 0.9
+        la.steps, la.warmup, la.sharded, la.no_cpu_baseline = a.long_steps, max(3, a.warmup), n > 1, True
+        ll = run_long(la, dev, dist, rank, n)
+        long_context = {k: ll[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup",
+                                           "ms_per_step", "scaling", "config", "roofline",
+                                           "host_issue_ms_per_step", "gpu_launches", "clocks")}
+        long_context["note"] = ("one 131072-token sequence; N=1 runs the fused one-GPU layer step, "
+                                "N>1 the head-sharded step (rank r holds KV heads [8r/N, 8(r+1)/N), "
+                                "NCCL for the cross-head exchanges, each layer's memory write on "
+                                "rank l mod N); its own timed region, max over ranks")
+
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": config_dict(a, n), "roofline": roofline, "e2e": e2e,
             "gpu_launches": KERNELS_PER_LAYER * a.layers * a.steps,
             "host_issue_ms_per_step": host_ms, "clocks": clocks.summary()}
+    if long_context is not None:
+        line["long_context"] = long_context
     if graph_note is not None:
         line["config"]["cuda_graph"] = False
         line["graph_note"] = graph_note
