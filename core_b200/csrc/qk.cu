@@ -67,6 +67,15 @@ struct Unit {
   int b, h, qb, kt;
   long long grp;
 };
+// Last key tile holding a key that some query of block qb sees; the units of
+// later tiles (above the causal diagonal: every key after every query of the
+// block) are skipped by all roles and produce no LSE terms and no records.
+__device__ __host__ __forceinline__ int kt_last(const Params& p, int qb) {
+  const long long last_q = (long long)p.q_start + (long long)qb * kTile + kTile - 1;
+  const long long kt = last_q / kTile;
+  return (int)(kt < p.n_kt - 1 ? kt : p.n_kt - 1);
+}
+
 __device__ __forceinline__ Unit decode(long long u, const Params& p) {
   Unit r;
   r.kt = (int)(u % p.n_kt);
@@ -152,6 +161,7 @@ __global__ void __launch_bounds__(kLseThreads, 1)
       int gcount = 0, it = 0;
       for (long long u = u0; u < u1; ++u) {
         Unit t = decode(u, p);
+        if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
         if (t.grp != cur) {
           if (gcount > 0 && !wait(bar_q_empty, (gcount - 1) & 1, 101)) break;
           mbar_arrive_expect_tx(bar_q_full, S::kQBytes);
@@ -179,6 +189,7 @@ __global__ void __launch_bounds__(kLseThreads, 1)
       bool ok = true;
       for (long long u = u0; u < u1 && ok; ++u) {
         Unit t = decode(u, p);
+        if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
         if (t.grp != cur) {
           if (!(ok = wait(bar_q_full, gcount & 1, 103))) break;
           cur = t.grp;
@@ -210,7 +221,8 @@ __global__ void __launch_bounds__(kLseThreads, 1)
         if (!ok) break;
         mma_commit(bar_k_empty(st));
         ++it;
-        const bool last_of_group = (u + 1 >= u1) || (decode(u + 1, p).grp != t.grp);
+        // the group's units after this one are in another CTA or above the diagonal
+        const bool last_of_group = (u + 1 >= u1) || (t.kt == kt_last(p, t.qb));
         if (last_of_group) mma_commit(bar_q_empty);
       }
     }
@@ -239,6 +251,7 @@ __global__ void __launch_bounds__(kLseThreads, 1)
     const unsigned long long sc2 = f2_pack(p.scale_log2, p.scale_log2);
     for (long long u = u0; u < u1 && ok; ++u) {
       Unit t = decode(u, p);
+      if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
       if (t.grp != cur) {
         if (cur >= 0) flush(cu);
         for (int g = 0; g < G; ++g) {
@@ -322,7 +335,7 @@ __global__ void lse_combine_kernel2(const Params p, int grid_ctas, float* __rest
     const int qb = t / kTile;
     const long long grp = ((long long)b * p.Hkv + h) * p.n_qb + qb;
     const int c_lo = cta_of_unit(grp * (long long)p.n_kt, p.U, grid_ctas);
-    const int c_hi = cta_of_unit((grp + 1) * (long long)p.n_kt - 1, p.U, grid_ctas);
+    const int c_hi = cta_of_unit(grp * (long long)p.n_kt + kt_last(p, qb), p.U, grid_ctas);
     nslots = (c_hi - c_lo + 1) * kLseTeams;
     s = p.part + i * p.slot_stride;
   }
@@ -473,6 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int gcount = 0, it = 0;
       for (long long u = u0; u < u1; ++u) {
         Unit t = decode(u, p);
+        if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
         if (t.grp != cur) {
           if (gcount > 0 && !wait(bar_q_empty, (gcount - 1) & 1, 201)) break;
           mbar_arrive_expect_tx(bar_q_full, S::kQBytes);
@@ -506,6 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (long long u = u0; u < u1 && ok; ++u) {
         Unit t = decode(u, p);
+        if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
         if (t.grp != cur) {
           if (!(ok = wait(bar_q_full, gcount & 1, 203))) break;
           cur = t.grp;
@@ -534,7 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         mma_commit(bar_k_empty(st));
         ++it;
-        const bool last_of_group = (u + 1 >= u1) || (decode(u + 1, p).grp != t.grp);
+        // the group's units after this one are in another CTA or above the diagonal
+        const bool last_of_group = (u + 1 >= u1) || (t.kt == kt_last(p, t.qb));
         if (last_of_group) mma_commit(bar_q_empty);
       }
     }
@@ -553,6 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (long long u = u0; u < u1 && ok; ++u) {
       Unit t = decode(u, p);
+      if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
       if (t.grp != cur) {
         // (re)load (-lse, log|C_t|) of this query block
         named_barrier(1, kEpiThreads);
@@ -956,9 +973,23 @@ __global__ void __launch_bounds__(kMergeThreads)
   int f5cnt = 0;
   uint32_t* sum_out = (p.summary != nullptr && live) ? p.summary + gi * p.sum_words : nullptr;
   const uint32_t* base = p.rec + (gi * p.Hkv + h) * (long long)p.n_qb * kRecWords;
-  for (int qb = 0; qb < p.n_qb; ++qb) {
-    const uint4* r = reinterpret_cast<const uint4*>(base + (long long)qb * kRecWords);
-    const uint4 r0 = r[0], r1 = r[1], r2 = r[2], r3 = r[3];
+  // Blocks before qb_min hold no query that sees this key (their units may
+  // have been skipped, leaving no record).  The lanes of a warp loop from the
+  // smallest qb_min among them, so that their shuffles stay together, and
+  // take empty statistics for the blocks before their own.
+  const int qb_min = max(key - p.q_start, 0) / kTile;
+  const int qb_lo = __reduce_min_sync(0xffffffffu, qb_min);
+  if (sum_out != nullptr && h == 0)
+    for (int qb = 0; qb < qb_lo; ++qb)
+      reinterpret_cast<uint4*>(sum_out + kSumHead)[qb] = make_uint4(0u, 0u, 0u, 0u);
+  for (int qb = qb_lo; qb < p.n_qb; ++qb) {
+    uint4 r0 = make_uint4(__float_as_uint(-INFINITY), __float_as_uint(-INFINITY),
+                          __float_as_uint(-INFINITY), __float_as_uint(-INFINITY));
+    uint4 r1 = r0, r2 = make_uint4(0u, 0u, 0u, 0u), r3 = make_uint4(0u, 0u, __float_as_uint(-INFINITY), 0u);
+    if (qb >= qb_min) {
+      const uint4* r = reinterpret_cast<const uint4*>(base + (long long)qb * kRecWords);
+      r0 = r[0]; r1 = r[1]; r2 = r[2]; r3 = r[3];
+    }
     top4_insert(top, __uint_as_float(r0.x));
     top4_insert(top, __uint_as_float(r0.y));
     top4_insert(top, __uint_as_float(r0.z));
@@ -1079,6 +1110,86 @@ __global__ void __launch_bounds__(kResolveThreads)
 }
 
 
+// The same resolution for query buffers longer than kMaxSlowNq (full-scope
+// prefill): the pair's relation values over its visible queries go to a
+// per-block global scratch row, the ceil(valid / 4)-th largest is found by a
+// four-pass radix select on order-preserving 32-bit keys (8-bit digits, block
+// histograms), and the sum of the top values is the sum of those above it
+// plus the tied copies of it.  Ties change nothing: equal values add equally.
+constexpr int kResolveLargeThreads = 256;
+
+__device__ __forceinline__ uint32_t float_order_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // ascending keys for ascending floats
+}
+
+__global__ void __launch_bounds__(kResolveLargeThreads)
+    qk_f6_resolve_large_kernel(const MergeParams p, float* __restrict__ scratch) {
+  __shared__ __align__(16) float s_k[kD];
+  __shared__ int s_hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_remaining;
+  __shared__ float s_red[kResolveLargeThreads / 32];
+  float* vals = scratch + (long long)blockIdx.x * p.nq;
+  const int count = min(*p.queue_count, p.queue_cap);
+  for (int it = blockIdx.x; it < count; it += gridDim.x) {
+    const int2 item = p.queue[it];
+    const int bb = (int)(item.x / p.L), kk = (int)(item.x % p.L), h = item.y;
+    const long long krow = (((long long)bb * p.Hkv + h) * p.L + kk) * kD;
+    for (int e = threadIdx.x; e < kD; e += kResolveLargeThreads)
+      s_k[e] = (p.kf != nullptr) ? p.kf[krow + e] : __bfloat162float(p.k[krow + e]);
+    __syncthreads();
+    const int t0 = max(kk - p.q_start, 0);  // first query that sees the key
+    const int n = p.nq - t0;                 // the key's valid count (>= 1)
+    for (int i = threadIdx.x; i < n; i += kResolveLargeThreads)
+      vals[i] = relation_exact(p, bb, h, kk, t0 + i, s_k);
+    __syncthreads();
+    const int kf = max((n + 3) / 4, 1);
+    if (threadIdx.x == 0) {
+      s_prefix = 0u;
+      s_remaining = kf;  // rank of the threshold among the values still matching the prefix
+    }
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < 256; i += kResolveLargeThreads) s_hist[i] = 0;
+      __syncthreads();
+      const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      const uint32_t prefix = s_prefix;
+      for (int i = threadIdx.x; i < n; i += kResolveLargeThreads) {
+        const uint32_t key = float_order_key(vals[i]);
+        if ((key & hi_mask) == prefix) atomicAdd(&s_hist[(key >> shift) & 255], 1);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        int rem = s_remaining, dgt = 255;
+        for (; dgt > 0; --dgt) {  // largest digits first
+          if (s_hist[dgt] >= rem) break;
+          rem -= s_hist[dgt];
+        }
+        s_prefix = prefix | ((uint32_t)dgt << shift);
+        s_remaining = rem;  // copies of the threshold among the top kf
+      }
+      __syncthreads();
+    }
+    const uint32_t thr = s_prefix;
+    float part = 0.f;
+    for (int i = threadIdx.x; i < n; i += kResolveLargeThreads) {
+      const float v = vals[i];
+      if (float_order_key(v) > thr) part += v;
+    }
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = part;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float sum = 0.f;
+      for (int w = 0; w < kResolveLargeThreads / 32; ++w) sum += s_red[w];
+      const uint32_t tu = (thr & 0x80000000u) ? (thr & 0x7FFFFFFFu) : ~thr;  // back to float bits
+      sum += (float)s_remaining * __uint_as_float(tu);
+      if (sum / (float)kf > 0.f) atomicAdd(p.f6_target + (long long)item.x * p.f6_stride, p.f6_inc);
+    }
+    __syncthreads();
+  }
+}
+
 // Cross-rank merge of head-sharded summaries (one sequence): for keys key0 +
 // [0, n) the n_parts summaries of the ranks' KV heads (each written by
 // qk_merge_kernel in summary mode over that rank's heads) combine into f1..f6
@@ -1196,7 +1307,7 @@ int plan_qk(const core_dims_t* d, int topk, int n_recent, QKPlan* out) {
   const long long groups = p.U / p.n_kt;
   for (long long g = 0; g < groups; ++g) {
     int lo = cta_of_unit(g * p.n_kt, p.U, out->grid);
-    int hi = cta_of_unit((g + 1) * p.n_kt - 1, p.U, out->grid);
+    int hi = cta_of_unit(g * p.n_kt + kt_last(p, (int)(g % p.n_qb)), p.U, out->grid);
     if (hi - lo + 1 > maxc) maxc = hi - lo + 1;
   }
   p.slot_stride = kLseTeams * maxc;
@@ -1235,6 +1346,13 @@ int launch_qk(const QKPlan& plan, const CUtensorMap& tmQ_lse, const CUtensorMap&
 
 }  // namespace
 
+// Blocks of qk_f6_resolve_large_kernel and their scratch rows (one relation
+// value per query of the buffer each).
+static int resolve_large_blocks() { return 2 * sm_count(); }
+static size_t resolve_scratch_floats(const core_dims_t* d) {
+  return (size_t)resolve_large_blocks() * d->n_queries;
+}
+
 static size_t queue_cap_for(const core_dims_t* d) {
   // undecided f6 heads: bounded by every (key, head) pair of the cache
   return (size_t)d->batch * d->seq_len * d->n_kv_heads;
@@ -1250,6 +1368,7 @@ extern "C" size_t core_qk_features_workspace_bytes(const core_dims_t* d) {
   z.take<uint32_t>(plan.rec_words);
   z.take<int>(1);
   z.take<int2>(queue_cap_for(d));
+  if (d->n_queries > kMaxSlowNq) z.take<float>(resolve_scratch_floats(d));
   return z.used;
 }
 
@@ -1297,14 +1416,13 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
   QKPlan plan;
   plan_qk(d, topk_qk, n_recent_queries, &plan);
   Params& p = plan.p;
-  if (p.nq > kMaxSlowNq)
-    return set_error(CORE_ERR_UNSUPPORTED, "core_qk_features: n_queries must be <= 2048");
   Carver c(workspace, workspace_bytes);
   p.part = c.take<float2>(plan.part_elems);
   float* lse_buf = c.take<float>((size_t)p.B * p.Hq * p.nq);
   p.rec = c.take<uint32_t>(plan.rec_words);
   int* queue_count = c.take<int>(1);
   int2* queue = c.take<int2>(queue_cap_for(d));
+  float* resolve_scratch = p.nq > kMaxSlowNq ? c.take<float>(resolve_scratch_floats(d)) : nullptr;
   if (c.overflow)
     return set_error(CORE_ERR_WORKSPACE, "core_qk_features: workspace too small");
   p.status = device_status();
@@ -1391,7 +1509,11 @@ int core::qk_features_impl(const core_dims_t* d, const void* q, const void* k, i
     }
   }
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_merge_kernel launch");
-  qk_f6_resolve_kernel<<<4 * sm_count(), kResolveThreads, 0, s>>>(mp);
+  if (p.nq <= kMaxSlowNq)
+    qk_f6_resolve_kernel<<<4 * sm_count(), kResolveThreads, 0, s>>>(mp);
+  else
+    qk_f6_resolve_large_kernel<<<resolve_large_blocks(), kResolveLargeThreads, 0, s>>>(mp,
+                                                                                 resolve_scratch);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "qk_f6_resolve_kernel launch");
   if (lse_out != nullptr) {
     e = cudaMemcpyAsync(lse_out, lse_buf, sizeof(float) * (size_t)p.B * p.Hq * p.nq,

@@ -41,10 +41,11 @@ def _discrete_mismatch(a, b, step):
     return float((d > 1e-6).mean()), float(d.max() / step)
 
 
-def _check_qk(q, k, got, ref, lse, ref_lse, R):
+def _check_qk(q, k, got, ref, lse, ref_lse, R, max_frac=0.01):
     lse_err = float(np.abs(lse - ref_lse).max())
     assert lse_err <= LSE_TOL * np.abs(ref_lse).max()
-    return check_qk_features_bounded(got, ref, R, flip_bound(q, k, lse_err), rtol=FEATURE_TOL)
+    return check_qk_features_bounded(got, ref, R, flip_bound(q, k, lse_err), rtol=FEATURE_TOL,
+                                     max_frac=max_frac)
 
 
 @pytest.mark.parametrize("name", BF16_CASES)
@@ -87,6 +88,52 @@ def test_qk_features_full_scope_prefill_2048():
     kn = k[0].float().cpu().numpy()
     ref, ref_lse, R = O.qk_features(qn, kn, groups=4, round_bf16=True)
     _check_qk(qn, kn, feats[0].cpu().numpy(), ref, lse[0].cpu().numpy(), ref_lse, R)
+
+
+def test_qk_features_full_scope_prefill_8192():
+    """Full-scope prefill beyond 2048 queries (every cached token a query):
+    fully masked units above the diagonal are skipped, the merge reads only
+    the query blocks that see each key, and undecided f6 heads go through the
+    radix-select resolver."""
+    from core_b200 import ops, synthetic
+    dev = _dev()
+    L = 8192
+    q, k, _ = synthetic.make_layer_inputs(seed=14, batch=1, n_kv_heads=2, n_q_heads=8,
+                                          seq_len=L, n_queries=L, device=dev)
+    feats, lse = ops.qk_features(q, k)
+    ops.status()
+    qn = q[0].float().cpu().numpy()
+    kn = k[0].float().cpu().numpy()
+    ref, ref_lse, R = O.qk_features(qn, kn, groups=4, round_bf16=True)
+    # a key is seen by up to 8192 queries here, so the keys touched by some
+    # one-ulp logit flip (each one still bounded) grow with the query count
+    _check_qk(qn, kn, feats[0].cpu().numpy(), ref, lse[0].cpu().numpy(), ref_lse, R, max_frac=0.05)
+
+
+def test_compress_layer_full_scope_16k():
+    """A 16K prefill scored by all its queries (the reference's default
+    prefill_qk_scope="all") through the fused layer step: it runs, keeps the
+    budget with the sinks, and its features are finite and in range."""
+    from core_b200 import engine, ops, synthetic
+    dev = _dev()
+    L, hkv, hq = 16384, 8, 32
+    q, k, v = synthetic.make_layer_inputs(seed=15, batch=1, n_kv_heads=hkv, n_q_heads=hq,
+                                          seq_len=L, n_queries=L, device=dev)
+    w = synthetic.make_layer_weights(seed=16, n_kv_heads=hkv, n_q_heads=hq, d_mem=512)
+    lw = engine.LayerWeights.prepare(geometry=w["geometry"], prototypes=w["prototypes"],
+                                     hadamard=w["hadamard"], mlp_params=w["mlp"], theta=w["theta"],
+                                     n_kv_heads=hkv, n_q_heads=hq, device=dev)
+    mem = engine.MemoryState.zeros(1, 512, hkv * 128, dev)
+    n_kept = engine.n_kept_for(L, 0.75, 4)
+    out = engine.compress_layer(q, k, v, lw, n_kept=n_kept, positions=torch.arange(L, device=dev)[None],
+                                original_length=L, is_prefill=True, memory=mem)
+    ops.status()
+    f = out["features"][0].cpu().numpy()
+    assert np.isfinite(f).all()
+    assert ((f[:, 4] >= 0) & (f[:, 4] <= 1) & (f[:, 5] >= 0) & (f[:, 5] <= 1)).all()
+    keep = out["keep"][0].cpu().numpy()
+    assert keep.size == n_kept and np.all(np.diff(keep) > 0) and np.all(keep[:4] == np.arange(4))
+    assert np.isfinite(mem.M.cpu().numpy()).all() and float(mem.Z[0]) > 0
 
 
 def test_qk_features_q512_L32768():
