@@ -87,6 +87,8 @@ SIGNATURES = {
     "core_coverage_features": (ctypes.c_int, [_D, _P, _P, _P, _F, _P, _I, _I, _P, _S, _P]),
     "core_prepare_geometry": (ctypes.c_int, [_P, _P, _I, _P, _P]),
     "core_indexer_scores": (ctypes.c_int, [_D, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P]),
+    "core_indexer_mlp_bytes": (_S, []),
+    "core_prepare_indexer_mlp": (ctypes.c_int, [_P, _P]),
     "core_topb_workspace_bytes": (_S, [_I, _I]),
     "core_topb_select": (ctypes.c_int, [_P, _I, _I, _I, _I, _P, _P, _P, _S, _P]),
     "core_memory_write_workspace_bytes": (_S, [_D, _I, _I]),

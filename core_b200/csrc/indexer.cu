@@ -2,19 +2,23 @@
 // the feature concatenation at core/kvpress_adapter.py:536 and
 // COREIndexerMLP, core/indexer.py:88-108).
 //
-// Persistent CTAs of 256 threads over tiles of 128 cached tokens; thread
-// (token t = tid % 128, half = tid / 128).
+// Persistent CTAs of 512 threads over tiles of 128 cached tokens; thread
+// (token t = tid % 128, quarter q = tid / 128).
+//   0. once per CTA: the three bf16 terms of W2 arrive as one prepared image
+//      (core_prepare_indexer_mlp: already split and in the SW128 K-major
+//      layout of a tcgen05 B operand) by bulk copies;
 //   1. auxiliary features: a_value from V with the reference's bf16 roundings
 //      (squares, per-head sums, the head mean, /d and log1p each round to
-//      bf16; heads split over the two halves and summed in head order),
+//      bf16; heads split over the quarters and summed in head order),
 //      a_age, a_sink, a_phase;
-//   2. layer 1 (14 -> 128, f32 FMAs, exact erf GELU): each half computes 64
+//   2. layer 1 (14 -> 128, f32 FMAs, exact erf GELU): each quarter computes 32
 //      hidden units and stores them as three bf16 terms (hi + mid + lo = the
 //      f32 value) in the SW128 K-major layout of a tcgen05 A operand;
-//   3. layer 2 (128 -> 128) on tcgen05: A = hidden terms, B = the three bf16
-//      terms of W2 (built once per CTA), the six products whose term orders
-//      sum to at most 2 accumulated in f32 in TMEM — f32-level accuracy;
-//   4. epilogue: TMEM -> registers, + b2, GELU, dot with w3, + b3.
+//   3. layer 2 (128 -> 128) on tcgen05: A = hidden terms, B = the W2 terms, the
+//      six products whose term orders sum to at most 2 accumulated in f32 in
+//      TMEM — f32-level accuracy;
+//   4. epilogue: TMEM -> registers, + b2, GELU, dot with w3 (32 outputs per
+//      quarter), the quarters' parts added, + b3.
 #include <cmath>
 
 #include "common.cuh"
@@ -26,7 +30,7 @@ namespace idx {
 constexpr int kIn = 14;
 constexpr int kHid = 128;
 constexpr int kTile = 128;     // tokens per tile (MMA M)
-constexpr int kThreads = 256;  // 128 tokens x 2 halves
+constexpr int kThreads = 512;  // 128 tokens x 4 quarters
 constexpr int kMaxHkv = 16;
 // packed global layout (floats): [w1 (128,14) | b1 | w2^T (in 128, out 128) | b2 | w3 | b3]
 constexpr int kGW1 = 0;
@@ -35,6 +39,13 @@ constexpr int kGW2T = kGB1 + kHid;
 constexpr int kGB2 = kGW2T + kHid * kHid;
 constexpr int kGW3 = kGB2 + kHid;
 constexpr int kGB3 = kGW3 + kHid;
+constexpr int kGFloats = kGB3 + 1;
+// after the f32 block, at a 1024-byte boundary: the W2 image (three bf16 terms
+// of the (out, in) K-major SW128 operand), written by core_prepare_indexer_mlp
+constexpr uint32_t kGImageOff = ((uint32_t)kGFloats * 4u + 1023u) & ~1023u;
+// word kGFloats holds this tag once the image is written: a packed buffer
+// without it is refused by the kernel instead of read past its end
+constexpr uint32_t kImageTag = 0x32574958u;
 // shared memory, from a 1024-byte aligned base
 constexpr uint32_t kTermBytes = kTile * kHid * 2;  // one bf16 term: two K atoms of 16 KB
 constexpr uint32_t kOffW = 0;                      // W2 terms (out, in), B operand
@@ -47,10 +58,12 @@ constexpr int kFB2 = kFB1 + kHid;
 constexpr int kFW3 = kFB2 + kHid;
 constexpr int kFB3 = kFW3 + kHid;                  // 4 floats
 constexpr int kFHs = kFB3 + 4;                     // per-head value energies [128][kMaxHkv]
-constexpr int kFPart = kFHs + kTile * kMaxHkv;     // half-1 partial scores [128]
-constexpr int kFFloats = kFPart + kTile;
+constexpr int kFPart = kFHs + kTile * kMaxHkv;     // quarters 1-3 partial scores [3][128]
+constexpr int kFFloats = kFPart + 3 * kTile;
 constexpr uint32_t kOffBar = kOffF + 4u * kFFloats;
-constexpr uint32_t kSmemBytes = kOffBar + 64 + 1024;  // + barrier, TMEM slot, alignment slack
+constexpr uint32_t kSmemBytes = kOffBar + 64 + 1024;  // + barriers, TMEM slot, alignment slack
+constexpr uint32_t kImageBytes = 3 * kTermBytes;
+constexpr size_t kPackedBytes = (size_t)kGImageOff + kImageBytes;
 static_assert(kSmemBytes <= 227u * 1024u, "shared memory budget");
 
 __device__ __forceinline__ float gelu(float x) {
@@ -106,21 +119,49 @@ struct Params {
   DeviceStatus* status;
 };
 
+// The W2 image of core_prepare_indexer_mlp: unit (o, c) = output row o, input
+// columns [8 c, 8 c + 8), split into three bf16 terms at the SW128 offset of
+// row o, K atom c / 8, chunk c % 8 in each 32 KB term.
+__global__ void indexer_w2_image_kernel(const float* __restrict__ packed, uint8_t* __restrict__ image) {
+  const int u = blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= kHid * (kHid / 8)) return;
+  const int o = u & (kHid - 1), c = u >> 7;
+  float x[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = packed[kGW2T + (8 * c + i) * kHid + o];
+  uint4 t0, t1, t2;
+  split3(x, t0, t1, t2);
+  const uint32_t off = sw128_chunk(o, c >> 3, c & 7);
+  *reinterpret_cast<uint4*>(image + off) = t0;
+  *reinterpret_cast<uint4*>(image + kTermBytes + off) = t1;
+  *reinterpret_cast<uint4*>(image + 2 * kTermBytes + off) = t2;
+  if (u == 0) reinterpret_cast<uint32_t*>(const_cast<float*>(packed))[kGFloats] = kImageTag;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     indexer_scores_kernel(const Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* sgen = smem_raw + (sbase - smem_u32(smem_raw));
   float* sf = reinterpret_cast<float*>(sgen + kOffF);
-  const uint32_t bar = sbase + kOffBar;
+  const uint32_t bar = sbase + kOffBar;        // layer-2 MMA done (one phase per tile)
+  const uint32_t bar_w2 = sbase + kOffBar + 8; // W2 image in shared memory
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + kOffBar + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + kOffBar + 24);
   const int tid = threadIdx.x, warp = tid >> 5;
   const int t = tid & (kTile - 1);  // token row of the tile == TMEM lane
-  const int half = tid >> 7;
+  const int quarter = tid >> 7;
 
   if (tid == 0) {
     mbar_init(bar, 1);
+    mbar_init(bar_w2, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -128,31 +169,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_u32(tmem_slot), 128);
     tmem_relinquish();
   }
-  // ---- once per CTA: W2 as three bf16 terms, (out, in) K-major SW128 ----
-  // unit u: output row o = u % 128, 8-column chunk c = u / 128 (coalesced reads of w2^T)
-  // all 64 values of this thread's 8 units are loaded before any is stored, so
-  // the global loads overlap
-  constexpr int kUnitsPerThread = kHid * (kHid / 8) / kThreads;
-  static_assert(kHid * (kHid / 8) % kThreads == 0, "W2 staging layout");
-  {
-    float x[kUnitsPerThread][8];
-#pragma unroll
-    for (int k = 0; k < kUnitsPerThread; ++k) {
-      const int u = tid + k * kThreads;
-      const int o = u & (kHid - 1), c = u >> 7;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[k][i] = p.mlp[kGW2T + (8 * c + i) * kHid + o];
-    }
-#pragma unroll
-    for (int k = 0; k < kUnitsPerThread; ++k) {
-      const int u = tid + k * kThreads;
-      const int o = u & (kHid - 1), c = u >> 7;
-      uint4 t0, t1, t2;
-      split3(x[k], t0, t1, t2);
-      const uint32_t off = sw128_chunk(o, c >> 3, c & 7);
-      st_shared_v4(sbase + kOffW + off, t0);
-      st_shared_v4(sbase + kOffW + kTermBytes + off, t1);
-      st_shared_v4(sbase + kOffW + 2 * kTermBytes + off, t2);
+  __syncthreads();
+  if (tid == 0) {  // the prepared W2 terms: three 32 KB bulk copies
+    if (reinterpret_cast<const uint32_t*>(p.mlp)[kGFloats] == kImageTag) {
+      mbar_arrive_expect_tx(bar_w2, kImageBytes);
+      const uint8_t* img = reinterpret_cast<const uint8_t*>(p.mlp) + kGImageOff;
+      for (int tm = 0; tm < 3; ++tm)
+        bulk_g2s(sbase + kOffW + tm * kTermBytes, img + tm * kTermBytes, kTermBytes, bar_w2);
+    } else {
+      *abort_flag = 1;
+      if (blockIdx.x == 0) record_error(p.status, CORE_ERR_INVALID_ARG, 612, 0);
     }
   }
   for (int i = tid; i < kHid * kIn; i += kThreads)
@@ -163,27 +189,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     sf[kFW3 + i] = p.mlp[kGW3 + i];
   }
   if (tid == 0) sf[kFB3] = p.mlp[kGB3];
-  fence_proxy_async_shared();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const bool have_image = *abort_flag == 0;
 
   const long long n = (long long)p.B * p.L;
   const long long n_tiles = (n + kTile - 1) / kTile;
   const float age_den = log1pf((float)(p.original_length - 1 > 1 ? p.original_length - 1 : 1));
   int iter = 0;
-  for (long long tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++iter) {
+  for (long long tile = blockIdx.x; have_image && tile < n_tiles; tile += gridDim.x, ++iter) {
     const long long gi = tile * kTile + t;
     const bool active = gi < n;
     const int b = active ? (int)(gi / p.L) : 0;
     const int i = active ? (int)(gi % p.L) : 0;
     // ---- 1. auxiliary features (features.py:886-921) ----
     if (active && p.head_sums != nullptr) {
-      for (int h = half; h < p.Hkv; h += 2)
+      for (int h = quarter; h < p.Hkv; h += 4)
         sf[kFHs + t * kMaxHkv + h] = p.head_sums[(long long)h * p.hs_stride + gi];
     } else if (active && p.vf != nullptr) {
-      for (int h = half; h < p.Hkv; h += 2) {
+      for (int h = quarter; h < p.Hkv; h += 4) {
         const float4* row =
             reinterpret_cast<const float4*>(p.vf + (((long long)b * p.Hkv + h) * p.L + i) * 128);
         float s = 0.f;
@@ -203,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         sf[kFHs + t * kMaxHkv + h] = s;
       }
     } else if (active) {
-      for (int h = half; h < p.Hkv; h += 2) {
+      for (int h = quarter; h < p.Hkv; h += 4) {
         const uint4* row =
             reinterpret_cast<const uint4*>(p.v + (((long long)b * p.Hkv + h) * p.L + i) * 128);
         uint4 w[16];  // the whole 256-byte row in flight at once
@@ -230,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < p.Hkv; ++h) hsum += sf[kFHs + t * kMaxHkv + h];
       const long long pos = p.positions[gi];
       const int T = p.original_length;
-      if (half == 0 && (pos < 0 || pos >= T)) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
+      if (quarter == 0 && (pos < 0 || pos >= T)) record_error(p.status, CORE_ERR_INVALID_ARG, 601, i);
       const float a_age = log1pf((float)(T - 1 - pos)) / age_den;
       bool sink = pos < p.n_sink;
       if (p.special != nullptr && p.special[gi]) sink = true;
@@ -248,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       x[11] = sink ? 1.0f : 0.0f;
       x[12] = a_value;
       x[13] = p.is_prefill ? 0.0f : 1.0f;
-      if (half == 0) {
+      if (quarter == 0) {
 #pragma unroll
         for (int k = 10; k < kIn; ++k) f[k] = x[k];
         bool finite = true;
@@ -260,13 +286,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int k = 0; k < kIn; ++k) x[k] = 0.f;
     }
-    // ---- 2. layer 1: hidden units [64 half, 64 half + 64) as three bf16 terms ----
+    // ---- 2. layer 1: hidden units [32 q, 32 q + 32) as three bf16 terms ----
 #pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 0; c < 4; ++c) {
       float hv[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const int k = 64 * half + 8 * c + e;
+        const int k = 32 * quarter + 8 * c + e;
         const float4* w1 = reinterpret_cast<const float4*>(sf + kFW1 + k * kW1Stride);
         const float4 a0 = w1[0], a1 = w1[1], a2 = w1[2], a3 = w1[3];
         float acc = 0.f;
@@ -288,7 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint4 t0, t1, t2;
       split3(hv, t0, t1, t2);
-      const uint32_t off = sw128_chunk(t, half, c);
+      // hidden 32 q + 8 c: K atom q / 2, chunk 4 (q % 2) + c
+      const uint32_t off = sw128_chunk(t, quarter >> 1, 4 * (quarter & 1) + c);
       st_shared_v4(sbase + kOffH + off, t0);
       st_shared_v4(sbase + kOffH + kTermBytes + off, t1);
       st_shared_v4(sbase + kOffH + 2 * kTermBytes + off, t2);
@@ -297,43 +324,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     // ---- 3. layer 2 on tcgen05: sum of hidden-term x weight-term products of order <= 2 ----
+    bool ok = true;
     if (tid == 0) {
+      if (iter == 0) ok = bounded_wait(bar_w2, 0, abort_flag, p.status, 611);
       tc_fence_after();
       constexpr uint32_t idesc = idesc_bf16(kTile, kHid, 0, 0);
       constexpr int kTa[6] = {2, 1, 0, 1, 0, 0};  // small products first
       constexpr int kTb[6] = {0, 1, 2, 0, 1, 0};
+      if (ok) {
 #pragma unroll
-      for (int pi = 0; pi < 6; ++pi) {
+        for (int pi = 0; pi < 6; ++pi) {
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t koff = (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u;
-          const uint64_t a = sdesc_kmajor(sbase + kOffH + (uint32_t)kTa[pi] * kTermBytes + koff);
-          const uint64_t bd = sdesc_kmajor(sbase + kOffW + (uint32_t)kTb[pi] * kTermBytes + koff);
-          mma_bf16(tmem, a, bd, idesc, (pi > 0 || ks > 0) ? 1u : 0u);
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t koff = (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u;
+            const uint64_t a = sdesc_kmajor(sbase + kOffH + (uint32_t)kTa[pi] * kTermBytes + koff);
+            const uint64_t bd = sdesc_kmajor(sbase + kOffW + (uint32_t)kTb[pi] * kTermBytes + koff);
+            mma_bf16(tmem, a, bd, idesc, (pi > 0 || ks > 0) ? 1u : 0u);
+          }
         }
+        mma_commit(bar);
       }
-      mma_commit(bar);
     }
-    bool ok = bounded_wait(bar, (uint32_t)(iter & 1), abort_flag, p.status, 610);
+    ok = __syncthreads_and(ok);
+    if (ok) ok = bounded_wait(bar, (uint32_t)(iter & 1), abort_flag, p.status, 610);
     ok = __syncthreads_and(ok);
     if (!ok) break;
     tc_fence_after();
-    // ---- 4. epilogue: outputs [64 half, 64 half + 64) of token t ----
+    // ---- 4. epilogue: outputs [32 q, 32 q + 32) of token t ----
     float part = 0.f;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
+    {
       float v[32];
-      tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(64 * half + 32 * q), v);
+      tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(32 * quarter), v);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const int o = 64 * half + 32 * q + j;
+        const int o = 32 * quarter + j;
         part = fmaf(sf[kFW3 + o], gelu(v[j] + sf[kFB2 + o]), part);
       }
     }
-    if (half == 1) sf[kFPart + t] = part;
+    if (quarter > 0) sf[kFPart + (quarter - 1) * kTile + t] = part;
     tc_fence_before();
     __syncthreads();
-    if (half == 0 && active) p.scores[gi] = (part + sf[kFPart + t]) + sf[kFB3];
+    if (quarter == 0 && active)
+      p.scores[gi] = ((part + sf[kFPart + t]) + (sf[kFPart + kTile + t] + sf[kFPart + 2 * kTile + t])) +
+                     sf[kFB3];
   }
   tc_fence_before();
   __syncthreads();
@@ -377,6 +410,19 @@ __global__ void value_head_sums_kernel(const __nv_bfloat16* __restrict__ v, int 
 
 using namespace core;
 using namespace core::idx;
+
+extern "C" size_t core_indexer_mlp_bytes(void) { return kPackedBytes; }
+
+extern "C" int core_prepare_indexer_mlp(float* mlp, void* stream) {
+  if (mlp == nullptr) return set_error(CORE_ERR_INVALID_ARG, "core_prepare_indexer_mlp: NULL buffer");
+  if (reinterpret_cast<uintptr_t>(mlp) % 16 != 0)
+    return set_error(CORE_ERR_INVALID_ARG, "core_prepare_indexer_mlp: buffer must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  constexpr int units = kHid * (kHid / 8);
+  indexer_w2_image_kernel<<<units / 128, 128, 0, s>>>(mlp, reinterpret_cast<uint8_t*>(mlp) + kGImageOff);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? CORE_OK : cuda_error(e, "indexer_w2_image_kernel launch");
+}
 
 extern "C" int core_indexer_scores(const core_dims_t* d, const void* v, const int64_t* positions,
                                    const uint8_t* special, int32_t original_length,

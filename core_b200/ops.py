@@ -162,11 +162,19 @@ def coverage_features(k: torch.Tensor, geometry_ext: torch.Tensor, prototypes: t
 
 
 def pack_mlp(mlp_params) -> torch.Tensor:
-    """[w1 (128,14) | b1 | w2^T (in 128, out 128) | b2 | w3 (128) | b3] as one f32
-    vector (nn.Linear weights are (out, in); layer 2 is stored transposed)."""
+    """The prepared indexer MLP of ``core_prepare_indexer_mlp``: [w1 (128,14) | b1 |
+    w2^T (in 128, out 128) | b2 | w3 (128) | b3] as f32 (nn.Linear weights are
+    (out, in); layer 2 is stored transposed), followed on the device by layer 2's
+    three-term bf16 tensor-core image."""
     w1, b1, w2, b2, w3, b3 = mlp_params
-    return torch.cat([w1.reshape(-1), b1.reshape(-1), w2.t().reshape(-1), b2.reshape(-1),
-                      w3.reshape(-1), b3.reshape(-1)]).to(torch.float32).contiguous()
+    flat = torch.cat([w1.reshape(-1), b1.reshape(-1), w2.t().reshape(-1), b2.reshape(-1),
+                      w3.reshape(-1), b3.reshape(-1)]).to(torch.float32)
+    _require_cuda(flat)
+    lib = _lib.load()
+    out = torch.zeros(lib.core_indexer_mlp_bytes() // 4, dtype=torch.float32, device=flat.device)
+    out[:flat.numel()] = flat
+    check(lib.core_prepare_indexer_mlp(_ptr(out), _stream(out.device)))
+    return out
 
 
 def indexer_scores(v: torch.Tensor, positions: torch.Tensor, features: torch.Tensor,

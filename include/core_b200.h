@@ -129,10 +129,23 @@ int core_prepare_geometry(const float* geometry, const float* hadamard, int32_t 
  *   special    : optional (B, L) uint8, 1 where the token id is a special id
  *   features   : (B, L, 14) f32; columns 0..9 already hold f1..f6 and the
  *                coverage features; columns 10..13 are written here
- *   mlp        : packed f32, 16-byte aligned: [w1 (128 out,14 in) | b1 (128) |
- *                w2 transposed (128 in,128 out) | b2 (128) | w3 (128) | b3 (1)]
+ *   mlp        : a prepared indexer MLP (core_prepare_indexer_mlp), 16-byte
+ *                aligned; an unprepared buffer fails with CORE_ERR_INVALID_ARG
+ *                (device status site 612) and leaves scores unwritten
  *   scores     : (B, L) f32
  * ------------------------------------------------------------------------- */
+/* Bytes of a prepared indexer MLP buffer (173056). */
+size_t core_indexer_mlp_bytes(void);
+/* Prepare an indexer MLP in place.  `mlp` (16-byte aligned, device memory,
+ * core_indexer_mlp_bytes() bytes) holds in its first 18561 floats
+ *   [w1 (128 out,14 in) | b1 (128) | w2 transposed (128 in,128 out) | b2 (128) |
+ *    w3 (128) | b3 (1)];
+ * this writes, behind them at byte 74752, layer 2's weights split into three
+ * bf16 terms (w = t0 + t1 + t2 to f32 precision) in the swizzled K-major
+ * layout of a tensor-core operand, and a tag the scoring kernels check.  Done
+ * once per set of weights (the reference's COREIndexerMLP parameters,
+ * core/indexer.py:88-108); no reference counterpart as a call. */
+int core_prepare_indexer_mlp(float* mlp, void* stream);
 int core_indexer_scores(const core_dims_t* dims, const void* v, const int64_t* positions,
                         const uint8_t* special, int32_t original_length, int32_t is_prefill,
                         int32_t n_sink, float* features, const float* mlp, float* scores,
@@ -245,7 +258,7 @@ int core_memory_readout_noalloc(const core_dims_t* dims, int32_t q_len, const vo
 typedef struct core_layer_weights {
   const void* geometry_ext;   /* (3, 128, Hkv*d) bf16 from core_prepare_geometry */
   const float* prototypes;    /* (64, 64) f32 */
-  const float* mlp;           /* packed indexer MLP (see core_indexer_scores) */
+  const float* mlp;           /* prepared indexer MLP (core_prepare_indexer_mlp) */
   const void* theta_split;    /* as core_memory_write's (by dims.dtype), or NULL: no write */
   int32_t d_mem;
 } core_layer_weights_t;
