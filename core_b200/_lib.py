@@ -120,6 +120,7 @@ SIGNATURES = {
                                                   _P, _P, _P, _S, _P]),
     "core_rope_queries": (ctypes.c_int, [_I, _I, _I, _I, _I, _P, ctypes.c_int64, _P, _P, _F, _P,
                                          _P, _I, _P, _P]),
+    "core_attention_prefill": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P, _P, _P, _F, _P]),
     "core_compress_layer_workspace_bytes": (_S, [_D, _I, _I]),
     "core_compress_layer": (ctypes.c_int, [_D, _P, _P, _P, _P, _P, _P,
                                            ctypes.POINTER(CoreLayerWeights),

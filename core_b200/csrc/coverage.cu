@@ -133,7 +133,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (long long u = u0; u < u1 && ok; ++u) {
         const int b = (int)(u / p.n_tiles), tile = (int)(u % p.n_tiles);
-        for (int h = 0; h < p.Hkv && ok; ++h) {
+        for (int hi = 0; hi < p.Hkv && ok; ++hi) {
+          // each token tile starts at its own head, so that the CTAs stream
+          // different W_ext tiles at any moment rather than the same lines of
+          // L2 (the order depends on the tile only, not on the grid)
+          const int h = (hi + tile) % p.Hkv;
           for (int ka = 0; ka < 2; ++ka, ++it) {
             const int st = it % kStages;
             if (it >= kStages && !(ok = wait(bar_empty(st), ((it / kStages) - 1) & 1, 301))) break;

@@ -79,6 +79,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                    const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  return make_tmap_16bit(map, base, rank, dims, strides_bytes, box, swizzle128, false);
+}
+
+int make_tmap_16bit(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128,
+                    bool f16) {
   auto enc = get_encode();
   if (enc == nullptr) return set_error(CORE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if (!aligned16(base)) return set_error(CORE_ERR_INVALID_ARG, "TMA base pointer not 16-byte aligned");
@@ -96,7 +102,8 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
       gstride[i - 1] = strides_bytes[i - 1];
     }
   }
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base),
+  CUresult r = enc(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   (cuuint32_t)rank, const_cast<void*>(base),
                    gdim, gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

@@ -29,6 +29,10 @@ int sm_count();
 // swizzle128: 128-byte swizzle (inner box must then be 64 bf16).
 int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                    const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128);
+// The same for bf16 (f16 = false) or f16 elements.
+int make_tmap_16bit(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128,
+                    bool f16);
 
 // Bump allocator over a caller-provided workspace (256-byte aligned pieces).
 struct Carver {

@@ -31,9 +31,6 @@ constexpr int kTok = 128;         // evicted tokens per phi unit (MMA N)
 constexpr int kProdThreads = 128; // 4 gathering warps
 constexpr int kMbarChunk = 64;    // tokens per M_bar K chunk
 
-__device__ __forceinline__ void st_shared_zero16(uint32_t dst) {
-  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
-}
 
 // ===========================================================================
 // softmax mass
@@ -267,9 +264,17 @@ constexpr uint32_t kPhiA = 2u * kPhiRows * 128;  // 32 KB: two Theta terms x 128
 constexpr uint32_t kPhiB = kTok * 128;           // 16 KB: 128 tokens x 64 columns
 constexpr uint32_t kPhiStage = kPhiA + kPhiB;
 constexpr int kPhiStages = 4;
-constexpr int kPhiLag = 2;  // gather groups in flight per producer thread (two stages of MMA slack)
 constexpr int kPhiThreads = 512;         // warps 0-3 gather, 4 MMA, 8-15 epilogue
 constexpr uint32_t kPhiSmem = kPhiStages * kPhiStage + 2 * kTok * 4 + 256 + 1024;
+
+// K chunk processed at step ci of a unit of token tile et: each token tile
+// starts at its own chunk, so that the CTAs stream different Theta tiles at
+// any moment instead of all reading the same 32 KB from the same L2 lines.
+// The order depends on the tile only, not on the grid.
+__device__ __forceinline__ int phi_chunk(int ci, int et, int n) {
+  const int c = ci + et % n;
+  return c < n ? c : c - n;
+}
 
 __global__ void __launch_bounds__(kPhiThreads, 1)
     mw_phi_kernel(const __grid_constant__ CUtensorMap tmT, const PhiParams p) {
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPhiStages; ++s) {
-      mbar_init(bar_full(s), 1 + kProdThreads / 32);  // TMA expect_tx + 4 gather warps
+      mbar_init(bar_full(s), 1 + kProdThreads);  // TMA expect_tx + every gathering thread
       mbar_init(bar_empty(s), 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -338,7 +343,8 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
                            : -1;
         toks[i] = (unsigned)ix < (unsigned)p.L ? ix : -1;
       }
-      for (int c = 0; c < n_chunks && ok; ++c, ++it) {
+      for (int ci = 0; ci < n_chunks && ok; ++ci, ++it) {
+        const int c = phi_chunk(ci, et, n_chunks);
         const int st = it % kPhiStages;
         if (it >= kPhiStages && !(ok = wait(bar_empty(st), ((it / kPhiStages) - 1) & 1, 901))) break;
         const uint32_t s_base = sbase + st * kPhiStage;
@@ -348,32 +354,23 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
             tma_load_3d(s_base + t * (kPhiRows * 128u), &tmT, bar_full(st), c * 64, dt * kPhiRows, t);
         }
         const int h = c >> 1, e0 = (c & 1) * 64;
-        // 128 rows x 8 sixteen-byte pieces = 1024 copies, 8 per thread
+        // 128 rows x 8 sixteen-byte pieces = 1024 copies, 8 per thread; rows
+        // outside the cache are zero-filled by the same copies
 #pragma unroll
         for (int i = 0; i < kPer; ++i) {
           const int j = tid + i * kProdThreads;
           const int r = j >> 3, q = j & 7;
           const uint32_t dst = s_base + kPhiA + (uint32_t)r * 128u + (uint32_t)((q ^ (r & 7)) << 4);
-          if (toks[i] >= 0)
-            cp_async16(dst, p.k + (((long long)b * p.Hkv + h) * p.L + toks[i]) * kD + e0 + q * 8);
-          else
-            st_shared_zero16(dst);
+          const __nv_bfloat16* src =
+              toks[i] >= 0 ? p.k + (((long long)b * p.Hkv + h) * p.L + toks[i]) * kD + e0 + q * 8 : p.k;
+          cp_async16_zfill(dst, src, toks[i] >= 0);
         }
-        cp_async_commit();
-        // kPhiLag gather groups stay in flight: publish the oldest one
-        if (it >= kPhiLag) {
-          cp_async_wait_group<kPhiLag>();
-          fence_proxy_async_shared();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_full((it - kPhiLag) % kPhiStages));
-        }
+        // the stage fills when every producer's copies have landed; the thread
+        // goes on to the next stage without waiting for them
+        cp_async_mbar_arrive(bar_full(st));
       }
     }
     cp_async_wait_all();
-    fence_proxy_async_shared();
-    __syncwarp();
-    if (ok && lane == 0)
-      for (int j = it > kPhiLag ? it - kPhiLag : 0; j < it; ++j) mbar_arrive(bar_full(j % kPhiStages));
   } else if (warp == 4) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(kPhiRows, kTok, 0, 0);
@@ -384,16 +381,17 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
         if (sub >= 2 && !(ok = wait(bar_tempty(buf), (n - 1) & 1, 902))) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * kTok);
-        for (int c = 0; c < n_chunks && ok; ++c, ++it) {
+        for (int ci = 0; ci < n_chunks && ok; ++ci, ++it) {
           const int st = it % kPhiStages;
           if (!(ok = wait(bar_full(st), (it / kPhiStages) & 1, 903))) break;
+          fence_proxy_async_shared();  // gathered rows (cp.async) before the MMA reads them
           tc_fence_after();
           const uint32_t s_base = sbase + st * kPhiStage;
           for (int ks = 0; ks < 4; ++ks) {
             const uint64_t bd = sdesc_kmajor(s_base + kPhiA + (uint32_t)ks * 32u);
             for (int t = 0; t < 2; ++t) {
               const uint64_t a = sdesc_kmajor(s_base + (uint32_t)t * kPhiRows * 128u + (uint32_t)ks * 32u);
-              mma_bf16(d, a, bd, idesc, (c > 0 || ks > 0 || t > 0) ? 1u : 0u);
+              mma_bf16(d, a, bd, idesc, (ci > 0 || ks > 0 || t > 0) ? 1u : 0u);
             }
           }
           mma_commit(bar_empty(st));
@@ -482,7 +480,6 @@ constexpr uint32_t kMbA = 2u * 128 * 128;           // two terms x 128 rows x 64
 constexpr uint32_t kMbBMax = 4u * kMbarChunk * 128; // up to 4 MN atoms x 64 token rows x 128 B
 constexpr uint32_t kMbStage = kMbA + kMbBMax;       // 64 KB
 constexpr int kMbStages = 3;
-constexpr int kMbLag = 1;  // gather groups in flight per producer thread (two stages of MMA slack)
 constexpr int kMbThreads = 384;  // warps 0-3 gather, 4 MMA, 8-11 epilogue
 
 // CT = value columns per output tile (256, or 128 when Hkv*d is an odd
@@ -513,7 +510,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMbStages; ++s) {
-      mbar_init(bar_full(s), 1 + kProdThreads / 32);
+      mbar_init(bar_full(s), 1 + kProdThreads);  // TMA expect_tx + every gathering thread
       mbar_init(bar_empty(s), 1);
     }
     mbar_init(bar_done, 1);
@@ -536,7 +533,6 @@ __global__ void __launch_bounds__(kMbThreads, 1)
   if (warp < 4) {
     const int tid = threadIdx.x;
     bool ok = true;
-    int last = 0;  // stages issued
     for (int kc = kc0, it = 0; kc < kc1 && ok; ++kc, ++it) {
       const int st = it % kMbStages;
       // token indices of this chunk, loaded before waiting for the stage
@@ -556,36 +552,22 @@ __global__ void __launch_bounds__(kMbThreads, 1)
           tma_load_2d(base + t * (128u * 128u), &tmW, bar_full(st), kc * kMbarChunk,
                       t * p.d_pad + jt * 128);
       }
-      // 64 token rows x kAtoms MN atoms x 8 pieces
+      // 64 token rows x kAtoms MN atoms x 8 pieces (rows outside the cache zero-filled)
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
         const int j = tid + i * kProdThreads;
         const int r = j / (kAtoms * 8), a = (j >> 3) % kAtoms, q = j & 7;
         const uint32_t dst = base + kMbA + (uint32_t)a * (kMbarChunk * 128u) + (uint32_t)r * 128u +
                              (uint32_t)((q ^ (r & 7)) << 4);
-        if (toks[i] >= 0) {
-          const int col = ct * CT + a * 64 + q * 8;  // column of the (Hkv*d) value row
-          const int h = col >> 7, e = col & 127;
-          cp_async16(dst, p.v + ((long long)h * p.L + toks[i]) * kD + e);
-        } else {
-          st_shared_zero16(dst);
-        }
+        const int col = ct * CT + a * 64 + q * 8;  // column of the (Hkv*d) value row
+        const int h = col >> 7, e = col & 127;
+        const __nv_bfloat16* src = toks[i] >= 0 ? p.v + ((long long)h * p.L + toks[i]) * kD + e : p.v;
+        cp_async16_zfill(dst, src, toks[i] >= 0);
       }
-      cp_async_commit();
-      // kMbLag gather groups stay in flight: publish the oldest one
-      if (it >= kMbLag) {
-        cp_async_wait_group<kMbLag>();
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_full((it - kMbLag) % kMbStages));
-      }
-      last = it + 1;
+      // the stage fills when every producer's copies have landed (no wait here)
+      cp_async_mbar_arrive(bar_full(st));
     }
     cp_async_wait_all();
-    fence_proxy_async_shared();
-    __syncwarp();
-    if (ok && lane == 0)
-      for (int j = last > kMbLag ? last - kMbLag : 0; j < last; ++j) mbar_arrive(bar_full(j % kMbStages));
   } else if (warp == 4) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(128, CT, 0, 1);
@@ -593,6 +575,7 @@ __global__ void __launch_bounds__(kMbThreads, 1)
       for (int kc = kc0, it = 0; kc < kc1 && ok; ++kc, ++it) {
         const int st = it % kMbStages;
         if (!(ok = wait(bar_full(st), (it / kMbStages) & 1, 912))) break;
+        fence_proxy_async_shared();  // gathered rows (cp.async) before the MMA reads them
         tc_fence_after();
         const uint32_t base = sbase + st * kMbStage;
         for (int ks = 0; ks < 4; ++ks) {

@@ -118,6 +118,48 @@ def qk_features(q: torch.Tensor, k: torch.Tensor, *, topk_qk: int = 4,
     return features, lse_out
 
 
+_ATTN_DTYPES = {torch.bfloat16: _lib.CORE_DTYPE_BF16, torch.float16: _lib.CORE_DTYPE_F16}
+
+
+def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                      softmax_scale: float | None = None, out: torch.Tensor | None = None):
+    """Causal attention with the row LSE (``flash_attn_func(..., causal=True,
+    return_attn_probs=True)`` as ``_core_flash_attention_forward`` calls it).
+
+    q: (B, Hq, Lq, 128), k, v: (B, Hkv, Lk, 128), bf16 or f16, any strides with
+    the head dim contiguous (the layout an HF attention module passes).
+    Returns (out (B, Lq, Hq, 128) in q's dtype, lse (B, Hq, Lq) f32).
+    """
+    _require_cuda(q, k, v)
+    if q.dtype not in _ATTN_DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise TypeError("attention_prefill takes q, k, v of one dtype, bfloat16 or float16")
+    B, Hq, Lq, d = q.shape
+    _, Hkv, Lk, _ = k.shape
+    if d != HEAD_DIM or k.shape[-1] != HEAD_DIM or v.shape != k.shape or k.shape[0] != B:
+        raise ValueError("attention_prefill: head_dim 128 and matching batch / K, V shapes")
+
+    def inner(t):
+        # the head dim must be contiguous and every other stride 16-byte aligned
+        if t.stride(-1) != 1 or any(s % 8 for s in t.stride()[:-1]) or t.data_ptr() % 16:
+            t = t.contiguous()
+        return t
+
+    q, k, v = inner(q), inner(k), inner(v)
+    dims = CoreDims(B, Hq, Hkv, HEAD_DIM, Lq, Lk, _ATTN_DTYPES[q.dtype])
+    if out is None:
+        out = torch.empty(B, Lq, Hq, HEAD_DIM, dtype=q.dtype, device=q.device)
+    elif out.shape != (B, Lq, Hq, HEAD_DIM) or not out.is_contiguous() or out.dtype != q.dtype:
+        raise ValueError("out must be a contiguous (B, Lq, Hq, 128) tensor of q's dtype")
+    lse = torch.empty(B, Hq, Lq, dtype=torch.float32, device=q.device)
+    scale = HEAD_DIM ** -0.5 if softmax_scale is None else float(softmax_scale)
+    arrs = [(ctypes.c_int64 * 3)(t.stride(0), t.stride(1), t.stride(2)) for t in (q, k, v)]
+    strides = [ctypes.cast(a, ctypes.c_void_p) for a in arrs]
+    check(_lib.load().core_attention_prefill(
+        ctypes.byref(dims), _ptr(q), strides[0], _ptr(k), strides[1], _ptr(v), strides[2],
+        _ptr(out), _ptr(lse), scale, _stream(q.device)))
+    return out, lse
+
+
 def split_bf16(w: torch.Tensor, terms: int) -> torch.Tensor:
     """f32 -> (terms, *w.shape) bf16 whose sum reproduces w (hi, mid, lo)."""
     _require_cuda(w)

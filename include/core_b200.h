@@ -416,6 +416,32 @@ int core_rope_queries(int32_t batch, int32_t n_tokens, int32_t n_q_heads, int32_
                       const void* cos, const void* sin, int32_t cos_batch, void* q_out,
                       void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Causal prefill attention that also returns the row log-sum-exp.
+ * Replaces the flash_attn_func call of _core_flash_attention_forward
+ * (core/kvpress_pipeline.py:24-91: causal, no dropout, return_attn_probs for
+ * softmax_lse only), whose LSE the press reuses as the QK relation pass's row
+ * normaliser (core/kvpress_adapter.py:400-438; core/fused_qk.py:444-456):
+ * pass `lse` to core_qk_features as lse_in.
+ *   dims      : batch, n_q_heads, n_kv_heads, head_dim = 128,
+ *               n_queries = Lq, seq_len = Lk (Lq <= Lk), dtype CORE_DTYPE_BF16
+ *               or CORE_DTYPE_F16
+ *   q         : (B, Hq, Lq, d) with element strides q_strides = {b, h, t};
+ *   k, v      : (B, Hkv, Lk, d) likewise; d contiguous, every stride a
+ *               multiple of 8 elements, base pointers 16-byte aligned
+ *   out       : (B, Lq, Hq, d) contiguous, dims.dtype (the layout
+ *               flash_attn_func returns)
+ *   lse       : (B, Hq, Lq) f32, natural log of sum_k exp(scale * q.k) over
+ *               the keys the row sees (FlashAttention's softmax_lse)
+ * Query row i sees keys 0 .. i + Lk - Lq (the bottom-right causal mask of
+ * FlashAttention 2).  Scores in f32 from 16-bit inputs, P rounded to dims.dtype
+ * for the P V product, f32 accumulation, as FlashAttention computes.
+ * ------------------------------------------------------------------------- */
+int core_attention_prefill(const core_dims_t* dims, const void* q, const int64_t* q_strides,
+                           const void* k, const int64_t* k_strides, const void* v,
+                           const int64_t* v_strides, void* out, float* lse, float softmax_scale,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif

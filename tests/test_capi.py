@@ -93,3 +93,27 @@ def test_readout_workspace_covers_a_call_without_gate():
     f = lib.core_memory_readout_workspace_bytes
     assert f(ctypes.byref(dims), 1, 512, 0) == f(ctypes.byref(dims), 1, 512, 1)
     assert f(ctypes.byref(dims), 1, 512, 64) >= 4 * (512 + 64 + 8 * 128)
+
+
+def test_attention_arguments_rejected_on_host():
+    """core_attention_prefill refuses bad shapes before any CUDA call."""
+    lib = _lib.load()
+    f = lib.core_attention_prefill
+    s = (ctypes.c_int64 * 3)(1 << 20, 1 << 14, 128)
+    sp = ctypes.cast(s, ctypes.c_void_p)
+    p = ctypes.c_void_p(256)
+    dims = _lib.CoreDims(1, 8, 2, 128, 64, 64, _lib.CORE_DTYPE_BF16)
+    assert f(ctypes.byref(dims), None, sp, p, sp, p, sp, p, p, 0.08, None) == -1
+    dims = _lib.CoreDims(1, 8, 2, 64, 64, 64, _lib.CORE_DTYPE_BF16)
+    assert f(ctypes.byref(dims), p, sp, p, sp, p, sp, p, p, 0.08, None) == -2
+    assert "head_dim" in _lib.last_error()
+    dims = _lib.CoreDims(1, 8, 2, 128, 65, 64, _lib.CORE_DTYPE_BF16)  # more queries than keys
+    assert f(ctypes.byref(dims), p, sp, p, sp, p, sp, p, p, 0.08, None) == -2
+    dims = _lib.CoreDims(1, 8, 2, 128, 64, 64, _lib.CORE_DTYPE_F32)
+    assert f(ctypes.byref(dims), p, sp, p, sp, p, sp, p, p, 0.08, None) == -2
+    assert "dtype" in _lib.last_error()
+    dims = _lib.CoreDims(1, 8, 3, 128, 64, 64, _lib.CORE_DTYPE_BF16)  # 8 heads over 3 KV heads
+    assert f(ctypes.byref(dims), p, sp, p, sp, p, sp, p, p, 0.08, None) == -1
+    dims = _lib.CoreDims(1, 8, 2, 128, 64, 64, _lib.CORE_DTYPE_BF16)
+    assert f(ctypes.byref(dims), p, sp, p, sp, p, sp, p, p, -1.0, None) == -1
+    assert "softmax_scale" in _lib.last_error()
