@@ -58,7 +58,7 @@ def parse():
     p.add_argument("--d-mem", type=int, default=512)
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", default="prefill", choices=["prefill", "decode", "long"],
+    p.add_argument("--workload", default="prefill", choices=["prefill", "decode", "long", "attention"],
                    help="prefill: the headline 32-layer compression step; decode: decode-time "
                         "recompression with the memory readout")
     p.add_argument("--decode-tokens", type=int, default=512)
@@ -323,6 +323,10 @@ def main():
             dist.barrier()
             dist.destroy_process_group()
         return
+    if a.workload == "attention":
+        line = run_attention(a, dev)
+        print(json.dumps(line), flush=True)
+        return
     if a.workload == "decode":
         line = run_decode(a, dev, dist, rank)
         if rank == 0:
@@ -481,6 +485,62 @@ def main():
 # ---------------------------------------------------------------------------
 LONG_METRIC = ("KV tokens compressed/sec, one 131072-token sequence, 32 layers, "
                "KV heads sharded across GPUs")
+
+
+def measured_peaks() -> dict:
+    """The pool's measured peaks (MEASURED_PEAKS.json), empty when absent."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    return json.load(open(path)) if os.path.exists(path) else {}
+
+
+def run_attention(a, dev):
+    """The prefill attention of one layer (32 query / 8 KV heads, d = 128,
+    bf16, causal over seq_len tokens) with its row LSE, on this library's
+    kernel and on flash_attn_func (the library call of the reference's
+    attention hook) when it runs here; CUDA events, max of nothing (one GPU)."""
+    from core_b200 import ops
+    L, Hq, Hkv = a.seq_len, 32, 8
+    g = torch.Generator(device="cpu").manual_seed(5)
+    q = (torch.randn(1, Hq, L, 128, generator=g) / 128 ** 0.5).to(dev, torch.bfloat16)
+    k = (torch.randn(1, Hkv, L, 128, generator=g) / 128 ** 0.5).to(dev, torch.bfloat16)
+    v = torch.randn(1, Hkv, L, 128, generator=g).to(dev, torch.bfloat16)
+    flops = 4.0 * 128 * Hq * L * (L + 1) / 2  # QK and PV over the visible (query, key) pairs
+
+    def timed(fn):
+        for _ in range(max(a.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / a.steps
+
+    out = torch.empty(1, L, Hq, 128, dtype=torch.bfloat16, device=dev)
+    with ClockSampler(dev.index or 0) as clk:
+        ms = timed(lambda: ops.attention_prefill(q, k, v, out=out))
+    ops.status(dev)
+    peak = measured_peaks().get("bf16_tflops")
+    line = {"metric": "prefill attention with row LSE, tokens/s (one layer, 32/8 heads, d 128, causal)",
+            "value": L / (ms * 1e-3), "unit": "tokens/s", "ms_per_call": ms, "steps": a.steps,
+            "seq_len": L, "dtype": "bf16", "tflops": flops / (ms * 1e-3) / 1e12,
+            "roofline": {"bound": "tensor", "peak": peak, "unit": "TFLOP/s",
+                         "frac": (flops / (ms * 1e-3) / 1e12 / peak) if peak else None,
+                         "peak_source": "measured bf16_tflops (burst)",
+                         "algorithmic": "4 d Hq L (L+1) / 2 FLOP per call"},
+            "clocks": clk.summary()}
+    try:
+        from flash_attn import flash_attn_func
+        qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        fms = timed(lambda: flash_attn_func(qt, kt, vt, dropout_p=0.0, softmax_scale=128 ** -0.5,
+                                            causal=True, return_attn_probs=True))
+        line["flash_attn"] = {"ms_per_call": fms, "tflops": flops / (fms * 1e-3) / 1e12,
+                              "version": __import__("flash_attn").__version__}
+    except Exception as e:  # noqa: BLE001
+        line["flash_attn"] = {"unavailable": str(e)[:200]}
+    return line
 
 
 def long_config(a, n):

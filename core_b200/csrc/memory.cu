@@ -257,21 +257,24 @@ struct PhiParams {
 
 // phi^T tile: M = 128 memory rows of Theta_f (A, two bf16 terms, TMA) x N = 128
 // gathered evicted tokens (B, cp.async), K = the 1024-wide key row in 64-column
-// chunks.  TMEM lanes are memory rows, columns are tokens, so the epilogue
-// writes W^T rows with contiguous token runs and sums b_bar along its own row.
+// chunks, two chunks per pipeline stage.  TMEM lanes are memory rows, columns
+// are tokens, so the epilogue writes W^T rows with contiguous token runs and
+// sums b_bar along its own row.  A stage carries 96 KB: a stage ring pays a
+// fixed synchronisation cost per stage, so fewer, larger stages stream faster.
 constexpr int kPhiRows = 128;                    // memory rows per unit (MMA M)
+constexpr int kPhiCps = 2;                       // 64-column K chunks per stage
 constexpr uint32_t kPhiA = 2u * kPhiRows * 128;  // 32 KB: two Theta terms x 128 rows x 64 columns
 constexpr uint32_t kPhiB = kTok * 128;           // 16 KB: 128 tokens x 64 columns
-constexpr uint32_t kPhiStage = kPhiA + kPhiB;
-constexpr int kPhiStages = 4;
+constexpr uint32_t kPhiStage = kPhiCps * (kPhiA + kPhiB);  // [A c0][A c1][B c0][B c1]
+constexpr int kPhiStages = 2;
 constexpr int kPhiThreads = 512;         // warps 0-3 gather, 4 MMA, 8-15 epilogue
 constexpr uint32_t kPhiSmem = kPhiStages * kPhiStage + 2 * kTok * 4 + 256 + 1024;
 
-// K chunk processed at step ci of a unit of token tile et: each token tile
-// starts at its own chunk, so that the CTAs stream different Theta tiles at
-// any moment instead of all reading the same 32 KB from the same L2 lines.
-// The order depends on the tile only, not on the grid.
-__device__ __forceinline__ int phi_chunk(int ci, int et, int n) {
+// K chunk pair processed at step ci of a unit of token tile et: each token
+// tile starts at its own pair, so that the CTAs stream different Theta tiles
+// at any moment instead of all reading the same lines of L2.  The order
+// depends on the tile only, not on the grid.
+__device__ __forceinline__ int phi_pair(int ci, int et, int n) {
   const int c = ci + et % n;
   return c < n ? c : c - n;
 }
@@ -295,7 +298,7 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int P = gridDim.x;
   const long long u0 = (long long)blockIdx.x * p.U / P, u1 = (long long)(blockIdx.x + 1) * p.U / P;
-  const int n_chunks = p.Hkv * 2;  // 64-column K chunks of the 1024-wide key row
+  const int n_pairs = p.Hkv;  // pairs of 64-column K chunks = heads of the 1024-wide key row
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPhiStages; ++s) {
@@ -343,27 +346,33 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
                            : -1;
         toks[i] = (unsigned)ix < (unsigned)p.L ? ix : -1;
       }
-      for (int ci = 0; ci < n_chunks && ok; ++ci, ++it) {
-        const int c = phi_chunk(ci, et, n_chunks);
+      for (int ci = 0; ci < n_pairs && ok; ++ci, ++it) {
+        const int h = phi_pair(ci, et, n_pairs);  // this stage: head h, both 64-column halves
         const int st = it % kPhiStages;
         if (it >= kPhiStages && !(ok = wait(bar_empty(st), ((it / kPhiStages) - 1) & 1, 901))) break;
         const uint32_t s_base = sbase + st * kPhiStage;
         if (tid == 0) {
-          mbar_arrive_expect_tx(bar_full(st), kPhiA);
-          for (int t = 0; t < 2; ++t)
-            tma_load_3d(s_base + t * (kPhiRows * 128u), &tmT, bar_full(st), c * 64, dt * kPhiRows, t);
+          mbar_arrive_expect_tx(bar_full(st), kPhiCps * kPhiA);
+          for (int half = 0; half < kPhiCps; ++half)
+            for (int t = 0; t < 2; ++t)
+              tma_load_3d(s_base + half * kPhiA + t * (kPhiRows * 128u), &tmT, bar_full(st),
+                          (2 * h + half) * 64, dt * kPhiRows, t);
         }
-        const int h = c >> 1, e0 = (c & 1) * 64;
-        // 128 rows x 8 sixteen-byte pieces = 1024 copies, 8 per thread; rows
-        // outside the cache are zero-filled by the same copies
+        // 2 halves x 128 rows x 8 sixteen-byte pieces = 2048 copies, 16 per
+        // thread; rows outside the cache are zero-filled by the same copies
 #pragma unroll
-        for (int i = 0; i < kPer; ++i) {
-          const int j = tid + i * kProdThreads;
-          const int r = j >> 3, q = j & 7;
-          const uint32_t dst = s_base + kPhiA + (uint32_t)r * 128u + (uint32_t)((q ^ (r & 7)) << 4);
-          const __nv_bfloat16* src =
-              toks[i] >= 0 ? p.k + (((long long)b * p.Hkv + h) * p.L + toks[i]) * kD + e0 + q * 8 : p.k;
-          cp_async16_zfill(dst, src, toks[i] >= 0);
+        for (int half = 0; half < kPhiCps; ++half) {
+#pragma unroll
+          for (int i = 0; i < kPer; ++i) {
+            const int j = tid + i * kProdThreads;
+            const int r = j >> 3, q = j & 7;
+            const uint32_t dst = s_base + kPhiCps * kPhiA + half * kPhiB + (uint32_t)r * 128u +
+                                 (uint32_t)((q ^ (r & 7)) << 4);
+            const __nv_bfloat16* src =
+                toks[i] >= 0 ? p.k + (((long long)b * p.Hkv + h) * p.L + toks[i]) * kD + half * 64 + q * 8
+                             : p.k;
+            cp_async16_zfill(dst, src, toks[i] >= 0);
+          }
         }
         // the stage fills when every producer's copies have landed; the thread
         // goes on to the next stage without waiting for them
@@ -381,17 +390,20 @@ __global__ void __launch_bounds__(kPhiThreads, 1)
         if (sub >= 2 && !(ok = wait(bar_tempty(buf), (n - 1) & 1, 902))) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * kTok);
-        for (int ci = 0; ci < n_chunks && ok; ++ci, ++it) {
+        for (int ci = 0; ci < n_pairs && ok; ++ci, ++it) {
           const int st = it % kPhiStages;
           if (!(ok = wait(bar_full(st), (it / kPhiStages) & 1, 903))) break;
           fence_proxy_async_shared();  // gathered rows (cp.async) before the MMA reads them
           tc_fence_after();
           const uint32_t s_base = sbase + st * kPhiStage;
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t bd = sdesc_kmajor(s_base + kPhiA + (uint32_t)ks * 32u);
-            for (int t = 0; t < 2; ++t) {
-              const uint64_t a = sdesc_kmajor(s_base + (uint32_t)t * kPhiRows * 128u + (uint32_t)ks * 32u);
-              mma_bf16(d, a, bd, idesc, (ci > 0 || ks > 0 || t > 0) ? 1u : 0u);
+          for (int half = 0; half < kPhiCps; ++half) {
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t bd = sdesc_kmajor(s_base + kPhiCps * kPhiA + half * kPhiB + (uint32_t)ks * 32u);
+              for (int t = 0; t < 2; ++t) {
+                const uint64_t a = sdesc_kmajor(s_base + half * kPhiA + (uint32_t)t * kPhiRows * 128u +
+                                                (uint32_t)ks * 32u);
+                mma_bf16(d, a, bd, idesc, (ci > 0 || half > 0 || ks > 0 || t > 0) ? 1u : 0u);
+              }
             }
           }
           mma_commit(bar_empty(st));
@@ -533,17 +545,26 @@ __global__ void __launch_bounds__(kMbThreads, 1)
   if (warp < 4) {
     const int tid = threadIdx.x;
     bool ok = true;
-    for (int kc = kc0, it = 0; kc < kc1 && ok; ++kc, ++it) {
-      const int st = it % kMbStages;
-      // token indices of this chunk, loaded before waiting for the stage
-      constexpr int kPer = kMbarChunk * kAtoms * 8 / kProdThreads;
-      int toks[kPer];
+    constexpr int kPer = kMbarChunk * kAtoms * 8 / kProdThreads;
+    // token indices of chunk kc (the rows this thread gathers); the loads of
+    // the next chunk's indices are issued one chunk ahead, so their latency
+    // overlaps the current chunk instead of stalling every chunk
+    auto load_idx = [&](int kc, int (&dst)[kPer]) {
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
         const int kidx = kc * kMbarChunk + (tid + i * kProdThreads) / (kAtoms * 8);
-        const int ix = kidx < p.n_evict ? (p.evict != nullptr ? p.evict[kidx] : kidx) : -1;
-        toks[i] = (unsigned)ix < (unsigned)p.L ? ix : -1;  // outside the cache: zero row
+        dst[i] = kidx < p.n_evict ? (p.evict != nullptr ? p.evict[kidx] : kidx) : -1;
       }
+    };
+    int nxt[kPer];
+    if (kc0 < kc1) load_idx(kc0, nxt);
+    for (int kc = kc0, it = 0; kc < kc1 && ok; ++kc, ++it) {
+      const int st = it % kMbStages;
+      int toks[kPer];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        toks[i] = (unsigned)nxt[i] < (unsigned)p.L ? nxt[i] : -1;  // outside the cache: zero row
+      if (kc + 1 < kc1) load_idx(kc + 1, nxt);
       if (it >= kMbStages && !(ok = wait(bar_empty(st), ((it / kMbStages) - 1) & 1, 911))) break;
       const uint32_t base = sbase + st * kMbStage;
       if (tid == 0) {
