@@ -74,6 +74,10 @@ def parse():
                    help="timed steps of the long-context step (131072 tokens, 512 queries, r=0.9; "
                         "head-sharded over the ranks) reported as long_context in the headline "
                         "line; 0 leaves it out")
+    p.add_argument("--batched-steps", type=int, default=3,
+                   help="timed steps of batched serving (8 sequences x 32768 tokens, r=0.75, "
+                        "32 layers, split over the ranks: 8/N sequences per rank) reported as "
+                        "batched_serving in the headline line; 0 leaves it out")
     p.add_argument("--sm-reserve", type=int, default=2,
                    help="SMs the persistent grids leave free for the other streams' kernels")
     a = p.parse_args()
@@ -295,46 +299,12 @@ def build_layers(a, dev, seed_base=1000):
     return parts, layers
 
 
-def main():
-    a = parse()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if a.impl == "reference":
-        run_reference(a, rank)
-        return
-    dist = None
-    if world > 1 or (a.workload == "long" and a.sharded):
-        import datetime
-
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    n = world
+def run_prefill_steps(a, dev, dist, rank, local):
+    """Build the synthetic 32-layer cache of this rank and time a.steps
+    compression steps (one step = all layers, a.batch sequences of a.seq_len
+    tokens), CUDA-graph replay unless a.graph is off.  Returns the timings and
+    the built inputs (the end-to-end leg reuses them)."""
     from core_b200 import engine, ops
-
-    if a.workload == "long":
-        line = run_long(a, dev, dist, rank, world)
-        if rank == 0:
-            print(json.dumps(line), flush=True)
-        if dist is not None:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
-    if a.workload == "attention":
-        line = run_attention(a, dev)
-        print(json.dumps(line), flush=True)
-        return
-    if a.workload == "decode":
-        line = run_decode(a, dev, dist, rank)
-        if rank == 0:
-            print(json.dumps(line), flush=True)
-        if dist is not None:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
     parts, layers = build_layers(a, dev, seed_base=rank_seed(rank))
     L = a.seq_len
     n_kept = engine.n_kept_for(L, a.ratio, 4)
@@ -416,6 +386,56 @@ def main():
         del graph
         torch.cuda.synchronize()
     ops.status(dev)
+    return dict(ms=ms, relation_ms=relation_ms, host_ms=host_ms, clocks=clocks,
+                graph_note=graph_note, parts=parts, layers=layers, ws=ws)
+
+
+def main():
+    a = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference(a, rank)
+        return
+    dist = None
+    if world > 1 or (a.workload == "long" and a.sharded):
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n = world
+    from core_b200 import engine, ops
+
+    if a.workload == "long":
+        line = run_long(a, dev, dist, rank, world)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    if a.workload == "attention":
+        line = run_attention(a, dev)
+        print(json.dumps(line), flush=True)
+        return
+    if a.workload == "decode":
+        line = run_decode(a, dev, dist, rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    r = run_prefill_steps(a, dev, dist, rank, local)
+    ms, relation_ms, host_ms, clocks, graph_note = (r["ms"], r["relation_ms"], r["host_ms"],
+                                                    r["clocks"], r["graph_note"])
+    parts, layers, ws = r["parts"], r["layers"], r["ws"]
+    del r
+    L = a.seq_len
     ms = max_over_ranks(ms, dist, dev)
     value = whole_job_rate(n, a.batch * L, ms / 1e3)
 
@@ -460,6 +480,29 @@ def main():
                                 "NCCL for the cross-head exchanges, each layer's memory write on "
                                 "rank l mod N); its own timed region, max over ranks")
 
+    # ---- batched serving on the same ranks: 8 x 32768 tokens split by sequence ----
+    batched = None
+    if a.batched_steps > 0 and 8 % n == 0:
+        layers = parts = ws = None  # the headline's inputs
+        torch.cuda.empty_cache()
+        ba = argparse.Namespace(**vars(a))
+        ba.batch, ba.seq_len, ba.n_queries, ba.ratio = 8 // n, 32768, 128, 0.75
+        ba.steps, ba.warmup = a.batched_steps, max(3, a.warmup)
+        br = run_prefill_steps(ba, dev, dist, rank, local)
+        bms = max_over_ranks(br["ms"], dist, dev)
+        del br["layers"], br["parts"], br["ws"]
+        torch.cuda.empty_cache()
+        batched = {"metric": "KV tokens compressed/sec, batched serving: 8 sequences x 32768 tokens, "
+                             "32 layers, split by sequence over the GPUs",
+                   "value": whole_job_rate(n, ba.batch * ba.seq_len, bms / 1e3), "unit": UNIT,
+                   "n_gpus": n, "steps": ba.steps, "warmup": ba.warmup, "ms_per_step": bms,
+                   "scaling": "strong", "config": config_dict(ba, n),
+                   "gpu_launches": KERNELS_PER_LAYER * ba.layers * ba.steps,
+                   "clocks": br["clocks"].summary(),
+                   "note": "8 sequences in all, 8/N per rank, each rank its own sequences and "
+                           "memory state (no collective on the data path); its own timed region, "
+                           "max over ranks"}
+
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -468,6 +511,8 @@ def main():
             "host_issue_ms_per_step": host_ms, "clocks": clocks.summary()}
     if long_context is not None:
         line["long_context"] = long_context
+    if batched is not None:
+        line["batched_serving"] = batched
     if graph_note is not None:
         line["config"]["cuda_graph"] = False
         line["graph_note"] = graph_note
