@@ -80,6 +80,10 @@ def parse():
                         "batched_serving in the headline line; 0 leaves it out")
     p.add_argument("--sm-reserve", type=int, default=2,
                    help="SMs the persistent grids leave free for the other streams' kernels")
+    p.add_argument("--sharded-sm-reserve", type=int, default=34,
+                   help="the same for the head-sharded step: NCCL's send/recv kernels (the "
+                        "K/V rows gathered into a layer's owner) hold up to 32 SMs while they "
+                        "run, and a persistent grid planned over those SMs would wait for them")
     a = p.parse_args()
     long = a.workload == "long"
     if a.seq_len is None:
@@ -596,6 +600,7 @@ def long_config(a, n):
             "n_kept": int(a.seq_len * (1 - a.ratio)), "d_mem": a.d_mem,
             "parallelism": f"head-sharded x{n}" if n > 1 or a.sharded else "1 GPU",
             "cuda_graph": bool(a.graph),
+            "sm_reserve": a.sharded_sm_reserve if n > 1 or a.sharded else a.sm_reserve,
             "l2": f"inputs larger than L2 ({a.layers} x {a.seq_len * 8 * 128 * 4 >> 20} MiB of K/V)"}
 
 
@@ -671,7 +676,7 @@ def run_long(a, dev, dist, rank, world):
         # memory write overlap the next layers' QK work.  The host issues every
         # layer's collectives in layer order on every rank.
         n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        budget = ops.sm_budget(max(1, n_sms - a.sm_reserve) if a.streams > 1 else 0)
+        budget = ops.sm_budget(max(1, n_sms - a.sharded_sm_reserve))
         streams = [torch.cuda.Stream(dev) for _ in range(max(1, a.streams))]
 
         def step(pairs):
