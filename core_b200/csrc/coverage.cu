@@ -651,27 +651,39 @@ __global__ void __launch_bounds__(kAssignThreads)
     const float inv = 1.0f / fmaxf(cn, 1e-6f);
 #pragma unroll
     for (int j = 0; j < kP; ++j) zc[j] *= inv;
-    // top-2 of this thread's 16 prototypes, ascending index (first maximum wins)
+    // top-2 of this thread's 16 prototypes, ascending index (first maximum
+    // wins).  Four prototypes at a time, each cosine its own chain of 64 FMAs
+    // in column order (the same sums as one at a time), so the chains overlap.
     float c1 = -INFINITY, c2 = -INFINITY;
     int m1 = part;
-    for (int mm = 0; mm < kNP / 4; ++mm) {
-      const int m = 4 * mm + part;
-      const float4* pr = reinterpret_cast<const float4*>(sP + m * kProtoStride);
-      float c = 0.f;
+#pragma unroll 1
+    for (int mg = 0; mg < kNP / 16; ++mg) {
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      const float4* pr[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        pr[q] = reinterpret_cast<const float4*>(sP + (16 * mg + 4 * q + part) * kProtoStride);
 #pragma unroll
       for (int j = 0; j < kP / 4; ++j) {
-        const float4 w = pr[j];
-        c = fmaf(zc[4 * j], w.x, c);
-        c = fmaf(zc[4 * j + 1], w.y, c);
-        c = fmaf(zc[4 * j + 2], w.z, c);
-        c = fmaf(zc[4 * j + 3], w.w, c);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 w = pr[q][j];
+          c[q] = fmaf(zc[4 * j], w.x, c[q]);
+          c[q] = fmaf(zc[4 * j + 1], w.y, c[q]);
+          c[q] = fmaf(zc[4 * j + 2], w.z, c[q]);
+          c[q] = fmaf(zc[4 * j + 3], w.w, c[q]);
+        }
       }
-      if (c > c1) {
-        c2 = c1;
-        c1 = c;
-        m1 = m;
-      } else if (c > c2) {
-        c2 = c;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int m = 16 * mg + 4 * q + part;
+        if (c[q] > c1) {
+          c2 = c1;
+          c1 = c[q];
+          m1 = m;
+        } else if (c[q] > c2) {
+          c2 = c[q];
+        }
       }
     }
     // merge across the 4 threads of the token; equal cosines go to the lower index

@@ -789,13 +789,18 @@ __global__ void __launch_bounds__(256)
 // ===========================================================================
 // recurrence
 // ===========================================================================
+// Blocks [0, m_blocks) update M, one element per thread; the blocks after
+// them update b, one warp per row (lane l sums tiles l, l + 32, ..., then the
+// warp adds the 32 lane sums as a tree), so that no thread walks all the
+// b_bar partials of a row alone.
 __global__ void mw_update_kernel(const float* __restrict__ mpart, int splits, int B, int d_mem,
                                  int d_pad, int kvw, const float* __restrict__ bpart, int n_et,
                                  const float* __restrict__ coef, float eta, float* __restrict__ M,
-                                 float* __restrict__ bst) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long nM = (long long)B * d_mem * kvw;
-  if (i < nM) {
+                                 float* __restrict__ bst, int m_blocks) {
+  if ((int)blockIdx.x < m_blocks) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long nM = (long long)B * d_mem * kvw;
+    if (i >= nM) return;
     const int c = (int)(i % kvw);
     const long long bj = i / kvw;
     const int j = (int)(bj % d_mem);
@@ -806,16 +811,21 @@ __global__ void mw_update_kernel(const float* __restrict__ mpart, int splits, in
     const float mbar = s * eta;
     const float gz = coef[b * 3], pie = coef[b * 3 + 1], den = coef[b * 3 + 2];
     M[i] = (gz * M[i] + pie * mbar) / den;
+    return;
   }
-  const long long nb = (long long)B * d_mem;
-  if (i < nb) {
-    const int j = (int)(i % d_mem);
-    const int b = (int)(i / d_mem);
-    float s = 0.f;
-    for (int t = 0; t < n_et; ++t) s += bpart[((long long)b * n_et + t) * d_pad + j];
+  const long long row = ((long long)(blockIdx.x - m_blocks) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= (long long)B * d_mem) return;  // whole warps: row is uniform in the warp
+  const int j = (int)(row % d_mem);
+  const int b = (int)(row / d_mem);
+  float s = 0.f;
+  for (int t = lane; t < n_et; t += 32) s += bpart[((long long)b * n_et + t) * d_pad + j];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) {
     const float bbar = s * eta;
     const float gz = coef[b * 3], pie = coef[b * 3 + 1], den = coef[b * 3 + 2];
-    bst[i] = (gz * bst[i] + pie * bbar) / den;
+    bst[row] = (gz * bst[row] + pie * bbar) / den;
   }
 }
 
@@ -997,8 +1007,11 @@ static int memory_write_impl(const core_dims_t* d, const void* k, const void* v,
   }
   }
   const long long n = (long long)d->batch * d_mem * m.kvw;
-  mw_update_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(mpart, m.splits, d->batch, d_mem, m.d_pad,
-                                                             m.kvw, bpart, m.n_et, coef, eta, M, b_state);
+  const int m_blocks = (int)((n + 255) / 256);
+  const int b_blocks = (int)(((long long)d->batch * d_mem * 32 + 255) / 256);  // a warp per row of b
+  mw_update_kernel<<<(unsigned)(m_blocks + b_blocks), 256, 0, s>>>(
+      mpart, m.splits, d->batch, d_mem, m.d_pad, m.kvw, bpart, m.n_et, coef, eta, M, b_state,
+      m_blocks);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_update_kernel launch");
   return CORE_OK;
 }
