@@ -30,7 +30,7 @@ namespace attn {
 
 constexpr int kD = 128;
 constexpr int kTile = 128;
-constexpr int kThreads = 256;                    // warp 0 TMA, warp 1 MMA, warps 4-7 softmax
+constexpr int kThreads = 384;  // warp 0 TMA, warp 1 MMA, warps 4-7 / 8-11 softmax (key halves)
 constexpr uint32_t kTileBytes = kTile * kD * 2;  // 32 KB: a Q, K, V or P tile
 constexpr uint32_t kAtomBytes = kTile * 128u;    // 16 KB: 64 columns of 128 rows
 constexpr int kStages = 2;
@@ -111,22 +111,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(bar_q_full, 1);
     mbar_init(bar_q_empty, 1);
-    mbar_init(bar_o_empty, 4);
+    mbar_init(bar_o_empty, 8);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar_k_full(s), 1);
       mbar_init(bar_k_empty(s), 1);
       mbar_init(bar_v_full(s), 1);
       mbar_init(bar_v_empty(s), 1);
       mbar_init(bar_s_full(s), 1);
-      mbar_init(bar_s_empty(s), 4);
-      mbar_init(bar_p_full(s), 4);
+      mbar_init(bar_s_empty(s), 8);
+      mbar_init(bar_p_full(s), 8);
       mbar_init(bar_pv_done(s), 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 512);  // S0 [0,128), S1 [128,256), O [256,384)
+    // S0 [0,128), S1 [128,256), O [256,384); columns 384.. carry the softmax
+    // groups' exchanges (row maxima by tile parity, then row sums)
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
@@ -217,10 +219,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp >= 4) {
-    // ---------------- softmax and epilogue: one thread per query row ----------------
+    // ---------------- softmax and epilogue ----------------
+    // Two warpgroups, one thread per query row in each: group h takes keys
+    // [64 h, 64 h + 64) of every tile and columns [64 h, 64 h + 64) of O.  The
+    // row maximum of a tile is exchanged through TMEM (warps 4 + w and 8 + w
+    // reach the same lanes): column 384 + 2 (tile parity) + h.  Each group
+    // keeps its own partial row sum; they meet in columns 388 + h and are added
+    // group 0 first.
+    const int half = (warp - 4) >> 2;
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(wq * 32) << 16);
+    const uint32_t x_col = lane_base + 3 * kTile;  // column 384 of this warp's lanes
+    const unsigned long long sc2 = f2_pack(p.scale_log2, p.scale_log2);
     int g0 = 0;
     bool ok = true;
     for (long long u = blockIdx.x; u < p.U && ok; u += P) {
@@ -228,80 +239,102 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int i = t.qt * kTile + r;  // query row within Lq
       const int lim = i + p.off;        // last key this row sees
       float m_used = -INFINITY, l = 0.f;
-      for (int j = 0; j < t.n_kt && ok; ++j) {
+      for (int j = 0; j < t.n_kt; ++j) {
         const int g = g0 + j, sb = g & 1;
-        if (!(ok = wait(bar_s_full(sb), (g >> 1) & 1, 1321))) break;
-        tc_fence_after();
-        const int key0 = j * kTile;
-        const bool masked = key0 + kTile - 1 > t.qt * kTile + p.off;  // some row of the tile masks keys
-        const uint32_t tS = lane_base + (uint32_t)(sb * kTile);
-        // pass 1: the tile's row maximum
+        bool got = ok && wait(bar_s_full(sb), (g >> 1) & 1, 1321);
+        got = __all_sync(0xffffffffu, got);
+        const int key0 = j * kTile + half * 64;  // first key of this group's half
+        // some row of the tile masks some key of this half
+        const bool masked = key0 + 63 > t.qt * kTile + p.off;
+        const uint32_t tS = lane_base + (uint32_t)(sb * kTile + half * 64);
         float mx = -INFINITY;
+        if (got) {
+          tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(tS + (uint32_t)(c * 32), v);
+          for (int c = 0; c < 2; ++c) {
+            float v[32];
+            tmem_ld32(tS + (uint32_t)(c * 32), v);
+            if (!masked) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const bool keep = !masked || key0 + c * 32 + e <= lim;
-            mx = fmaxf(mx, keep ? v[e] : -INFINITY);
+              for (int e = 0; e < 32; e += 2) mx = fmax3(mx, v[e], v[e + 1]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) mx = fmaxf(mx, key0 + c * 32 + e <= lim ? v[e] : -INFINITY);
+            }
           }
+          tmem_st1(x_col + (uint32_t)((g & 1) * 2 + half), mx);
+          tc_fence_before();
         }
+        // the groups' halves meet here (also a uniform decision after the waits)
+        if (!named_barrier_and(1, 256, got)) { ok = false; break; }
+        tc_fence_after();
+        mx = fmaxf(mx, tmem_ld1(x_col + (uint32_t)((g & 1) * 2 + (half ^ 1))));
         const float mt = mx * p.scale_log2;  // the scale is positive
         const bool raise = mt > m_used + kRescaleLog2;
-        // TMEM loads and stores are warp-collective: the warp rescales together,
-        // rows that keep their maximum with a factor of exactly 1
+        // both groups take the same decision for a row (same m_used, same mt);
+        // TMEM loads and stores are warp-collective, so a warp rescales
+        // together, rows that keep their maximum with a factor of exactly 1
+        // A wait that gives up below only clears `ok` (warp-uniform): the
+        // groups must reach the same named barriers, so the failure stops them
+        // together at the next one.
         if (__any_sync(0xffffffffu, raise)) {
           if (j > 0) {
-            // rescale O and l once the previous P V product has landed in TMEM
+            // rescale this group's O columns and l once the previous P V product has landed
             const int gp = g - 1;
-            if (!(ok = wait(bar_pv_done(gp & 1), (gp >> 1) & 1, 1322))) break;
+            ok = __all_sync(0xffffffffu, wait(bar_pv_done(gp & 1), (gp >> 1) & 1, 1322));
+          }
+          if (j > 0 && ok) {
             tc_fence_after();
             const float f = raise ? ex2_approx(m_used - mt) : 1.0f;
             l *= f;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
+              const uint32_t ta = lane_base + 2 * kTile + (uint32_t)(half * 64 + c * 32);
               float o[32];
-              tmem_ld32(lane_base + 2 * kTile + (uint32_t)(c * 32), o);
+              tmem_ld32(ta, o);
 #pragma unroll
               for (int e = 0; e < 32; ++e) o[e] *= f;
-              tmem_st32(lane_base + 2 * kTile + (uint32_t)(c * 32), o);
+              tmem_st32(ta, o);
             }
           }
           if (raise) m_used = mt;
         }
         const float msub = m_used == -INFINITY ? 0.f : m_used;
         // the P buffer was last read by the P V product of tile g - 2
-        if (g >= 2 && !(ok = wait(bar_pv_done(sb), ((g >> 1) - 1) & 1, 1323))) break;
-        // pass 2: P = exp2(s * scale * log2e - m), the row sum, P into shared memory
-        float sum = 0.f;
-        const uint32_t prow = sP + sb * kTileBytes + (uint32_t)r * 128u;
+        if (ok && g >= 2) ok = __all_sync(0xffffffffu, wait(bar_pv_done(sb), ((g >> 1) - 1) & 1, 1323));
+        if (!ok) continue;  // the next barrier stops both groups
+        // pass 2: P = exp2(s * scale * log2e - m), the partial row sum, P into shared memory
+        const unsigned long long neg2 = f2_pack(-msub, -msub);
+        unsigned long long acc = 0ull;
+        const uint32_t prow = sP + sb * kTileBytes + (uint32_t)half * kAtomBytes + (uint32_t)r * 128u;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           float v[32];
           tmem_ld32(tS + (uint32_t)(c * 32), v);
+          if (masked) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (key0 + c * 32 + e > lim) v[e] = -INFINITY;  // exp2(-inf) = 0
+          }
           uint32_t h[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const bool k0 = !masked || key0 + c * 32 + e <= lim;
-            const bool k1 = !masked || key0 + c * 32 + e + 1 <= lim;
-            const float p0 = k0 ? ex2_approx(fmaf(v[e], p.scale_log2, -msub)) : 0.f;
-            const float p1 = k1 ? ex2_approx(fmaf(v[e + 1], p.scale_log2, -msub)) : 0.f;
-            sum += p0 + p1;
+            const unsigned long long y = f2_fma(f2_pack(v[e], v[e + 1]), sc2, neg2);
+            const float p0 = ex2_approx(f2_lo(y)), p1 = ex2_approx(f2_hi(y));
+            acc = f2_add(acc, f2_pack(p0, p1));
             h[e >> 1] = pack2<kF16>(p0, p1);
           }
-          // row r, keys [32c, 32c + 32): atom c / 2, 16-byte chunks 4 (c & 1) .. + 3
-          const uint32_t atom = prow + (uint32_t)(c >> 1) * kAtomBytes;
+          // row r, keys [64 half + 32 c, + 32): atom `half`, 16-byte chunks 4 c .. 4 c + 3
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            const int chunk = (c & 1) * 4 + q;
-            const uint32_t dst = atom + (uint32_t)((chunk ^ (r & 7)) << 4);
+            const int chunk = c * 4 + q;
+            const uint32_t dst = prow + (uint32_t)((chunk ^ (r & 7)) << 4);
             asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(h[4 * q]),
                          "r"(h[4 * q + 1]), "r"(h[4 * q + 2]), "r"(h[4 * q + 3])
                          : "memory");
           }
         }
-        l += sum;
+        l += f2_lo(acc) + f2_hi(acc);
         fence_proxy_async_shared();  // P (generic stores) before the MMA reads it
         tc_fence_before();
         __syncwarp();
@@ -310,17 +343,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(bar_p_full(sb));
         }
       }
-      if (!ok) break;
-      // epilogue: O / l and the row LSE
+      // epilogue: O / l and the row LSE (a failure above arrives here with
+      // ok cleared, so both groups take this barrier and stop together)
       const int gl = g0 + t.n_kt - 1;
-      if (!(ok = wait(bar_pv_done(gl & 1), (gl >> 1) & 1, 1324))) break;
+      bool got = ok && wait(bar_pv_done(gl & 1), (gl >> 1) & 1, 1324);
+      got = __all_sync(0xffffffffu, got);
+      if (got) {
+        tmem_st1(x_col + 4u + (uint32_t)half, l);
+        tc_fence_before();
+      }
+      if (!named_barrier_and(1, 256, got)) { ok = false; break; }
       tc_fence_after();
-      const float inv_l = 1.0f / l;
-      uint16_t* orow = static_cast<uint16_t*>(p.out) + (((long long)t.b * p.Lq + i) * p.Hq + t.qh) * kD;
+      const float lo = tmem_ld1(x_col + 4u + (uint32_t)(half ^ 1));
+      const float ltot = half == 0 ? l + lo : lo + l;  // group 0's sum first
+      const float inv_l = 1.0f / ltot;
+      uint16_t* orow = static_cast<uint16_t*>(p.out) + (((long long)t.b * p.Lq + i) * p.Hq + t.qh) * kD + half * 64;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float o[32];
-        tmem_ld32(lane_base + 2 * kTile + (uint32_t)(c * 32), o);
+        tmem_ld32(lane_base + 2 * kTile + (uint32_t)(half * 64 + c * 32), o);
         if (i < p.Lq) {
           uint32_t h[16];
 #pragma unroll
@@ -330,11 +371,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int q = 0; q < 4; ++q) dst[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
         }
       }
-      if (i < p.Lq)
-        p.lse[((long long)t.b * p.Hq + t.qh) * p.Lq + i] = (m_used + log2f(l)) * 0.69314718055994531f;
+      if (half == 0 && i < p.Lq)
+        p.lse[((long long)t.b * p.Hq + t.qh) * p.Lq + i] = (m_used + log2f(ltot)) * 0.69314718055994531f;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_o_empty);
+      // the row sums are read before any group rewrites them: the next unit's
+      // write follows its first tile barrier
       g0 += t.n_kt;
     }
   }

@@ -268,6 +268,24 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       : "memory");
 }
 
+// One 32-bit column of 32 lanes: thread t stores / loads lane (lane_base + t).
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr), "r"(__float_as_uint(v))
+      : "memory");
+}
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r)
+      : "r"(taddr)
+      : "memory");
+  return __uint_as_float(r);
+}
+
 // ---------------------------------------------------------------------------
 // Descriptors
 // ---------------------------------------------------------------------------
