@@ -88,6 +88,23 @@ __device__ __forceinline__ Unit decode(long long u, const Params& p) {
 }
 
 
+// The unit after t, for walking a CTA's contiguous range (key tile fastest,
+// then query block, KV head, batch row) without decode()'s 64-bit divisions.
+__device__ __forceinline__ void advance(Unit& t, const Params& p) {
+  if (++t.kt == p.n_kt) {
+    t.kt = 0;
+    ++t.grp;
+    if (++t.qb == p.n_qb) {
+      t.qb = 0;
+      if (++t.h == p.Hkv) {
+        t.h = 0;
+        ++t.b;
+      }
+    }
+  }
+}
+
+
 // ===========================================================================
 // 1. LSE partial kernel
 // ===========================================================================
@@ -159,8 +176,8 @@ __global__ void __launch_bounds__(kLseThreads, 1)
     if (lane == 0) {
       long long cur = -1;
       int gcount = 0, it = 0;
-      for (long long u = u0; u < u1; ++u) {
-        Unit t = decode(u, p);
+      Unit t = decode(u0, p);
+      for (long long u = u0; u < u1; ++u, advance(t, p)) {
         if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
         if (t.grp != cur) {
           if (gcount > 0 && !wait(bar_q_empty, (gcount - 1) & 1, 101)) break;
@@ -187,8 +204,8 @@ __global__ void __launch_bounds__(kLseThreads, 1)
       long long cur = -1;
       int gcount = 0, it = 0, sub = 0;
       bool ok = true;
-      for (long long u = u0; u < u1 && ok; ++u) {
-        Unit t = decode(u, p);
+      Unit t = decode(u0, p);
+      for (long long u = u0; u < u1 && ok; ++u, advance(t, p)) {
         if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
         if (t.grp != cur) {
           if (!(ok = wait(bar_q_full, gcount & 1, 103))) break;
@@ -249,8 +266,8 @@ __global__ void __launch_bounds__(kLseThreads, 1)
       }
     };
     const unsigned long long sc2 = f2_pack(p.scale_log2, p.scale_log2);
-    for (long long u = u0; u < u1 && ok; ++u) {
-      Unit t = decode(u, p);
+    Unit t = decode(u0, p);
+    for (long long u = u0; u < u1 && ok; ++u, advance(t, p)) {
       if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
       if (t.grp != cur) {
         if (cur >= 0) flush(cu);
@@ -484,8 +501,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       long long cur = -1;
       int gcount = 0, it = 0;
-      for (long long u = u0; u < u1; ++u) {
-        Unit t = decode(u, p);
+      Unit t = decode(u0, p);
+      for (long long u = u0; u < u1; ++u, advance(t, p)) {
         if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
         if (t.grp != cur) {
           if (gcount > 0 && !wait(bar_q_empty, (gcount - 1) & 1, 201)) break;
@@ -518,8 +535,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       long long cur = -1;
       int gcount = 0, it = 0, sub = 0;
       bool ok = true;
-      for (long long u = u0; u < u1 && ok; ++u) {
-        Unit t = decode(u, p);
+      Unit t = decode(u0, p);
+      for (long long u = u0; u < u1 && ok; ++u, advance(t, p)) {
         if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
         if (t.grp != cur) {
           if (!(ok = wait(bar_q_full, gcount & 1, 203))) break;
@@ -567,8 +584,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     long long cur = -1;
     int sub = 0;
     bool ok = true;
-    for (long long u = u0; u < u1 && ok; ++u) {
-      Unit t = decode(u, p);
+    Unit t = decode(u0, p);
+    for (long long u = u0; u < u1 && ok; ++u, advance(t, p)) {
       if (t.kt > kt_last(p, t.qb)) continue;  // above the causal diagonal
       if (t.grp != cur) {
         // (re)load (-lse, log|C_t|) of this query block
