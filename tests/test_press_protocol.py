@@ -103,3 +103,25 @@ def test_unsupported_policies_fail_loudly():
                               compression_ratio=0.5, span_block_size=8)
     with pytest.raises(NotImplementedError):
         press._check_policy()
+
+
+def test_factory_defaults_match_the_standalone_cli():
+    """The reference's standalone CLI loads the press with
+    decoding_compression_interval=128 and no target or buffer size
+    (kvpress/tests/test_core_protocol.py:76-92); the CLI itself is out of
+    scope here, but the factory it calls keeps the same defaults, and the
+    registry key resolves to it."""
+    import inspect
+    sig = inspect.signature(P.load_core_prefill_decoding_press)
+    assert sig.parameters["decoding_compression_interval"].default == 128
+    assert sig.parameters["decoding_target_size"].default is None
+    assert sig.parameters["decoding_hidden_states_buffer_size"].default is None
+    assert sig.parameters["compression_ratio"].default is None
+    assert P.PRESS_REGISTRY["core_full"] is P.load_core_prefill_decoding_press
+    # no target size: decode recompression returns to the retained prefill budget
+    pre = SimpleNamespace(compression_ratio=0.5, compress=Mock(), reset_cache=Mock())
+    dec = P.COREDecodingPress(base_press=pre, compression_interval=128, target_size=1)
+    assert dec.hidden_states_buffer_size == 128
+    combo = P.COREPrefillDecodingPress(prefilling_press=pre, decoding_press=dec)
+    combo.begin_sequence(8192)
+    assert dec.target_size == 4096
