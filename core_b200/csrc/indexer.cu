@@ -379,20 +379,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Per-(head, token) value sums of squares in the arithmetic of the indexer's
 // auxiliary block (squares rounded to bf16 and added in index order, the sum
 // rounded to bf16): out[h * out_stride + b * L + token].  One thread per row,
-// like the indexer, so the sums agree bit for bit.  Many small blocks keep
-// enough loads in flight for HBM; the indexer then reads 4 bytes per row.
-__global__ void value_head_sums_kernel(const __nv_bfloat16* __restrict__ v, int B, int Hkv, int L,
-                                       float* __restrict__ out, long long out_stride) {
-  const long long row = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= (long long)B * Hkv * L) return;
-  const uint4* rowp = reinterpret_cast<const uint4*>(v + row * 128);
-  uint4 w[16];  // the whole 256-byte row in flight at once
+// like the indexer, so the sums agree bit for bit.  Each warp first copies
+// its 32 rows (8 KB) into shared memory with coalesced 16-byte cp.async
+// pieces, all in flight at once; rows are padded to 17 pieces so that the
+// lanes' row reads afterwards hit distinct banks.
+constexpr int kVhsWarps = 4;
+constexpr int kVhsRowsPerBlock = kVhsWarps * 32;
+constexpr int kVhsPad = 17;  // uint4 pieces per staged row (16 + 1)
+
+__global__ void __launch_bounds__(kVhsWarps * 32)
+    value_head_sums_kernel(const __nv_bfloat16* __restrict__ v, int B, int Hkv, int L,
+                           float* __restrict__ out, long long out_stride) {
+  __shared__ __align__(16) uint4 s_rows[kVhsWarps][32 * kVhsPad];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long rows = (long long)B * Hkv * L;
+  const long long row0 = (long long)blockIdx.x * kVhsRowsPerBlock + warp * 32;
+  if (row0 >= rows) return;  // whole warp
+  const int nrows = rows - row0 < 32 ? (int)(rows - row0) : 32;
+  const uint4* src = reinterpret_cast<const uint4*>(v) + row0 * 16;
+  uint4* stage = s_rows[warp];
+  const uint32_t sbase = smem_u32(stage);
 #pragma unroll
-  for (int c = 0; c < 16; ++c) w[c] = __ldg(rowp + c);
+  for (int i = 0; i < 16; ++i) {
+    const int q = lane + 32 * i;  // piece q of the warp's rows: row q / 16, piece q % 16
+    if ((q >> 4) < nrows) cp_async16(sbase + (uint32_t)(((q >> 4) * kVhsPad + (q & 15)) * 16), src + q);
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncwarp();
+  if (lane >= nrows) return;
+  const uint4* rowp = stage + lane * kVhsPad;
   float s = 0.f;
 #pragma unroll
   for (int c = 0; c < 16; ++c) {
-    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w[c]);
+    const uint4 w = rowp[c];
+    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&w);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 f2 = __bfloat1622float2(h2[e]);
@@ -400,6 +421,7 @@ __global__ void value_head_sums_kernel(const __nv_bfloat16* __restrict__ v, int 
       s += bf16_round(f2.y * f2.y);
     }
   }
+  const long long row = row0 + lane;
   const long long bh = row / L;
   const int b = (int)(bh / Hkv), h = (int)(bh % Hkv), t = (int)(row % L);
   out[(long long)h * out_stride + (long long)b * L + t] = bf16_round(s);
@@ -481,7 +503,8 @@ extern "C" int core_value_head_sums(const core_dims_t* d, const void* v, float* 
     return set_error(CORE_ERR_INVALID_ARG, "core_value_head_sums: out_stride < seq_len");
   const long long rows = (long long)d->n_kv_heads * d->seq_len;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  value_head_sums_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
+  value_head_sums_kernel<<<(unsigned)((rows + kVhsRowsPerBlock - 1) / kVhsRowsPerBlock),
+                           kVhsRowsPerBlock, 0, s>>>(
       static_cast<const __nv_bfloat16*>(v), 1, d->n_kv_heads, d->seq_len, out, out_stride);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? CORE_OK : cuda_error(e, "value_head_sums_kernel launch");
@@ -557,7 +580,8 @@ int indexer_scores_split(const core_dims_t* d, const void* v, const int64_t* pos
   if (cv.overflow) return set_error(CORE_ERR_WORKSPACE, "core_indexer_scores: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long rows = BL * d->n_kv_heads;
-  value_head_sums_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(
+  value_head_sums_kernel<<<(unsigned)((rows + kVhsRowsPerBlock - 1) / kVhsRowsPerBlock),
+                           kVhsRowsPerBlock, 0, s>>>(
       static_cast<const __nv_bfloat16*>(v), d->batch, d->n_kv_heads, d->seq_len, hs, BL);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "value_head_sums_kernel launch");

@@ -829,6 +829,59 @@ __global__ void mw_update_kernel(const float* __restrict__ mpart, int splits, in
   }
 }
 
+// The same update with four columns of M per thread: block (x, y) with
+// y < B d_mem takes float4 groups [256 x, 256 x + 256) of row y of M, so the
+// row is a block index and no thread divides; blocks y >= B d_mem (x = 0)
+// update b as above, one warp per row.  Every element is computed with the
+// same expressions, in the same split order, as mw_update_kernel.
+__global__ void mw_update4_kernel(const float4* __restrict__ mpart, int splits, int B, int d_mem,
+                                  int d_pad, int kvw4, const float* __restrict__ bpart, int n_et,
+                                  const float* __restrict__ coef, float eta, float4* __restrict__ M,
+                                  float* __restrict__ bst) {
+  const int rows = B * d_mem;
+  const int y = blockIdx.y;
+  if (y < rows) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= kvw4) return;
+    const int b = y / d_mem, j = y - b * d_mem;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4 t = mpart[(((long long)sp * B + b) * d_pad + j) * kvw4 + c];
+      s.x += t.x;
+      s.y += t.y;
+      s.z += t.z;
+      s.w += t.w;
+    }
+    const float gz = coef[b * 3], pie = coef[b * 3 + 1], den = coef[b * 3 + 2];
+    float4* mp = M + (long long)y * kvw4 + c;
+    float4 m = *mp;
+    float mbar = s.x * eta;
+    m.x = (gz * m.x + pie * mbar) / den;
+    mbar = s.y * eta;
+    m.y = (gz * m.y + pie * mbar) / den;
+    mbar = s.z * eta;
+    m.z = (gz * m.z + pie * mbar) / den;
+    mbar = s.w * eta;
+    m.w = (gz * m.w + pie * mbar) / den;
+    *mp = m;
+    return;
+  }
+  if (blockIdx.x != 0) return;
+  const int row = (y - rows) * (int)(blockDim.x >> 5) + (int)(threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;  // whole warps: row is uniform in the warp
+  const int b = row / d_mem, j = row - b * d_mem;
+  float sb = 0.f;
+  for (int t = lane; t < n_et; t += 32) sb += bpart[((long long)b * n_et + t) * d_pad + j];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sb += __shfl_xor_sync(0xffffffffu, sb, o);
+  if (lane == 0) {
+    const float bbar = sb * eta;
+    const float gz = coef[b * 3], pie = coef[b * 3 + 1], den = coef[b * 3 + 2];
+    bst[row] = (gz * bst[row] + pie * bbar) / den;
+  }
+}
+
 }  // namespace mw
 }  // namespace core
 
@@ -1007,11 +1060,22 @@ static int memory_write_impl(const core_dims_t* d, const void* k, const void* v,
   }
   }
   const long long n = (long long)d->batch * d_mem * m.kvw;
-  const int m_blocks = (int)((n + 255) / 256);
-  const int b_blocks = (int)(((long long)d->batch * d_mem * 32 + 255) / 256);  // a warp per row of b
-  mw_update_kernel<<<(unsigned)(m_blocks + b_blocks), 256, 0, s>>>(
-      mpart, m.splits, d->batch, d_mem, m.d_pad, m.kvw, bpart, m.n_et, coef, eta, M, b_state,
-      m_blocks);
+  const long long rows = (long long)d->batch * d_mem;
+  const long long b_rows = (rows + 7) / 8;  // 8 warps, one row of b each, per block
+  if (m.kvw % 4 == 0 && reinterpret_cast<uintptr_t>(M) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(mpart) % 16 == 0 && rows + b_rows <= 65535) {
+    const int kvw4 = m.kvw / 4;
+    const dim3 grid((unsigned)((kvw4 + 255) / 256), (unsigned)(rows + b_rows));
+    mw_update4_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const float4*>(mpart), m.splits,
+                                           d->batch, d_mem, m.d_pad, kvw4, bpart, m.n_et, coef, eta,
+                                           reinterpret_cast<float4*>(M), b_state);
+  } else {
+    const int m_blocks = (int)((n + 255) / 256);
+    const int b_blocks = (int)(((long long)d->batch * d_mem * 32 + 255) / 256);  // a warp per row of b
+    mw_update_kernel<<<(unsigned)(m_blocks + b_blocks), 256, 0, s>>>(
+        mpart, m.splits, d->batch, d_mem, m.d_pad, m.kvw, bpart, m.n_et, coef, eta, M, b_state,
+        m_blocks);
+  }
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_error(e, "mw_update_kernel launch");
   return CORE_OK;
 }
