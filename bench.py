@@ -64,7 +64,10 @@ def parse():
     p.add_argument("--decode-tokens", type=int, default=512)
     p.add_argument("--interval", type=int, default=128)
     p.add_argument("--decode-ratio", type=float, default=0.5)
-    p.add_argument("--streams", type=int, default=3, help="layers compressed concurrently")
+    p.add_argument("--streams", type=int, default=4, help="layers compressed concurrently")
+    p.add_argument("--sharded-streams", type=int, default=3,
+                   help="the same for the head-sharded step (its layers' collectives are "
+                        "issued in layer order on every rank)")
     p.add_argument("--sharded", action="store_true",
                    help="--workload long: the head-sharded step even on one rank (under torchrun)")
     p.add_argument("--graph", action=argparse.BooleanOptionalAction, default=True,
@@ -78,7 +81,7 @@ def parse():
                    help="timed steps of batched serving (8 sequences x 32768 tokens, r=0.75, "
                         "32 layers, split over the ranks: 8/N sequences per rank) reported as "
                         "batched_serving in the headline line; 0 leaves it out")
-    p.add_argument("--sm-reserve", type=int, default=2,
+    p.add_argument("--sm-reserve", type=int, default=8,
                    help="SMs the persistent grids leave free for the other streams' kernels")
     p.add_argument("--sharded-sm-reserve", type=int, default=34,
                    help="the same for the head-sharded step: NCCL's send/recv kernels (the "
@@ -621,6 +624,7 @@ def long_config(a, n):
             "parallelism": f"head-sharded x{n}" if n > 1 or a.sharded else "1 GPU",
             "cuda_graph": bool(a.graph),
             "sm_reserve": a.sharded_sm_reserve if n > 1 or a.sharded else a.sm_reserve,
+            "layers_in_flight": a.sharded_streams if n > 1 or a.sharded else a.streams,
             "l2": f"inputs larger than L2 ({a.layers} x {a.seq_len * 8 * 128 * 4 >> 20} MiB of K/V)"}
 
 
@@ -697,7 +701,7 @@ def run_long(a, dev, dist, rank, world):
         # layer's collectives in layer order on every rank.
         n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
         budget = ops.sm_budget(max(1, n_sms - a.sharded_sm_reserve))
-        streams = [torch.cuda.Stream(dev) for _ in range(max(1, a.streams))]
+        streams = [torch.cuda.Stream(dev) for _ in range(max(1, a.sharded_streams))]
 
         def step(pairs):
             main = torch.cuda.current_stream(dev)
