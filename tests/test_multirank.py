@@ -65,3 +65,24 @@ def test_reference_arm_only_on_rank_zero(capsys):
     line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["cpu_baseline"]["kind"] == "port"
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["value"] > 0
+
+
+def test_bench_defaults_in_the_reported_config():
+    """The headline step runs four layers in flight on 140 SMs' persistent
+    grids; the head-sharded long-context step keeps three streams and leaves
+    34 SMs to NCCL.  The JSON line reports what ran."""
+    import sys
+    import bench
+    argv = sys.argv
+    try:
+        sys.argv = ["bench.py"]
+        a = bench.parse()
+    finally:
+        sys.argv = argv
+    c = bench.config_dict(a, 1)
+    assert (c["layers_in_flight"], c["sm_reserve"]) == (4, 8)
+    assert c["seq_len"] == 16384 and c["query_buffer"] == 128 and c["compression_ratio"] == 0.75
+    a.seq_len, a.n_queries, a.ratio = 131072, 512, 0.9
+    lc = bench.long_config(a, 2)
+    assert (lc["layers_in_flight"], lc["sm_reserve"]) == (3, 34)
+    assert bench.long_config(a, 1)["layers_in_flight"] == 4
